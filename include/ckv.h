@@ -1,0 +1,222 @@
+/*
+ * ckv.h -- C ABI of the B200-native CircuitKV prefill scoring + eviction path.
+ *
+ * The library replaces, for one prefill layer, the reference's
+ * CircuitKVCluster.update_kv(key_states, query_states, value_states,
+ * attention_mask, num_key_value_groups)
+ * (KVCache-Factory/pyramidkv/pyramidkv_utils.py:2775-3519): window attention,
+ * entropy-aware head pooling, the absorbing-Markov (Neumann) importance solve,
+ * smoothing, rank-MAX selection, and the K/V gather.  It also replaces the
+ * influence-walker pair of circuit_kv._C.CircuitGraph
+ * (CircuitKV/csrc/pybind.cpp:263-300, circuit_manager.cpp:1190-1311).
+ *
+ * Conventions
+ *   - All tensor arguments are raw device pointers; strides are in ELEMENTS.
+ *   - Every entry point returns an int status (CKV_OK == 0, negative on error),
+ *     never throws, and never synchronises the host.  Work is enqueued on the
+ *     caller's stream.  ckv_last_error_string() describes the last failure of
+ *     the calling thread.
+ *   - The caller owns all memory: inputs, outputs and a workspace sized by
+ *     ckv_workspace_size().  A workspace may be reused by calls that are
+ *     ordered on one stream; calls that overlap on the GPU need separate
+ *     workspaces.
+ *   - Device-side failures (a bounded wait that ran out, an inconsistent
+ *     count) are recorded in the workspace's status word and read back with
+ *     ckv_read_status(); no kernel traps.
+ */
+#ifndef CKV_H_
+#define CKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ckv_stream_t;   /* == cudaStream_t */
+
+enum ckv_status {
+  CKV_OK = 0,
+  CKV_ERR_ARG = -1,          /* bad shape, stride, pointer or parameter */
+  CKV_ERR_DTYPE = -2,        /* unsupported dtype */
+  CKV_ERR_UNSUPPORTED = -3,  /* a parameter combination this build does not implement */
+  CKV_ERR_WORKSPACE = -4,    /* workspace too small or misaligned */
+  CKV_ERR_CUDA = -5,         /* a CUDA runtime call failed */
+  CKV_ERR_DEVICE = -6        /* a kernel recorded a failure in the status word */
+};
+
+enum ckv_dtype { CKV_BF16 = 0, CKV_FP16 = 1, CKV_FP32 = 2 };
+
+/* combination_mode of PU:1308 */
+enum ckv_combination {
+  CKV_COMB_DIS = 0,        /* MAX(rank QI, rank HI) (default) */
+  CKV_COMB_MAX = 1,        /* MAX(rank H2O, rank influence); "geometric" and "sum" take this branch */
+  CKV_COMB_WEIGHTED = 2,   /* h2o_weight * rank H2O + (1 - h2o_weight) * rank influence */
+  CKV_COMB_UNION = 3,      /* union of QI / HI top-k split by qi_ratio */
+  CKV_COMB_UNION_DA = 4    /* union on DA-weighted QI / HI */
+};
+
+/*
+ * Mirrors the kwargs of CircuitKVCluster.__init__ (PU:1244-1331) that the
+ * prefill path reads.  Booleans are 0/1.  ckv_default_params() fills the
+ * values KVCache-Factory's run_longbench.py passes by default
+ * (run_longbench.py:295-296, 505-548).
+ */
+typedef struct ckv_params {
+  int32_t window_size;          /* W */
+  int32_t max_capacity_prompt;  /* B: total kept tokens incl. sinks and window */
+  int32_t sink_size;
+  int32_t neumann_iterations;
+  float neumann_temperature;
+  float neumann_gamma;
+  float qi_gamma;               /* per-head mode; already resolved (no None) */
+  float hi_gamma;
+  int32_t combination_mode;     /* enum ckv_combination */
+  float h2o_weight;
+  float qi_ratio;
+  int32_t ablate_qi;
+  int32_t ablate_hi;
+  int32_t per_head_eviction;
+  int32_t true_hub_hi;
+  int32_t entropy_adaptive;
+  int32_t smoothing_kernel;
+  int32_t smooth_hi_only;
+  int32_t use_gaussian;
+  int32_t qi_kernel_size;
+  int32_t hi_kernel_size;
+  float gaussian_sigma;
+  int32_t entropy_aware;
+  int32_t top_k_heads;
+  int32_t head_selection_mode;  /* 0 = entropy, 1 = mass */
+  int32_t hi_pooling_mode;      /* 0 = mean, 1 = max */
+  float hi_mass_threshold;
+  int32_t hi_top_k_heads;
+  float hi_mass_cdf;
+  int32_t use_bridge_importance;
+  int32_t bi_kernel_size;
+} ckv_params;
+
+/*
+ * One layer's inputs, batch 1 (the reference's bsz == 1 semantics).
+ * q: [num_heads, n, head_dim] view; only its last W rows are read.
+ * k, v: the DISTINCT KV heads, [num_kv_heads, n, head_dim] view.  For the
+ * reference's repeat_kv'd [1, H, n, D] tensors pass kv_head_stride =
+ * groups * (their head stride): query head h reads KV head h / groups.
+ */
+typedef struct ckv_layer {
+  const void* q;
+  int64_t q_head_stride, q_tok_stride;
+  const void* k;
+  int64_t k_head_stride, k_tok_stride;
+  const void* v;
+  int64_t v_head_stride, v_tok_stride;
+  int32_t n;             /* sequence length (q_len of PU:2806) */
+  int32_t num_heads;     /* H (query heads) */
+  int32_t num_kv_heads;  /* H / num_key_value_groups */
+  int32_t head_dim;      /* D (128) */
+  int32_t dtype;         /* enum ckv_dtype, shared by q, k, v and the K/V outputs */
+} ckv_layer;
+
+/* Outputs of one layer.  out_k / out_v: contiguous [H, out_len, D] in the input
+ * dtype.  out_idx: the kept prefix positions in ascending order (sinks
+ * included, local window excluded) -- [out_len - W] for shared eviction,
+ * [H, out_len - W] for per-head eviction.  out_scores (optional, may be NULL):
+ * fp32 [n] combined score of every position (shared eviction only). */
+typedef struct ckv_outputs {
+  void* out_k;
+  void* out_v;
+  int32_t* out_idx;
+  float* out_scores;
+} ckv_outputs;
+
+/* Fill *p with the CLI defaults of the reference (see above). */
+void ckv_default_params(ckv_params* p);
+
+/* Number of tokens each head keeps for a layer of length n (== n when
+ * n < max_capacity_prompt: the reference returns its inputs unchanged). */
+int ckv_output_len(const ckv_params* p, int32_t n, int32_t* out_len);
+
+/* Workspace bytes one ckv_score_evict call on a layer of (n, H, D) needs. */
+int ckv_workspace_size(const ckv_params* p, int32_t n, int32_t num_heads, int32_t num_kv_heads,
+                       int32_t head_dim, size_t* bytes);
+
+/* Replaces CircuitKVCluster.update_kv (PU:2775-3519) for one layer with
+ * n >= max_capacity_prompt.  Enqueues the whole path on `stream`. */
+int ckv_score_evict(const ckv_params* p, const ckv_layer* layer, void* workspace,
+                    size_t workspace_bytes, const ckv_outputs* out, ckv_stream_t stream);
+
+/* Many independent layers / sequences (each with batch-1 semantics, ragged n
+ * allowed) in one call: equivalent to `count` ckv_score_evict calls whose
+ * workspaces are consecutive slices of `workspace` (each slice sized by
+ * ckv_workspace_size for that layer, rounded up to 256 bytes). */
+int ckv_score_evict_batched(const ckv_params* p, const ckv_layer* layers, int32_t count,
+                            void* workspace, size_t workspace_bytes, const ckv_outputs* outs,
+                            ckv_stream_t stream);
+
+/* Reads (synchronising on `stream`) and clears the device status word of a
+ * workspace: 0 when every kernel since the last read finished normally. */
+int ckv_read_status(void* workspace, ckv_stream_t stream, int32_t* device_status);
+
+/* ---- stage entry points (used by the parity tests; same kernels as above) --- */
+
+/* Selection from given fp32 score vectors (PU:3131-3196 + PU:2591-2644 /
+ * PU:2489-2589): smoothing (dis mode), ranks, combination, keep mask and
+ * compaction.  For dis: a = QI, b = HI, c = BI or NULL.  For max / weighted:
+ * a = influence, b = H2O.  For union modes: a = QI, b = HI (already
+ * DA-weighted for union_da).  Writes out_idx (ascending kept prefix positions,
+ * length returned in *kept on the host after a synchronise) and optionally
+ * out_scores [n]. */
+int ckv_select_scores(const ckv_params* p, int32_t n, const float* a, const float* b,
+                      const float* c, void* workspace, size_t workspace_bytes, int32_t* out_idx,
+                      float* out_scores, ckv_stream_t stream);
+
+/* The absorption solve alone (PU:2060-2206, or PU:1939-2058 when rows_hi is
+ * NULL and single_chain != 0): pooled window rows [W, n] fp32 in, finished
+ * [n] scores out (sinks = 1% of the total, divided by the max). */
+int ckv_neumann_rows(const ckv_params* p, int32_t n, const float* rows_qi, const float* rows_hi,
+                     int32_t single_chain, void* workspace, size_t workspace_bytes,
+                     float* out_qi, float* out_hi, int32_t* out_steps, ckv_stream_t stream);
+
+/* Window attention statistics and pooling alone (PU:2874-2999): per-head
+ * entropy and transient mass [H] (fp32), the chosen head sets as bit masks
+ * (bit h set), and the pooled rows [W, n] fp32 (rows_hi untouched when HI
+ * reuses the QI matrix). */
+int ckv_window_pool(const ckv_params* p, const ckv_layer* layer, void* workspace,
+                    size_t workspace_bytes, float* out_entropy, float* out_mass,
+                    uint64_t* out_qi_heads, uint64_t* out_hi_heads, float* rows_qi, float* rows_hi,
+                    ckv_stream_t stream);
+
+/* ---- influence walker (legacy use_neumann=False path) ------------------------
+ * Replaces CircuitGraph.update_and_step_influence_walker + get_influence_scores
+ * (CircuitKV/csrc/pybind.cpp:263-300; circuit_manager.cpp:1190-1311;
+ * influence_walker.cu:66-456) on the structured full_attn defined by pooled
+ * window rows [W, n] fp32 (PU:3003-3027).  rng_mode 0 = Philox4x32-10
+ * (counter-based; stream = (seed, walker id, step)), 1 = PCG-XSH-RR seeded as
+ * the reference (seed + 3000 by CircuitGraph, per walker pcg_init(seed + id, id)).
+ * Writes normalised scores [n] (and raw visit counts [n] if visits != NULL). */
+int ckv_influence_walk(const ckv_params* p, int32_t n, const float* rows, int32_t current_idx,
+                       int32_t num_walkers, int32_t max_steps, int32_t sink_size, float temperature,
+                       float explore_temp, float explore_ratio, uint64_t seed, int32_t rng_mode,
+                       void* workspace, size_t workspace_bytes, float* scores, float* visits,
+                       ckv_stream_t stream);
+
+/* Per-stage timing (no counterpart in the reference; for benchmarks): while
+ * set, each ckv_score_evict call on this thread records events[0] before its
+ * first kernel and events[i] after its i-th stage (window moments, pooling,
+ * pooling re-run, sweep maps, sweep terms, aux, selection, gather: 9 events).
+ * Records are graph-capturable (external event records).  The array must stay
+ * valid while set; count 0 clears it. */
+int ckv_set_stage_events(void* const* events, int32_t count);
+
+/* Human-readable description of the calling thread's last error. */
+const char* ckv_last_error_string(void);
+
+/* Library version string ("circuitkv-b200 <semver>"). */
+const char* ckv_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CKV_H_ */

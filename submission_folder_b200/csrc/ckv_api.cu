@@ -1,0 +1,449 @@
+// C ABI of the CircuitKV prefill scoring + eviction path (include/ckv.h):
+// parameter checks, the per-layer plan and workspace carve-up, and the launch
+// sequence that replaces CircuitKVCluster.update_kv
+// (KVCache-Factory/pyramidkv/pyramidkv_utils.py:2775-3519).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "ckv_common.cuh"
+#include "ckv_gather.h"
+#include "ckv_neumann.h"
+#include "ckv_plan.h"
+#include "ckv_select.h"
+#include "ckv_window.h"
+
+namespace ckv {
+
+static thread_local std::string g_last_error = "no error";
+
+// Optional per-stage timing: events recorded (as graph-capturable external
+// records) before the first and after every kernel of a layer call.
+static thread_local cudaEvent_t* g_stage_events = nullptr;
+static thread_local int g_stage_count = 0;
+static thread_local int g_stage_next = 0;
+
+void stage_mark(cudaStream_t st) {
+  if (g_stage_events && g_stage_next < g_stage_count)
+    cudaEventRecordWithFlags(g_stage_events[g_stage_next++], st, cudaEventRecordExternal);
+}
+
+static int fail(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return CKV_ERR_CUDA;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan* out,
+              const char** why) {
+  Plan pl;
+  memset(&pl, 0, sizeof(pl));
+  if (dtype != CKV_BF16 && dtype != CKV_FP16 && dtype != CKV_FP32) { *why = "dtype must be bf16, fp16 or fp32"; return CKV_ERR_DTYPE; }
+  if (n <= 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0) { *why = "need n > 0 and num_heads divisible by num_kv_heads"; return CKV_ERR_ARG; }
+  if (H > kMaxHeads) { *why = "at most 64 query heads"; return CKV_ERR_UNSUPPORTED; }
+  if (D != kHeadDim) { *why = "head_dim must be 128"; return CKV_ERR_UNSUPPORTED; }
+  if (p.window_size <= 0 || p.sink_size < 0) { *why = "window_size must be > 0 and sink_size >= 0"; return CKV_ERR_ARG; }
+  if (p.neumann_iterations < 1 || p.neumann_iterations > kMaxIters) { *why = "neumann_iterations must be in [1, 16]"; return CKV_ERR_UNSUPPORTED; }
+  pl.n = n; pl.H = H; pl.Hkv = Hkv; pl.G = H / Hkv; pl.D = D; pl.dtype = dtype;
+  pl.W = p.window_size; pl.s = p.sink_size; pl.K = p.neumann_iterations;
+  pl.mode = p.combination_mode;
+  pl.per_head = p.per_head_eviction;
+  if (pl.mode < 0 || pl.mode > CKV_COMB_UNION_DA) { *why = "unknown combination_mode"; return CKV_ERR_ARG; }
+  if (n < p.max_capacity_prompt) {
+    // the reference returns its inputs unchanged (PU:2864)
+    pl.out_len = n;
+    pl.total = align256(sizeof(Header));
+    *out = pl;
+    return CKV_OK;
+  }
+  if (pl.per_head) { *why = "per_head_eviction is not built yet"; return CKV_ERR_UNSUPPORTED; }
+  if (pl.mode == CKV_COMB_WEIGHTED) { *why = "combination_mode 'weighted' is not built yet"; return CKV_ERR_UNSUPPORTED; }
+  if (pl.W > kMaxWindow) { *why = "window_size must be <= 128"; return CKV_ERR_UNSUPPORTED; }
+  pl.rows_per_warp = (dtype == CKV_FP32) ? 16 : 32;
+  pl.rows_per_batch = kWarps * pl.rows_per_warp;
+  if (pl.W % pl.rows_per_warp != 0 || pl.rows_per_batch % pl.W != 0) {
+    *why = "window_size must be 32, 64 or 128 (16-bit) / 16, 32, 64 or 128 (fp32)";
+    return CKV_ERR_UNSUPPORTED;
+  }
+  if (pl.W > pl.rows_per_batch) { *why = "window_size too large for this dtype"; return CKV_ERR_UNSUPPORTED; }
+  pl.heads_per_batch = pl.rows_per_batch / pl.W;
+  if (pl.heads_per_batch > H) pl.heads_per_batch = H;
+  if (H % pl.heads_per_batch != 0) { *why = "num_heads must be a multiple of the heads per window batch"; return CKV_ERR_UNSUPPORTED; }
+  // a batch smaller than rows_per_batch would leave warps idle: require full batches
+  if (pl.heads_per_batch * pl.W != pl.rows_per_batch) { *why = "num_heads * window_size too small"; return CKV_ERR_UNSUPPORTED; }
+  pl.nbatch = H / pl.heads_per_batch;
+  int ktiles = 0;
+  for (int b = 0; b < pl.nbatch; ++b) {
+    const int h0 = b * pl.heads_per_batch;
+    const int ng = (h0 + pl.heads_per_batch - 1) / pl.G - h0 / pl.G + 1;
+    ktiles = ng > ktiles ? ng : ktiles;
+  }
+  pl.ktiles_per_batch = ktiles;
+  pl.n_p = n - pl.W;
+  if (pl.n_p < pl.s) { *why = "sequence shorter than sink_size + window_size"; return CKV_ERR_UNSUPPORTED; }
+  // keep-set sizes (PU:2616-2644)
+  const int target = p.max_capacity_prompt > pl.s + pl.W ? p.max_capacity_prompt : pl.s + pl.W;
+  const int forced = pl.s + pl.W;                 // n - W >= s
+  const int cand = n - forced;
+  int remaining = target - forced;
+  if (remaining < 0) remaining = 0;
+  pl.kk = remaining < cand ? remaining : cand;
+  pl.out_len = pl.s + pl.kk + pl.W;
+  if (pl.kk + pl.s + pl.W > 8192) { *why = "budget above 8192 tokens is not supported"; return CKV_ERR_UNSUPPORTED; }
+  if (pl.mode == CKV_COMB_UNION || pl.mode == CKV_COMB_UNION_DA) {
+    if (2 * pl.kk > 8192) { *why = "union budget above 4096 tokens is not supported"; return CKV_ERR_UNSUPPORTED; }
+  }
+  pl.nchains = (pl.mode == CKV_COMB_MAX || pl.mode == CKV_COMB_WEIGHTED) ? 1 : 2;
+  pl.hi_rows = (pl.nchains == 2 && p.entropy_aware) ? 1 : 0;
+  pl.ncol_tiles = (n + kColTile - 1) / kColTile;
+  pl.n_pad = pl.ncol_tiles * kColTile;
+  int chunks = (296 + pl.nbatch - 1) / pl.nbatch;
+  if (chunks > pl.ncol_tiles) chunks = pl.ncol_tiles;
+  if (chunks < 1) chunks = 1;
+  pl.tiles_per_chunk = (pl.ncol_tiles + chunks - 1) / chunks;
+  pl.nstat_chunks = (pl.ncol_tiles + pl.tiles_per_chunk - 1) / pl.tiles_per_chunk;
+  pl.nscan = (pl.n_p + kScanChunk - 1) / kScanChunk;
+  if (pl.nscan < 1) pl.nscan = 1;
+  if (window_smem_bytes(pl, true) > 227 * 1024 || window_smem_bytes(pl, false) > 227 * 1024) {
+    *why = "window tile does not fit in shared memory"; return CKV_ERR_UNSUPPORTED;
+  }
+  // workspace carve-up
+  size_t off = align256(sizeof(Header));
+  auto take = [&](size_t bytes) { const size_t o = off; off = align256(off + bytes); return o; };
+  const size_t HW = (size_t)H * pl.W;
+  pl.off_stats = take((size_t)pl.nstat_chunks * HW * 16);
+  pl.off_lse = take(HW * 4);
+  pl.off_spec = take((size_t)4 * H * 4);
+  pl.off_epart = take((size_t)pl.ncol_tiles * HW * 4);
+  pl.off_mpart = take((size_t)pl.ncol_tiles * HW * 4);
+  pl.off_rows_qi = take((size_t)pl.W * pl.n_pad * 4);
+  pl.off_rows_hi = take((size_t)pl.W * pl.n_pad * 4);
+  pl.off_colsum = take((size_t)2 * pl.n_pad * 4);
+  pl.off_gtile = take((size_t)2 * pl.ncol_tiles * 4);
+  pl.off_rspart = take((size_t)2 * pl.ncol_tiles * pl.W * 4);
+  pl.off_wk = take((size_t)2 * pl.K * pl.W * 4);
+  pl.off_yk = take((size_t)2 * (pl.K + 1) * pl.W * 4);
+  pl.off_ymax = take((size_t)2 * (pl.K + 1) * 4);
+  pl.off_bk = take((size_t)2 * pl.K * pl.n_p * 4 + 4);
+  pl.off_cg = take((size_t)2 * pl.n_p * 8 + 8);
+  pl.off_agg = take((size_t)2 * pl.nscan * 2 * kMaxIters * 4);
+  pl.off_cum = take((size_t)2 * (pl.K + 1) * pl.n_p * 4 + 4);
+  pl.off_cmax = take((size_t)2 * pl.nscan * (kMaxIters + 1) * 4);
+  pl.sel_bytes = (size_t)6 * n * 4 + (size_t)n * 4 + (size_t)n;
+  pl.off_sel = take(pl.sel_bytes);
+  pl.off_ph = off;
+  pl.total = off;
+  *out = pl;
+  return CKV_OK;
+}
+
+static int check_layer(const ckv_layer* L) {
+  if (!L || !L->q || !L->k || !L->v) return fail(CKV_ERR_ARG, "null layer or tensor pointer");
+  const size_t es = L->dtype == CKV_FP32 ? 4 : 2;
+  auto al = [&](const void* p, int64_t hs, int64_t ts) {
+    return ((uintptr_t)p % 16 == 0) && ((hs * (int64_t)es) % 16 == 0) && ((ts * (int64_t)es) % 16 == 0);
+  };
+  if (!al(L->q, L->q_head_stride, L->q_tok_stride) || !al(L->k, L->k_head_stride, L->k_tok_stride) ||
+      !al(L->v, L->v_head_stride, L->v_tok_stride))
+    return fail(CKV_ERR_ARG, "tensor pointers and strides must be 16-byte aligned (contiguous head_dim rows)");
+  return CKV_OK;
+}
+
+static int check_ws(const Plan& pl, void* ws, size_t bytes) {
+  if (!ws || (uintptr_t)ws % 256 != 0) return fail(CKV_ERR_WORKSPACE, "workspace must be 256-byte aligned and non-null");
+  if (bytes < pl.total) return fail(CKV_ERR_WORKSPACE, "workspace too small (see ckv_workspace_size)");
+  return CKV_OK;
+}
+
+static int launch_gather_layer(const Plan& pl, const ckv_layer* L, const ckv_outputs* out,
+                               const int32_t* idx, int identity, cudaStream_t st) {
+  GatherArgs g;
+  g.k = L->k; g.khs = L->k_head_stride; g.kts = L->k_tok_stride;
+  g.v = L->v; g.vhs = L->v_head_stride; g.vts = L->v_tok_stride;
+  g.out_k = out->out_k; g.out_v = out->out_v; g.idx = idx;
+  g.n = pl.n; g.W = identity ? 0 : pl.W; g.H = pl.H; g.Hkv = pl.Hkv; g.G = pl.G; g.D = pl.D;
+  g.out_len = pl.out_len; g.per_head = pl.per_head; g.identity = identity;
+  const cudaError_t e = launch_gather(g, pl.dtype, st);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "gather launch");
+}
+
+static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* workspace,
+                           size_t ws_bytes, const ckv_outputs* out, cudaStream_t st) {
+  if (!p || !out || !out->out_k || !out->out_v) return fail(CKV_ERR_ARG, "null params or outputs");
+  int rc = check_layer(L);
+  if (rc) return rc;
+  Plan pl;
+  const char* why = "";
+  rc = make_plan(*p, L->n, L->num_heads, L->num_kv_heads, L->head_dim, L->dtype, &pl, &why);
+  if (rc) return fail(rc, why);
+  if (L->n < p->max_capacity_prompt) return launch_gather_layer(pl, L, out, nullptr, 1, st);
+  if (!out->out_idx) return fail(CKV_ERR_ARG, "out_idx is required");
+  rc = check_ws(pl, workspace, ws_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(Header), st);
+  if (e != cudaSuccess) return cuda_fail(e, "workspace header reset");
+  g_stage_next = 0;
+  stage_mark(st);
+  WinArgs wa;
+  wa.q = L->q; wa.qhs = L->q_head_stride; wa.qts = L->q_tok_stride;
+  wa.k = L->k; wa.khs = L->k_head_stride; wa.kts = L->k_tok_stride;
+  wa.ws = ws; wa.fixup_pass = 0; wa.p = *p; wa.pl = pl;
+  for (int s = 0; s < 3; ++s) {
+    e = launch_window_stage(wa, s, st);
+    if (e != cudaSuccess) return cuda_fail(e, "window kernels");
+    stage_mark(st);
+  }
+  e = launch_sweep(pl, *p, ws, st);
+  if (e != cudaSuccess) return cuda_fail(e, "sweep kernels");
+  stage_mark(st);
+  if (pl.mode == CKV_COMB_MAX || (pl.mode == CKV_COMB_DIS && p->use_bridge_importance)) {
+    e = launch_aux(pl, *p, ws, st);
+    if (e != cudaSuccess) return cuda_fail(e, "aux kernel");
+  }
+  stage_mark(st);
+  SelArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.pl = pl; sa.p = *p; sa.ws = ws; sa.out_idx = out->out_idx; sa.out_scores = out->out_scores;
+  e = launch_select(sa, st);
+  if (e != cudaSuccess) return cuda_fail(e, "select kernel");
+  stage_mark(st);
+  const int rc2 = launch_gather_layer(pl, L, out, out->out_idx, 0, st);
+  stage_mark(st);
+  return rc2;
+}
+
+}  // namespace ckv
+
+using namespace ckv;
+
+extern "C" {
+
+void ckv_default_params(ckv_params* p) {
+  if (!p) return;
+  memset(p, 0, sizeof(*p));
+  p->window_size = 64;
+  p->max_capacity_prompt = 2048;
+  p->sink_size = 4;
+  p->neumann_iterations = 10;
+  p->neumann_temperature = 1.0f;
+  p->neumann_gamma = 1.0f;
+  p->qi_gamma = 1.0f;
+  p->hi_gamma = 1.0f;
+  p->combination_mode = CKV_COMB_DIS;
+  p->h2o_weight = 0.5f;
+  p->qi_ratio = 0.5f;
+  p->entropy_adaptive = 1;
+  p->use_gaussian = 1;
+  p->qi_kernel_size = 3;
+  p->hi_kernel_size = 5;
+  p->gaussian_sigma = 1.0f;
+  p->entropy_aware = 1;
+  p->top_k_heads = 10;
+  p->hi_mass_threshold = 0.5f;
+  p->bi_kernel_size = 5;
+}
+
+int ckv_output_len(const ckv_params* p, int32_t n, int32_t* out_len) {
+  if (!p || !out_len) return fail(CKV_ERR_ARG, "null argument");
+  Plan pl;
+  const char* why = "";
+  const int rc = make_plan(*p, n, 32, 8, 128, CKV_BF16, &pl, &why);
+  if (rc) return fail(rc, why);
+  *out_len = pl.out_len;
+  return CKV_OK;
+}
+
+int ckv_workspace_size(const ckv_params* p, int32_t n, int32_t num_heads, int32_t num_kv_heads,
+                       int32_t head_dim, size_t* bytes) {
+  if (!p || !bytes) return fail(CKV_ERR_ARG, "null argument");
+  size_t best = 0;
+  for (int dt = 0; dt < 3; ++dt) {   // large enough for any dtype
+    Plan pl;
+    const char* why = "";
+    const int rc = make_plan(*p, n, num_heads, num_kv_heads, head_dim, dt, &pl, &why);
+    if (rc == CKV_OK && pl.total > best) best = pl.total;
+    if (rc != CKV_OK && dt == 0) return fail(rc, why);
+  }
+  *bytes = best;
+  return CKV_OK;
+}
+
+int ckv_score_evict(const ckv_params* p, const ckv_layer* layer, void* workspace,
+                    size_t workspace_bytes, const ckv_outputs* out, ckv_stream_t stream) {
+  return score_evict_one(p, layer, workspace, workspace_bytes, out, (cudaStream_t)stream);
+}
+
+int ckv_score_evict_batched(const ckv_params* p, const ckv_layer* layers, int32_t count,
+                            void* workspace, size_t workspace_bytes, const ckv_outputs* outs,
+                            ckv_stream_t stream) {
+  if (!p || !layers || !outs || count < 0) return fail(CKV_ERR_ARG, "null argument");
+  char* base = static_cast<char*>(workspace);
+  size_t used = 0;
+  for (int i = 0; i < count; ++i) {
+    size_t need = 0;
+    int rc = ckv_workspace_size(p, layers[i].n, layers[i].num_heads, layers[i].num_kv_heads,
+                                layers[i].head_dim, &need);
+    if (rc) return rc;
+    need = align256(need);
+    if (used + need > workspace_bytes) return fail(CKV_ERR_WORKSPACE, "batched workspace too small");
+    rc = score_evict_one(p, &layers[i], base + used, need, &outs[i], (cudaStream_t)stream);
+    if (rc) return rc;
+    used += need;
+  }
+  return CKV_OK;
+}
+
+int ckv_read_status(void* workspace, ckv_stream_t stream, int32_t* device_status) {
+  if (!workspace || !device_status) return fail(CKV_ERR_ARG, "null argument");
+  Header h;
+  cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(Header), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  *device_status = h.status;
+  const int32_t zero = 0;
+  e = cudaMemcpyAsync(workspace, &zero, sizeof(zero), cudaMemcpyHostToDevice, (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clear status");
+  return CKV_OK;
+}
+
+int ckv_select_scores(const ckv_params* p, int32_t n, const float* a, const float* b,
+                      const float* c, void* workspace, size_t workspace_bytes, int32_t* out_idx,
+                      float* out_scores, ckv_stream_t stream) {
+  if (!p || !a || !b || !out_idx) return fail(CKV_ERR_ARG, "null argument");
+  Plan pl;
+  const char* why = "";
+  int rc = make_plan(*p, n, 32, 8, 128, CKV_BF16, &pl, &why);
+  if (rc) return fail(rc, why);
+  if (n < p->max_capacity_prompt) return fail(CKV_ERR_ARG, "n < max_capacity_prompt: nothing to select");
+  rc = check_ws(pl, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(Header), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "workspace header reset");
+  SelArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.pl = pl; sa.p = *p; sa.ws = ws; sa.out_idx = out_idx; sa.out_scores = out_scores;
+  sa.given = 1; sa.ga = a; sa.gb = b; sa.gc = c;
+  e = launch_select(sa, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "select kernel");
+}
+
+int ckv_neumann_rows(const ckv_params* p, int32_t n, const float* rows_qi, const float* rows_hi,
+                     int32_t single_chain, void* workspace, size_t workspace_bytes, float* out_qi,
+                     float* out_hi, int32_t* out_steps, ckv_stream_t stream) {
+  if (!p || !rows_qi || !out_qi) return fail(CKV_ERR_ARG, "null argument");
+  ckv_params q = *p;
+  q.combination_mode = single_chain ? CKV_COMB_MAX : CKV_COMB_DIS;
+  q.entropy_aware = (rows_hi != nullptr && !single_chain) ? 1 : 0;
+  q.max_capacity_prompt = 0;   // only the solve: any n is scored
+  if (q.max_capacity_prompt < q.sink_size + q.window_size) q.max_capacity_prompt = q.sink_size + q.window_size;
+  Plan pl;
+  const char* why = "";
+  int rc = make_plan(q, n, 32, 8, 128, CKV_BF16, &pl, &why);
+  if (rc) return fail(rc, why);
+  rc = check_ws(pl, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(Header), st);
+  const int nrows = pl.hi_rows ? 2 : 1;
+  for (int r = 0; r < nrows && e == cudaSuccess; ++r) {
+    char* dst = ws + (r == 0 ? pl.off_rows_qi : pl.off_rows_hi);
+    e = cudaMemsetAsync(dst, 0, (size_t)pl.W * pl.n_pad * 4, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(dst, (size_t)pl.n_pad * 4, r == 0 ? rows_qi : rows_hi, (size_t)n * 4,
+                            (size_t)n * 4, pl.W, cudaMemcpyDeviceToDevice, st);
+  }
+  if (e == cudaSuccess) e = launch_rows_prep(pl, q, ws, st);
+  if (e == cudaSuccess) e = launch_sweep(pl, q, ws, st);
+  if (e != cudaSuccess) return cuda_fail(e, "neumann stage");
+  // finished scores of both chains into a [2][n] scratch, then split
+  float* fin = reinterpret_cast<float*>(ws + pl.off_sel) + 6 * (size_t)n;   // past the select vectors
+  (void)fin;
+  SelArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.pl = pl; sa.p = q; sa.ws = ws; sa.finish_only = 1;
+  sa.out_scores = reinterpret_cast<float*>(ws + pl.off_sel) + 3 * (size_t)n;   // [2][n] in the sm area
+  e = launch_select(sa, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(out_qi, sa.out_scores, (size_t)n * 4, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && out_hi && pl.nchains > 1)
+    e = cudaMemcpyAsync(out_hi, sa.out_scores + n, (size_t)n * 4, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && out_steps)
+    e = cudaMemcpyAsync(out_steps, &reinterpret_cast<Header*>(ws)->steps, 4, cudaMemcpyDeviceToDevice, st);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "neumann stage output");
+}
+
+int ckv_window_pool(const ckv_params* p, const ckv_layer* layer, void* workspace,
+                    size_t workspace_bytes, float* out_entropy, float* out_mass,
+                    uint64_t* out_qi_heads, uint64_t* out_hi_heads, float* rows_qi, float* rows_hi,
+                    ckv_stream_t stream) {
+  if (!p) return fail(CKV_ERR_ARG, "null params");
+  int rc = check_layer(layer);
+  if (rc) return rc;
+  ckv_params q = *p;
+  if (q.max_capacity_prompt > layer->n) q.max_capacity_prompt = layer->n;
+  Plan pl;
+  const char* why = "";
+  rc = make_plan(q, layer->n, layer->num_heads, layer->num_kv_heads, layer->head_dim, layer->dtype, &pl, &why);
+  if (rc) return fail(rc, why);
+  rc = check_ws(pl, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(Header), st);
+  WinArgs wa;
+  wa.q = layer->q; wa.qhs = layer->q_head_stride; wa.qts = layer->q_tok_stride;
+  wa.k = layer->k; wa.khs = layer->k_head_stride; wa.kts = layer->k_tok_stride;
+  wa.ws = ws; wa.fixup_pass = 0; wa.p = q; wa.pl = pl;
+  if (e == cudaSuccess) e = launch_window(wa, st);
+  const float* exact = reinterpret_cast<const float*>(ws + pl.off_spec) + 2 * pl.H;
+  Header* hdr = reinterpret_cast<Header*>(ws);
+  if (e == cudaSuccess && out_entropy) e = cudaMemcpyAsync(out_entropy, exact, pl.H * 4, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && out_mass) e = cudaMemcpyAsync(out_mass, exact + pl.H, pl.H * 4, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && out_qi_heads) e = cudaMemcpyAsync(out_qi_heads, &hdr->qi_heads, 8, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && out_hi_heads) e = cudaMemcpyAsync(out_hi_heads, &hdr->hi_heads, 8, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && rows_qi)
+    e = cudaMemcpy2DAsync(rows_qi, (size_t)pl.n * 4, ws + pl.off_rows_qi, (size_t)pl.n_pad * 4,
+                          (size_t)pl.n * 4, pl.W, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && rows_hi && pl.hi_rows)
+    e = cudaMemcpy2DAsync(rows_hi, (size_t)pl.n * 4, ws + pl.off_rows_hi, (size_t)pl.n_pad * 4,
+                          (size_t)pl.n * 4, pl.W, cudaMemcpyDeviceToDevice, st);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "window stage");
+}
+
+int ckv_influence_walk(const ckv_params* p, int32_t n, const float* rows, int32_t current_idx,
+                       int32_t num_walkers, int32_t max_steps, int32_t sink_size, float temperature,
+                       float explore_temp, float explore_ratio, uint64_t seed, int32_t rng_mode,
+                       void* workspace, size_t workspace_bytes, float* scores, float* visits,
+                       ckv_stream_t stream) {
+  (void)p; (void)n; (void)rows; (void)current_idx; (void)num_walkers; (void)max_steps;
+  (void)sink_size; (void)temperature; (void)explore_temp; (void)explore_ratio; (void)seed;
+  (void)rng_mode; (void)workspace; (void)workspace_bytes; (void)scores; (void)visits; (void)stream;
+  return fail(CKV_ERR_UNSUPPORTED, "influence walker is not built yet");
+}
+
+int ckv_set_stage_events(void* const* events, int32_t count) {
+  if (count < 0 || (count > 0 && !events)) return fail(CKV_ERR_ARG, "bad stage event list");
+  g_stage_events = count ? reinterpret_cast<cudaEvent_t*>(const_cast<void**>(events)) : nullptr;
+  g_stage_count = count;
+  g_stage_next = 0;
+  return CKV_OK;
+}
+
+const char* ckv_last_error_string(void) { return g_last_error.c_str(); }
+
+const char* ckv_version(void) { return "circuitkv-b200 0.1.0"; }
+
+}  // extern "C"

@@ -1,0 +1,136 @@
+// Shared device helpers for the CircuitKV sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ckv.h"
+
+#define CKV_DEV __device__ __forceinline__
+
+namespace ckv {
+
+constexpr int kMaxHeads = 64;      // head sets are 64-bit masks
+constexpr int kMaxIters = 16;      // Neumann terms carried by the sweep (neumann_iterations <= 16)
+constexpr int kMaxWindow = 128;    // window rows handled by the window kernels
+constexpr int kHeadDim = 128;
+
+// Device status bits recorded in the workspace header (never a trap).
+enum : int32_t {
+  kStatusTimeout = 1,      // a bounded wait gave up
+  kStatusCount = 2,        // a selection produced an unexpected count
+  kStatusNonFinite = 4     // non-finite scores were seen
+};
+
+// ---------------------------------------------------------------------------
+// dtype traits
+// ---------------------------------------------------------------------------
+template <int DT> struct Elem;
+template <> struct Elem<CKV_BF16> { using T = __nv_bfloat16; };
+template <> struct Elem<CKV_FP16> { using T = __half; };
+template <> struct Elem<CKV_FP32> { using T = float; };
+
+CKV_DEV float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+CKV_DEV float to_f32(__half x) { return __half2float(x); }
+CKV_DEV float to_f32(float x) { return x; }
+
+// Round an fp32 value to the storage dtype and back (round to nearest even),
+// as the reference's 16-bit matmul output and scalar division do.
+template <int DT> CKV_DEV float round_dt(float x);
+template <> CKV_DEV float round_dt<CKV_BF16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+template <> CKV_DEV float round_dt<CKV_FP16>(float x) { return __half2float(__float2half_rn(x)); }
+template <> CKV_DEV float round_dt<CKV_FP32>(float x) { return x; }
+
+// 2^x on the MUFU unit (PTX ex2.approx.ftz.f32; relative error ~2^-22).
+CKV_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---------------------------------------------------------------------------
+// order-preserving float <-> uint32 keys (ascending key == ascending float)
+// ---------------------------------------------------------------------------
+CKV_DEV uint32_t float_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---------------------------------------------------------------------------
+// warp / block reductions
+// ---------------------------------------------------------------------------
+CKV_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+CKV_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+CKV_DEV int warp_sum_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reduction through `scratch` (>= 32 floats).  All threads get the result.
+template <bool kMax>
+__device__ __forceinline__ float block_reduce(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = kMax ? warp_max(v) : warp_sum(v);
+  __syncthreads();
+  if (lane == 0) scratch[wid] = v;
+  __syncthreads();
+  float r = (lane < nw) ? scratch[lane] : (kMax ? -INFINITY : 0.f);
+  if (wid == 0) r = kMax ? warp_max(r) : warp_sum(r);
+  if (threadIdx.x == 0) scratch[0] = r;
+  __syncthreads();
+  r = scratch[0];
+  __syncthreads();
+  return r;
+}
+
+// Exclusive block scan of ints (returns exclusive prefix; *total = block sum).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) scratch[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int s = (lane < nw) ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < nw) scratch[lane] = s;
+  }
+  __syncthreads();
+  int base = (wid > 0) ? scratch[wid - 1] : 0;
+  int t = scratch[nw - 1];
+  __syncthreads();
+  if (total) *total = t;
+  return base + x - v;
+}
+
+// Record a device-side failure in the workspace status word.
+CKV_DEV void set_status(int32_t* status, int32_t bit) {
+  if (status) atomicOr(status, bit);
+}
+
+}  // namespace ckv

@@ -1,0 +1,66 @@
+// Host/device plan of one layer call: sizes, tiling and the workspace carve-up.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/ckv.h"
+
+namespace ckv {
+
+constexpr int kColTile = 64;        // key columns per MMA tile
+constexpr int kScanChunk = 256;     // prefix positions per sweep chunk (one CTA)
+constexpr int kWarps = 8;           // warps of the window kernels
+
+// Workspace header (first 256 bytes of every layer workspace).
+struct alignas(16) Header {
+  int32_t status;          // device failure bits (kStatus*)
+  uint32_t cnt_stats;      // arrival counter of the stats kernel
+  uint32_t cnt_pool;       // arrival counter of the pooling kernel
+  int32_t fixup;           // 1: the speculative head sets were wrong, pooling re-runs
+  uint64_t qi_heads;       // head set max-pooled into the QI rows
+  uint64_t hi_heads;       // head set pooled into the HI rows
+  int32_t hi_mode;         // 0 mean, 1 max, 2 HI reuses the QI rows
+  int32_t n_hi;            // heads in the HI set
+  int32_t steps;           // Neumann terms taken (early stop)
+  int32_t kept;            // prefix positions kept (selection output count)
+  int32_t pad[52];
+};
+static_assert(sizeof(Header) == 256, "header must be 256 bytes");
+
+struct Plan {
+  // shapes
+  int n, H, Hkv, G, D, W, s, K, dtype;
+  int n_p;            // n - W: prefix rows (structured transitions)
+  int out_len;        // tokens kept per head
+  int kk;             // tokens chosen by top-k (out_len - s - W)
+  int mode;           // combination mode
+  int per_head;       // per-head eviction
+  int nchains;        // 2 (QI, HI) or 1 (single-chain influence)
+  int hi_rows;        // 1 when the HI chain has its own pooled rows
+  // window tiling
+  int rows_per_warp;  // 32 (16-bit MMA) or 16 (fp32 SIMT)
+  int rows_per_batch; // kWarps * rows_per_warp
+  int heads_per_batch;
+  int nbatch;         // H / heads_per_batch
+  int ktiles_per_batch;  // distinct KV heads one batch touches
+  int ncol_tiles;     // ceil(n / kColTile)
+  int nstat_chunks;   // column chunks of the stats kernel
+  int tiles_per_chunk;
+  int n_pad;          // ncol_tiles * kColTile
+  // sweep tiling
+  int nscan;          // ceil(n_p / kScanChunk)
+  // workspace offsets (bytes from the layer workspace base)
+  size_t off_stats, off_lse, off_lastlogit, off_spec, off_epart, off_mpart;
+  size_t off_rows_qi, off_rows_hi, off_colsum, off_gtile, off_rspart;
+  size_t off_wk, off_yk, off_ymax, off_bk, off_cg, off_agg, off_cum, off_cmax;
+  size_t off_sel, off_ph;
+  size_t sel_bytes;
+  size_t total;
+};
+
+// Fills *pl for one layer; returns CKV_OK or an error status with a message.
+int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan* pl,
+              const char** why);
+
+}  // namespace ckv

@@ -1,0 +1,28 @@
+// Launch interface of the selection kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "ckv_plan.h"
+
+namespace ckv {
+
+struct SelArgs {
+  Plan pl;
+  ckv_params p;
+  char* ws;
+  int32_t* out_idx;
+  float* out_scores;     // optional [2][n]: the two vectors the ranks are taken of
+  int given;             // 1: score vectors come from ga / gb / gc instead of the sweep
+  const float* ga;
+  const float* gb;
+  const float* gc;
+  int finish_only;       // 1: stop after the finished chain scores (written to out_scores)
+};
+
+size_t select_smem_bytes();
+cudaError_t launch_select(const SelArgs& a, cudaStream_t st);
+// H2O column sums of full_attn (mode max / weighted) and bridge importance (dis + bridge).
+cudaError_t launch_aux(const Plan& pl, const ckv_params& p, char* ws, cudaStream_t st);
+
+}  // namespace ckv

@@ -1,0 +1,27 @@
+// Launch interface of the window-attention kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "ckv_plan.h"
+
+namespace ckv {
+
+struct WinArgs {
+  const void* q;
+  int64_t qhs, qts;
+  const void* k;
+  int64_t khs, kts;
+  char* ws;          // layer workspace base
+  int fixup_pass;    // pooling kernel: 1 = the re-run launched after a wrong speculation
+  ckv_params p;
+  Plan pl;
+};
+
+size_t window_smem_bytes(const Plan& pl, bool pool);
+cudaError_t launch_window(const WinArgs& a, cudaStream_t st);
+cudaError_t launch_window_stage(const WinArgs& a, int stage, cudaStream_t st);
+// Column sums / row sums / window chain of pooled rows already in the workspace.
+cudaError_t launch_rows_prep(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st);
+
+}  // namespace ckv

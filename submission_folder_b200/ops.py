@@ -1,0 +1,170 @@
+"""Torch-facing wrappers of the C ABI (device memory and streams come from torch).
+
+Every function here runs the sm_100a kernels of ``libckv.so`` on the tensors'
+CUDA device and the current torch stream.  Host (CPU) tensors are copied to
+the GPU first and results copied back; nothing runs on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import Layer, Outputs, Params, check
+
+_DT = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}
+
+_workspaces = {}
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """A cached uint8 workspace of at least ``nbytes`` on ``device`` (256-byte aligned)."""
+    key = (device.type, device.index)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def workspace_size(p: Params, n: int, heads: int, kv_heads: int, head_dim: int) -> int:
+    out = ctypes.c_size_t()
+    check(_lib.load().ckv_workspace_size(ctypes.byref(p), n, heads, kv_heads, head_dim,
+                                         ctypes.byref(out)), "ckv_workspace_size")
+    return out.value
+
+
+def output_len(p: Params, n: int) -> int:
+    out = ctypes.c_int32()
+    check(_lib.load().ckv_output_len(ctypes.byref(p), n, ctypes.byref(out)), "ckv_output_len")
+    return out.value
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    if not torch.cuda.is_available():
+        raise RuntimeError("the CircuitKV B200 kernels need a CUDA device; none is available")
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("tensor is not on a CUDA device")
+
+
+def make_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Layer:
+    """``q`` ``[H, n, D]``, ``k``/``v`` ``[Hkv, n, D]`` views (head_dim contiguous)."""
+    if q.dtype not in _DT or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must share one dtype among bf16 / fp16 / fp32")
+    for t in (q, k, v):
+        if t.dim() != 3 or t.stride(-1) != 1:
+            raise ValueError("expected [heads, n, head_dim] views with contiguous head_dim")
+    L = Layer()
+    L.q, L.q_head_stride, L.q_tok_stride = q.data_ptr(), q.stride(0), q.stride(1)
+    L.k, L.k_head_stride, L.k_tok_stride = k.data_ptr(), k.stride(0), k.stride(1)
+    L.v, L.v_head_stride, L.v_tok_stride = v.data_ptr(), v.stride(0), v.stride(1)
+    L.n, L.num_heads, L.num_kv_heads, L.head_dim = q.shape[1], q.shape[0], k.shape[0], q.shape[2]
+    L.dtype = _lib.DTYPE_CODES[_DT[q.dtype]]
+    return L
+
+
+def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                want_scores: bool = False) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                                     Optional[torch.Tensor]]:
+    """One layer: returns ``(k_out [H,B,D], v_out [H,B,D], keep_idx [B-W] int32, scores)``.
+
+    ``scores`` (when requested) is ``[2, n]`` fp32: the two vectors ranked by the
+    selection (QI / HI after smoothing for "dis"; influence / H2O for "max").
+    """
+    _require_cuda(q, k, v)
+    H, n, D = q.shape
+    L = make_layer(q, k, v)
+    out_len = output_len(p, n)
+    dev = q.device
+    k_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
+    v_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
+    nidx = max(out_len - p.window_size, 1)
+    idx = torch.empty(nidx, dtype=torch.int32, device=dev)
+    scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
+    ws = workspace(workspace_size(p, n, H, k.shape[0], D), dev)
+    O = Outputs()
+    O.out_k, O.out_v, O.out_idx, O.out_scores = k_out.data_ptr(), v_out.data_ptr(), idx.data_ptr(), _ptr(scores)
+    check(_lib.load().ckv_score_evict(ctypes.byref(p), ctypes.byref(L), ctypes.c_void_p(ws.data_ptr()),
+                                      ws.numel(), ctypes.byref(O), _stream(dev)), "ckv_score_evict")
+    if n < p.max_capacity_prompt:
+        idx = torch.arange(max(n - p.window_size, 0), dtype=torch.int32, device=dev)
+    return k_out, v_out, idx, scores
+
+
+def read_status(dev: torch.device) -> int:
+    """Device status word of the cached workspace (synchronises)."""
+    ws = _workspaces.get((dev.type, dev.index))
+    if ws is None:
+        return 0
+    st = ctypes.c_int32()
+    check(_lib.load().ckv_read_status(ctypes.c_void_p(ws.data_ptr()), _stream(dev), ctypes.byref(st)),
+          "ckv_read_status")
+    return st.value
+
+
+def select_scores(p: Params, a: torch.Tensor, b: torch.Tensor, c: Optional[torch.Tensor] = None,
+                  want_scores: bool = False):
+    """Selection stage alone from fp32 score vectors on the GPU; returns (keep_idx, scores)."""
+    _require_cuda(a, b, c)
+    n = a.numel()
+    dev = a.device
+    out_len = output_len(p, n)
+    idx = torch.empty(max(out_len - p.window_size, 1), dtype=torch.int32, device=dev)
+    scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
+    ws = workspace(workspace_size(p, n, 32, 8, 128), dev)
+    a, b = a.float().contiguous(), b.float().contiguous()
+    c = None if c is None else c.float().contiguous()
+    check(_lib.load().ckv_select_scores(ctypes.byref(p), n, a.data_ptr(), b.data_ptr(), _ptr(c),
+                                        ctypes.c_void_p(ws.data_ptr()), ws.numel(), idx.data_ptr(),
+                                        _ptr(scores), _stream(dev)), "ckv_select_scores")
+    return idx, scores
+
+
+def neumann_rows(p: Params, rows_qi: torch.Tensor, rows_hi: Optional[torch.Tensor],
+                 single_chain: bool = False):
+    """Absorption solve alone from pooled rows ``[W, n]``; returns (qi, hi, steps tensor)."""
+    _require_cuda(rows_qi, rows_hi)
+    W, n = rows_qi.shape
+    dev = rows_qi.device
+    out_qi = torch.empty(n, dtype=torch.float32, device=dev)
+    out_hi = torch.empty(n, dtype=torch.float32, device=dev)
+    steps = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = workspace(workspace_size(p, n, 32, 8, 128), dev)
+    rq = rows_qi.float().contiguous()
+    rh = None if rows_hi is None else rows_hi.float().contiguous()
+    check(_lib.load().ckv_neumann_rows(ctypes.byref(p), n, rq.data_ptr(), _ptr(rh), int(single_chain),
+                                       ctypes.c_void_p(ws.data_ptr()), ws.numel(), out_qi.data_ptr(),
+                                       out_hi.data_ptr(), steps.data_ptr(), _stream(dev)),
+          "ckv_neumann_rows")
+    return out_qi, out_hi, steps
+
+
+def window_pool(p: Params, q: torch.Tensor, k: torch.Tensor):
+    """Window statistics + pooling alone: (entropy [H], mass [H], qi_set, hi_set, rows_qi, rows_hi)."""
+    _require_cuda(q, k)
+    H, n, D = q.shape
+    dev = q.device
+    L = make_layer(q, k, k)
+    ent = torch.empty(H, dtype=torch.float32, device=dev)
+    mass = torch.empty(H, dtype=torch.float32, device=dev)
+    sets = torch.zeros(2, dtype=torch.int64, device=dev)
+    rq = torch.empty(p.window_size, n, dtype=torch.float32, device=dev)
+    rh = torch.empty(p.window_size, n, dtype=torch.float32, device=dev)
+    ws = workspace(workspace_size(p, max(n, p.max_capacity_prompt), H, k.shape[0], D), dev)
+    check(_lib.load().ckv_window_pool(ctypes.byref(p), ctypes.byref(L), ctypes.c_void_p(ws.data_ptr()),
+                                      ws.numel(), ent.data_ptr(), mass.data_ptr(), sets.data_ptr(),
+                                      sets.data_ptr() + 8, rq.data_ptr(), rh.data_ptr(), _stream(dev)),
+          "ckv_window_pool")
+    return ent, mass, sets, rq, rh
