@@ -25,13 +25,15 @@ __global__ void __launch_bounds__(256) k_gather(const GatherArgs a) {
   if (a.per_head) {
     const int h = blockIdx.y;                      // query head
     const int g = h / a.G;
-    const int tok = (t < nk) ? a.idx[(size_t)h * nk + t] : (a.n - a.W + (t - nk));
+    int tok = (t < nk) ? a.idx[(size_t)h * nk + t] : (a.n - a.W + (t - nk));
+    if (tok < 0 || tok >= a.n) tok = 0;   // never expected: keeps the read in bounds
     const uint4* s = reinterpret_cast<const uint4*>(src + g * hs + (int64_t)tok * ts);
     uint4* d = reinterpret_cast<uint4*>(dst + ((size_t)h * a.out_len + t) * a.D);
     for (int v = lane; v < nvec; v += 32) d[v] = __ldg(s + v);
   } else {
     const int g = blockIdx.y;                      // KV head
-    const int tok = a.identity ? t : ((t < nk) ? a.idx[t] : (a.n - a.W + (t - nk)));
+    int tok = a.identity ? t : ((t < nk) ? a.idx[t] : (a.n - a.W + (t - nk)));
+    if (tok < 0 || tok >= a.n) tok = 0;   // never expected: keeps the read in bounds
     const uint4* s = reinterpret_cast<const uint4*>(src + g * hs + (int64_t)tok * ts);
     for (int v = lane; v < nvec; v += 32) {
       const uint4 x = __ldg(s + v);

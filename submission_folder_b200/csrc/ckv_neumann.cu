@@ -313,11 +313,16 @@ template <int KM>
 static cudaError_t launch_sweep_t(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st) {
   const size_t s1 = sizeof(float) * ((size_t)pl.K * pl.W + kScanChunk * 2 * KM + 64);
   const size_t s2 = sizeof(float) * (2 * (size_t)kScanChunk * 2 * KM + 64);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_sweep_chunks<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(k_sweep_apply<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
+  static size_t have1 = 0, have2 = 0;
+  if (s1 > have1) {
+    const cudaError_t e = cudaFuncSetAttribute(k_sweep_chunks<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1);
+    if (e != cudaSuccess) return e;
+    have1 = s1;
+  }
+  if (s2 > have2) {
+    const cudaError_t e = cudaFuncSetAttribute(k_sweep_apply<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
+    if (e != cudaSuccess) return e;
+    have2 = s2;
   }
   const dim3 grid(pl.nscan, pl.nchains);
   k_sweep_chunks<KM><<<grid, kScanChunk, s1, st>>>(pl, prm, ws);

@@ -381,15 +381,19 @@ __device__ void select_union(const Plan& pl, const ckv_params& prm, const float*
 // Kept prefix positions (sinks + chosen) in ascending order into out_idx.
 __device__ int compact(const Plan& pl, const uint8_t* keep, int32_t* out_idx, SelShared& sh) {
   const int lim = pl.n - pl.W;
+  const int cap = pl.s + pl.kk;   // out_idx capacity
   int written = 0;
   for (int base = 0; base < lim; base += blockDim.x) {
     const int i = base + threadIdx.x;
     const bool k = (i < lim) && (i < pl.s || keep[i]);
     int tot;
     const int before = block_exclusive_scan(k ? 1 : 0, sh.scan, &tot);
-    if (k) out_idx[written + before] = i;
+    if (k && written + before < cap) out_idx[written + before] = i;
     written += tot;
   }
+  // a short selection (never expected) leaves valid positions behind: pad with the last sink
+  for (int i = written + threadIdx.x; i < cap; i += blockDim.x) out_idx[i] = 0;
+  __syncthreads();
   return written;
 }
 
@@ -589,7 +593,9 @@ size_t select_smem_bytes() { return sizeof(SelShared); }
 cudaError_t launch_select(const SelArgs& a, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SelShared));
+    const cudaError_t e = cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)sizeof(SelShared));
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   k_select<<<1, kSelThreads, sizeof(SelShared), st>>>(a);

@@ -805,6 +805,12 @@ __global__ void __launch_bounds__(256) k_rows_chain(const Plan pl, const ckv_par
 cudaError_t launch_rows_prep(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st) {
   k_rows_prep<<<dim3(pl.ncol_tiles, pl.hi_rows ? 2 : 1), 256, 0, st>>>(pl, prm, ws);
   const size_t sm = sizeof(float) * ((size_t)pl.W * pl.W + 5 * pl.W + 64);
+  static size_t have = 0;
+  if (sm > have) {
+    const cudaError_t e = cudaFuncSetAttribute(k_rows_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+    have = sm;
+  }
   k_rows_chain<<<1, 256, sm, st>>>(pl, prm, ws);
   return cudaGetLastError();
 }
@@ -835,11 +841,16 @@ size_t window_smem_bytes(const Plan& pl, bool pool) {
 template <int DT>
 static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st) {
   const Plan& pl = a.pl;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaFuncSetAttribute(k_window_stats<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_window_pool<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr_done = true;
+  // opt in to the dynamic shared memory this launch needs (kernels also hold a little static smem)
+  static size_t set_stats = 0, set_pool = 0;
+  const size_t need = stage == 0 ? stats_smem<DT>(pl) : pool_smem<DT>(pl);
+  size_t& have = stage == 0 ? set_stats : set_pool;
+  if (need > have) {
+    const cudaError_t e = stage == 0
+        ? cudaFuncSetAttribute(k_window_stats<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need)
+        : cudaFuncSetAttribute(k_window_pool<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need);
+    if (e != cudaSuccess) return e;
+    have = need;
   }
   if (stage == 0) {
     k_window_stats<DT><<<dim3(pl.nstat_chunks, pl.nbatch), 256, stats_smem<DT>(pl), st>>>(a);
