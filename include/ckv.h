@@ -171,6 +171,21 @@ int ckv_select_scores(const ckv_params* p, int32_t n, const float* a, const floa
                       const float* c, void* workspace, size_t workspace_bytes, int32_t* out_idx,
                       float* out_scores, ckv_stream_t stream);
 
+/* ckv_select_scores without a workspace argument.  No counterpart in the
+ * reference: it is for callers that cannot allocate device memory for us -- a
+ * serving engine that reserved almost all HBM for its KV-cache pool at start-up
+ * (a per-call cudaMalloc would fail or fragment the pool, and cudaMalloc
+ * synchronises the device), or a C / FFI caller with no device allocator.  The
+ * scratch is a static __device__ array inside the library sized for n <= 32768
+ * (about 0.9 MiB held on every GPU that loads the library until exit); larger n
+ * is rejected with CKV_ERR_ARG.  The first call on each device looks up the
+ * array's device address (make it before any stream capture).  All calls share
+ * the array: calls that overlap on the GPU race, so order them on one stream.
+ * Same results as ckv_select_scores; calls no cudaMalloc / cudaFree. */
+int ckv_select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const float* b,
+                              const float* c, int32_t* out_idx, float* out_scores,
+                              ckv_stream_t stream);
+
 /* The absorption solve alone (PU:2060-2206, or PU:1939-2058 when rows_hi is
  * NULL and single_chain != 0): pooled window rows [W, n] fp32 in, finished
  * [n] scores out (sinks = 1% of the total, divided by the max). */

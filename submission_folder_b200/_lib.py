@@ -19,7 +19,8 @@ COMB_CODES = {"dis": 0, "max": 1, "weighted": 2, "union": 3, "union_da": 4}
 
 EXPORTED = (
     "ckv_default_params", "ckv_output_len", "ckv_workspace_size", "ckv_score_evict",
-    "ckv_score_evict_batched", "ckv_read_status", "ckv_select_scores", "ckv_neumann_rows",
+    "ckv_score_evict_batched", "ckv_read_status", "ckv_select_scores", "ckv_select_scores_noalloc",
+    "ckv_neumann_rows",
     "ckv_window_pool", "ckv_influence_walk", "ckv_set_stage_events", "ckv_last_error_string",
     "ckv_version",
 )
@@ -111,6 +112,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "ckv_score_evict_batched": (i32, [P, L, i32, vp, sz, O, vp]),
         "ckv_read_status": (i32, [vp, vp, ctypes.POINTER(i32)]),
         "ckv_select_scores": (i32, [P, i32, vp, vp, vp, vp, sz, vp, vp, vp]),
+        "ckv_select_scores_noalloc": (i32, [P, i32, vp, vp, vp, vp, vp, vp]),
         "ckv_neumann_rows": (i32, [P, i32, vp, vp, i32, vp, sz, vp, vp, vp, vp]),
         "ckv_window_pool": (i32, [P, L, vp, sz, vp, vp, vp, vp, vp, vp, vp]),
         "ckv_influence_walk": (i32, [P, i32, vp, i32, i32, i32, i32, f32, f32, f32, u64, i32, vp, sz,

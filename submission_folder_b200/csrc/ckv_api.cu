@@ -339,6 +339,14 @@ int ckv_select_scores(const ckv_params* p, int32_t n, const float* a, const floa
   return e == cudaSuccess ? CKV_OK : cuda_fail(e, "select kernel");
 }
 
+int ckv_select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const float* b,
+                              const float* c, int32_t* out_idx, float* out_scores,
+                              ckv_stream_t stream) {
+  const char* why = "";
+  const int rc = select_scores_noalloc(p, n, a, b, c, out_idx, out_scores, (cudaStream_t)stream, &why);
+  return rc ? fail(rc, why) : CKV_OK;
+}
+
 int ckv_neumann_rows(const ckv_params* p, int32_t n, const float* rows_qi, const float* rows_hi,
                      int32_t single_chain, void* workspace, size_t workspace_bytes, float* out_qi,
                      float* out_hi, int32_t* out_steps, ckv_stream_t stream) {

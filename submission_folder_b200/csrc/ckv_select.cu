@@ -14,6 +14,10 @@
 // histogram over M bins.  Tie rules follow the reference on CUDA tensors: equal
 // scores rank by index (stable argsort), equal combined scores at the k-th value
 // are taken lowest index first (topk).
+#include <string.h>
+
+#include <mutex>
+
 #include "ckv_common.cuh"
 #include "ckv_select.h"
 
@@ -600,6 +604,76 @@ cudaError_t launch_select(const SelArgs& a, cudaStream_t st) {
   }
   k_select<<<1, kSelThreads, sizeof(SelShared), st>>>(a);
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Selection with no workspace argument (ckv_select_scores_noalloc)
+// ---------------------------------------------------------------------------
+// Some callers cannot hand this library device memory: a serving engine that has
+// reserved nearly all HBM for its KV-cache pool at start-up (a per-call cudaMalloc
+// there either fails or fragments the pool, and cudaMalloc also synchronises the
+// device), or plain-C / FFI callers that have no device allocator of their own.
+// For them the selection stage keeps its scratch in this file-scope array: header
+// (256 B) + the selection area (29 bytes per position) for up to 32768 positions,
+// about 0.9 MiB that every GPU which loads the library holds until the process
+// exits.  All calls share it and it keeps the last call's contents, so calls that
+// overlap on the GPU (different streams, or different host threads on one device)
+// race; order them on one stream.
+constexpr int kNoAllocMaxN = 32768;
+constexpr size_t kNoAllocBytes = 256 + (size_t)29 * kNoAllocMaxN;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_noalloc_scratch per device, looked up once per device with
+// that device current (the host-side symbol is only a stand-in, not a device address).
+constexpr int kMaxDevices = 64;
+static void* g_noalloc_addr[kMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+
+static cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[dev] = ptr;
+  }
+  *out = g_noalloc_addr[dev];
+  return cudaSuccess;
+}
+
+int select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const float* b,
+                          const float* c, int32_t* out_idx, float* out_scores, cudaStream_t st,
+                          const char** why) {
+  if (!p || !a || !b || !out_idx) { *why = "null argument"; return CKV_ERR_ARG; }
+  if (n > kNoAllocMaxN) {
+    *why = "ckv_select_scores_noalloc: n exceeds the static scratch limit of 32768 positions";
+    return CKV_ERR_ARG;
+  }
+  if (n < p->max_capacity_prompt) { *why = "n < max_capacity_prompt: nothing to select"; return CKV_ERR_ARG; }
+  Plan pl;
+  int rc = make_plan(*p, n, 32, 8, 128, CKV_BF16, &pl, why);
+  if (rc) return rc;
+  // only the header and the selection area are touched by the given-scores path
+  pl.off_sel = 256;
+  pl.total = 256 + pl.sel_bytes;
+  if (pl.total > kNoAllocBytes) { *why = "selection scratch larger than the static array"; return CKV_ERR_ARG; }
+  void* base = nullptr;
+  cudaError_t e = noalloc_scratch(&base);
+  if (e != cudaSuccess) { *why = cudaGetErrorString(e); return CKV_ERR_CUDA; }
+  char* ws = static_cast<char*>(base);
+  e = cudaMemsetAsync(ws, 0, sizeof(Header), st);   // status and counters start at zero
+  if (e != cudaSuccess) { *why = cudaGetErrorString(e); return CKV_ERR_CUDA; }
+  SelArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.pl = pl; sa.p = *p; sa.ws = ws; sa.out_idx = out_idx; sa.out_scores = out_scores;
+  sa.given = 1; sa.ga = a; sa.gb = b; sa.gc = c;
+  e = launch_select(sa, st);
+  if (e != cudaSuccess) { *why = cudaGetErrorString(e); return CKV_ERR_CUDA; }
+  return CKV_OK;
 }
 
 }  // namespace ckv
