@@ -103,16 +103,24 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
     if (2 * pl.kk > 8192) { *why = "union budget above 4096 tokens is not supported"; return CKV_ERR_UNSUPPORTED; }
   }
   pl.nchains = (pl.mode == CKV_COMB_MAX || pl.mode == CKV_COMB_WEIGHTED) ? 1 : 2;
+  pl.tc = (dtype != CKV_FP32 && (pl.G * pl.W) % 128 == 0 && pl.G * pl.W <= 512 && pl.W <= 128) ? 1 : 0;
+  // tensor-core pooling pass: 4 query heads per KV group, window 64 (the Llama / Mistral shapes)
+  pl.tc_pool = (pl.tc && pl.G == 4 && pl.W == 64) ? 1 : 0;
   pl.hi_rows = (pl.nchains == 2 && p.entropy_aware) ? 1 : 0;
   pl.ncol_tiles = (n + kColTile - 1) / kColTile;
   pl.n_pad = pl.ncol_tiles * kColTile;
-  int chunks = (296 + pl.nbatch - 1) / pl.nbatch;
+  // moments pass: one wave of CTAs (tensor-core path: one CTA per SM per KV group)
+  int chunks = pl.tc ? 148 / Hkv : (296 + pl.nbatch - 1) / pl.nbatch;
   if (chunks > pl.ncol_tiles) chunks = pl.ncol_tiles;
   if (chunks < 1) chunks = 1;
   pl.tiles_per_chunk = (pl.ncol_tiles + chunks - 1) / chunks;
   pl.nstat_chunks = (pl.ncol_tiles + pl.tiles_per_chunk - 1) / pl.tiles_per_chunk;
   pl.nscan = (pl.n_p + kScanChunk - 1) / kScanChunk;
   if (pl.nscan < 1) pl.nscan = 1;
+  pl.tc_nclusters = pl.ncol_tiles < 148 ? pl.ncol_tiles : 148;   // CTAs of the tensor-core pooling pass
+  pl.e_parts = pl.tc_pool ? 2 * pl.tc_nclusters : pl.ncol_tiles;   // TC: one partial per (CTA, column half)
+  pl.rs_parts = pl.ncol_tiles;
+  pl.g_slice = kColTile;
   if (window_smem_bytes(pl, true) > 227 * 1024 || window_smem_bytes(pl, false) > 227 * 1024) {
     *why = "window tile does not fit in shared memory"; return CKV_ERR_UNSUPPORTED;
   }
@@ -120,16 +128,17 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   size_t off = align256(sizeof(Header));
   auto take = [&](size_t bytes) { const size_t o = off; off = align256(off + bytes); return o; };
   const size_t HW = (size_t)H * pl.W;
-  pl.off_stats = take((size_t)pl.nstat_chunks * HW * 16);
+  pl.off_stats = take(((size_t)pl.nstat_chunks * HW * 16 > (2 * HW + 2 * (size_t)pl.W) * 4)
+                         ? (size_t)pl.nstat_chunks * HW * 16 : (2 * HW + 2 * (size_t)pl.W) * 4);
   pl.off_lse = take(HW * 4);
   pl.off_spec = take((size_t)4 * H * 4);
-  pl.off_epart = take((size_t)pl.ncol_tiles * HW * 4);
-  pl.off_mpart = take((size_t)pl.ncol_tiles * HW * 4);
+  pl.off_epart = take((size_t)2 * pl.ncol_tiles * HW * 4);
+  pl.off_mpart = take((size_t)2 * pl.ncol_tiles * HW * 4);
   pl.off_rows_qi = take((size_t)pl.W * pl.n_pad * 4);
   pl.off_rows_hi = take((size_t)pl.W * pl.n_pad * 4);
   pl.off_colsum = take((size_t)2 * pl.n_pad * 4);
-  pl.off_gtile = take((size_t)2 * pl.ncol_tiles * 4);
-  pl.off_rspart = take((size_t)2 * pl.ncol_tiles * pl.W * 4);
+  pl.off_gtile = take((size_t)2 * pl.ncol_tiles * 8 * 4);
+  pl.off_rspart = take((size_t)2 * pl.ncol_tiles * 8 * pl.W * 4);
   pl.off_wk = take((size_t)2 * pl.K * pl.W * 4);
   pl.off_yk = take((size_t)2 * (pl.K + 1) * pl.W * 4);
   pl.off_ymax = take((size_t)2 * (pl.K + 1) * 4);
@@ -200,7 +209,10 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
   wa.ws = ws; wa.fixup_pass = 0; wa.p = *p; wa.pl = pl;
   for (int s = 0; s < 3; ++s) {
     e = launch_window_stage(wa, s, st);
-    if (e != cudaSuccess) return cuda_fail(e, "window kernels");
+    if (e != cudaSuccess) {
+      static const char* names[3] = {"window moments", "window pooling", "window pooling re-run"};
+      return cuda_fail(e, names[s]);
+    }
     stage_mark(st);
   }
   e = launch_sweep(pl, *p, ws, st);
@@ -362,6 +374,11 @@ int ckv_neumann_rows(const ckv_params* p, int32_t n, const float* rows_qi, const
   if (rc) return fail(rc, why);
   rc = check_ws(pl, workspace, workspace_bytes);
   if (rc) return rc;
+  // rows given by the caller: 64-column partial layout of the prep kernel
+  pl.tc_pool = 0;
+  pl.rs_parts = pl.ncol_tiles;
+  pl.g_slice = kColTile;
+  pl.e_parts = pl.ncol_tiles;
   char* ws = static_cast<char*>(workspace);
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(Header), st);
@@ -415,7 +432,13 @@ int ckv_window_pool(const ckv_params* p, const ckv_layer* layer, void* workspace
   wa.q = layer->q; wa.qhs = layer->q_head_stride; wa.qts = layer->q_tok_stride;
   wa.k = layer->k; wa.khs = layer->k_head_stride; wa.kts = layer->k_tok_stride;
   wa.ws = ws; wa.fixup_pass = 0; wa.p = q; wa.pl = pl;
-  if (e == cudaSuccess) e = launch_window(wa, st);
+  for (int s = 0; s < 3 && e == cudaSuccess; ++s) {
+    e = launch_window_stage(wa, s, st);
+    if (e != cudaSuccess) {
+      static const char* names[3] = {"window moments", "window pooling", "window pooling re-run"};
+      return cuda_fail(e, names[s]);
+    }
+  }
   const float* exact = reinterpret_cast<const float*>(ws + pl.off_spec) + 2 * pl.H;
   Header* hdr = reinterpret_cast<Header*>(ws);
   if (e == cudaSuccess && out_entropy) e = cudaMemcpyAsync(out_entropy, exact, pl.H * 4, cudaMemcpyDeviceToDevice, st);

@@ -134,3 +134,24 @@ CKV_DEV void set_status(int32_t* status, int32_t bit) {
 }
 
 }  // namespace ckv
+
+#include <mutex>
+#include <unordered_map>
+
+namespace ckv {
+
+// Opt a kernel in to `bytes` of dynamic shared memory.  The attribute is per
+// kernel and only ever raised (a smaller request never lowers it under a larger
+// launch issued elsewhere).
+inline cudaError_t ensure_dynamic_smem(const void* func, size_t bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, size_t> have;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& h = have[func];
+  if (bytes <= h) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) h = bytes;
+  return e;
+}
+
+}  // namespace ckv

@@ -61,6 +61,9 @@ template <int KM> CKV_DEV void apply(const Map<KM>& M, const float* S, float* ou
   }
 }
 
+// Maps live in shared memory with a stride of 2*KM+1 floats (odd: no bank conflicts).
+template <int KM> __host__ __device__ constexpr int map_stride() { return 2 * KM + 1; }
+
 template <int KM> CKV_DEV void store_map(float* dst, const Map<KM>& m) {
 #pragma unroll
   for (int i = 0; i < KM; ++i) { dst[i] = m.a[i]; dst[KM + i] = m.u[i]; }
@@ -141,19 +144,20 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_chunks(const Plan pl, cons
   const float gamma = prm.neumann_gamma;
   const float* rows = reinterpret_cast<const float*>(ws + (src ? pl.off_rows_hi : pl.off_rows_qi));
   const float* colsum = reinterpret_cast<const float*>(ws + pl.off_colsum) + (size_t)src * pl.n_pad;
-  const float* gtile = reinterpret_cast<const float*>(ws + pl.off_gtile) + (size_t)src * pl.ncol_tiles;
+  const float* gtile = reinterpret_cast<const float*>(ws + pl.off_gtile) + (size_t)src * pl.ncol_tiles * 8;
   const float* wk = reinterpret_cast<const float*>(ws + pl.off_wk) + (size_t)ch * K * pl.W;
   float* bk_out = reinterpret_cast<float*>(ws + pl.off_bk) + (size_t)ch * K * pl.n_p;
   float2* cg_out = reinterpret_cast<float2*>(ws + pl.off_cg) + (size_t)ch * pl.n_p;
   float* agg = reinterpret_cast<float*>(ws + pl.off_agg) + ((size_t)ch * pl.nscan) * 2 * KM;
 
   float* sW = sm;                            // [K][W]
-  float* sMaps = sW + K * pl.W;              // [kScanChunk][2*KM]
-  float* scratch = sMaps + kScanChunk * 2 * KM;   // 32 floats
+  float* sMaps = sW + K * pl.W;              // [kScanChunk][2*KM+1]
+  float* scratch = sMaps + kScanChunk * map_stride<KM>();   // 32 floats
   for (int i = threadIdx.x; i < K * pl.W; i += blockDim.x) sW[i] = wk[i];
 
-  // G offset of this chunk: sum of g over all earlier positions (64-column tile totals)
-  const int tiles_before = (chunk * kScanChunk) / kColTile;
+  // G offset of this chunk: sum of g over all earlier positions (partial totals of
+  // g_slice columns each)
+  const int tiles_before = (chunk * kScanChunk) / pl.g_slice;
   float off = 0.f;
   for (int t = threadIdx.x; t < tiles_before; t += blockDim.x) off += gtile[t];
   off = block_reduce<false>(off, scratch);
@@ -171,12 +175,19 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_chunks(const Plan pl, cons
 #pragma unroll
   for (int k = 0; k < KM; ++k) bk[k] = 0.f;
   if (j < pl.n_p && j >= pl.s) {
-    for (int r = 0; r < pl.W; ++r) {
-      float v = rows[(size_t)r * pl.n_pad + j];
-      if (tempered) v = v > 0.f ? powf(v, invT) : 0.f;
+    // 16 independent row loads in flight per batch (the rows are L2-resident)
+    for (int r0 = 0; r0 < pl.W; r0 += 16) {
+      float v[16];
 #pragma unroll
-      for (int k = 0; k < KM; ++k)
-        if (k < K) bk[k] = fmaf(v, sW[k * pl.W + r], bk[k]);
+      for (int u = 0; u < 16; ++u) v[u] = __ldcg(rows + (size_t)(r0 + u) * pl.n_pad + j);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        float x = v[u];
+        if (tempered) x = x > 0.f ? powf(x, invT) : 0.f;
+#pragma unroll
+        for (int k = 0; k < KM; ++k)
+          if (k < K) bk[k] = fmaf(x, sW[k * pl.W + r0 + u], bk[k]);
+      }
     }
   }
   if (j < pl.n_p) {
@@ -186,13 +197,13 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_chunks(const Plan pl, cons
     cg_out[j] = make_float2(c, g);
   }
   Map<KM> m = position_map<KM>(pl, ch, j, c, g, bk, gamma, start_value(pl, ch, j));
-  store_map(sMaps + threadIdx.x * 2 * KM, m);
+  store_map(sMaps + threadIdx.x * map_stride<KM>(), m);
   __syncthreads();
   for (int d = 1; d < kScanChunk; d <<= 1) {
     if ((threadIdx.x % (2 * d)) == 0) {
-      const Map<KM> L = load_map<KM>(sMaps + threadIdx.x * 2 * KM);
-      const Map<KM> R = load_map<KM>(sMaps + (threadIdx.x + d) * 2 * KM);
-      store_map(sMaps + threadIdx.x * 2 * KM, compose(L, R));
+      const Map<KM> L = load_map<KM>(sMaps + threadIdx.x * map_stride<KM>());
+      const Map<KM> R = load_map<KM>(sMaps + (threadIdx.x + d) * map_stride<KM>());
+      store_map(sMaps + threadIdx.x * map_stride<KM>(), compose(L, R));
     }
     __syncthreads();
   }
@@ -216,9 +227,9 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_apply(const Plan pl, const
   float* cum = reinterpret_cast<float*>(ws + pl.off_cum) + (size_t)ch * (K + 1) * pl.n_p;
   float* cmax = reinterpret_cast<float*>(ws + pl.off_cmax) + ((size_t)ch * pl.nscan + chunk) * (kMaxIters + 1);
 
-  float* bufA = sm;                               // [kScanChunk][2*KM]
-  float* bufB = bufA + kScanChunk * 2 * KM;       // [kScanChunk][2*KM]
-  float* scratch = bufB + kScanChunk * 2 * KM;    // 64 floats
+  float* bufA = sm;                               // [kScanChunk][2*KM+1]
+  float* bufB = bufA + kScanChunk * map_stride<KM>();   // [kScanChunk][2*KM+1]
+  float* scratch = bufB + kScanChunk * map_stride<KM>();   // (kScanChunk/32) * (kMaxIters+1) floats
 
   // 1) fold the maps of all later chunks (tree over at most kScanChunk maps per round)
   float Sin[KM];
@@ -235,13 +246,13 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_apply(const Plan pl, const
       Map<KM> m;
       if ((int)threadIdx.x < cnt) m = load_map<KM>(agg + (size_t)(lo + threadIdx.x) * 2 * KM);
       else map_identity(m);
-      store_map(bufA + threadIdx.x * 2 * KM, m);
+      store_map(bufA + threadIdx.x * map_stride<KM>(), m);
       __syncthreads();
       for (int d = 1; d < kScanChunk; d <<= 1) {
         if ((threadIdx.x % (2 * d)) == 0) {
-          const Map<KM> L = load_map<KM>(bufA + threadIdx.x * 2 * KM);
-          const Map<KM> R = load_map<KM>(bufA + (threadIdx.x + d) * 2 * KM);
-          store_map(bufA + threadIdx.x * 2 * KM, compose(L, R));
+          const Map<KM> L = load_map<KM>(bufA + threadIdx.x * map_stride<KM>());
+          const Map<KM> R = load_map<KM>(bufA + (threadIdx.x + d) * map_stride<KM>());
+          store_map(bufA + threadIdx.x * map_stride<KM>(), compose(L, R));
         }
         __syncthreads();
       }
@@ -264,20 +275,20 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_apply(const Plan pl, const
       if (k < K) bk[k] = bk_in[(size_t)k * pl.n_p + j];
   }
   const float x0 = start_value(pl, ch, j);
-  store_map(bufA + threadIdx.x * 2 * KM, position_map<KM>(pl, ch, j, c, g, bk, gamma, x0));
+  store_map(bufA + threadIdx.x * map_stride<KM>(), position_map<KM>(pl, ch, j, c, g, bk, gamma, x0));
   __syncthreads();
   float* src = bufA;
   float* dst = bufB;
   for (int d = 1; d < kScanChunk; d <<= 1) {
-    Map<KM> m = load_map<KM>(src + threadIdx.x * 2 * KM);
-    if (threadIdx.x + d < kScanChunk) m = compose(m, load_map<KM>(src + (threadIdx.x + d) * 2 * KM));
-    store_map(dst + threadIdx.x * 2 * KM, m);
+    Map<KM> m = load_map<KM>(src + threadIdx.x * map_stride<KM>());
+    if (threadIdx.x + d < kScanChunk) m = compose(m, load_map<KM>(src + (threadIdx.x + d) * map_stride<KM>()));
+    store_map(dst + threadIdx.x * map_stride<KM>(), m);
     __syncthreads();
     float* t = src; src = dst; dst = t;
   }
   // carry after all positions > j
   float S[KM];
-  if (threadIdx.x + 1 < kScanChunk) apply(load_map<KM>(src + (threadIdx.x + 1) * 2 * KM), Sin, S);
+  if (threadIdx.x + 1 < kScanChunk) apply(load_map<KM>(src + (threadIdx.x + 1) * map_stride<KM>()), Sin, S);
   else {
 #pragma unroll
     for (int k = 0; k < KM; ++k) S[k] = Sin[k];
@@ -301,28 +312,30 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_apply(const Plan pl, const
       }
     }
   }
-  // block max of every term index
-  for (int k = 1; k <= K; ++k) {
-    float v = valid ? mx[k] : 0.f;
-    v = block_reduce<true>(v, scratch);
-    if (threadIdx.x == 0) cmax[k] = v;
+  // block max of every term index: warp shuffles, one barrier
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 1; k <= KM; ++k) {
+    float v = (valid && k <= K) ? mx[k] : 0.f;
+    v = warp_max(v);
+    if (lane == 0) scratch[wid * (kMaxIters + 1) + k] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x >= 1 && threadIdx.x <= K) {
+    float v = 0.f;
+    for (int w = 0; w < kScanChunk / 32; ++w) v = fmaxf(v, scratch[w * (kMaxIters + 1) + threadIdx.x]);
+    cmax[threadIdx.x] = v;
   }
 }
 
 template <int KM>
 static cudaError_t launch_sweep_t(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st) {
-  const size_t s1 = sizeof(float) * ((size_t)pl.K * pl.W + kScanChunk * 2 * KM + 64);
-  const size_t s2 = sizeof(float) * (2 * (size_t)kScanChunk * 2 * KM + 64);
-  static size_t have1 = 0, have2 = 0;
-  if (s1 > have1) {
-    const cudaError_t e = cudaFuncSetAttribute(k_sweep_chunks<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1);
+  const size_t s1 = sizeof(float) * ((size_t)pl.K * pl.W + kScanChunk * map_stride<KM>() + 64);
+  const size_t s2 = sizeof(float) * (2 * (size_t)kScanChunk * map_stride<KM>() + (kScanChunk / 32) * (kMaxIters + 1) + 64);
+  {
+    cudaError_t e = ensure_dynamic_smem((const void*)k_sweep_chunks<KM>, s1);
+    if (e == cudaSuccess) e = ensure_dynamic_smem((const void*)k_sweep_apply<KM>, s2);
     if (e != cudaSuccess) return e;
-    have1 = s1;
-  }
-  if (s2 > have2) {
-    const cudaError_t e = cudaFuncSetAttribute(k_sweep_apply<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
-    if (e != cudaSuccess) return e;
-    have2 = s2;
   }
   const dim3 grid(pl.nscan, pl.nchains);
   k_sweep_chunks<KM><<<grid, kScanChunk, s1, st>>>(pl, prm, ws);

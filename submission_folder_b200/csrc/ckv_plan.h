@@ -12,7 +12,7 @@ constexpr int kColTile = 64;        // key columns per MMA tile
 constexpr int kScanChunk = 256;     // prefix positions per sweep chunk (one CTA)
 constexpr int kWarps = 8;           // warps of the window kernels
 
-// Workspace header (first 256 bytes of every layer workspace).
+// Workspace header (first 512 bytes of every layer workspace).
 struct alignas(16) Header {
   int32_t status;          // device failure bits (kStatus*)
   uint32_t cnt_stats;      // arrival counter of the stats kernel
@@ -25,8 +25,9 @@ struct alignas(16) Header {
   int32_t steps;           // Neumann terms taken (early stop)
   int32_t kept;            // prefix positions kept (selection output count)
   int32_t pad[52];
+  uint32_t cnt_group[64];  // arrival counters per head group of the stats kernel
 };
-static_assert(sizeof(Header) == 256, "header must be 256 bytes");
+static_assert(sizeof(Header) == 512, "header must be 512 bytes");
 
 struct Plan {
   // shapes
@@ -37,6 +38,12 @@ struct Plan {
   int mode;           // combination mode
   int per_head;       // per-head eviction
   int nchains;        // 2 (QI, HI) or 1 (single-chain influence)
+  int tc;             // 1: window moments on tcgen05 tensor cores (16-bit inputs, G*W a multiple of 128)
+  int tc_pool;        // 1: pooling pass on tcgen05 with one cluster CTA per KV group
+  int tc_nclusters;   // clusters of the tensor-core pooling pass
+  int e_parts;        // exact entropy / mass partials per row
+  int rs_parts;       // row-sum partials per chain
+  int g_slice;        // columns per g-total partial (64 or 8)
   int hi_rows;        // 1 when the HI chain has its own pooled rows
   // window tiling
   int rows_per_warp;  // 32 (16-bit MMA) or 16 (fp32 SIMT)

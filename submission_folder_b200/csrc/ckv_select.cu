@@ -6,14 +6,20 @@
 //   keep mask        PU:2591-2644;  union keep mask PU:2489-2589
 //   compaction       PU:3496-3501 (kept prefix positions in ascending order)
 //
-// One CTA of 1024 threads per layer.  Ranks are needed only near the top: the
-// kept set of MAX(rank a, rank b) over candidates is contained in the union of
-// the top-M of a and of b (M = kept + forced), so each vector is reduced to its
-// top-M by a 4-pass radix select, the M survivors are bitonic-sorted and get
-// ranks n-1, n-2, ...; the threshold of the combined rank is then found with a
-// histogram over M bins.  Tie rules follow the reference on CUDA tensors: equal
-// scores rank by index (stable argsort), equal combined scores at the k-th value
-// are taken lowest index first (topk).
+// One thread-block cluster per layer, one CTA (1024 threads) per score vector
+// (QI / HI [/ bridge], or influence / H2O).  Each CTA keeps its vector in shared
+// memory (global scratch above 36864 positions), finishes and smooths it, and
+// reduces it to its top-M by a 4-pass radix select (per-warp histograms) and a
+// bitonic sort of the M survivors: ranks are needed only near the top, since the
+// kept set of MAX(rank a, rank b) over the candidates lies in the union of the
+// top-M of each vector (M = kept + forced).  CTA 0 reads the other CTAs' lists
+// through distributed shared memory, builds the combined ranks, finds the
+// threshold with a histogram over M bins and compacts the kept positions.
+// Ordered passes (ties by index, compaction) count set predicates per 32-position
+// chunk with a warp ballot and do one block scan over the chunk counts.  Tie rules
+// follow the reference on CUDA tensors: equal scores rank by index (stable
+// argsort); equal combined scores at the k-th value are taken lowest index first.
+#include <cooperative_groups.h>
 #include <string.h>
 
 #include <mutex>
@@ -21,51 +27,121 @@
 #include "ckv_common.cuh"
 #include "ckv_select.h"
 
+namespace cg = cooperative_groups;
+
 namespace ckv {
 
 constexpr int kSelThreads = 1024;
-constexpr int kMaxSort = 8192;   // largest top-M list sorted in shared memory
+constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kMaxSort = 8192;         // largest top-M list sorted in shared memory
+constexpr int kSmemScoresMax = 36864;  // vectors up to this length stay in shared memory
 
-struct SelShared {
-  unsigned long long sortbuf[kMaxSort];
-  int hist[256];
-  int scan[64];
-  int misc[16];
-  float fscratch[64];
+struct SelLayout {
+  int n, nchunk;
+  bool smem_scores;
+  size_t off_x, off_sort, off_cnt_a, off_cnt_b, off_bits, off_misc, total;
+};
+
+__host__ __device__ inline SelLayout sel_layout(int n) {
+  SelLayout L;
+  L.n = n;
+  L.nchunk = (n + 31) / 32;
+  L.smem_scores = n <= kSmemScoresMax;
+  size_t off = 0;
+  auto take = [&](size_t b) { const size_t o = off; off = (off + b + 15) & ~(size_t)15; return o; };
+  L.off_sort = take(sizeof(unsigned long long) * kMaxSort);   // also the per-warp histograms
+  L.off_x = take(L.smem_scores ? sizeof(float) * (size_t)n : 0);
+  L.off_cnt_a = take(sizeof(int) * (size_t)L.nchunk);
+  L.off_cnt_b = take(sizeof(int) * (size_t)L.nchunk);
+  L.off_bits = take(sizeof(uint32_t) * (size_t)L.nchunk);
+  L.off_misc = take(sizeof(int) * 256);
+  L.total = off;
+  return L;
+}
+
+struct SelSmem {
+  unsigned long long* sortbuf;
+  int* hist;        // [kSelWarps][256] (aliases sortbuf)
+  float* x;         // score vector (shared or global)
+  int* cnt_a;
+  int* cnt_b;
+  uint32_t* bits;
+  int* misc;        // [0..63] scan scratch, [64..] scalars
+  float* fmisc;
 };
 
 // ---------------------------------------------------------------------------
-// helpers
+// block helpers
 // ---------------------------------------------------------------------------
-// Which positions a top-M selection may draw from.
+CKV_DEV uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// In-place exclusive scan of cnt[0..m); returns the total.  All threads.
+__device__ int scan_counts(int* cnt, int m, int* scratch) {
+  const int per = (m + blockDim.x - 1) / blockDim.x;
+  const int lo = threadIdx.x * per, hi = min(m, lo + per);
+  int local = 0;
+  for (int i = lo; i < hi; ++i) local += cnt[i];
+  int total;
+  int run = block_exclusive_scan(local, scratch, &total);
+  for (int i = lo; i < hi; ++i) { const int c = cnt[i]; cnt[i] = run; run += c; }
+  __syncthreads();
+  return total;
+}
+
+// Ballot counts of pred(i) per 32-position chunk into cnt (index order).
+template <class Pred>
+__device__ void chunk_counts(int n, int* cnt, Pred pred) {
+  const int lane = threadIdx.x & 31;
+  for (int base = threadIdx.x - lane; base < n; base += blockDim.x) {
+    const int i = base + lane;
+    const unsigned b = __ballot_sync(0xffffffffu, i < n && pred(i));
+    if (lane == 0) cnt[base >> 5] = __popc(b);
+  }
+  __syncthreads();
+}
+
+// Rank (in index order) of position i among those with pred true, given the scanned chunk counts.
+CKV_DEV int chunk_rank(const int* cnt, int i, unsigned ball) {
+  return cnt[i >> 5] + __popc(ball & lanemask_lt());
+}
+
+// ---------------------------------------------------------------------------
+// top-M of one vector
+// ---------------------------------------------------------------------------
 struct Range {
-  int n;        // positions [0, n)
-  int lo, hi;   // when restricted: only [lo, hi) (the non-forced candidates)
+  int n, lo, hi;
   bool restricted;
   CKV_DEV bool ok(int i) const { return i < n && (!restricted || (i >= lo && i < hi)); }
 };
 
-// Radix select of the M largest keys among valid positions.  Returns the boundary
-// key (*kstar), the count strictly above it (*above) and how many boundary-key
-// elements complete the M (*take).
-__device__ void radix_select(const float* v, const Range& rg, int M, SelShared& sh, uint32_t* kstar,
+__device__ void radix_select(const float* v, const Range& rg, int M, SelSmem& sh, uint32_t* kstar,
                              int* above, int* take) {
   uint32_t prefix = 0, pmask = 0;
-  int remaining = M;
-  int gt = 0;
+  int remaining = M, gt = 0;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int* myhist = sh.hist + wid * 256;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) sh.hist[i] = 0;
+    for (int i = threadIdx.x; i < kSelWarps * 256; i += blockDim.x) sh.hist[i] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < rg.n; i += blockDim.x) {
       if (!rg.ok(i)) continue;
       const uint32_t k = float_key(v[i]);
-      if ((k & pmask) == prefix) atomicAdd(&sh.hist[(k >> shift) & 255], 1);
+      if ((k & pmask) == prefix) atomicAdd(&myhist[(k >> shift) & 255], 1);
     }
     __syncthreads();
-    if (threadIdx.x < 32) {
-      const int lane = threadIdx.x;
-      // lane l owns digits [8*(31-l), 8*(31-l)+8): lane 0 the highest digits
+    // fold the per-warp histograms into warp 0's row
+    if (threadIdx.x < 256) {
+      int s = 0;
+      for (int w = 0; w < kSelWarps; ++w) s += sh.hist[w * 256 + threadIdx.x];
+      sh.hist[threadIdx.x] = s;
+    }
+    __syncthreads();
+    if (wid == 0) {
       int loc[8], s = 0;
 #pragma unroll
       for (int d = 0; d < 8; ++d) { loc[d] = sh.hist[8 * (31 - lane) + (7 - d)]; s += loc[d]; }
@@ -76,8 +152,7 @@ __device__ void radix_select(const float* v, const Range& rg, int M, SelShared& 
         if (lane >= o) incl += y;
       }
       const int excl = incl - s;
-      const bool here = excl < remaining && incl >= remaining;
-      const unsigned ball = __ballot_sync(0xffffffffu, here);
+      const unsigned ball = __ballot_sync(0xffffffffu, excl < remaining && incl >= remaining);
       const int owner = ball ? (__ffs(ball) - 1) : 31;
       if (lane == owner) {
         int cum = excl, digit = 8 * (31 - lane);
@@ -86,16 +161,15 @@ __device__ void radix_select(const float* v, const Range& rg, int M, SelShared& 
           if (cum + loc[d] >= remaining) { digit = 8 * (31 - lane) + (7 - d); break; }
           cum += loc[d];
         }
-        sh.misc[0] = digit;
-        sh.misc[1] = remaining - cum;   // still needed inside this digit
-        sh.misc[2] = cum;               // above, inside the current prefix
+        sh.misc[64] = digit;
+        sh.misc[65] = remaining - cum;
+        sh.misc[66] = cum;
       }
     }
     __syncthreads();
-    const uint32_t digit = (uint32_t)sh.misc[0];
-    gt += sh.misc[2];
-    remaining = sh.misc[1];
-    prefix |= digit << shift;
+    gt += sh.misc[66];
+    remaining = sh.misc[65];
+    prefix |= (uint32_t)sh.misc[64] << shift;
     pmask |= 0xFFu << shift;
     __syncthreads();
   }
@@ -104,44 +178,39 @@ __device__ void radix_select(const float* v, const Range& rg, int M, SelShared& 
   *take = remaining;
 }
 
-// Collect the top-M (key, index) composites into sh.sortbuf[0..M) and sort them
-// descending.  prefer_high: ties at the boundary keep the highest indices and
-// rank higher index higher (stable ascending rank); otherwise lowest indices first.
-__device__ void top_sorted(const float* v, const Range& rg, int M, bool prefer_high, SelShared& sh) {
+// The top-M (key, index) composites of v over rg, sorted descending, in sh.sortbuf[0..M).
+// prefer_high: at the boundary key keep the highest indices and rank a higher index
+// higher (stable ascending ranks); otherwise the lowest indices, ranked first (topk).
+__device__ void top_sorted(const float* v, const Range& rg, int M, bool prefer_high, SelSmem& sh) {
   uint32_t kstar;
   int above, take;
   radix_select(v, rg, M, sh, &kstar, &above, &take);
-  if (threadIdx.x == 0) { sh.misc[4] = 0; sh.misc[5] = 0; }
+  const int lane = threadIdx.x & 31;
+  // ties at the boundary key: rank them in index order
+  chunk_counts(rg.n, sh.cnt_a, [&](int i) { return rg.ok(i) && float_key(v[i]) == kstar; });
+  const int nties = scan_counts(sh.cnt_a, (rg.n + 31) / 32, sh.misc);
+  if (threadIdx.x == 0) sh.misc[67] = 0;
   __syncthreads();
-  // strictly above the boundary
-  for (int i = threadIdx.x; i < rg.n; i += blockDim.x) {
-    if (!rg.ok(i)) continue;
-    const uint32_t k = float_key(v[i]);
-    if (k > kstar) {
-      const int slot = atomicAdd(&sh.misc[4], 1);
-      const uint32_t tie = prefer_high ? (uint32_t)i : ~(uint32_t)i;
-      sh.sortbuf[slot] = ((unsigned long long)k << 32) | tie;
+  for (int base = threadIdx.x - lane; base < rg.n; base += blockDim.x) {
+    const int i = base + lane;
+    bool ok = i < rg.n && rg.ok(i);
+    const uint32_t k = ok ? float_key(v[i]) : 0u;
+    const uint32_t tie = prefer_high ? (uint32_t)i : ~(uint32_t)i;
+    // strictly above: warp-aggregated slot allocation
+    const unsigned ab = __ballot_sync(0xffffffffu, ok && k > kstar);
+    int basepos = 0;
+    if (lane == 0 && ab) basepos = atomicAdd(&sh.misc[67], __popc(ab));
+    basepos = __shfl_sync(0xffffffffu, basepos, 0);
+    if (ok && k > kstar) sh.sortbuf[basepos + __popc(ab & lanemask_lt())] = ((unsigned long long)k << 32) | tie;
+    // boundary ties in index order
+    const unsigned tb = __ballot_sync(0xffffffffu, ok && k == kstar);
+    if (ok && k == kstar) {
+      const int r = chunk_rank(sh.cnt_a, i, tb);
+      const int ord = prefer_high ? (nties - 1 - r) : r;   // highest index first when prefer_high
+      if (ord < take) sh.sortbuf[above + ord] = ((unsigned long long)kstar << 32) | tie;
     }
   }
-  // boundary ties: `take` of them, by index order (tiles of blockDim positions)
-  const int ntiles = (rg.n + blockDim.x - 1) / blockDim.x;
-  int taken = 0;
-  for (int tt = 0; tt < ntiles && taken < take; ++tt) {
-    const int t = prefer_high ? (ntiles - 1 - tt) : tt;
-    const int i = prefer_high ? (t * (int)blockDim.x + (int)(blockDim.x - 1 - threadIdx.x))
-                              : (t * (int)blockDim.x + (int)threadIdx.x);
-    const bool is_tie = i >= 0 && rg.ok(i) && float_key(v[i]) == kstar;
-    int tot;
-    const int before = block_exclusive_scan(is_tie ? 1 : 0, sh.scan, &tot);
-    if (is_tie && taken + before < take) {
-      const int slot = above + taken + before;
-      const uint32_t tie = prefer_high ? (uint32_t)i : ~(uint32_t)i;
-      sh.sortbuf[slot] = ((unsigned long long)kstar << 32) | tie;
-    }
-    taken += tot;
-  }
   __syncthreads();
-  // bitonic sort (descending) of the next power of two >= M
   int P = 1;
   while (P < M) P <<= 1;
   for (int i = M + threadIdx.x; i < P; i += blockDim.x) sh.sortbuf[i] = 0ull;
@@ -152,8 +221,7 @@ __device__ void top_sorted(const float* v, const Range& rg, int M, bool prefer_h
         const int l = i ^ j;
         if (l > i) {
           const unsigned long long a = sh.sortbuf[i], b = sh.sortbuf[l];
-          const bool desc = (i & k) == 0;
-          if (desc ? (a < b) : (a > b)) { sh.sortbuf[i] = b; sh.sortbuf[l] = a; }
+          if (((i & k) == 0) ? (a < b) : (a > b)) { sh.sortbuf[i] = b; sh.sortbuf[l] = a; }
         }
       }
       __syncthreads();
@@ -167,29 +235,34 @@ CKV_DEV int sorted_index(unsigned long long e, bool prefer_high) {
 }
 
 // ---------------------------------------------------------------------------
-// phase 0: finished scores from the sweep (PU:2186-2204)
+// finished chain scores (PU:2186-2204)
 // ---------------------------------------------------------------------------
-__device__ int early_stop_steps(const Plan& pl, const char* ws, SelShared& sh) {
+__device__ int early_stop_steps(const Plan& pl, const char* ws, float* scratch) {
   const float* cmax = reinterpret_cast<const float*>(ws + pl.off_cmax);
   const float* ymax = reinterpret_cast<const float*>(ws + pl.off_ymax);
+  // max over chunks of every (chain, term) at once: thread t handles (ch, k) pairs by warps
+  __shared__ float tmax[2][kMaxIters + 1];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int q = wid; q < pl.nchains * pl.K; q += kSelWarps) {
+    const int ch = q / pl.K, k = 1 + q % pl.K;
+    float m = 0.f;
+    if (pl.n_p > pl.s)
+      for (int c = lane; c < pl.nscan; c += 32)
+        m = fmaxf(m, __ldcg(cmax + ((size_t)ch * pl.nscan + c) * (kMaxIters + 1) + k));
+    m = warp_max(m);
+    if (lane == 0) tmax[ch][k] = fmaxf(m, __ldcg(ymax + ch * (pl.K + 1) + k));
+  }
+  __syncthreads();
   int steps = pl.K;
   for (int k = 1; k <= pl.K; ++k) {
-    bool all_small = true;
-    for (int ch = 0; ch < pl.nchains; ++ch) {
-      float m = 0.f;
-      if (pl.n_p > pl.s)
-        for (int c = threadIdx.x; c < pl.nscan; c += blockDim.x)
-          m = fmaxf(m, __ldcg(cmax + ((size_t)ch * pl.nscan + c) * (kMaxIters + 1) + k));
-      m = block_reduce<true>(m, sh.fscratch);
-      m = fmaxf(m, __ldcg(ymax + ch * (pl.K + 1) + k));
-      if (!(m < 1e-8f)) all_small = false;
-    }
-    if (all_small) { steps = k; break; }
+    bool small = true;
+    for (int ch = 0; ch < pl.nchains; ++ch) small = small && (tmax[ch][k] < 1e-8f);
+    if (small) { steps = k; break; }
   }
+  (void)scratch;
   return steps;
 }
 
-// Raw chain result at transient position j (sum of terms 0..steps).
 CKV_DEV float raw_result(const Plan& pl, const char* ws, int ch, int j, int steps) {
   if (j < pl.n_p) {
     const float* cum = reinterpret_cast<const float*>(ws + pl.off_cum) + (size_t)ch * (pl.K + 1) * pl.n_p;
@@ -202,22 +275,21 @@ CKV_DEV float raw_result(const Plan& pl, const char* ws, int ch, int j, int step
   return s;
 }
 
+// Writes the finished scores of chain ch into out (global, [n]).
 __device__ void finish_chain(const Plan& pl, const char* ws, int ch, int steps, float* out,
-                             SelShared& sh) {
+                             float* fscratch) {
   const int n = pl.n, s = pl.s;
   float tot = 0.f, mx = 0.f;
   for (int j = s + threadIdx.x; j < n; j += blockDim.x) {
     const float v = raw_result(pl, ws, ch, j, steps);
     out[j] = v;
     tot += v;
-  }
-  tot = block_reduce<false>(tot, sh.fscratch);
-  const float sinkv = tot * 0.01f;
-  for (int j = threadIdx.x; j < n; j += blockDim.x) {
-    const float v = (j < s) ? sinkv : out[j];
     mx = fmaxf(mx, v);
   }
-  mx = block_reduce<true>(mx, sh.fscratch);
+  tot = block_reduce<false>(tot, fscratch);
+  mx = block_reduce<true>(mx, fscratch);
+  const float sinkv = tot * 0.01f;
+  mx = fmaxf(mx, s > 0 ? sinkv : 0.f);
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
     float v = (j < s) ? sinkv : out[j];
     if (mx > 0.f) v = v / mx;
@@ -260,241 +332,238 @@ __device__ void smooth(const float* in, float* out, int n, int k, bool gaussian,
 }
 
 // ---------------------------------------------------------------------------
-// phase 2: keep sets
+// the cluster kernel
 // ---------------------------------------------------------------------------
-// Marks kept candidate positions in `keep` (1 byte per position, pre-zeroed).
-// Rank-MAX family: vectors vs[0..nv) with their ablation flags.
-__device__ void select_rank_max(const Plan& pl, const float* const* vs, const bool* zeroed, int nv,
-                                int* combR, uint8_t* keep, SelShared& sh, int32_t* status) {
-  const int n = pl.n, kk = pl.kk;
-  const int lo = pl.s, hi = pl.n - pl.W;   // candidates [s, n-W)
-  if (kk <= 0) return;
-  int live = 0;
-  for (int v = 0; v < nv; ++v) live += zeroed[v] ? 0 : 1;
-  if (live == 0) {
-    // every combined score is 0: topk takes the lowest candidate indices
-    for (int i = lo + threadIdx.x; i < lo + kk; i += blockDim.x) keep[i] = 1;
-    __syncthreads();
-    return;
-  }
-  const int M = min(n, kk + pl.s + pl.W);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) combR[i] = -1;
-  __syncthreads();
-  Range all{n, 0, n, false};
-  for (int v = 0; v < nv; ++v) {
-    if (zeroed[v]) continue;
-    top_sorted(vs[v], all, M, true, sh);
-    for (int p = threadIdx.x; p < M; p += blockDim.x) {
-      const int idx = sorted_index(sh.sortbuf[p], true);
-      atomicMax(&combR[idx], n - 1 - p);
-    }
-    __syncthreads();
-  }
-  // histogram of combined ranks >= n-M over the candidates
-  int* hist = reinterpret_cast<int*>(sh.sortbuf);   // M ints
-  for (int i = threadIdx.x; i < M; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-    const int r = __ldcg(combR + i);
-    if (r >= n - M) atomicAdd(&hist[r - (n - M)], 1);
-  }
-  __syncthreads();
-  {
-    // threshold: thread t owns bins from the top, [M - (t+1)c, M - t c)
-    const int c = (M + blockDim.x - 1) / blockDim.x;
-    const int bhi = M - (int)threadIdx.x * c, blo = max(0, bhi - c);
-    int local = 0;
-    for (int b = blo; b < bhi; ++b) local += hist[b];
-    int tot;
-    const int above = block_exclusive_scan(local, sh.scan, &tot);
-    if (threadIdx.x == 0) { sh.misc[8] = n; sh.misc[9] = 0; }
-    __syncthreads();
-    if (above < kk && above + local >= kk) {
-      int cum = above;
-      for (int b = bhi - 1; b >= blo; --b) {
-        if (cum + hist[b] >= kk) { sh.misc[8] = (n - M) + b; sh.misc[9] = kk - cum; break; }
-        cum += hist[b];
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && sh.misc[8] == n) set_status(status, kStatusCount);
-  }
-  const int t = sh.misc[8], need = sh.misc[9];
-  // above the threshold: keep; at the threshold: the lowest `need` indices
-  int taken = 0;
-  for (int base = lo; base < hi; base += blockDim.x) {
-    const int i = base + threadIdx.x;
-    const int r = (i < hi) ? __ldcg(combR + i) : -1;
-    if (r > t) keep[i] = 1;
-    const bool tie = (r == t);
-    int tot;
-    const int before = block_exclusive_scan(tie ? 1 : 0, sh.scan, &tot);
-    if (tie && taken + before < need) keep[i] = 1;
-    taken += tot;
-  }
-  __syncthreads();
-}
+__device__ void set_bit(uint32_t* bits, int i) { atomicOr(bits + (i >> 5), 1u << (i & 31)); }
+CKV_DEV bool get_bit(const uint32_t* bits, int i) { return (bits[i >> 5] >> (i & 31)) & 1u; }
 
-// Union keep set (PU:2489-2589).
-__device__ void select_union(const Plan& pl, const ckv_params& prm, const float* qi, const float* hi,
-                             uint8_t* keep, SelShared& sh) {
-  const int n = pl.n;
-  const int lo = pl.s, hiend = pl.n - pl.W;
-  const int cand = hiend - lo;
-  const int remaining = pl.kk;   // remaining budget (<= candidates already)
-  if (remaining <= 0 || cand <= 0) return;
-  const int qb = (int)((float)remaining * prm.qi_ratio);
-  const int hb = remaining - qb;
-  const int qk = min(qb, cand), hk = min(hb, cand);
-  Range rg{n, lo, hiend, true};
-  // QI top qk (lowest index among ties)
-  if (qk > 0) {
-    top_sorted(qi, rg, qk, false, sh);
-    for (int p = threadIdx.x; p < qk; p += blockDim.x) keep[sorted_index(sh.sortbuf[p], false)] = 1;
-    __syncthreads();
-  }
-  // HI extended list in topk order; the first hk always join, then fill
-  const int ext = min(cand, hb + qb + max(0, remaining));   // upper bound on what the fill can use
-  top_sorted(hi, rg, ext, false, sh);
-  for (int p = threadIdx.x; p < hk; p += blockDim.x) keep[sorted_index(sh.sortbuf[p], false)] = 1;
-  __syncthreads();
-  // count the union
-  int cnt = 0;
-  for (int i = lo + threadIdx.x; i < hiend; i += blockDim.x) cnt += keep[i];
-  cnt = (int)block_reduce<false>((float)cnt, sh.fscratch);
-  if (cnt < remaining && threadIdx.x < 32) {
-    // fill from the HI list in order, skipping members (one warp, 32 at a time)
-    int have = cnt;
-    for (int base = 0; base < ext && have < remaining; base += 32) {
-      const int p = base + threadIdx.x;
-      int idx = -1;
-      bool add = false;
-      if (p < ext) {
-        idx = sorted_index(sh.sortbuf[p], false);
-        add = keep[idx] == 0;
-      }
-      const unsigned ball = __ballot_sync(0xffffffffu, add);
-      const int rank = __popc(ball & ((1u << threadIdx.x) - 1));
-      if (add && have + rank < remaining) keep[idx] = 1;
-      have += __popc(ball);
-    }
-  }
-  __syncthreads();
-}
-
-// Kept prefix positions (sinks + chosen) in ascending order into out_idx.
-__device__ int compact(const Plan& pl, const uint8_t* keep, int32_t* out_idx, SelShared& sh) {
-  const int lim = pl.n - pl.W;
-  const int cap = pl.s + pl.kk;   // out_idx capacity
-  int written = 0;
-  for (int base = 0; base < lim; base += blockDim.x) {
-    const int i = base + threadIdx.x;
-    const bool k = (i < lim) && (i < pl.s || keep[i]);
-    int tot;
-    const int before = block_exclusive_scan(k ? 1 : 0, sh.scan, &tot);
-    if (k && written + before < cap) out_idx[written + before] = i;
-    written += tot;
-  }
-  // a short selection (never expected) leaves valid positions behind: pad with the last sink
-  for (int i = written + threadIdx.x; i < cap; i += blockDim.x) out_idx[i] = 0;
-  __syncthreads();
-  return written;
-}
-
-// ---------------------------------------------------------------------------
-// the kernel
-// ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kSelThreads) k_select(SelArgs a) {
   extern __shared__ __align__(16) char smraw[];
-  SelShared& sh = *reinterpret_cast<SelShared*>(smraw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int v = (int)cluster.block_rank();     // which score vector this CTA owns
   const Plan& pl = a.pl;
   const ckv_params& prm = a.p;
   char* ws = a.ws;
   Header* hdr = reinterpret_cast<Header*>(ws);
   const int n = pl.n;
-  float* sc = reinterpret_cast<float*>(ws + pl.off_sel);            // [3][n] finished scores
-  float* sm = sc + 3 * (size_t)n;                                   // [3][n] smoothed / weighted
-  int* combR = reinterpret_cast<int*>(sm + 3 * (size_t)n);          // [n]
-  uint8_t* keep = reinterpret_cast<uint8_t*>(combR + n);            // [n]
-
-  // ---- phase 0: finished scores
-  int steps = 0;
-  if (a.given) {
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-      sc[j] = a.ga[j];
-      sc[n + j] = a.gb ? a.gb[j] : 0.f;
-      sc[2 * n + j] = a.gc ? a.gc[j] : 0.f;
-    }
-    __syncthreads();
-  } else {
-    steps = early_stop_steps(pl, ws, sh);
-    for (int ch = 0; ch < pl.nchains; ++ch) finish_chain(pl, ws, ch, steps, sc + (size_t)ch * n, sh);
-    if (threadIdx.x == 0) hdr->steps = steps;
-  }
-  if (a.finish_only) {
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-      a.out_scores[j] = sc[j];
-      if (pl.nchains > 1) a.out_scores[n + j] = sc[n + j];
-    }
-    return;
-  }
-  for (int i = threadIdx.x; i < n; i += blockDim.x) keep[i] = 0;
-  __syncthreads();
-
+  const SelLayout L = sel_layout(n);
+  SelSmem sh;
+  sh.sortbuf = reinterpret_cast<unsigned long long*>(smraw + L.off_sort);
+  sh.hist = reinterpret_cast<int*>(sh.sortbuf);
+  float* sc = reinterpret_cast<float*>(ws + pl.off_sel);               // [3][n] finished scores
+  float* gx = sc + 3 * (size_t)n;                                      // [3][n] global vectors
+  int* gcomb = reinterpret_cast<int*>(gx + 3 * (size_t)n);             // [n]
+  sh.x = L.smem_scores ? reinterpret_cast<float*>(smraw + L.off_x) : gx + (size_t)v * n;
+  sh.cnt_a = reinterpret_cast<int*>(smraw + L.off_cnt_a);
+  sh.cnt_b = reinterpret_cast<int*>(smraw + L.off_cnt_b);
+  sh.bits = reinterpret_cast<uint32_t*>(smraw + L.off_bits);
+  sh.misc = reinterpret_cast<int*>(smraw + L.off_misc);
+  sh.fmisc = reinterpret_cast<float*>(sh.misc + 128);
   const int mode = pl.mode;
-  if (mode == CKV_COMB_DIS) {
-    int qk = prm.qi_kernel_size != 0 ? prm.qi_kernel_size : prm.smoothing_kernel;
-    const int hk = prm.hi_kernel_size != 0 ? prm.hi_kernel_size : prm.smoothing_kernel;
-    if (prm.smooth_hi_only && qk > 1) qk = 0;
-    const float qsig = prm.use_gaussian ? prm.gaussian_sigma * 0.5f : 1.0f;
-    smooth(sc, sm, n, qk, prm.use_gaussian, qsig);
-    smooth(sc + n, sm + n, n, hk, prm.use_gaussian, prm.gaussian_sigma);
-    const bool bridge = prm.use_bridge_importance && (a.given ? a.gc != nullptr : true);
-    if (bridge) smooth(sc + 2 * n, sm + 2 * n, n, prm.bi_kernel_size, prm.use_gaussian, prm.gaussian_sigma);
-    if (a.out_scores)
-      for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        a.out_scores[j] = sm[j];
-        a.out_scores[n + j] = sm[n + j];
-      }
-    const float* vs[3] = {sm, sm + n, sm + 2 * n};
-    const bool z[3] = {prm.ablate_qi != 0, prm.ablate_hi != 0, false};
-    select_rank_max(pl, vs, z, bridge ? 3 : 2, combR, keep, sh, &hdr->status);
-  } else if (mode == CKV_COMB_MAX) {
-    // a = influence (chain 0), b = H2O column sums
-    if (a.out_scores)
-      for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        a.out_scores[j] = sc[j];
-        a.out_scores[n + j] = sc[n + j];
-      }
-    const float* vs[2] = {sc, sc + n};
-    const bool z[2] = {false, false};
-    select_rank_max(pl, vs, z, 2, combR, keep, sh, &hdr->status);
-  } else {   // union / union_da
-    if (mode == CKV_COMB_UNION_DA && !a.given) {
-      // DA = column sums of the QI window rows, clamped at 1e-8 (PU:3086-3091)
+  const bool dis = mode == CKV_COMB_DIS;
+
+  // ---- phase 0: this CTA's vector into sc[v], then (smoothed) into x
+  float* mysc = sc + (size_t)v * n;
+  if (a.given) {
+    const float* g = v == 0 ? a.ga : (v == 1 ? a.gb : a.gc);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) mysc[j] = g[j];
+    __syncthreads();
+  } else if (v < pl.nchains) {
+    const int steps = early_stop_steps(pl, ws, sh.fmisc);
+    finish_chain(pl, ws, v, steps, mysc, sh.fmisc);
+    if (v == 0 && threadIdx.x == 0) hdr->steps = steps;
+    if (mode == CKV_COMB_UNION_DA) {
       const float* colsum = reinterpret_cast<const float*>(ws + pl.off_colsum);
-      for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        const float da = fmaxf(colsum[j], 1e-8f);
-        sc[j] = sc[j] * da;
-        sc[n + j] = sc[n + j] * da;
-      }
+      for (int j = threadIdx.x; j < n; j += blockDim.x) mysc[j] = mysc[j] * fmaxf(colsum[j], 1e-8f);
       __syncthreads();
     }
-    if (a.out_scores)
-      for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        a.out_scores[j] = sc[j];
-        a.out_scores[n + j] = sc[n + j];
+  }
+  if (a.finish_only) {
+    if (v < pl.nchains)
+      for (int j = threadIdx.x; j < n; j += blockDim.x) a.out_scores[(size_t)v * n + j] = mysc[j];
+    return;
+  }
+  if (dis) {
+    int k;
+    float sig;
+    if (v == 0) {
+      k = prm.qi_kernel_size != 0 ? prm.qi_kernel_size : prm.smoothing_kernel;
+      if (prm.smooth_hi_only && k > 1) k = 0;
+      sig = prm.use_gaussian ? prm.gaussian_sigma * 0.5f : 1.0f;
+    } else if (v == 1) {
+      k = prm.hi_kernel_size != 0 ? prm.hi_kernel_size : prm.smoothing_kernel;
+      sig = prm.gaussian_sigma;
+    } else {
+      k = prm.bi_kernel_size;
+      sig = prm.gaussian_sigma;
+    }
+    smooth(mysc, sh.x, n, k, prm.use_gaussian, sig);
+  } else {
+    for (int j = threadIdx.x; j < n; j += blockDim.x) sh.x[j] = mysc[j];
+    __syncthreads();
+  }
+  if (a.out_scores && v < 2)
+    for (int j = threadIdx.x; j < n; j += blockDim.x) a.out_scores[(size_t)v * n + j] = sh.x[j];
+
+  // ---- phase 1: this vector's top list
+  const int lo = pl.s, hi = pl.n - pl.W;   // candidates [s, n-W)
+  const int kk = pl.kk;
+  const bool uni = mode == CKV_COMB_UNION || mode == CKV_COMB_UNION_DA;
+  int M = 0;
+  if (uni) {
+    const int remaining = kk, cand = hi - lo;
+    const int qb = (int)((float)remaining * prm.qi_ratio), hb = remaining - qb;
+    M = (v == 0) ? min(qb, cand) : min(cand, hb + qb + remaining);
+    if (threadIdx.x == 0) { sh.misc[70] = min(qb, cand); sh.misc[71] = min(hb, cand); }
+    if (M > 0) top_sorted(sh.x, Range{n, lo, hi, true}, M, false, sh);
+  } else {
+    const bool zeroed = (dis && v == 0 && prm.ablate_qi) || (dis && v == 1 && prm.ablate_hi);
+    M = min(n, kk + pl.s + pl.W);
+    if (!zeroed && kk > 0) top_sorted(sh.x, Range{n, 0, n, false}, M, true, sh);
+  }
+  if (threadIdx.x == 0) sh.misc[72] = M;
+  cluster.sync();
+
+  // ---- phase 2 (CTA 0): combine, threshold, compact
+  if (v == 0) {
+    const int nv = cluster.num_blocks();
+    for (int i = threadIdx.x; i < L.nchunk; i += blockDim.x) sh.bits[i] = 0u;
+    __syncthreads();
+    if (kk > 0 && uni) {
+      const int qk = sh.misc[70], hk = sh.misc[71];
+      const unsigned long long* hl = cluster.map_shared_rank(sh.sortbuf, 1);
+      const int ext = *cluster.map_shared_rank(sh.misc + 72, 1);
+      for (int p = threadIdx.x; p < qk; p += blockDim.x) set_bit(sh.bits, sorted_index(sh.sortbuf[p], false));
+      __syncthreads();
+      for (int p = threadIdx.x; p < hk; p += blockDim.x) set_bit(sh.bits, sorted_index(hl[p], false));
+      __syncthreads();
+      int cnt = 0;
+      for (int i = threadIdx.x; i < L.nchunk; i += blockDim.x) cnt += __popc(sh.bits[i]);
+      cnt = (int)block_reduce<false>((float)cnt, sh.fmisc);
+      if (cnt < kk && threadIdx.x < 32) {
+        int have = cnt;
+        for (int base = 0; base < ext && have < kk; base += 32) {
+          const int p = base + threadIdx.x;
+          int idx = -1;
+          bool add = false;
+          if (p < ext) { idx = sorted_index(hl[p], false); add = !get_bit(sh.bits, idx); }
+          const unsigned ball = __ballot_sync(0xffffffffu, add);
+          if (add && have + __popc(ball & lanemask_lt()) < kk) set_bit(sh.bits, idx);
+          have += __popc(ball);
+        }
       }
-    select_union(pl, prm, sc, sc + n, keep, sh);
+      __syncthreads();
+    } else if (kk > 0) {
+      int live = 0;
+      for (int u = 0; u < nv; ++u) live += *cluster.map_shared_rank(sh.misc + 72, u) > 0 &&
+                                           !((dis && u == 0 && prm.ablate_qi) || (dis && u == 1 && prm.ablate_hi));
+      const int Mx = min(n, kk + pl.s + pl.W);
+      if (live == 0) {
+        for (int i = lo + threadIdx.x; i < lo + kk; i += blockDim.x) set_bit(sh.bits, i);
+        __syncthreads();
+      } else {
+        // combined ranks of the union of the top lists (others: below every kept rank)
+        int* comb = L.smem_scores ? reinterpret_cast<int*>(sh.x) : gcomb;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) comb[i] = -1;
+        __syncthreads();
+        for (int u = 0; u < nv; ++u) {
+          const bool zeroed = (dis && u == 0 && prm.ablate_qi) || (dis && u == 1 && prm.ablate_hi);
+          if (zeroed) continue;
+          const unsigned long long* lst = cluster.map_shared_rank(sh.sortbuf, u);
+          for (int p = threadIdx.x; p < Mx; p += blockDim.x)
+            atomicMax(&comb[sorted_index(lst[p], true)], n - 1 - p);
+        }
+        __syncthreads();
+        // histogram of combined ranks >= n - Mx over the candidates (cnt_b reused as bins)
+        // bins over [n - Mx, n): CTA 0's own list has been consumed, its buffer is free
+        int* hbuf = sh.hist;
+        for (int i = threadIdx.x; i < Mx; i += blockDim.x) hbuf[i] = 0;
+        __syncthreads();
+        for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+          const int r = comb[i];
+          if (r >= n - Mx) atomicAdd(&hbuf[r - (n - Mx)], 1);
+        }
+        __syncthreads();
+        {
+          const int c = (Mx + blockDim.x - 1) / blockDim.x;
+          const int bhi = Mx - (int)threadIdx.x * c, blo = max(0, bhi - c);
+          int local = 0;
+          for (int b = blo; b < bhi; ++b) local += hbuf[b];
+          int tot;
+          const int above = block_exclusive_scan(local, sh.misc, &tot);
+          if (threadIdx.x == 0) { sh.misc[80] = n; sh.misc[81] = 0; }
+          __syncthreads();
+          if (above < kk && above + local >= kk) {
+            int cum = above;
+            for (int b = bhi - 1; b >= blo; --b) {
+              if (cum + hbuf[b] >= kk) { sh.misc[80] = (n - Mx) + b; sh.misc[81] = kk - cum; break; }
+              cum += hbuf[b];
+            }
+          }
+          __syncthreads();
+          if (threadIdx.x == 0 && sh.misc[80] == n) set_status(&hdr->status, kStatusCount);
+        }
+        const int t = sh.misc[80], need = sh.misc[81];
+        // at the threshold: the lowest `need` candidate indices
+        chunk_counts(n, sh.cnt_a, [&](int i) { return i >= lo && i < hi && comb[i] == t; });
+        scan_counts(sh.cnt_a, L.nchunk, sh.misc);
+        const int lane = threadIdx.x & 31;
+        for (int base = threadIdx.x - lane; base < n; base += blockDim.x) {
+          const int i = base + lane;
+          const bool cand = i < n && i >= lo && i < hi;
+          const int r = cand ? comb[i] : -1;
+          const unsigned tb = __ballot_sync(0xffffffffu, cand && r == t);
+          if (cand && (r > t || (r == t && chunk_rank(sh.cnt_a, i, tb) < need))) set_bit(sh.bits, i);
+        }
+        __syncthreads();
+      }
+    }
+    // compaction: sinks + chosen, ascending
+    const int cap = pl.s + kk;
+    chunk_counts(hi, sh.cnt_a, [&](int i) { return i < pl.s || get_bit(sh.bits, i); });
+    const int total = scan_counts(sh.cnt_a, (hi + 31) / 32, sh.misc);
+    const int lane = threadIdx.x & 31;
+    for (int base = threadIdx.x - lane; base < hi; base += blockDim.x) {
+      const int i = base + lane;
+      const bool kp = i < hi && (i < pl.s || get_bit(sh.bits, i));
+      const unsigned b = __ballot_sync(0xffffffffu, kp);
+      if (kp) {
+        const int r = chunk_rank(sh.cnt_a, i, b);
+        if (r < cap) a.out_idx[r] = i;
+      }
+    }
+    for (int i = total + threadIdx.x; i < cap; i += blockDim.x) a.out_idx[i] = 0;
+    if (threadIdx.x == 0) {
+      hdr->kept = total;
+      if (total != cap) set_status(&hdr->status, kStatusCount);
+    }
   }
-  __syncthreads();
-  const int written = compact(pl, keep, a.out_idx, sh);
-  if (threadIdx.x == 0) {
-    hdr->kept = written;
-    if (written != pl.s + pl.kk) set_status(&hdr->status, kStatusCount);
-  }
+  cluster.sync();   // the other CTAs' lists stay alive until CTA 0 is done
 }
 
+size_t select_smem_bytes_n(int n) { return sel_layout(n).total; }
+
+cudaError_t launch_select(const SelArgs& a, cudaStream_t st) {
+  const Plan& pl = a.pl;
+  const bool bridge = pl.mode == CKV_COMB_DIS && a.p.use_bridge_importance &&
+                      (a.given ? a.gc != nullptr : true);
+  const int nv = a.finish_only ? pl.nchains : (bridge ? 3 : 2);
+  const size_t smem = sel_layout(pl.n).total;
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_select, smem); if (e != cudaSuccess) return e; }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nv, 1, 1);
+  cfg.blockDim = dim3(kSelThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = nv;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_select, a);
+}
 
 // ---------------------------------------------------------------------------
 // H2O column sums and bridge importance (one CTA)
@@ -592,20 +661,6 @@ cudaError_t launch_aux(const Plan& pl, const ckv_params& p, char* ws, cudaStream
   return cudaGetLastError();
 }
 
-size_t select_smem_bytes() { return sizeof(SelShared); }
-
-cudaError_t launch_select(const SelArgs& a, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)sizeof(SelShared));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  k_select<<<1, kSelThreads, sizeof(SelShared), st>>>(a);
-  return cudaGetLastError();
-}
-
 // ---------------------------------------------------------------------------
 // Selection with no workspace argument (ckv_select_scores_noalloc)
 // ---------------------------------------------------------------------------
@@ -620,7 +675,7 @@ cudaError_t launch_select(const SelArgs& a, cudaStream_t st) {
 // overlap on the GPU (different streams, or different host threads on one device)
 // race; order them on one stream.
 constexpr int kNoAllocMaxN = 32768;
-constexpr size_t kNoAllocBytes = 256 + (size_t)29 * kNoAllocMaxN;
+constexpr size_t kNoAllocBytes = sizeof(Header) + (size_t)29 * kNoAllocMaxN;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 // Device address of g_noalloc_scratch per device, looked up once per device with
@@ -658,8 +713,8 @@ int select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const 
   int rc = make_plan(*p, n, 32, 8, 128, CKV_BF16, &pl, why);
   if (rc) return rc;
   // only the header and the selection area are touched by the given-scores path
-  pl.off_sel = 256;
-  pl.total = 256 + pl.sel_bytes;
+  pl.off_sel = sizeof(Header);
+  pl.total = sizeof(Header) + pl.sel_bytes;
   if (pl.total > kNoAllocBytes) { *why = "selection scratch larger than the static array"; return CKV_ERR_ARG; }
   void* base = nullptr;
   cudaError_t e = noalloc_scratch(&base);

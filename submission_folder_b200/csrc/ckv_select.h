@@ -20,7 +20,7 @@ struct SelArgs {
   int finish_only;       // 1: stop after the finished chain scores (written to out_scores)
 };
 
-size_t select_smem_bytes();
+size_t select_smem_bytes_n(int n);
 cudaError_t launch_select(const SelArgs& a, cudaStream_t st);
 // H2O column sums of full_attn (mode max / weighted) and bridge importance (dis + bridge).
 // Selection stage with its scratch in a static device array (no workspace argument).

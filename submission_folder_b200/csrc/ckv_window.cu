@@ -19,16 +19,25 @@
 // (PU:2874-2877).
 #include <math.h>
 
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "ckv_common.cuh"
 #include "ckv_plan.h"
+#include "ckv_tc.cuh"
 #include "ckv_window.h"
 
 namespace ckv {
 
 __device__ void window_pool_finish(const WinArgs& a, char* smem);
-__device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem);
+__device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh);
+CKV_DEV float sum_parts(const float* base, int nparts, size_t stride, int first, int step);
+__device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem,
+                                  bool use_rowsums);
 
 constexpr float kGeps = 1.8420680743952367e-07f;   // -1e-8 * ln(1e-8): a clamped entry
+constexpr float kLog2Eps = -26.575424759098897f;     // log2(1e-8)
 
 // ---------------------------------------------------------------------------
 // shared-memory staging
@@ -154,9 +163,11 @@ template <int DT> struct WarpTile {
 };
 
 // Reference rounding of a logit: dtype(dtype(acc) / sqrt(D)) for 16-bit inputs, acc / sqrt(D) for fp32.
+// (bf16: the reciprocal product of the reference's CUDA division by a scalar; fp16 divides.)
 template <int DT> CKV_DEV float logit_of(float acc, float scale) {
   if constexpr (DT == CKV_FP32) return __fdiv_rn(acc, scale);
-  return round_dt<DT>(__fdiv_rn(round_dt<DT>(acc), scale));
+  if constexpr (DT == CKV_FP16) return round_dt<DT>(__fdiv_rn(round_dt<DT>(acc), scale));
+  return round_dt<DT>(round_dt<DT>(acc) * __frcp_rn(scale));
 }
 
 // ---------------------------------------------------------------------------
@@ -182,65 +193,67 @@ CKV_DEV Moments merge(const Moments& a, const Moments& b) {
 // ---------------------------------------------------------------------------
 // head selection (PU:2905-2999) from per-head entropy and transient mass
 // ---------------------------------------------------------------------------
+// Called by every thread of the block (>= 64 threads); ent / mass in shared or
+// global memory, visible to all.  Ranks are computed one head per thread.
 __device__ void select_heads(const ckv_params& p, int H, const float* ent, const float* mass,
                              uint64_t* qi_set, uint64_t* hi_set, int* hi_mode, int* n_hi) {
+  __shared__ unsigned long long sq, sh_, ssel;
+  __shared__ int s_order[kMaxHeads];
+  __shared__ int s_mode, s_nhi;
   const uint64_t all = (H >= 64) ? ~0ull : ((1ull << H) - 1);
+  const int h = threadIdx.x;
+  if (h == 0) { sq = 0; sh_ = 0; ssel = 0; }
+  __syncthreads();
   if (!p.entropy_aware) {
     *qi_set = all; *hi_set = all; *hi_mode = 2; *n_hi = H;
     return;
   }
-  // QI: the k lowest entropies (or highest masses); ties resolved by head index.
   const int k = min(p.top_k_heads, H);
-  uint64_t q = 0;
-  for (int h = 0; h < H; ++h) {
-    int better = 0;
+  int rank_q = 0, rank_m = 0;
+  if (h < H) {
     for (int o = 0; o < H; ++o) {
-      bool b;
-      if (p.head_selection_mode == 1) b = mass[o] > mass[h] || (mass[o] == mass[h] && o < h);
-      else b = ent[o] < ent[h] || (ent[o] == ent[h] && o < h);
-      better += b ? 1 : 0;
+      const bool bq = (p.head_selection_mode == 1) ? (mass[o] > mass[h] || (mass[o] == mass[h] && o < h))
+                                                   : (ent[o] < ent[h] || (ent[o] == ent[h] && o < h));
+      rank_q += bq ? 1 : 0;
+      rank_m += (mass[o] > mass[h] || (mass[o] == mass[h] && o < h)) ? 1 : 0;   // descending mass
     }
-    if (better < k) q |= 1ull << h;
+    if (rank_q < k) atomicOr(&sq, 1ull << h);
+    s_order[rank_m] = h;
   }
-  *qi_set = q;
-  if (p.hi_pooling_mode == 1) { *hi_set = all; *hi_mode = 1; *n_hi = H; return; }
-  uint64_t hs = all;
-  if (p.hi_mass_cdf > 0.f) {
-    float total = 0.f;
-    for (int h = 0; h < H; ++h) total += mass[h];
-    if (total > 0.f) {
-      // heads in descending mass order until the cumulative share reaches the threshold
-      int need = 1;
-      float cum = 0.f;
-      int order[kMaxHeads];
-      for (int h = 0; h < H; ++h) {
-        int pos = 0;
-        for (int o = 0; o < H; ++o)
-          pos += (mass[o] > mass[h] || (mass[o] == mass[h] && o < h)) ? 1 : 0;
-        order[pos] = h;
+  __syncthreads();
+  if (h == 0) {
+    uint64_t hs = all;
+    int mode = 0;
+    if (p.hi_pooling_mode == 1) {
+      mode = 1;
+    } else if (p.hi_mass_cdf > 0.f) {
+      float total = 0.f;
+      for (int o = 0; o < H; ++o) total += mass[o];
+      if (total > 0.f) {
+        float cum = 0.f;
+        int below = 0;
+        for (int i = 0; i < H; ++i) { cum += mass[s_order[i]]; if (cum / total < p.hi_mass_cdf) ++below; }
+        const int need = min(below + 1, H);
+        hs = 0;
+        for (int i = 0; i < need; ++i) hs |= 1ull << s_order[i];
       }
-      int below = 0;
-      for (int i = 0; i < H; ++i) { cum += mass[order[i]]; if (cum / total < p.hi_mass_cdf) ++below; }
-      need = min(below + 1, H);
+    } else if (p.hi_top_k_heads > 0) {
+      const int kh = min(p.hi_top_k_heads, H);
       hs = 0;
-      for (int i = 0; i < need; ++i) hs |= 1ull << order[i];
-    }
-  } else if (p.hi_top_k_heads > 0) {
-    const int kh = min(p.hi_top_k_heads, H);
-    hs = 0;
-    for (int h = 0; h < H; ++h) {
-      int better = 0;
+      for (int i = 0; i < kh; ++i) hs |= 1ull << s_order[i];
+    } else if (p.hi_mass_threshold > 0.f) {
+      hs = 0;
       for (int o = 0; o < H; ++o)
-        better += (mass[o] > mass[h] || (mass[o] == mass[h] && o < h)) ? 1 : 0;
-      if (better < kh) hs |= 1ull << h;
+        if (mass[o] >= p.hi_mass_threshold) hs |= 1ull << o;
+      if (hs == 0) hs = all;
     }
-  } else if (p.hi_mass_threshold > 0.f) {
-    hs = 0;
-    for (int h = 0; h < H; ++h)
-      if (mass[h] >= p.hi_mass_threshold) hs |= 1ull << h;
-    if (hs == 0) hs = all;
+    sh_ = hs;
+    s_mode = mode;
+    s_nhi = __popcll(hs);
   }
-  *hi_set = hs; *hi_mode = 0; *n_hi = __popcll(hs);
+  __syncthreads();
+  *qi_set = sq; *hi_set = sh_; *hi_mode = s_mode; *n_hi = s_nhi;
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------
@@ -416,50 +429,92 @@ __global__ void __launch_bounds__(256) k_window_stats(WinArgs a) {
       }
     }
 
-  // ---- the last CTA merges the chunks and speculates the head sets ----
+  stats_finish(a, smem, bg.h0, pl.heads_per_batch);
+}
+
+// Last-CTA steps of the moments pass (PU:2905-2999).  The last CTA of each head
+// group merges the chunk partials of the group's rows into their log-sum-exp, the
+// unclamped entropy and the transient mass, and writes the group's per-head means;
+// the last group then speculates the head sets from them.
+__device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
+  const Plan& pl = a.pl;
+  const float4* part = reinterpret_cast<const float4*>(a.ws + pl.off_stats);
+  Header* hdr = reinterpret_cast<Header*>(a.ws);
   __shared__ bool last;
   __threadfence();
   __syncthreads();
-  Header* hdr = reinterpret_cast<Header*>(a.ws);
-  if (threadIdx.x == 0) {
-    const uint32_t total = gridDim.x * gridDim.y;
-    last = atomicAdd(&hdr->cnt_stats, 1u) == total - 1;
-  }
+  if (threadIdx.x == 0) last = atomicAdd(&hdr->cnt_group[blockIdx.y], 1u) == gridDim.x - 1;
   __syncthreads();
   if (!last) return;
   __threadfence();
   float* lse = reinterpret_cast<float*>(a.ws + pl.off_lse);
   float* spec = reinterpret_cast<float*>(a.ws + pl.off_spec);   // [H] entropy, [H] mass
-  float* rowE = reinterpret_cast<float*>(smem);                  // [H*W]
-  float* rowM = rowE + pl.H * pl.W;
-  for (int i = threadIdx.x; i < pl.H * pl.W; i += blockDim.x) {
+  const int nrows = nh * pl.W, i0 = h0 * pl.W;
+  float* rowE = reinterpret_cast<float*>(smem);                  // [nrows]
+  float* rowM = rowE + nrows;
+  // tpr consecutive lanes share a row; each merges every tpr-th chunk, 8 loads in flight
+  int tpr = 1;
+  while (tpr < 8 && tpr * 2 * nrows <= (int)blockDim.x) tpr *= 2;
+  const int sub = threadIdx.x % tpr;
+  for (int base = 0; base < nrows * tpr; base += blockDim.x) {
+    const int li = (base + threadIdx.x) / tpr;
+    const bool valid = li < nrows;
     Moments M{-INFINITY, 0.f, 0.f, 0.f};
-    for (int c = 0; c < pl.nstat_chunks; ++c) {
-      const float4 v = __ldcg(part + (size_t)c * pl.H * pl.W + i);
-      M = merge(M, Moments{v.x, v.y, v.z, v.w});
+    if (valid) {
+      for (int c0 = sub; c0 < pl.nstat_chunks; c0 += 8 * tpr) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (c0 + u * tpr < pl.nstat_chunks) v[u] = __ldcg(part + (size_t)(c0 + u * tpr) * pl.H * pl.W + i0 + li);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (c0 + u * tpr < pl.nstat_chunks) M = merge(M, Moments{v[u].x, v[u].y, v[u].z, v[u].w});
+      }
     }
-    const float l2z = log2f(M.z);
-    lse[i] = M.m + l2z;
-    const int r = i % pl.W;
-    rowE[i] = l2z * kLn2 - kLn2 * (M.t / M.z) + (float)(pl.W - 1 - r) * kGeps;
-    rowM[i] = 1.f - M.s / M.z;
+    for (int o = 1; o < tpr; o <<= 1) {   // lanes of one row are consecutive within a warp
+      Moments O;
+      O.m = __shfl_xor_sync(0xffffffffu, M.m, o);
+      O.z = __shfl_xor_sync(0xffffffffu, M.z, o);
+      O.t = __shfl_xor_sync(0xffffffffu, M.t, o);
+      O.s = __shfl_xor_sync(0xffffffffu, M.s, o);
+      M = merge(M, O);
+    }
+    if (valid && sub == 0) {
+      const float l2z = log2f(M.z);
+      lse[i0 + li] = M.m + l2z;
+      const int r = li % pl.W;
+      rowE[li] = l2z * kLn2 - kLn2 * (M.t / M.z) + (float)(pl.W - 1 - r) * kGeps;
+      rowM[li] = 1.f - M.s / M.z;
+    }
   }
   __syncthreads();
-  for (int h = threadIdx.x; h < pl.H; h += blockDim.x) {
+  for (int hl = threadIdx.x; hl < nh; hl += blockDim.x) {
     float e = 0.f, m = 0.f;
-    for (int r = 0; r < pl.W; ++r) { e += rowE[h * pl.W + r]; m += rowM[h * pl.W + r]; }
-    spec[h] = e / (float)pl.W;
-    spec[pl.H + h] = m / (float)pl.W;
+    for (int r = 0; r < pl.W; ++r) { e += rowE[hl * pl.W + r]; m += rowM[hl * pl.W + r]; }
+    spec[h0 + hl] = e / (float)pl.W;
+    spec[pl.H + h0 + hl] = m / (float)pl.W;
   }
+  // the last group selects the heads
+  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    uint64_t qs, hs;
-    int hm, nh;
-    select_heads(a.p, pl.H, spec, spec + pl.H, &qs, &hs, &hm, &nh);
+    hdr->cnt_group[blockIdx.y] = 0;
+    last = atomicAdd(&hdr->cnt_stats, 1u) == gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float* sSpec = rowE;                                           // [2H]
+  for (int h = threadIdx.x; h < 2 * pl.H; h += blockDim.x) sSpec[h] = __ldcg(spec + h);
+  __syncthreads();
+  uint64_t qs, hs;
+  int hm, nhi;
+  select_heads(a.p, pl.H, sSpec, sSpec + pl.H, &qs, &hs, &hm, &nhi);
+  if (threadIdx.x == 0) {
     hdr->qi_heads = qs;
     hdr->hi_heads = hs;
     hdr->hi_mode = hm;
-    hdr->n_hi = nh;
+    hdr->n_hi = nhi;
     hdr->fixup = 0;
     hdr->cnt_stats = 0;
   }
@@ -607,7 +662,7 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
     __syncthreads();
     for (int r = threadIdx.x; r < pl.W; r += blockDim.x) {
       const int i = r / 4, w = 2 * (r % 4);
-      rspart[((size_t)ch * pl.ncol_tiles + tile) * pl.W + r] = sRed[i][w] + sRed[i][w + 1];
+      rspart[((size_t)ch * pl.rs_parts + tile) * pl.W + r] = sRed[i][w] + sRed[i][w + 1];
     }
     if (threadIdx.x < kColTile) {
       const int jj = j0 + threadIdx.x;
@@ -623,21 +678,10 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
       if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = g;
     }
     __syncthreads();
-    if (threadIdx.x == 0) gtile[(size_t)ch * pl.ncol_tiles + tile] = red[0] + red[1];
+    if (threadIdx.x == 0) gtile[(size_t)ch * pl.ncol_tiles * 8 + tile] = red[0] + red[1];
     __syncthreads();
   }
 
-  // ---- the last CTA verifies the head sets and runs the window chain ----
-  __shared__ bool last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    last = atomicAdd(&hdr->cnt_pool, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  window_pool_finish(a, smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -646,33 +690,25 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
 __device__ void window_pool_finish(const WinArgs& a, char* smem) {
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
-  const float* epart = reinterpret_cast<const float*>(a.ws + pl.off_epart);
-  const float* mpart = reinterpret_cast<const float*>(a.ws + pl.off_mpart);
   float* exact = reinterpret_cast<float*>(a.ws + pl.off_spec) + 2 * pl.H;   // [H] ent, [H] mass
-  float* rowE = reinterpret_cast<float*>(smem);
-  float* rowM = rowE + pl.H * pl.W;
-  for (int i = threadIdx.x; i < pl.H * pl.W; i += blockDim.x) {
-    float e = 0.f, m = 0.f;
-    for (int t = 0; t < pl.ncol_tiles; ++t) {
-      e += __ldcg(epart + (size_t)t * pl.H * pl.W + i);
-      m += __ldcg(mpart + (size_t)t * pl.H * pl.W + i);
-    }
-    rowE[i] = e;
-    rowM[i] = m;
-  }
+  const float* rowE = reinterpret_cast<const float*>(a.ws + pl.off_stats);   // [H*W] (k_pool_reduce)
+  const float* rowM = rowE + pl.H * pl.W;
+  float* sE = reinterpret_cast<float*>(smem);       // [H*W]
+  float* sM = sE + pl.H * pl.W;                     // [H*W]
+  for (int i = threadIdx.x; i < pl.H * pl.W; i += blockDim.x) { sE[i] = __ldcg(rowE + i); sM[i] = __ldcg(rowM + i); }
   __syncthreads();
   for (int h = threadIdx.x; h < pl.H; h += blockDim.x) {
     float e = 0.f, m = 0.f;
-    for (int r = 0; r < pl.W; ++r) { e += rowE[h * pl.W + r]; m += rowM[h * pl.W + r]; }
+    for (int r = 0; r < pl.W; ++r) { e += sE[h * pl.W + r]; m += sM[h * pl.W + r]; }
     exact[h] = e / (float)pl.W;
     exact[pl.H + h] = m / (float)pl.W;
   }
   __syncthreads();
   __shared__ int redo;
+  uint64_t qs, hs;
+  int hm, nh;
+  select_heads(a.p, pl.H, exact, exact + pl.H, &qs, &hs, &hm, &nh);
   if (threadIdx.x == 0) {
-    uint64_t qs, hs;
-    int hm, nh;
-    select_heads(a.p, pl.H, exact, exact + pl.H, &qs, &hs, &hm, &nh);
     redo = (qs != hdr->qi_heads || hs != hdr->hi_heads || hm != hdr->hi_mode) ? 1 : 0;
     if (redo && !a.fixup_pass) {
       hdr->qi_heads = qs;
@@ -688,14 +724,15 @@ __device__ void window_pool_finish(const WinArgs& a, char* smem) {
   __syncthreads();
   if (redo) return;   // the fixup launch redoes the pooling and this step
 
-  run_window_chains(a.pl, a.p, a.ws, reinterpret_cast<float*>(smem));
+  run_window_chains(a.pl, a.p, a.ws, reinterpret_cast<float*>(smem), true);
 }
 
 // Row sums (tempered) of the pooled rows and the W x W window chain of each
 // absorbing chain: y_0 (query one-hot or uniform), y_{k+1} = gamma * Pww^T y_k.
 // Writes y_k, the weights w_k = gamma * y_k / rowsum used by the prefix sweep,
-// and max_c y_k.  One CTA; `smem` >= W*W + 5*W + 32 floats.
-__device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem) {
+// and max_c y_k.  One CTA; `smem` >= W*W + 7*W + 32 floats.
+__device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem,
+                                  bool use_rowsums) {
   // row sums (tempered), then the W x W window chain of each absorbing chain
   const int W = pl.W, K = pl.K;
   const bool tempered = prm.neumann_temperature != 1.0f && prm.neumann_temperature > 0.f;
@@ -714,10 +751,11 @@ __device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* w
     const float* rows = reinterpret_cast<const float*>(ws + (own && ch == 1 ? pl.off_rows_hi
                                                                                : pl.off_rows_qi));
     const int src = own ? ch : 0;
+    const float* rowS = reinterpret_cast<const float*>(ws + pl.off_stats) + 2 * pl.H * W;   // from k_pool_reduce
     for (int r = threadIdx.x; r < W; r += blockDim.x) {
-      float s = 0.f;
-      for (int t = 0; t < pl.ncol_tiles; ++t)
-        s += __ldcg(rspart + ((size_t)src * pl.ncol_tiles + t) * W + r);
+      float s;
+      if (use_rowsums) s = __ldcg(rowS + ch * W + r);
+      else s = sum_parts(rspart + (size_t)src * pl.rs_parts * W + r, pl.rs_parts, (size_t)W, 0, 1);
       sRs[r] = fmaxf(s, 1e-8f);
     }
     __syncthreads();
@@ -744,11 +782,17 @@ __device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* w
       mx = block_reduce<true>(mx, smem + W * W + 3 * W);
       if (threadIdx.x == 0) ymax[ch * (K + 1) + k] = mx;
       if (k < K) {
-        for (int c = threadIdx.x; c < W; c += blockDim.x) {
+        // y_{k+1}[c] = gamma * sum_{r >= c} Pw[r, c] y_k[r], four row groups per column
+        float* sPart = smem + W * W + 3 * W + 32;           // [4][W]
+        for (int idx = threadIdx.x; idx < 4 * W; idx += blockDim.x) {
+          const int c = idx % W, q = idx / W;
           float s = 0.f;
-          for (int r = c; r < W; ++r) s = fmaf(sPw[r * W + c], cur[r], s);
-          nxt[c] = gam * s;
+          for (int r = c + q; r < W; r += 4) s = fmaf(sPw[r * W + c], cur[r], s);
+          sPart[q * W + c] = s;
         }
+        __syncthreads();
+        for (int c = threadIdx.x; c < W; c += blockDim.x)
+          nxt[c] = gam * ((sPart[c] + sPart[W + c]) + (sPart[2 * W + c] + sPart[3 * W + c]));
       }
       __syncthreads();
     }
@@ -784,7 +828,7 @@ __global__ void __launch_bounds__(256) k_rows_prep(const Plan pl, const ckv_para
     }
   }
   g = block_reduce<false>(g, red);
-  if (threadIdx.x == 0) gtile[(size_t)ch * pl.ncol_tiles + tile] = g;
+  if (threadIdx.x == 0) gtile[(size_t)ch * pl.ncol_tiles * 8 + tile] = g;
   // row sums over this tile
   for (int r = threadIdx.x; r < pl.W; r += blockDim.x) {
     float s = 0.f;
@@ -793,26 +837,660 @@ __global__ void __launch_bounds__(256) k_rows_prep(const Plan pl, const ckv_para
       if (tempered) v = v > 0.f ? powf(v, invT) : 0.f;
       s += v;
     }
-    rspart[((size_t)ch * pl.ncol_tiles + tile) * pl.W + r] = s;
+    rspart[((size_t)ch * pl.rs_parts + tile) * pl.W + r] = s;
   }
 }
 
 __global__ void __launch_bounds__(256) k_rows_chain(const Plan pl, const ckv_params prm, char* ws) {
   extern __shared__ __align__(16) float fsmem[];
-  run_window_chains(pl, prm, ws, fsmem);
+  run_window_chains(pl, prm, ws, fsmem, false);
 }
 
 cudaError_t launch_rows_prep(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st) {
   k_rows_prep<<<dim3(pl.ncol_tiles, pl.hi_rows ? 2 : 1), 256, 0, st>>>(pl, prm, ws);
-  const size_t sm = sizeof(float) * ((size_t)pl.W * pl.W + 5 * pl.W + 64);
-  static size_t have = 0;
-  if (sm > have) {
-    const cudaError_t e = cudaFuncSetAttribute(k_rows_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    if (e != cudaSuccess) return e;
-    have = sm;
-  }
+  const size_t sm = sizeof(float) * ((size_t)pl.W * pl.W + 9 * pl.W + 64);
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_rows_chain, sm); if (e != cudaSuccess) return e; }
   k_rows_chain<<<1, 256, sm, st>>>(pl, prm, ws);
   return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------------------
+// pass 1 on the 5th-generation tensor cores (bf16 / fp16)
+// ---------------------------------------------------------------------------
+// One CTA per (column chunk, KV group).  The group's G*W window-query rows stay in
+// shared memory (TMA, 128-byte swizzle, two 64-element K panels); K tiles of TN
+// keys stream through a `stages`-deep TMA ring.  One thread issues the UMMAs of a
+// tile (M = 128 rows per m-tile, N = TN, K = 128 in 8 steps) into one of two TMEM
+// accumulator buffers and commits them to an mbarrier, so the MMAs of tile t+1
+// run while all 8 warps drain tile t: each thread owns one accumulator row
+// (TMEM lane) and folds its logits into that row's running moments without
+// shuffles.  Logits are rounded as the reference does for 16-bit inputs:
+// dtype(dtype(acc) * fp32(1/sqrt(D))).
+CKV_DEV char* align1024(char* p) {
+  return reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
+}
+
+// Round a pair of fp32 accumulators as the reference rounds a 16-bit logit.
+template <int DT> CKV_DEV void round_pair(float a, float b, float rs, float& x, float& y);
+template <> CKV_DEV void round_pair<CKV_BF16>(float a, float b, float rs, float& x, float& y) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(b), "f"(a));
+  float u = __uint_as_float(p << 16) * rs, v = __uint_as_float(p & 0xffff0000u) * rs;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v), "f"(u));
+  x = __uint_as_float(p << 16);
+  y = __uint_as_float(p & 0xffff0000u);
+}
+// fp16 keeps 3 more mantissa bits than bf16, so dividing (the reference on CPU) and
+// multiplying by the reciprocal (its CUDA scalar division) round apart often enough to
+// matter: fp16 divides.  (bf16: no difference in 1M sampled logits.)
+template <> CKV_DEV void round_pair<CKV_FP16>(float a, float b, float rs, float& x, float& y) {
+  const float sd = 11.313708305358887f;   // fp32(sqrt(128))
+  (void)rs;
+  x = __half2float(__float2half_rn(__fdiv_rn(__half2float(__float2half_rn(a)), sd)));
+  y = __half2float(__float2half_rn(__fdiv_rn(__half2float(__float2half_rn(b)), sd)));
+}
+
+template <int DT>
+__global__ void __launch_bounds__(512, 1)
+    k_tc_stats(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
+  extern __shared__ char smem_raw[];
+  const Plan& pl = a.pl;
+  Header* hdr = reinterpret_cast<Header*>(a.ws);
+  int32_t* status = &hdr->status;
+  const int chunk = blockIdx.x, g = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = pl.G * pl.W;                 // window-query rows of the group
+  const int m_tiles = R / 128;
+  const int TN = a.tc_tn, S = a.tc_stages;
+  const int ntn = (pl.n + TN - 1) / TN;
+  const int t0 = chunk * a.tc_tpc, t1 = min(t0 + a.tc_tpc, ntn);
+  const int ntile = max(0, t1 - t0);
+  char* sA = align1024(smem_raw);
+  char* sB = sA + 2 * R * 128;
+  __shared__ __align__(8) uint64_t bar_q, bar_k[4], bar_mma[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+  const uint32_t ncols = (2 * m_tiles * TN <= 256) ? 256u : 512u;
+  if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar_q, 1);
+    for (int i = 0; i < 4; ++i) tc::mbar_init(&bar_k[i], 1);
+    tc::mbar_init(&bar_mma[0], 1);
+    tc::mbar_init(&bar_mma[1], 1);
+    tc::fence_barrier_init();
+    abort_sh = 0;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
+
+  auto issue_tile = [&](int i) {   // thread 0: UMMAs of local tile i into buffer i & 1
+    const int s = i % S;
+    const uint32_t dcol = (uint32_t)((i & 1) * m_tiles * TN);
+    for (int mt = 0; mt < m_tiles; ++mt) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int p = ks >> 2, koff = (ks & 3) * 32;
+        const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(sA + p * R * 128 + mt * 128 * 128 + koff));
+        const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(sB + (s * 2 + p) * TN * 128 + koff));
+        tc::umma_f16(tmem + dcol + mt * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
+      }
+    }
+    tc::umma_commit(&bar_mma[i & 1]);
+  };
+  auto load_tile = [&](int i) {    // thread 0: TMA of local tile i into stage i % S
+    const int s = i % S;
+    tc::mbar_expect_tx(&bar_k[s], (uint32_t)TN * 256u);
+    for (int p = 0; p < 2; ++p)
+      tc::tma_load_3d(sB + (s * 2 + p) * TN * 128, &tmk, &bar_k[s], p * 64, (t0 + i) * TN, g);
+  };
+
+  if (ntile > 0 && threadIdx.x == 0) {
+    tc::mbar_expect_tx(&bar_q, (uint32_t)R * 256u);
+    for (int hl = 0; hl < pl.G; ++hl)
+      for (int p = 0; p < 2; ++p)
+        tc::tma_load_3d(sA + p * R * 128 + hl * pl.W * 128, &tmq, &bar_q, p * 64, pl.n - pl.W, g * pl.G + hl);
+    for (int i = 0; i < min(S, ntile); ++i) load_tile(i);
+    bool ok = tc::mbar_wait(&bar_q, 0, status) && tc::mbar_wait(&bar_k[0], 0, status);
+    if (ok) { tc::fence_after_sync(); issue_tile(0); }
+    else abort_sh = 1;
+  }
+
+  // 16 warps: TMEM lane group lg, m-tile mt, column split sp of nsplit
+  const int lg = warp & 3;
+  const int nsplit = 16 / (4 * m_tiles);               // 4, 2 or 1
+  const int mt = (warp >> 2) % m_tiles, sp = (warp >> 2) / m_tiles;
+  const int cw = TN / nsplit;                          // columns per thread per tile (>= 32)
+  const int row = mt * 128 + 32 * lg + lane;
+  const int r = row % pl.W;
+  const int lim = pl.n - pl.W + r;                     // last visible key of this window row
+  Moments M{-INFINITY, 0.f, 0.f, 0.f};
+  const float rs = 1.0f / sqrtf((float)pl.D);
+  __syncthreads();
+
+  for (int i = 0; i < ntile; ++i) {
+    if (abort_sh) break;
+    const int t = t0 + i;
+    if (threadIdx.x == 0 && i + 1 < ntile) {
+      if (tc::mbar_wait(&bar_k[(i + 1) % S], ((i + 1) / S) & 1, status)) { tc::fence_after_sync(); issue_tile(i + 1); }
+      else abort_sh = 1;
+    }
+    if (!tc::mbar_wait(&bar_mma[i & 1], (i >> 1) & 1, status)) abort_sh = 1;
+    tc::fence_after_sync();
+    if (threadIdx.x == 0 && i + S < ntile && !abort_sh) load_tile(i + S);
+    const uint32_t base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)((i & 1) * m_tiles * TN + mt * TN);
+    for (int c = sp * cw; c < (sp + 1) * cw; c += 32) {
+      float v[32];
+      __syncwarp();
+      tc::tmem_ld32(base + c, v);
+      const int jb = t * TN + c;
+      float x[32];
+#pragma unroll
+      for (int k = 0; k < 32; k += 2) round_pair<DT>(v[k], v[k + 1], rs, x[k], x[k + 1]);
+      if (jb + 31 > lim) {   // the masked / out-of-range tail of the row (last tiles only)
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (jb + k > lim) x[k] = -1e30f;
+      }
+      float cm = x[0];
+#pragma unroll
+      for (int k = 1; k < 32; ++k) cm = fmaxf(cm, x[k]);
+      const float cm2 = cm * kLog2e;
+      if (cm2 > M.m) {
+        if (M.m != -INFINITY) {
+          const float d = cm2 - M.m;
+          const float sc = ex2(-d);
+          M.t = sc * (M.t - d * M.z);
+          M.z *= sc;
+          M.s *= sc;
+        }
+        M.m = cm2;
+      }
+      const float nm = -M.m;
+      float z0 = 0.f, z1 = 0.f, t0a = 0.f, t1a = 0.f;
+#pragma unroll
+      for (int k = 0; k < 32; k += 2) {
+        const float d0 = fmaf(x[k], kLog2e, nm), d1 = fmaf(x[k + 1], kLog2e, nm);
+        const float e0 = ex2(d0), e1 = ex2(d1);
+        z0 += e0;
+        z1 += e1;
+        t0a = fmaf(e0, d0, t0a);
+        t1a = fmaf(e1, d1, t1a);
+      }
+      M.z += z0 + z1;
+      M.t += t0a + t1a;
+      if (jb < pl.s) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (jb + k < pl.s) M.s += ex2(fmaf(x[k], kLog2e, nm));
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+  }
+
+  // merge the column splits of each row, then write this chunk's partial moments
+  float4* part = reinterpret_cast<float4*>(a.ws + pl.off_stats);
+  tc::fence_before_sync();
+  __syncthreads();
+  float4* msh = reinterpret_cast<float4*>(sB);        // K stages are free now: [nsplit][R]
+  msh[sp * R + row] = make_float4(M.m, M.z, M.t, M.s);
+  __syncthreads();
+  if (sp == 0) {
+    for (int q = 1; q < nsplit; ++q) {
+      const float4 o = msh[q * R + row];
+      M = merge(M, Moments{o.x, o.y, o.z, o.w});
+    }
+    const int h = g * pl.G + row / pl.W;
+    part[((size_t)chunk * pl.H + h) * pl.W + r] = make_float4(M.m, M.z, M.t, M.s);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 0) tc::tmem_dealloc(tmem, ncols);
+  stats_finish(a, smem_raw, (int)blockIdx.y * pl.G, pl.G);
+}
+
+// ---- TMA descriptors (host) -------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// [heads, n, 128] view with element strides (head, token) -> a 3-D tiled map with a
+// (64 x box_rows x 1) box, 128-byte swizzle, zero fill beyond n.
+static bool make_tmap(CUtensorMap* m, const void* base, int dtype, int n, int heads, int64_t hs,
+                      int64_t ts, int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {128, (cuuint64_t)n, (cuuint64_t)heads};
+  const cuuint64_t strides[2] = {(cuuint64_t)ts * 2, (cuuint64_t)hs * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, dtype == CKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+size_t tc_stats_smem(const Plan& pl, int TN, int S) {
+  return 1024 + (size_t)2 * pl.G * pl.W * 128 + (size_t)S * 2 * TN * 128;
+}
+
+template <int DT>
+static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
+  WinArgs a = a0;
+  const Plan& pl = a.pl;
+  const int m_tiles = pl.G * pl.W / 128;
+  a.tc_tn = m_tiles <= 2 ? 128 : 64;
+  a.tc_stages = 4;
+  const int ntn = (pl.n + a.tc_tn - 1) / a.tc_tn;
+  a.tc_tpc = (ntn + pl.nstat_chunks - 1) / pl.nstat_chunks;
+  CUtensorMap tq, tk;
+  if (!make_tmap(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W) ||
+      !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, a.tc_tn))
+    return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
+  const size_t smem = tc_stats_smem(pl, a.tc_tn, a.tc_stages);
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_stats<DT>, smem); if (e != cudaSuccess) return e; }
+  k_tc_stats<DT><<<dim3(pl.nstat_chunks, pl.Hkv), 512, smem, st>>>(tq, tk, a);
+  return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------------------
+// pass 2 on the tensor cores (W = 64, 4 query heads per KV group)
+// ---------------------------------------------------------------------------
+// Persistent CTAs (one per SM) walk 64-key column tiles; each tile is processed for
+// all KV groups in turn.  Per group, TMA streams the group's 256 window-query rows
+// and its K tile through a two-stage ring (the queries of the next group load
+// while this group computes), one thread issues the UMMAs (two m-tiles of 128 rows,
+// N = 64) into one of two TMEM buffers, and the epilogue runs with one thread per
+// TMEM lane and 32-column half: lane L of m-tile 0 holds (head 4g + L/64, row L%64),
+// lane L of m-tile 1 holds head 4g + 2 + L/64 for the same row, so each thread pools
+// its head pair in registers.  Pair partials go through shared memory; every thread
+// then folds the two pairs of 16 (row, column) elements into register accumulators
+// that run across the groups (QI max over selected heads, HI sum over HI heads).
+// Per tile the pooled rows, column sums, row-sum partials and g totals are written
+// exactly as by the SIMT pooling kernel; per row the exact clamped entropy and the
+// transient mass accumulate across the CTA's tiles in TMEM and are written once per
+// CTA and column half.  The last CTA of the grid
+// verifies the head sets and runs the window chain (window_pool_finish).
+constexpr int kP2TN = 64;                 // keys per tile
+constexpr int kP2Stages = 2;              // (queries, K tile) stages
+
+size_t tc_pool_smem(const Plan& pl) {
+  const size_t R = (size_t)pl.G * pl.W;   // 256
+  return 1024 + (size_t)kP2Stages * (R * 256 + (size_t)kP2TN * 256) + (size_t)2 * 128 * kP2TN * 4;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256, 1)
+    k_tc_pool(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
+  extern __shared__ char smem_raw[];
+  const Plan& pl = a.pl;
+  Header* hdr = reinterpret_cast<Header*>(a.ws);
+  if (a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->fixup) == 0) return;
+  int32_t* status = &hdr->status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = pl.W, G = pl.G, R = G * W;          // 64, 4, 256
+  const int TN = kP2TN, S = kP2Stages;
+  const int ntn = (pl.n + TN - 1) / TN;
+  const int ngroups = pl.Hkv;
+  const int my_tiles = (ntn - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // tiles b, b+grid, ...
+  const int nsteps = max(0, my_tiles) * ngroups;                                       // (tile, group) steps
+  char* stg = align1024(smem_raw);
+  const int stage_bytes = R * 256 + TN * 256;
+  float* pq = reinterpret_cast<float*>(stg + S * stage_bytes);   // [128 lanes][64 cols] pair max
+  float* ph = pq + 128 * TN;                                     // [128 lanes][64 cols] pair sum
+  __shared__ __align__(8) uint64_t bar_ld[kP2Stages], bar_mma[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+  // columns [0, 256): two accumulator buffers of two m-tiles; [256, 384): per (column
+  // half, group) running entropy / mass sums of this thread's two heads
+  const uint32_t ncols = 512;
+  if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) tc::mbar_init(&bar_ld[i], 1);
+    tc::mbar_init(&bar_mma[0], 1);
+    tc::mbar_init(&bar_mma[1], 1);
+    tc::fence_barrier_init();
+    abort_sh = 0;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
+  const uint64_t qset = hdr->qi_heads, hset = hdr->hi_heads;
+  const bool hmax = hdr->hi_mode == 1;
+  const int nhi = hdr->n_hi;
+  const bool hi_rows = pl.hi_rows != 0;
+  const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);
+
+  // step s -> (tile, group)
+  auto step_tile = [&](int s) { return (int)blockIdx.x + (s / ngroups) * (int)gridDim.x; };
+  auto load_step = [&](int s) {            // thread 0
+    const int st = s % S, t = step_tile(s), g = s % ngroups;
+    char* base = stg + st * stage_bytes;
+    tc::mbar_expect_tx(&bar_ld[st], (uint32_t)(R * 256 + TN * 256));
+    for (int hl = 0; hl < G; ++hl)
+      for (int p = 0; p < 2; ++p)
+        tc::tma_load_3d(base + p * R * 128 + hl * W * 128, &tmq, &bar_ld[st], p * 64, pl.n - W, g * G + hl);
+    for (int p = 0; p < 2; ++p)
+      tc::tma_load_3d(base + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, t * TN, g);
+  };
+  auto issue_step = [&](int s) {           // thread 0
+    const int st = s % S;
+    const char* base = stg + st * stage_bytes;
+    const uint32_t dcol = (uint32_t)((s & 1) * 2 * TN);
+    for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int p = ks >> 2, koff = (ks & 3) * 32;
+        const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(base + p * R * 128 + mt * 128 * 128 + koff));
+        const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(base + R * 256 + p * TN * 128 + koff));
+        tc::umma_f16(tmem + dcol + mt * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
+      }
+    }
+    tc::umma_commit(&bar_mma[s & 1]);
+  };
+  if (nsteps > 0 && threadIdx.x == 0) {
+    for (int s = 0; s < min(S, nsteps); ++s) load_step(s);
+    if (tc::mbar_wait(&bar_ld[0], 0, status)) { tc::fence_after_sync(); issue_step(0); }
+    else abort_sh = 1;
+  }
+
+  // epilogue identity: TMEM lane group lg, column half ch; rows of m-tiles 0 and 1
+  const int lg = warp & 3, ch = warp >> 2;
+  const int L = 32 * lg + lane;                       // TMEM lane
+  const int r = L % W;
+  const int pair = L / W;                             // 0: heads (0, 2) of the group, 1: (1, 3)
+  const int lim = pl.n - W + r;
+  float* epart = reinterpret_cast<float*>(a.ws + pl.off_epart);   // [2 * ncol_tiles][H][W]
+  float* mpart = reinterpret_cast<float*>(a.ws + pl.off_mpart);
+  // pooling identity: column pc, rows pr0 + 4k
+  const int pc = threadIdx.x % TN, pr0 = threadIdx.x / TN;
+  constexpr int kRows = 16;                          // W / 4
+  float qacc[kRows], hacc[kRows];
+  const float rs = 1.0f / sqrtf((float)pl.D);
+  const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
+  const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
+  // running sums: column 256 + 64 ch + 4 g + {entropy a, entropy b, mass a, mass b}
+  const uint32_t acc_base = tmem + ((uint32_t)(32 * lg) << 16) + 256u + (uint32_t)(64 * ch);
+  {
+    const float z[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int g = 0; g < ngroups; ++g) tc::tmem_st4(acc_base + 4 * g, z);
+  }
+  __syncthreads();
+
+  for (int s = 0; s < nsteps; ++s) {
+    const bool alive = !abort_sh;
+    const int t = step_tile(s), g = s % ngroups;
+    const int j0 = t * TN;
+    if (g == 0) {
+#pragma unroll
+      for (int k = 0; k < kRows; ++k) { qacc[k] = 0.f; hacc[k] = 0.f; }
+    }
+    if (alive && threadIdx.x == 0 && s + 1 < nsteps) {
+      if (tc::mbar_wait(&bar_ld[(s + 1) % S], ((s + 1) / S) & 1, status)) { tc::fence_after_sync(); issue_step(s + 1); }
+      else abort_sh = 1;
+    }
+    if (alive && !tc::mbar_wait(&bar_mma[s & 1], (s >> 1) & 1, status)) abort_sh = 1;
+    tc::fence_after_sync();
+    if (alive && threadIdx.x == 0 && s + S < nsteps && !abort_sh) load_step(s + S);
+    // this thread's two heads: g*G + pair and g*G + 2 + pair
+    const int ha = g * G + pair, hb = ha + 2;
+    const bool qa = (qset >> ha) & 1ull, qb = (qset >> hb) & 1ull;
+    const bool hA = (hset >> ha) & 1ull, hB = (hset >> hb) & 1ull;
+    if (alive) {
+      float ent[2] = {0.f, 0.f}, mass[2] = {0.f, 0.f};   // this step's partials of the two heads
+      const float La = lse[ha * W + r], Lb = lse[hb * W + r];
+      float va[32], vb[32];
+      const uint32_t base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)((s & 1) * 2 * TN + ch * 32);
+      tc::tmem_ld32(base, va);
+      tc::tmem_ld32(base + TN, vb);
+      const int jb = j0 + ch * 32;
+      const bool interior = (jb + 31 <= lim) && (jb >= pl.s);
+      float qv[32], hv[32];
+#pragma unroll
+      for (int k = 0; k < 32; k += 2) {
+        float xa0, xa1, xb0, xb1;
+        round_pair<DT>(va[k], va[k + 1], rs, xa0, xa1);
+        round_pair<DT>(vb[k], vb[k + 1], rs, xb0, xb1);
+        va[k] = xa0; va[k + 1] = xa1; vb[k] = xb0; vb[k + 1] = xb1;
+      }
+      // head membership as 0/1 factors (p * 1 == p, p * 0 == 0 for finite p >= 0)
+      const float fqa = qa ? 1.f : 0.f, fqb = qb ? 1.f : 0.f;
+      const float fha = hA ? 1.f : 0.f, fhb = hB ? 1.f : 0.f;
+      if (interior) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float da = fmaf(va[k], kLog2e, -La), db = fmaf(vb[k], kLog2e, -Lb);
+          const float pa = ex2(da), pb = ex2(db);
+          ent[0] = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent[0]);
+          ent[1] = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent[1]);
+          mass[0] += pa;
+          mass[1] += pb;
+          qv[k] = fmaxf(pa * fqa, pb * fqb);
+          hv[k] = hmax ? fmaxf(pa * fha, pb * fhb) : fmaf(pa, fha, pb * fhb);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int j = jb + k;
+          const float da = fmaf(va[k], kLog2e, -La), db = fmaf(vb[k], kLog2e, -Lb);
+          float pa = ex2(da), pb = ex2(db);
+          if (j <= lim) {
+            ent[0] = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent[0]);
+            ent[1] = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent[1]);
+            if (j >= pl.s) { mass[0] += pa; mass[1] += pb; }
+          } else {
+            pa = 0.f; pb = 0.f;
+            if (j < pl.n) {   // masked: probability 0, clamped to 1e-8
+              ent[0] = fmaf(1e-8f, kLog2Eps, ent[0]);
+              ent[1] = fmaf(1e-8f, kLog2Eps, ent[1]);
+            }
+          }
+          qv[k] = fmaxf(pa * fqa, pb * fqb);
+          hv[k] = hmax ? fmaxf(pa * fha, pb * fhb) : fmaf(pa, fha, pb * fhb);
+        }
+      }
+      // exact entropy (log2 units) / mass: add this tile's sums to the running sums
+      {
+        float acc[4];
+        tc::tmem_ld4(acc_base + 4 * g, acc);
+        acc[0] += ent[0]; acc[1] += ent[1]; acc[2] += mass[0]; acc[3] += mass[1];
+        tc::tmem_st4(acc_base + 4 * g, acc);
+      }
+      // pair partials: [lane][column], 16-byte chunks XOR-swizzled by lane
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int cchunk = (ch * 8 + k) ^ (L & 15);
+        reinterpret_cast<float4*>(pq + L * TN)[cchunk] = make_float4(qv[4 * k], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3]);
+        reinterpret_cast<float4*>(ph + L * TN)[cchunk] = make_float4(hv[4 * k], hv[4 * k + 1], hv[4 * k + 2], hv[4 * k + 3]);
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    // fold the two pairs of every (row, column) into the accumulators; the swizzled
+    // column of row rr depends on rr & 15, i.e. on k & 3 for rr = pr0 + 4k
+    {
+      int coff[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) coff[u] = (((pc >> 2) ^ ((pr0 + 4 * u) & 15)) << 2) + (pc & 3);
+#pragma unroll
+      for (int k = 0; k < kRows; ++k) {
+        const int rr = pr0 + 4 * k;
+        const int ia = rr * TN + coff[k & 3], ib = (rr + W) * TN + coff[k & 3];
+        const float q0 = pq[ia], q1 = pq[ib];
+        const float h0 = ph[ia], h1 = ph[ib];
+        qacc[k] = fmaxf(qacc[k], fmaxf(q0, q1));
+        hacc[k] = hmax ? fmaxf(hacc[k], fmaxf(h0, h1)) : hacc[k] + (h0 + h1);
+      }
+    }
+    __syncthreads();
+    if (g == ngroups - 1) {
+      // ---- the tile is complete: pooled rows and their sums (SIMT-kernel layout)
+      float* rows_qi = reinterpret_cast<float*>(a.ws + pl.off_rows_qi);
+      float* rows_hi = reinterpret_cast<float*>(a.ws + pl.off_rows_hi);
+      float* colsum = reinterpret_cast<float*>(a.ws + pl.off_colsum);
+      float* gtile = reinterpret_cast<float*>(a.ws + pl.off_gtile);
+      float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);
+      const int j = j0 + pc;
+      const int nch = hi_rows ? 2 : 1;
+      float (*colpart)[kP2TN] = reinterpret_cast<float (*)[kP2TN]>(pq);          // [4][TN] (pair area is free)
+      float (*redrow)[kP2TN] = reinterpret_cast<float (*)[kP2TN]>(pq + 4 * kP2TN);  // [8][TN]
+      float* gsum = pq + 12 * kP2TN;                                               // [2]
+      for (int c2 = 0; c2 < nch; ++c2) {
+        float* rows = c2 == 0 ? rows_qi : rows_hi;
+        float cs = 0.f;
+#pragma unroll
+        for (int k = 0; k < kRows; ++k) {
+          const int rr = pr0 + 4 * k;
+          float v = c2 == 0 ? qacc[k] : (hmax ? hacc[k] : hacc[k] / (float)nhi);
+          if (j >= pl.n) v = 0.f;
+          rows[(size_t)rr * pl.n_pad + j] = v;
+          cs += v;
+          float rv = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
+          rv = warp_sum(rv);
+          if (lane == 0) redrow[warp][k] = rv;     // warp covers 32 columns of row rr
+        }
+        colpart[pr0][pc] = cs;
+        __syncthreads();
+        if (threadIdx.x < W) {
+          const int rr = threadIdx.x, k = rr / 4, w0 = 2 * (rr % 4);
+          rspart[((size_t)c2 * pl.rs_parts + t) * W + rr] = redrow[w0][k] + redrow[w0 + 1][k];
+        }
+        if (threadIdx.x < TN) {
+          const int jj = j0 + threadIdx.x;
+          const float c = colpart[0][threadIdx.x] + colpart[1][threadIdx.x] + colpart[2][threadIdx.x] +
+                          colpart[3][threadIdx.x];
+          colsum[(size_t)c2 * pl.n_pad + jj] = c;
+          float gg = 0.f;
+          if (jj < pl.n_p) {
+            gg = fmaxf(c, 1e-6f);
+            if (tempered) gg = powf(gg, invT);
+          }
+          gg = warp_sum(gg);
+          if (lane == 0) gsum[warp] = gg;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) gtile[(size_t)c2 * pl.ncol_tiles * 8 + t] = gsum[0] + gsum[1];
+        __syncthreads();
+      }
+    }
+  }
+  // one exact entropy / mass partial per (CTA, column half, head, row)
+  for (int g = 0; g < ngroups; ++g) {
+    float acc[4];
+    tc::tmem_ld4(acc_base + 4 * g, acc);
+    const int ha = g * G + pair, hb = ha + 2;
+    const size_t slot = (size_t)(blockIdx.x * 2 + ch) * pl.H;
+    epart[(slot + ha) * W + r] = -acc[0] * kLn2;
+    epart[(slot + hb) * W + r] = -acc[1] * kLn2;
+    mpart[(slot + ha) * W + r] = acc[2];
+    mpart[(slot + hb) * W + r] = acc[3];
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 0) tc::tmem_dealloc(tmem, ncols);
+}
+
+template <int DT>
+static cudaError_t launch_tc_pool(const WinArgs& a0, cudaStream_t st) {
+  WinArgs a = a0;
+  const Plan& pl = a.pl;
+  CUtensorMap tq, tk;
+  if (!make_tmap(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W) ||
+      !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kP2TN))
+    return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
+  const size_t smem = tc_pool_smem(pl);
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool<DT>, smem); if (e != cudaSuccess) return e; }
+  k_tc_pool<DT><<<pl.tc_nclusters, 256, smem, st>>>(tq, tk, a);
+  return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------------------
+// exact entropy / mass: reduce the pooling pass's partials, then (last CTA) verify
+// the head sets and run the window chain
+// ---------------------------------------------------------------------------
+// Reduces, per row, a strided set of partials with 8 loads in flight per thread.
+CKV_DEV float sum_parts(const float* base, int nparts, size_t stride, int first, int step) {
+  float acc = 0.f;
+  for (int t = first; t < nparts; t += 8 * step) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = (t + u * step < nparts) ? __ldcg(base + (size_t)(t + u * step) * stride) : 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc += v[u];
+  }
+  return acc;
+}
+
+// Thread (row lane, stream): 32 rows per CTA, 16 partial streams (one per warp).
+// Rows [0, H*W) are the exact entropy of each (head, window row), [H*W, 2*H*W) its
+// transient mass, [2*H*W, 2*H*W + 2W) the row sums of the pooled QI / HI rows; the
+// three outputs are contiguous in the stats area.
+constexpr int kReduceStreams = 16;
+
+__global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) {
+  const Plan& pl = a.pl;
+  Header* hdr = reinterpret_cast<Header*>(a.ws);
+  if (a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->fixup) == 0) return;
+  extern __shared__ __align__(16) char rsmem[];
+  const float* epart = reinterpret_cast<const float*>(a.ws + pl.off_epart);
+  const float* mpart = reinterpret_cast<const float*>(a.ws + pl.off_mpart);
+  const float* rspart = reinterpret_cast<const float*>(a.ws + pl.off_rspart);
+  float* out = reinterpret_cast<float*>(a.ws + pl.off_stats);   // [H*W] entropy, [H*W] mass, [2][W] row sums
+  const int HW = pl.H * pl.W;
+  const int nrows = 2 * HW + 2 * pl.W;
+  const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
+  const int row = blockIdx.x * 32 + lane;
+  __shared__ float sp[kReduceStreams][32];
+  float e = 0.f;
+  if (row < HW) {
+    e = sum_parts(epart + row, pl.e_parts, (size_t)HW, q, kReduceStreams);
+  } else if (row < 2 * HW) {
+    e = sum_parts(mpart + (row - HW), pl.e_parts, (size_t)HW, q, kReduceStreams);
+  } else if (row < nrows) {
+    const int ch = (row - 2 * HW) / pl.W, rr = (row - 2 * HW) % pl.W;
+    const int src = (ch == 1 && pl.hi_rows) ? 1 : 0;
+    e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, pl.rs_parts, (size_t)pl.W, q, kReduceStreams);
+  }
+  sp[q][lane] = e;
+  __syncthreads();
+  if (threadIdx.x < 32 && row < nrows) {
+    float t = 0.f;
+    for (int k = 0; k < kReduceStreams; ++k) t += sp[k][threadIdx.x];
+    out[row] = t;
+  }
+  __shared__ bool last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(&hdr->cnt_pool, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  window_pool_finish(a, rsmem);
+}
+
+size_t pool_reduce_smem(const Plan& pl) {
+  const size_t chains = (size_t)pl.W * pl.W + 5 * pl.W + 4 * pl.W + 64;
+  const size_t rows = (size_t)2 * pl.H * pl.W;
+  return sizeof(float) * (chains > rows ? chains : rows);
 }
 
 // ---------------------------------------------------------------------------
@@ -841,23 +1519,32 @@ size_t window_smem_bytes(const Plan& pl, bool pool) {
 template <int DT>
 static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st) {
   const Plan& pl = a.pl;
-  // opt in to the dynamic shared memory this launch needs (kernels also hold a little static smem)
-  static size_t set_stats = 0, set_pool = 0;
-  const size_t need = stage == 0 ? stats_smem<DT>(pl) : pool_smem<DT>(pl);
-  size_t& have = stage == 0 ? set_stats : set_pool;
-  if (need > have) {
-    const cudaError_t e = stage == 0
-        ? cudaFuncSetAttribute(k_window_stats<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need)
-        : cudaFuncSetAttribute(k_window_pool<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need);
+  // opt in to the dynamic shared memory of the SIMT kernels (tensor-core launchers do their own)
+  {
+    const cudaError_t e = stage == 0 ? ensure_dynamic_smem((const void*)k_window_stats<DT>, stats_smem<DT>(pl))
+                                     : ensure_dynamic_smem((const void*)k_window_pool<DT>, pool_smem<DT>(pl));
     if (e != cudaSuccess) return e;
-    have = need;
   }
   if (stage == 0) {
+    if constexpr (DT != CKV_FP32) {
+      if (pl.tc) return launch_tc_stats<DT>(a, st);
+    }
     k_window_stats<DT><<<dim3(pl.nstat_chunks, pl.nbatch), 256, stats_smem<DT>(pl), st>>>(a);
   } else {
     WinArgs b = a;
     b.fixup_pass = stage == 2 ? 1 : 0;
-    k_window_pool<DT><<<pl.ncol_tiles, 256, pool_smem<DT>(pl), st>>>(b);
+    bool launched = false;
+    if constexpr (DT != CKV_FP32) {
+      if (pl.tc_pool) {
+        const cudaError_t e = launch_tc_pool<DT>(b, st);
+        if (e != cudaSuccess) return e;
+        launched = true;
+      }
+    }
+    if (!launched) k_window_pool<DT><<<pl.ncol_tiles, 256, pool_smem<DT>(pl), st>>>(b);
+    const size_t rsm = pool_reduce_smem(pl);
+    { const cudaError_t e = ensure_dynamic_smem((const void*)k_pool_reduce, rsm); if (e != cudaSuccess) return e; }
+    k_pool_reduce<<<(2 * pl.H * pl.W + 2 * pl.W + 31) / 32, 32 * kReduceStreams, rsm, st>>>(b);
   }
   return cudaGetLastError();
 }

@@ -14,6 +14,9 @@ struct WinArgs {
   int64_t khs, kts;
   char* ws;          // layer workspace base
   int fixup_pass;    // pooling kernel: 1 = the re-run launched after a wrong speculation
+  int tc_tn;         // tensor-core path: key columns per MMA tile
+  int tc_tpc;        // tensor-core path: tiles per column chunk of the moments pass
+  int tc_stages;     // tensor-core path: K-tile stages in shared memory
   ckv_params p;
   Plan pl;
 };
