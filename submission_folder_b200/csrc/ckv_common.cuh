@@ -64,6 +64,17 @@ CKV_DEV uint32_t float_key(float f) {
 // ---------------------------------------------------------------------------
 // warp / block reductions
 // ---------------------------------------------------------------------------
+// a / b correctly rounded, from y = RN(1/b) computed once per divisor: Markstein's
+// correction (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Develop. 34(1), 1990).  q0 = RN(a*y) lies within
+// one ulp of a/b, the residual a - b*q0 is exact in one FMA, and RN(q0 + residual*y)
+// is RN(a/b) when no intermediate underflows or overflows.  Replaces a full IEEE
+// division in loops that divide many values by the same divisor.
+CKV_DEV float div_rcp(float a, float b, float y) {
+  const float q0 = __fmul_rn(a, y);
+  return __fmaf_rn(__fmaf_rn(-q0, b, a), y, q0);
+}
+
 CKV_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -33,28 +33,35 @@ namespace ckv {
 
 constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
-constexpr int kMaxSort = 8192;         // largest top-M list sorted in shared memory
-constexpr int kSmemScoresMax = 36864;  // vectors up to this length stay in shared memory
+constexpr int kMaxSort = 8192;          // largest top-M list sorted in shared memory
+constexpr int kSliceSmemMax = 16384;    // slice positions kept in shared memory
 
+// Shared memory of one CTA: a sort buffer (used by the vector's leader CTA; the
+// per-warp radix histograms alias it), the CTA's slice of its score vector, per
+// 32-position chunk counts, scalars, and the histograms / scalars that the other
+// CTAs of the cluster read through distributed shared memory.
 struct SelLayout {
-  int n, nchunk;
-  bool smem_scores;
-  size_t off_x, off_sort, off_cnt_a, off_cnt_b, off_bits, off_misc, total;
+  int n, P, S, nchunk;
+  bool smem_x;
+  size_t off_sort, off_x, off_cnt, off_misc, off_hx, off_xch, total;
 };
 
-__host__ __device__ inline SelLayout sel_layout(int n) {
+__host__ __device__ inline SelLayout sel_layout(int n, int P) {
   SelLayout L;
   L.n = n;
-  L.nchunk = (n + 31) / 32;
-  L.smem_scores = n <= kSmemScoresMax;
+  L.P = P;
+  const int per = (n + P - 1) / P;
+  L.S = (per + 31) & ~31;
+  L.nchunk = L.S / 32;
+  L.smem_x = L.S <= kSliceSmemMax;
   size_t off = 0;
   auto take = [&](size_t b) { const size_t o = off; off = (off + b + 15) & ~(size_t)15; return o; };
-  L.off_sort = take(sizeof(unsigned long long) * kMaxSort);   // also the per-warp histograms
-  L.off_x = take(L.smem_scores ? sizeof(float) * (size_t)n : 0);
-  L.off_cnt_a = take(sizeof(int) * (size_t)L.nchunk);
-  L.off_cnt_b = take(sizeof(int) * (size_t)L.nchunk);
-  L.off_bits = take(sizeof(uint32_t) * (size_t)L.nchunk);
+  L.off_sort = take(sizeof(unsigned long long) * kMaxSort);
+  L.off_x = take(L.smem_x ? sizeof(float) * (size_t)L.S : 0);
+  L.off_cnt = take(sizeof(int) * (size_t)(L.nchunk > 0 ? L.nchunk : 1));
   L.off_misc = take(sizeof(int) * 256);
+  L.off_hx = take(sizeof(int) * 2 * 256);
+  L.off_xch = take(sizeof(float) * 16);
   L.total = off;
   return L;
 }
@@ -62,12 +69,12 @@ __host__ __device__ inline SelLayout sel_layout(int n) {
 struct SelSmem {
   unsigned long long* sortbuf;
   int* hist;        // [kSelWarps][256] (aliases sortbuf)
-  float* x;         // score vector (shared or global)
-  int* cnt_a;
-  int* cnt_b;
-  uint32_t* bits;
+  int* cnt;         // per 32-position chunk counts of a range
   int* misc;        // [0..63] scan scratch, [64..] scalars
-  float* fmisc;
+  float* fmisc;     // misc + 128: reduction scratch
+  int* hx;          // [2][256] this CTA's histogram, read by the vector's other CTAs
+  float* xch;       // exchanged scalars: [0] total, [1] max; ints at [2..]
+  int* ixch;
 };
 
 // ---------------------------------------------------------------------------
@@ -92,52 +99,61 @@ __device__ int scan_counts(int* cnt, int m, int* scratch) {
   return total;
 }
 
-// Ballot counts of pred(i) per 32-position chunk into cnt (index order).
+// Ballot counts of pred(i) per 32-position chunk of [b0, b1) into cnt (b0 32-aligned).
 template <class Pred>
-__device__ void chunk_counts(int n, int* cnt, Pred pred) {
+__device__ void chunk_counts(int b0, int b1, int* cnt, Pred pred) {
   const int lane = threadIdx.x & 31;
-  for (int base = threadIdx.x - lane; base < n; base += blockDim.x) {
+  for (int base = b0 + (int)threadIdx.x - lane; base < b1; base += blockDim.x) {
     const int i = base + lane;
-    const unsigned b = __ballot_sync(0xffffffffu, i < n && pred(i));
-    if (lane == 0) cnt[base >> 5] = __popc(b);
+    const unsigned b = __ballot_sync(0xffffffffu, i < b1 && pred(i));
+    if (lane == 0) cnt[(base - b0) >> 5] = __popc(b);
   }
   __syncthreads();
 }
 
-// Rank (in index order) of position i among those with pred true, given the scanned chunk counts.
-CKV_DEV int chunk_rank(const int* cnt, int i, unsigned ball) {
-  return cnt[i >> 5] + __popc(ball & lanemask_lt());
+// Rank (in index order) of position i among those with pred true in [b0, ..), given the scanned chunk counts.
+CKV_DEV int chunk_rank(const int* cnt, int b0, int i, unsigned ball) {
+  return cnt[(i - b0) >> 5] + __popc(ball & lanemask_lt());
+}
+
+CKV_DEV int sorted_index(unsigned long long e, bool prefer_high) {
+  const uint32_t lo = (uint32_t)(e & 0xffffffffull);
+  return (int)(prefer_high ? lo : ~lo);
 }
 
 // ---------------------------------------------------------------------------
-// top-M of one vector
+// top-M of one vector, spread over the P CTAs that hold its slices
 // ---------------------------------------------------------------------------
-struct Range {
-  int n, lo, hi;
-  bool restricted;
-  CKV_DEV bool ok(int i) const { return i < n && (!restricted || (i >= lo && i < hi)); }
-};
-
-__device__ void radix_select(const float* v, const Range& rg, int M, SelSmem& sh, uint32_t* kstar,
-                             int* above, int* take) {
+// Radix select (4 passes of 8 bits) of the M-th largest key over positions
+// [lo, hi) of the vector; each CTA counts its slice [b0, b1) (values x[i - b0]),
+// the P histograms are summed through distributed shared memory, and every CTA of
+// the vector takes the same digit.  Called by every CTA of the cluster.
+__device__ void radix_select(cg::cluster_group& cl, const float* x, int b0, int b1, int lo, int hi, int M,
+                             int vbase, int P, SelSmem& sh, uint32_t* kstar, int* above, int* take) {
   uint32_t prefix = 0, pmask = 0;
   int remaining = M, gt = 0;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   int* myhist = sh.hist + wid * 256;
+  const int r0 = max(b0, lo), r1 = min(b1, hi);
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
     for (int i = threadIdx.x; i < kSelWarps * 256; i += blockDim.x) sh.hist[i] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < rg.n; i += blockDim.x) {
-      if (!rg.ok(i)) continue;
-      const uint32_t k = float_key(v[i]);
+    for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
+      const uint32_t k = float_key(x[i - b0]);
       if ((k & pmask) == prefix) atomicAdd(&myhist[(k >> shift) & 255], 1);
     }
     __syncthreads();
-    // fold the per-warp histograms into warp 0's row
+    int* hx = sh.hx + (pass & 1) * 256;
     if (threadIdx.x < 256) {
       int s = 0;
       for (int w = 0; w < kSelWarps; ++w) s += sh.hist[w * 256 + threadIdx.x];
+      hx[threadIdx.x] = s;
+    }
+    cl.sync();
+    if (threadIdx.x < 256) {
+      int s = 0;
+      for (int q = 0; q < P; ++q) s += cl.map_shared_rank(hx, vbase + q)[threadIdx.x];
       sh.hist[threadIdx.x] = s;
     }
     __syncthreads();
@@ -178,69 +194,81 @@ __device__ void radix_select(const float* v, const Range& rg, int M, SelSmem& sh
   *take = remaining;
 }
 
-// The top-M (key, index) composites of v over rg, sorted descending, in sh.sortbuf[0..M).
-// prefer_high: at the boundary key keep the highest indices and rank a higher index
-// higher (stable ascending ranks); otherwise the lowest indices, ranked first (topk).
-__device__ void top_sorted(const float* v, const Range& rg, int M, bool prefer_high, SelSmem& sh) {
+// The top-M (key, index) composites of the vector over [lo, hi), sorted descending,
+// in the leader CTA's sort buffer.  prefer_high: at the boundary key keep the highest
+// indices and rank a higher index higher (stable ascending ranks); otherwise the
+// lowest indices, ranked first (topk).  Called by every CTA of the cluster.
+__device__ void top_sorted(cg::cluster_group& cl, const float* x, int b0, int b1, int lo, int hi, int M,
+                           bool prefer_high, int vbase, int P, bool leader, SelSmem& sh) {
   uint32_t kstar;
   int above, take;
-  radix_select(v, rg, M, sh, &kstar, &above, &take);
+  radix_select(cl, x, b0, b1, lo, hi, M, vbase, P, sh, &kstar, &above, &take);
   const int lane = threadIdx.x & 31;
-  // ties at the boundary key: rank them in index order
-  chunk_counts(rg.n, sh.cnt_a, [&](int i) { return rg.ok(i) && float_key(v[i]) == kstar; });
-  const int nties = scan_counts(sh.cnt_a, (rg.n + 31) / 32, sh.misc);
-  if (threadIdx.x == 0) sh.misc[67] = 0;
-  __syncthreads();
-  for (int base = threadIdx.x - lane; base < rg.n; base += blockDim.x) {
+  const int r0 = max(b0, lo), r1 = min(b1, hi);
+  auto in_range = [&](int i) { return i >= r0 && i < r1; };
+  // boundary ties of this slice in index order; slices of lower rank come first
+  chunk_counts(b0, b1, sh.cnt, [&](int i) { return in_range(i) && float_key(x[i - b0]) == kstar; });
+  const int my_ties = scan_counts(sh.cnt, (b1 - b0 + 31) / 32, sh.misc);
+  if (threadIdx.x == 0) {
+    sh.ixch[2] = my_ties;
+    if (leader) sh.misc[67] = 0;
+  }
+  cl.sync();
+  int tie_base = 0, nties = 0;
+  const int part = (int)cl.block_rank() - vbase;
+  for (int q = 0; q < P; ++q) {
+    const int c = cl.map_shared_rank(sh.ixch, vbase + q)[2];
+    if (q < part) tie_base += c;
+    nties += c;
+  }
+  unsigned long long* dst = cl.map_shared_rank(sh.sortbuf, vbase);
+  int* dcnt = cl.map_shared_rank(sh.misc + 67, vbase);
+  for (int base = b0 + (int)threadIdx.x - lane; base < b1; base += blockDim.x) {
     const int i = base + lane;
-    bool ok = i < rg.n && rg.ok(i);
-    const uint32_t k = ok ? float_key(v[i]) : 0u;
+    const bool ok = i < b1 && in_range(i);
+    const uint32_t k = ok ? float_key(x[i - b0]) : 0u;
     const uint32_t tie = prefer_high ? (uint32_t)i : ~(uint32_t)i;
-    // strictly above: warp-aggregated slot allocation
+    // strictly above: warp-aggregated slot allocation in the leader's buffer
     const unsigned ab = __ballot_sync(0xffffffffu, ok && k > kstar);
     int basepos = 0;
-    if (lane == 0 && ab) basepos = atomicAdd(&sh.misc[67], __popc(ab));
+    if (lane == 0 && ab) basepos = atomicAdd(dcnt, __popc(ab));
     basepos = __shfl_sync(0xffffffffu, basepos, 0);
-    if (ok && k > kstar) sh.sortbuf[basepos + __popc(ab & lanemask_lt())] = ((unsigned long long)k << 32) | tie;
-    // boundary ties in index order
+    if (ok && k > kstar) dst[basepos + __popc(ab & lanemask_lt())] = ((unsigned long long)k << 32) | tie;
     const unsigned tb = __ballot_sync(0xffffffffu, ok && k == kstar);
     if (ok && k == kstar) {
-      const int r = chunk_rank(sh.cnt_a, i, tb);
+      const int r = tie_base + chunk_rank(sh.cnt, b0, i, tb);
       const int ord = prefer_high ? (nties - 1 - r) : r;   // highest index first when prefer_high
-      if (ord < take) sh.sortbuf[above + ord] = ((unsigned long long)kstar << 32) | tie;
+      if (ord < take) dst[above + ord] = ((unsigned long long)kstar << 32) | tie;
     }
   }
-  __syncthreads();
-  int P = 1;
-  while (P < M) P <<= 1;
-  for (int i = M + threadIdx.x; i < P; i += blockDim.x) sh.sortbuf[i] = 0ull;
-  __syncthreads();
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        const int l = i ^ j;
-        if (l > i) {
-          const unsigned long long a = sh.sortbuf[i], b = sh.sortbuf[l];
-          if (((i & k) == 0) ? (a < b) : (a > b)) { sh.sortbuf[i] = b; sh.sortbuf[l] = a; }
+  cl.sync();
+  if (leader) {
+    int P2 = 1;
+    while (P2 < M) P2 <<= 1;
+    for (int i = M + threadIdx.x; i < P2; i += blockDim.x) sh.sortbuf[i] = 0ull;
+    __syncthreads();
+    for (int k = 2; k <= P2; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < P2; i += blockDim.x) {
+          const int l = i ^ j;
+          if (l > i) {
+            const unsigned long long a = sh.sortbuf[i], b = sh.sortbuf[l];
+            if (((i & k) == 0) ? (a < b) : (a > b)) { sh.sortbuf[i] = b; sh.sortbuf[l] = a; }
+          }
         }
+        __syncthreads();
       }
-      __syncthreads();
     }
   }
-}
-
-CKV_DEV int sorted_index(unsigned long long e, bool prefer_high) {
-  const uint32_t lo = (uint32_t)(e & 0xffffffffull);
-  return (int)(prefer_high ? lo : ~lo);
 }
 
 // ---------------------------------------------------------------------------
 // finished chain scores (PU:2186-2204)
 // ---------------------------------------------------------------------------
-__device__ int early_stop_steps(const Plan& pl, const char* ws, float* scratch) {
+__device__ int early_stop_steps(const Plan& pl, const char* ws) {
   const float* cmax = reinterpret_cast<const float*>(ws + pl.off_cmax);
   const float* ymax = reinterpret_cast<const float*>(ws + pl.off_ymax);
-  // max over chunks of every (chain, term) at once: thread t handles (ch, k) pairs by warps
+  // max over chunks of every (chain, term): one warp per pair
   __shared__ float tmax[2][kMaxIters + 1];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int q = wid; q < pl.nchains * pl.K; q += kSelWarps) {
@@ -259,7 +287,6 @@ __device__ int early_stop_steps(const Plan& pl, const char* ws, float* scratch) 
     for (int ch = 0; ch < pl.nchains; ++ch) small = small && (tmax[ch][k] < 1e-8f);
     if (small) { steps = k; break; }
   }
-  (void)scratch;
   return steps;
 }
 
@@ -275,39 +302,10 @@ CKV_DEV float raw_result(const Plan& pl, const char* ws, int ch, int j, int step
   return s;
 }
 
-// Writes the finished scores of chain ch into out (global, [n]).
-__device__ void finish_chain(const Plan& pl, const char* ws, int ch, int steps, float* out,
-                             float* fscratch) {
-  const int n = pl.n, s = pl.s;
-  float tot = 0.f, mx = 0.f;
-  for (int j = s + threadIdx.x; j < n; j += blockDim.x) {
-    const float v = raw_result(pl, ws, ch, j, steps);
-    out[j] = v;
-    tot += v;
-    mx = fmaxf(mx, v);
-  }
-  tot = block_reduce<false>(tot, fscratch);
-  mx = block_reduce<true>(mx, fscratch);
-  const float sinkv = tot * 0.01f;
-  mx = fmaxf(mx, s > 0 ? sinkv : 0.f);
-  for (int j = threadIdx.x; j < n; j += blockDim.x) {
-    float v = (j < s) ? sinkv : out[j];
-    if (mx > 0.f) v = v / mx;
-    out[j] = v;
-  }
-  __syncthreads();
-}
-
-// Zero-padded conv1d (PU:1921-1936) from `in` to `out`; copies when k <= 1 or n <= k.
-__device__ void smooth(const float* in, float* out, int n, int k, bool gaussian, float sigma) {
-  if (k <= 1 || n <= k) {
-    for (int j = threadIdx.x; j < n; j += blockDim.x) out[j] = in[j];
-    __syncthreads();
-    return;
-  }
-  float w[32];
-  float wsum = 0.f;
+// Smoothing kernel taps of a zero-padded conv1d (PU:1884-1919).
+CKV_DEV int smooth_taps(int k, bool gaussian, float sigma, float (&w)[32]) {
   const int kk = min(k, 32);
+  float wsum = 0.f;
   for (int t = 0; t < kk; ++t) {
     if (gaussian) {
       const float x = (float)t - (float)(k - 1) * 0.5f;
@@ -319,245 +317,354 @@ __device__ void smooth(const float* in, float* out, int n, int k, bool gaussian,
   }
   if (gaussian)
     for (int t = 0; t < kk; ++t) w[t] = w[t] / wsum;
-  const int pad = k / 2;
-  for (int j = threadIdx.x; j < n; j += blockDim.x) {
-    float acc = 0.f;
-    for (int t = 0; t < kk; ++t) {
-      const int src = j + t - pad;
-      if (src >= 0 && src < n) acc = fmaf(w[t], in[src], acc);
-    }
-    out[j] = acc;
-  }
-  __syncthreads();
+  return kk;
 }
 
 // ---------------------------------------------------------------------------
 // the cluster kernel
 // ---------------------------------------------------------------------------
-__device__ void set_bit(uint32_t* bits, int i) { atomicOr(bits + (i >> 5), 1u << (i & 31)); }
-CKV_DEV bool get_bit(const uint32_t* bits, int i) { return (bits[i >> 5] >> (i & 31)) & 1u; }
-
-__global__ void __launch_bounds__(kSelThreads) k_select(SelArgs a) {
+// Cluster of nv * P CTAs: CTA rank c owns slice c % P of score vector c / P
+// (32-aligned slices of S positions) for the finishing, smoothing and top-M
+// phases, and slice c of the positions (T positions) for the combination and
+// compaction phases.  Every cluster barrier below is taken by every CTA.
+__global__ void __launch_bounds__(kSelThreads, 1) k_select(SelArgs a) {
   extern __shared__ __align__(16) char smraw[];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int v = (int)cluster.block_rank();     // which score vector this CTA owns
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks();
+  const int rank = (int)cl.block_rank();
+  const int P = a.parts;
+  const int v = rank / P, part = rank % P, vbase = v * P;
+  const bool leader = part == 0;
   const Plan& pl = a.pl;
   const ckv_params& prm = a.p;
   char* ws = a.ws;
   Header* hdr = reinterpret_cast<Header*>(ws);
   const int n = pl.n;
-  const SelLayout L = sel_layout(n);
+  const SelLayout L = sel_layout(n, P);
   SelSmem sh;
   sh.sortbuf = reinterpret_cast<unsigned long long*>(smraw + L.off_sort);
   sh.hist = reinterpret_cast<int*>(sh.sortbuf);
-  float* sc = reinterpret_cast<float*>(ws + pl.off_sel);               // [3][n] finished scores
-  float* gx = sc + 3 * (size_t)n;                                      // [3][n] global vectors
-  int* gcomb = reinterpret_cast<int*>(gx + 3 * (size_t)n);             // [n]
-  sh.x = L.smem_scores ? reinterpret_cast<float*>(smraw + L.off_x) : gx + (size_t)v * n;
-  sh.cnt_a = reinterpret_cast<int*>(smraw + L.off_cnt_a);
-  sh.cnt_b = reinterpret_cast<int*>(smraw + L.off_cnt_b);
-  sh.bits = reinterpret_cast<uint32_t*>(smraw + L.off_bits);
+  sh.cnt = reinterpret_cast<int*>(smraw + L.off_cnt);
   sh.misc = reinterpret_cast<int*>(smraw + L.off_misc);
   sh.fmisc = reinterpret_cast<float*>(sh.misc + 128);
+  sh.hx = reinterpret_cast<int*>(smraw + L.off_hx);
+  sh.xch = reinterpret_cast<float*>(smraw + L.off_xch);
+  sh.ixch = reinterpret_cast<int*>(sh.xch);
+  float* sc = reinterpret_cast<float*>(ws + pl.off_sel);               // [3][n] finished scores
+  float* gx = sc + 3 * (size_t)n;                                      // [3][n] slices not held in smem
+  int* gcomb = reinterpret_cast<int*>(gx + 3 * (size_t)n);             // [n] combined ranks
+  int* gbins = reinterpret_cast<int*>(gx);                             // [n] rank histogram (after the lists)
+  uint32_t* gbits = reinterpret_cast<uint32_t*>(gcomb + n);            // [ceil(n/32)] keep bits
+  const int b0 = min(n, part * L.S), b1 = min(n, b0 + L.S);            // vector slice
+  float* x = L.smem_x ? reinterpret_cast<float*>(smraw + L.off_x) : gx + (size_t)v * n + b0;
+  const int T = (((n + C - 1) / C) + 31) & ~31;
+  const int g0 = min(n, rank * T), g1 = min(n, g0 + T);               // position slice
   const int mode = pl.mode;
   const bool dis = mode == CKV_COMB_DIS;
+  const bool uni = mode == CKV_COMB_UNION || mode == CKV_COMB_UNION_DA;
+  const int lane = threadIdx.x & 31;
 
-  // ---- phase 0: this CTA's vector into sc[v], then (smoothed) into x
+  // combined ranks start below every kept rank; keep bits start clear
+  for (int i = g0 + threadIdx.x; i < g1; i += blockDim.x) gcomb[i] = -1;
+  for (int i = g0 / 32 + threadIdx.x; i < (g1 + 31) / 32; i += blockDim.x) gbits[i] = 0u;
+
+  // ---- phase 0: finished scores of this slice into sc[v] (PU:2186-2204)
   float* mysc = sc + (size_t)v * n;
+  const bool chain = !a.given && v < pl.nchains;
+  int steps = 0;
   if (a.given) {
     const float* g = v == 0 ? a.ga : (v == 1 ? a.gb : a.gc);
-    for (int j = threadIdx.x; j < n; j += blockDim.x) mysc[j] = g[j];
-    __syncthreads();
-  } else if (v < pl.nchains) {
-    const int steps = early_stop_steps(pl, ws, sh.fmisc);
-    finish_chain(pl, ws, v, steps, mysc, sh.fmisc);
-    if (v == 0 && threadIdx.x == 0) hdr->steps = steps;
-    if (mode == CKV_COMB_UNION_DA) {
-      const float* colsum = reinterpret_cast<const float*>(ws + pl.off_colsum);
-      for (int j = threadIdx.x; j < n; j += blockDim.x) mysc[j] = mysc[j] * fmaxf(colsum[j], 1e-8f);
-      __syncthreads();
+    for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) mysc[j] = g[j];
+  } else if (chain) {
+    steps = early_stop_steps(pl, ws);
+    float tot = 0.f, mx = 0.f;
+    for (int j = max(b0, pl.s) + threadIdx.x; j < b1; j += blockDim.x) {
+      const float r = raw_result(pl, ws, v, j, steps);
+      mysc[j] = r;
+      tot += r;
+      mx = fmaxf(mx, r);
     }
+    tot = block_reduce<false>(tot, sh.fmisc);
+    mx = block_reduce<true>(mx, sh.fmisc);
+    if (threadIdx.x == 0) { sh.xch[0] = tot; sh.xch[1] = mx; }
+  }
+  cl.sync();
+  if (chain) {
+    float tot = 0.f, mx = 0.f;
+    for (int q = 0; q < P; ++q) {
+      const float* r = cl.map_shared_rank(sh.xch, vbase + q);
+      tot += r[0];
+      mx = fmaxf(mx, r[1]);
+    }
+    const float sinkv = tot * 0.01f;
+    mx = fmaxf(mx, pl.s > 0 ? sinkv : 0.f);
+    const float* colsum = reinterpret_cast<const float*>(ws + pl.off_colsum);
+    const float imx = mx > 0.f ? 1.0f / mx : 0.f;
+    for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) {
+      float val = (j < pl.s) ? sinkv : mysc[j];
+      if (mx > 0.f) val = div_rcp(val, mx, imx);
+      if (mode == CKV_COMB_UNION_DA) val = val * fmaxf(__ldcg(colsum + j), 1e-8f);
+      mysc[j] = val;
+    }
+    if (rank == 0 && threadIdx.x == 0) hdr->steps = steps;
   }
   if (a.finish_only) {
-    if (v < pl.nchains)
-      for (int j = threadIdx.x; j < n; j += blockDim.x) a.out_scores[(size_t)v * n + j] = mysc[j];
+    if (chain)
+      for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) a.out_scores[(size_t)v * n + j] = mysc[j];
+    cl.sync();   // the exchanged totals stay readable until every CTA has them
     return;
   }
-  if (dis) {
-    int k;
-    float sig;
-    if (v == 0) {
-      k = prm.qi_kernel_size != 0 ? prm.qi_kernel_size : prm.smoothing_kernel;
-      if (prm.smooth_hi_only && k > 1) k = 0;
-      sig = prm.use_gaussian ? prm.gaussian_sigma * 0.5f : 1.0f;
-    } else if (v == 1) {
-      k = prm.hi_kernel_size != 0 ? prm.hi_kernel_size : prm.smoothing_kernel;
-      sig = prm.gaussian_sigma;
-    } else {
-      k = prm.bi_kernel_size;
-      sig = prm.gaussian_sigma;
-    }
-    smooth(mysc, sh.x, n, k, prm.use_gaussian, sig);
-  } else {
-    for (int j = threadIdx.x; j < n; j += blockDim.x) sh.x[j] = mysc[j];
-    __syncthreads();
-  }
-  if (a.out_scores && v < 2)
-    for (int j = threadIdx.x; j < n; j += blockDim.x) a.out_scores[(size_t)v * n + j] = sh.x[j];
+  cl.sync();   // finished vectors complete: smoothing reads the neighbouring slices
 
-  // ---- phase 1: this vector's top list
+  // ---- phase 1: smoothing (PU:1921-1936, PU:3131-3160) of the slice into x
+  {
+    int k = 0;
+    float sig = 1.0f;
+    if (dis) {
+      if (v == 0) {
+        k = prm.qi_kernel_size != 0 ? prm.qi_kernel_size : prm.smoothing_kernel;
+        if (prm.smooth_hi_only && k > 1) k = 0;
+        sig = prm.use_gaussian ? prm.gaussian_sigma * 0.5f : 1.0f;
+      } else if (v == 1) {
+        k = prm.hi_kernel_size != 0 ? prm.hi_kernel_size : prm.smoothing_kernel;
+        sig = prm.gaussian_sigma;
+      } else {
+        k = prm.bi_kernel_size;
+        sig = prm.gaussian_sigma;
+      }
+    }
+    if (k <= 1 || n <= k) {
+      for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) x[j - b0] = mysc[j];
+    } else {
+      float w[32];
+      const int kk = smooth_taps(k, prm.use_gaussian != 0, sig, w);
+      const int pad = k / 2;
+      for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) {
+        float acc = 0.f;
+        for (int t = 0; t < kk; ++t) {
+          const int src = j + t - pad;
+          if (src >= 0 && src < n) acc = fmaf(w[t], __ldcg(mysc + src), acc);
+        }
+        x[j - b0] = acc;
+      }
+    }
+    __syncthreads();
+    if (a.out_scores && v < 2)
+      for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) a.out_scores[(size_t)v * n + j] = x[j - b0];
+  }
+
+  // ---- phase 2: this vector's top list, sorted, in its leader CTA
   const int lo = pl.s, hi = pl.n - pl.W;   // candidates [s, n-W)
   const int kk = pl.kk;
-  const bool uni = mode == CKV_COMB_UNION || mode == CKV_COMB_UNION_DA;
-  int M = 0;
-  if (uni) {
-    const int remaining = kk, cand = hi - lo;
-    const int qb = (int)((float)remaining * prm.qi_ratio), hb = remaining - qb;
-    M = (v == 0) ? min(qb, cand) : min(cand, hb + qb + remaining);
-    if (threadIdx.x == 0) { sh.misc[70] = min(qb, cand); sh.misc[71] = min(hb, cand); }
-    if (M > 0) top_sorted(sh.x, Range{n, lo, hi, true}, M, false, sh);
-  } else {
-    const bool zeroed = (dis && v == 0 && prm.ablate_qi) || (dis && v == 1 && prm.ablate_hi);
-    M = min(n, kk + pl.s + pl.W);
-    if (!zeroed && kk > 0) top_sorted(sh.x, Range{n, 0, n, false}, M, true, sh);
-  }
-  if (threadIdx.x == 0) sh.misc[72] = M;
-  cluster.sync();
+  const int cand = hi - lo;
+  const int qb = (int)((float)kk * prm.qi_ratio), hb = kk - qb;
+  const int Mx = min(n, kk + pl.s + pl.W);
+  int M;
+  if (uni) M = (v == 0) ? min(qb, cand) : min(cand, hb + qb + kk);
+  else M = Mx;
+  M = max(M, 1);
+  if (uni) top_sorted(cl, x, b0, b1, lo, hi, M, false, vbase, P, leader, sh);
+  else top_sorted(cl, x, b0, b1, 0, n, M, true, vbase, P, leader, sh);
+  cl.sync();   // sorted lists ready
 
-  // ---- phase 2 (CTA 0): combine, threshold, compact
-  if (v == 0) {
-    const int nv = cluster.num_blocks();
-    for (int i = threadIdx.x; i < L.nchunk; i += blockDim.x) sh.bits[i] = 0u;
+  // ---- phase 3: combination (PU:3177-3196 rank MAX; PU:2489-2589 union)
+  auto zeroed = [&](int u) { return (dis && u == 0 && prm.ablate_qi) || (dis && u == 1 && prm.ablate_hi); };
+  const int nv = C / P;
+  int live = 0;
+  for (int u = 0; u < nv; ++u) live += zeroed(u) ? 0 : 1;
+  const bool rankmax = !uni && kk > 0 && live > 0;
+  for (int i = g0 + threadIdx.x; i < min(g1, Mx); i += blockDim.x) gbins[i] = 0;
+  if (rankmax) {
+    // combined rank of every listed position: MAX over the vectors of n - 1 - list position
+    for (int u = 0; u < nv; ++u) {
+      if (zeroed(u)) continue;
+      const unsigned long long* lst = cl.map_shared_rank(sh.sortbuf, u * P);
+      for (int p = rank * (int)blockDim.x + threadIdx.x; p < Mx; p += C * (int)blockDim.x)
+        atomicMax(&gcomb[sorted_index(lst[p], true)], n - 1 - p);
+    }
+  }
+  cl.sync();
+  if (rankmax)
+    for (int i = max(g0, lo) + threadIdx.x; i < min(g1, hi); i += blockDim.x) {
+      const int r = __ldcg(gcomb + i);
+      if (r >= n - Mx) atomicAdd(&gbins[r - (n - Mx)], 1);
+    }
+  cl.sync();
+  int t = n, need = 0;
+  if (rankmax) {
+    // threshold: the combined rank at which the kept count reaches kk (every CTA alike)
+    const int c = (Mx + blockDim.x - 1) / blockDim.x;
+    const int bhi = Mx - (int)threadIdx.x * c, blo = max(0, bhi - c);
+    int local = 0;
+    for (int b = blo; b < bhi; ++b) local += __ldcg(gbins + b);
+    int tot;
+    const int above = block_exclusive_scan(local, sh.misc, &tot);
+    if (threadIdx.x == 0) { sh.misc[80] = n; sh.misc[81] = 0; }
     __syncthreads();
-    if (kk > 0 && uni) {
-      const int qk = sh.misc[70], hk = sh.misc[71];
-      const unsigned long long* hl = cluster.map_shared_rank(sh.sortbuf, 1);
-      const int ext = *cluster.map_shared_rank(sh.misc + 72, 1);
-      for (int p = threadIdx.x; p < qk; p += blockDim.x) set_bit(sh.bits, sorted_index(sh.sortbuf[p], false));
-      __syncthreads();
-      for (int p = threadIdx.x; p < hk; p += blockDim.x) set_bit(sh.bits, sorted_index(hl[p], false));
-      __syncthreads();
-      int cnt = 0;
-      for (int i = threadIdx.x; i < L.nchunk; i += blockDim.x) cnt += __popc(sh.bits[i]);
-      cnt = (int)block_reduce<false>((float)cnt, sh.fmisc);
-      if (cnt < kk && threadIdx.x < 32) {
-        int have = cnt;
-        for (int base = 0; base < ext && have < kk; base += 32) {
-          const int p = base + threadIdx.x;
-          int idx = -1;
-          bool add = false;
-          if (p < ext) { idx = sorted_index(hl[p], false); add = !get_bit(sh.bits, idx); }
-          const unsigned ball = __ballot_sync(0xffffffffu, add);
-          if (add && have + __popc(ball & lanemask_lt()) < kk) set_bit(sh.bits, idx);
-          have += __popc(ball);
-        }
-      }
-      __syncthreads();
-    } else if (kk > 0) {
-      int live = 0;
-      for (int u = 0; u < nv; ++u) live += *cluster.map_shared_rank(sh.misc + 72, u) > 0 &&
-                                           !((dis && u == 0 && prm.ablate_qi) || (dis && u == 1 && prm.ablate_hi));
-      const int Mx = min(n, kk + pl.s + pl.W);
-      if (live == 0) {
-        for (int i = lo + threadIdx.x; i < lo + kk; i += blockDim.x) set_bit(sh.bits, i);
-        __syncthreads();
-      } else {
-        // combined ranks of the union of the top lists (others: below every kept rank)
-        int* comb = L.smem_scores ? reinterpret_cast<int*>(sh.x) : gcomb;
-        for (int i = threadIdx.x; i < n; i += blockDim.x) comb[i] = -1;
-        __syncthreads();
-        for (int u = 0; u < nv; ++u) {
-          const bool zeroed = (dis && u == 0 && prm.ablate_qi) || (dis && u == 1 && prm.ablate_hi);
-          if (zeroed) continue;
-          const unsigned long long* lst = cluster.map_shared_rank(sh.sortbuf, u);
-          for (int p = threadIdx.x; p < Mx; p += blockDim.x)
-            atomicMax(&comb[sorted_index(lst[p], true)], n - 1 - p);
-        }
-        __syncthreads();
-        // histogram of combined ranks >= n - Mx over the candidates (cnt_b reused as bins)
-        // bins over [n - Mx, n): CTA 0's own list has been consumed, its buffer is free
-        int* hbuf = sh.hist;
-        for (int i = threadIdx.x; i < Mx; i += blockDim.x) hbuf[i] = 0;
-        __syncthreads();
-        for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-          const int r = comb[i];
-          if (r >= n - Mx) atomicAdd(&hbuf[r - (n - Mx)], 1);
-        }
-        __syncthreads();
-        {
-          const int c = (Mx + blockDim.x - 1) / blockDim.x;
-          const int bhi = Mx - (int)threadIdx.x * c, blo = max(0, bhi - c);
-          int local = 0;
-          for (int b = blo; b < bhi; ++b) local += hbuf[b];
-          int tot;
-          const int above = block_exclusive_scan(local, sh.misc, &tot);
-          if (threadIdx.x == 0) { sh.misc[80] = n; sh.misc[81] = 0; }
-          __syncthreads();
-          if (above < kk && above + local >= kk) {
-            int cum = above;
-            for (int b = bhi - 1; b >= blo; --b) {
-              if (cum + hbuf[b] >= kk) { sh.misc[80] = (n - Mx) + b; sh.misc[81] = kk - cum; break; }
-              cum += hbuf[b];
-            }
-          }
-          __syncthreads();
-          if (threadIdx.x == 0 && sh.misc[80] == n) set_status(&hdr->status, kStatusCount);
-        }
-        const int t = sh.misc[80], need = sh.misc[81];
-        // at the threshold: the lowest `need` candidate indices
-        chunk_counts(n, sh.cnt_a, [&](int i) { return i >= lo && i < hi && comb[i] == t; });
-        scan_counts(sh.cnt_a, L.nchunk, sh.misc);
-        const int lane = threadIdx.x & 31;
-        for (int base = threadIdx.x - lane; base < n; base += blockDim.x) {
-          const int i = base + lane;
-          const bool cand = i < n && i >= lo && i < hi;
-          const int r = cand ? comb[i] : -1;
-          const unsigned tb = __ballot_sync(0xffffffffu, cand && r == t);
-          if (cand && (r > t || (r == t && chunk_rank(sh.cnt_a, i, tb) < need))) set_bit(sh.bits, i);
-        }
-        __syncthreads();
+    if (above < kk && above + local >= kk) {
+      int cum = above;
+      for (int b = bhi - 1; b >= blo; --b) {
+        const int hb_ = __ldcg(gbins + b);
+        if (cum + hb_ >= kk) { sh.misc[80] = (n - Mx) + b; sh.misc[81] = kk - cum; break; }
+        cum += hb_;
       }
     }
-    // compaction: sinks + chosen, ascending
-    const int cap = pl.s + kk;
-    chunk_counts(hi, sh.cnt_a, [&](int i) { return i < pl.s || get_bit(sh.bits, i); });
-    const int total = scan_counts(sh.cnt_a, (hi + 31) / 32, sh.misc);
-    const int lane = threadIdx.x & 31;
-    for (int base = threadIdx.x - lane; base < hi; base += blockDim.x) {
-      const int i = base + lane;
-      const bool kp = i < hi && (i < pl.s || get_bit(sh.bits, i));
-      const unsigned b = __ballot_sync(0xffffffffu, kp);
-      if (kp) {
-        const int r = chunk_rank(sh.cnt_a, i, b);
-        if (r < cap) a.out_idx[r] = i;
+    __syncthreads();
+    t = sh.misc[80];
+    need = sh.misc[81];
+    if (rank == 0 && threadIdx.x == 0 && t == n) set_status(&hdr->status, kStatusCount);
+    chunk_counts(g0, g1, sh.cnt, [&](int i) { return i >= lo && i < hi && __ldcg(gcomb + i) == t; });
+    const int mine = scan_counts(sh.cnt, (g1 - g0 + 31) / 32, sh.misc);
+    if (threadIdx.x == 0) sh.ixch[3] = mine;
+  }
+  cl.sync();
+  if (rankmax) {
+    // at the threshold: the lowest `need` candidate indices
+    int base = 0;
+    for (int q = 0; q < rank; ++q) base += cl.map_shared_rank(sh.ixch, q)[3];
+    for (int b = g0 + (int)threadIdx.x - lane; b < g1; b += blockDim.x) {
+      const int i = b + lane;
+      const bool cnd = i < g1 && i >= lo && i < hi;
+      const int r = cnd ? __ldcg(gcomb + i) : -1;
+      const unsigned tb = __ballot_sync(0xffffffffu, cnd && r == t);
+      const bool keep = cnd && (r > t || (r == t && base + chunk_rank(sh.cnt, g0, i, tb) < need));
+      const unsigned word = __ballot_sync(0xffffffffu, keep);
+      if (lane == 0) gbits[i >> 5] = word;
+    }
+  } else if (!uni && kk > 0) {
+    // every vector ablated: the first kk candidates
+    for (int b = g0 + (int)threadIdx.x - lane; b < g1; b += blockDim.x) {
+      const int i = b + lane;
+      const unsigned word = __ballot_sync(0xffffffffu, i < g1 && i >= lo && i < lo + kk);
+      if (lane == 0) gbits[i >> 5] = word;
+    }
+  } else if (uni && kk > 0 && rank == 0) {
+    // union: QI top qk, HI top hk, then fill from the HI list in order
+    const int qk = min(qb, cand), hk = min(hb, cand);
+    const unsigned long long* l0 = sh.sortbuf;
+    const unsigned long long* l1 = cl.map_shared_rank(sh.sortbuf, P);
+    const int ext = min(cand, hb + qb + kk);
+    for (int p = threadIdx.x; p < qk; p += blockDim.x) {
+      const int i = sorted_index(l0[p], false);
+      atomicOr(gbits + (i >> 5), 1u << (i & 31));
+    }
+    for (int p = threadIdx.x; p < hk; p += blockDim.x) {
+      const int i = sorted_index(l1[p], false);
+      atomicOr(gbits + (i >> 5), 1u << (i & 31));
+    }
+    __syncthreads();
+    int cnt = 0;
+    for (int i = threadIdx.x; i < (n + 31) / 32; i += blockDim.x) cnt += __popc(__ldcg(gbits + i));
+    cnt = (int)block_reduce<false>((float)cnt, sh.fmisc);
+    if (cnt < kk && threadIdx.x < 32) {
+      int have = cnt;
+      for (int base = 0; base < ext && have < kk; base += 32) {
+        const int p = base + threadIdx.x;
+        int idx = -1;
+        bool add = false;
+        if (p < ext) {
+          idx = sorted_index(l1[p], false);
+          add = !((__ldcg(gbits + (idx >> 5)) >> (idx & 31)) & 1u);
+        }
+        const unsigned ball = __ballot_sync(0xffffffffu, add);
+        if (add && have + __popc(ball & lanemask_lt()) < kk) atomicOr(gbits + (idx >> 5), 1u << (idx & 31));
+        have += __popc(ball);
       }
     }
+  }
+  cl.sync();   // keep bits complete
+
+  // ---- phase 4: compaction (PU:3496-3501): sinks + chosen, ascending
+  const int cap = pl.s + kk;
+  const int h1 = min(g1, hi);
+  auto kept = [&](int i) { return i < h1 && (i < pl.s || ((__ldcg(gbits + (i >> 5)) >> (i & 31)) & 1u)); };
+  int mine = 0;
+  if (g0 < h1) {
+    chunk_counts(g0, h1, sh.cnt, kept);
+    mine = scan_counts(sh.cnt, (h1 - g0 + 31) / 32, sh.misc);
+  }
+  if (threadIdx.x == 0) sh.ixch[4] = mine;
+  cl.sync();
+  int base = 0, total = 0;
+  for (int q = 0; q < C; ++q) {
+    const int c = cl.map_shared_rank(sh.ixch, q)[4];
+    if (q < rank) base += c;
+    total += c;
+  }
+  for (int b = g0 + (int)threadIdx.x - lane; b < h1; b += blockDim.x) {
+    const int i = b + lane;
+    const bool kp = kept(i);
+    const unsigned bb = __ballot_sync(0xffffffffu, kp);
+    if (kp) {
+      const int r = base + chunk_rank(sh.cnt, g0, i, bb);
+      if (r < cap) a.out_idx[r] = i;
+    }
+  }
+  if (rank == C - 1) {
     for (int i = total + threadIdx.x; i < cap; i += blockDim.x) a.out_idx[i] = 0;
     if (threadIdx.x == 0) {
       hdr->kept = total;
       if (total != cap) set_status(&hdr->status, kStatusCount);
     }
   }
-  cluster.sync();   // the other CTAs' lists stay alive until CTA 0 is done
+  cl.sync();   // shared memory stays readable until every CTA is done with it
 }
 
-size_t select_smem_bytes_n(int n) { return sel_layout(n).total; }
+// CTAs per score vector: up to 16 CTAs per cluster where the device schedules that
+// cluster size, else the portable 8.
+static int select_parts(int nv, size_t smem, cudaStream_t st) {
+  static std::mutex mu;
+  static int cached[64][4] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev][nv] != 0) return cached[dev][nv];
+  int parts = 8 / nv;
+  if (cudaFuncSetAttribute(k_select, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    const int p16 = 16 / nv;
+    cfg.gridDim = dim3(nv * p16, 1, 1);
+    cfg.blockDim = dim3(kSelThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = nv * p16;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int nclusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&nclusters, k_select, &cfg) == cudaSuccess && nclusters >= 1) parts = p16;
+    cudaGetLastError();
+  }
+  cached[dev][nv] = parts;
+  return parts;
+}
 
-cudaError_t launch_select(const SelArgs& a, cudaStream_t st) {
+size_t select_smem_bytes_n(int n) { return sel_layout(n, 2).total; }
+
+cudaError_t launch_select(const SelArgs& a0, cudaStream_t st) {
+  SelArgs a = a0;
   const Plan& pl = a.pl;
   const bool bridge = pl.mode == CKV_COMB_DIS && a.p.use_bridge_importance &&
                       (a.given ? a.gc != nullptr : true);
   const int nv = a.finish_only ? pl.nchains : (bridge ? 3 : 2);
-  const size_t smem = sel_layout(pl.n).total;
-  { const cudaError_t e = ensure_dynamic_smem((const void*)k_select, smem); if (e != cudaSuccess) return e; }
+  const bool uni = pl.mode == CKV_COMB_UNION || pl.mode == CKV_COMB_UNION_DA;
+  if (pl.kk + pl.s + pl.W > kMaxSort || (uni && 2 * pl.kk > kMaxSort)) return cudaErrorInvalidValue;   // make_plan rejects these
+  // the shared memory layout depends on the slice length, hence on the CTAs per vector
+  const size_t s8 = sel_layout(pl.n, 8 / nv).total, s16 = sel_layout(pl.n, 16 / nv).total;
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_select, s8 > s16 ? s8 : s16); if (e != cudaSuccess) return e; }
+  a.parts = select_parts(nv, s16, st);
+  const size_t smem = sel_layout(pl.n, a.parts).total;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nv, 1, 1);
+  cfg.gridDim = dim3(nv * a.parts, 1, 1);
   cfg.blockDim = dim3(kSelThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = nv;
+  attr[0].val.clusterDim.x = nv * a.parts;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;

@@ -18,15 +18,16 @@ struct SelArgs {
   const float* gb;
   const float* gc;
   int finish_only;       // 1: stop after the finished chain scores (written to out_scores)
+  int parts;             // CTAs per score vector (set by launch_select)
 };
 
 size_t select_smem_bytes_n(int n);
 cudaError_t launch_select(const SelArgs& a, cudaStream_t st);
-// H2O column sums of full_attn (mode max / weighted) and bridge importance (dis + bridge).
 // Selection stage with its scratch in a static device array (no workspace argument).
 int select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const float* b,
                           const float* c, int32_t* out_idx, float* out_scores, cudaStream_t st,
                           const char** why);
+// H2O column sums of full_attn (mode max / weighted) and bridge importance (dis + bridge).
 cudaError_t launch_aux(const Plan& pl, const ckv_params& p, char* ws, cudaStream_t st);
 
 }  // namespace ckv

@@ -164,10 +164,11 @@ template <int DT> struct WarpTile {
 
 // Reference rounding of a logit: dtype(dtype(acc) / sqrt(D)) for 16-bit inputs, acc / sqrt(D) for fp32.
 // (bf16: the reciprocal product of the reference's CUDA division by a scalar; fp16 divides.)
-template <int DT> CKV_DEV float logit_of(float acc, float scale) {
-  if constexpr (DT == CKV_FP32) return __fdiv_rn(acc, scale);
-  if constexpr (DT == CKV_FP16) return round_dt<DT>(__fdiv_rn(round_dt<DT>(acc), scale));
-  return round_dt<DT>(round_dt<DT>(acc) * __frcp_rn(scale));
+// Logit of one accumulator; inv_scale = RN(1 / scale).
+template <int DT> CKV_DEV float logit_of(float acc, float scale, float inv_scale) {
+  if constexpr (DT == CKV_FP32) return div_rcp(acc, scale, inv_scale);
+  if constexpr (DT == CKV_FP16) return round_dt<DT>(div_rcp(round_dt<DT>(acc), scale, inv_scale));
+  return round_dt<DT>(round_dt<DT>(acc) * inv_scale);
 }
 
 // ---------------------------------------------------------------------------
@@ -330,6 +331,7 @@ __global__ void __launch_bounds__(256) k_window_stats(WinArgs a) {
   const int hl = row0 / pl.W;                        // batch-local head (W is a multiple of rows/warp)
   const int kt = (bg.h0 + hl) / pl.G - bg.g0;        // K tile of this warp's KV head
   const float scale = sqrtf((float)pl.D);
+  const float inv_scale = 1.0f / scale;
   const int t0 = chunk * pl.tiles_per_chunk;
   const int t1 = min(t0 + pl.tiles_per_chunk, pl.ncol_tiles);
 
@@ -374,7 +376,7 @@ __global__ void __launch_bounds__(256) k_window_stats(WinArgs a) {
           for (int e = 0; e < 2; ++e) {
             const int j = j0 + nt * 8 + 2 * (lane & 3) + e;
             float v = -INFINITY;
-            if (j <= lim) v = logit_of<DT>(acc[mt][nt][2 * hf + e], scale) * kLog2e;
+            if (j <= lim) v = logit_of<DT>(acc[mt][nt][2 * hf + e], scale, inv_scale) * kLog2e;
             y[nt * 2 + e] = v;
             tmax = fmaxf(tmax, v);
           }
@@ -481,18 +483,26 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
     }
     if (valid && sub == 0) {
       const float l2z = log2f(M.z);
+      const float iz = 1.0f / M.z;
       lse[i0 + li] = M.m + l2z;
       const int r = li % pl.W;
-      rowE[li] = l2z * kLn2 - kLn2 * (M.t / M.z) + (float)(pl.W - 1 - r) * kGeps;
-      rowM[li] = 1.f - M.s / M.z;
+      rowE[li] = l2z * kLn2 - kLn2 * div_rcp(M.t, M.z, iz) + (float)(pl.W - 1 - r) * kGeps;
+      rowM[li] = 1.f - div_rcp(M.s, M.z, iz);
     }
   }
   __syncthreads();
-  for (int hl = threadIdx.x; hl < nh; hl += blockDim.x) {
-    float e = 0.f, m = 0.f;
-    for (int r = 0; r < pl.W; ++r) { e += rowE[hl * pl.W + r]; m += rowM[hl * pl.W + r]; }
-    spec[h0 + hl] = e / (float)pl.W;
-    spec[pl.H + h0 + hl] = m / (float)pl.W;
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int hl = warp; hl < nh; hl += nw) {
+      float e = 0.f, m = 0.f;
+      for (int r = lane; r < pl.W; r += 32) { e += rowE[hl * pl.W + r]; m += rowM[hl * pl.W + r]; }
+      e = warp_sum(e);
+      m = warp_sum(m);
+      if (lane == 0) {
+        spec[h0 + hl] = e / (float)pl.W;
+        spec[pl.H + h0 + hl] = m / (float)pl.W;
+      }
+    }
   }
   // the last group selects the heads
   __threadfence();
@@ -547,10 +557,12 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
 
   const uint64_t qset = hdr->qi_heads, hset = hdr->hi_heads;
   const int hmode = hdr->hi_mode, nhi = hdr->n_hi;
+  const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
   const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);
   float* epart = reinterpret_cast<float*>(a.ws + pl.off_epart);
   float* mpart = reinterpret_cast<float*>(a.ws + pl.off_mpart);
   const float scale = sqrtf((float)pl.D);
+  const float inv_scale = 1.0f / scale;
 
   // pooling-pass mapping: column c = tid % 64, rows r = tid / 64 + 4 i
   const int pc = threadIdx.x % kColTile;
@@ -590,7 +602,7 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
             const int j = j0 + nt * 8 + 2 * (lane & 3) + e;
             float p = 0.f;
             if (j <= lim) {
-              const float y = logit_of<DT>(acc[mt][nt][2 * hf + e], scale) * kLog2e;
+              const float y = logit_of<DT>(acc[mt][nt][2 * hf + e], scale, inv_scale) * kLog2e;
               const float d = y - L;
               p = ex2(d);
               ent += (p >= 1e-8f) ? -p * d * kLn2 : kGeps;
@@ -648,7 +660,7 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
     for (int i = 0; i < kRowsPerThread; ++i) {
       const int r = pr0 + 4 * i;
       if (r < pl.W) {   // uniform per warp: a warp's 32 threads share r
-        float v = ch == 0 ? qacc[i] : (hmode == 1 ? hacc[i] : hacc[i] / (float)nhi);
+        float v = ch == 0 ? qacc[i] : (hmode == 1 ? hacc[i] : hacc[i] * inv_nhi);
         if (j >= pl.n) v = 0.f;
         rows[(size_t)r * pl.n_pad + j] = v;
         cs += v;
@@ -692,22 +704,44 @@ __device__ void window_pool_finish(const WinArgs& a, char* smem) {
   Header* hdr = reinterpret_cast<Header*>(a.ws);
   float* exact = reinterpret_cast<float*>(a.ws + pl.off_spec) + 2 * pl.H;   // [H] ent, [H] mass
   const float* rowE = reinterpret_cast<const float*>(a.ws + pl.off_stats);   // [H*W] (k_pool_reduce)
-  const float* rowM = rowE + pl.H * pl.W;
-  float* sE = reinterpret_cast<float*>(smem);       // [H*W]
-  float* sM = sE + pl.H * pl.W;                     // [H*W]
-  for (int i = threadIdx.x; i < pl.H * pl.W; i += blockDim.x) { sE[i] = __ldcg(rowE + i); sM[i] = __ldcg(rowM + i); }
+  float* sE = reinterpret_cast<float*>(smem);       // [H*W] entropy, then [H*W] mass
+  float* sM = sE + pl.H * pl.W;
+  float* sHead = sE + 2 * pl.H * pl.W;              // [H] entropy, [H] mass means
+  const int HW2 = 2 * pl.H * pl.W;                  // rowM follows rowE
+  for (int base = threadIdx.x; base < HW2; base += 8 * blockDim.x) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * (int)blockDim.x;
+      v[u] = i < HW2 ? __ldcg(rowE + i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * (int)blockDim.x;
+      if (i < HW2) sE[i] = v[u];
+    }
+  }
   __syncthreads();
-  for (int h = threadIdx.x; h < pl.H; h += blockDim.x) {
-    float e = 0.f, m = 0.f;
-    for (int r = 0; r < pl.W; ++r) { e += sE[h * pl.W + r]; m += sM[h * pl.W + r]; }
-    exact[h] = e / (float)pl.W;
-    exact[pl.H + h] = m / (float)pl.W;
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int h = warp; h < pl.H; h += nw) {
+      float e = 0.f, m = 0.f;
+      for (int r = lane; r < pl.W; r += 32) { e += sE[h * pl.W + r]; m += sM[h * pl.W + r]; }
+      e = warp_sum(e);
+      m = warp_sum(m);
+      if (lane == 0) {
+        sHead[h] = e / (float)pl.W;
+        sHead[pl.H + h] = m / (float)pl.W;
+        exact[h] = sHead[h];
+        exact[pl.H + h] = sHead[pl.H + h];
+      }
+    }
   }
   __syncthreads();
   __shared__ int redo;
   uint64_t qs, hs;
   int hm, nh;
-  select_heads(a.p, pl.H, exact, exact + pl.H, &qs, &hs, &hm, &nh);
+  select_heads(a.p, pl.H, sHead, sHead + pl.H, &qs, &hs, &hm, &nh);
   if (threadIdx.x == 0) {
     redo = (qs != hdr->qi_heads || hs != hdr->hi_heads || hm != hdr->hi_mode) ? 1 : 0;
     if (redo && !a.fixup_pass) {
@@ -730,74 +764,140 @@ __device__ void window_pool_finish(const WinArgs& a, char* smem) {
 // Row sums (tempered) of the pooled rows and the W x W window chain of each
 // absorbing chain: y_0 (query one-hot or uniform), y_{k+1} = gamma * Pww^T y_k.
 // Writes y_k, the weights w_k = gamma * y_k / rowsum used by the prefix sweep,
-// and max_c y_k.  One CTA; `smem` >= W*W + 7*W + 32 floats.
+// and max_c y_k.  One CTA.  Staging: one warp per window row, lanes over columns,
+// 8 rows in flight per warp.  Iteration: the chains run side by side, each on
+// half of the warps with its own named barrier; warp j of a chain sums its block
+// of rows for every column, and the block partials are added in row order.
+// `smem` >= chains_smem_floats(W) floats.
+__host__ __device__ constexpr size_t chains_smem_floats(int W) { return (size_t)2 * W * W + 8 * W + 2 * 32 * kMaxWindow + 64; }
+
 __device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem,
                                   bool use_rowsums) {
-  // row sums (tempered), then the W x W window chain of each absorbing chain
+  constexpr int kCols = kMaxWindow / 32;                      // columns per lane
   const int W = pl.W, K = pl.K;
   const bool tempered = prm.neumann_temperature != 1.0f && prm.neumann_temperature > 0.f;
   const float invT = tempered ? 1.0f / prm.neumann_temperature : 1.0f;
   const float gam = prm.neumann_gamma;
   const float* rspart = reinterpret_cast<const float*>(ws + pl.off_rspart);
+  const float* rowS = reinterpret_cast<const float*>(ws + pl.off_stats) + 2 * pl.H * W;   // from k_pool_reduce
   float* wk = reinterpret_cast<float*>(ws + pl.off_wk);     // [2][K][W]
   float* yk = reinterpret_cast<float*>(ws + pl.off_yk);     // [2][K+1][W]
   float* ymax = reinterpret_cast<float*>(ws + pl.off_ymax); // [2][K+1]
-  float* sPw = smem;                                          // [W][W]
-  float* sRs = smem + W * W;                                  // [W]
-  float* sY = sRs + W;                                        // [2][W]
+  float* sPw = smem;                                          // [2][W][W]
+  float* sRs = smem + 2 * W * W;                              // [2][W]
+  float* sY = sRs + 2 * W;                                    // [2][2][W]
+  float* sPart = sY + 4 * W;                                  // [2][32][W]
+  float* sMx = sPart + 2 * 32 * kMaxWindow;                   // [2][32]
+  float* sInv = sMx + 64;                                     // [2][W] reciprocal row sums
   const int nchain = pl.nchains;
-  for (int ch = 0; ch < nchain; ++ch) {
-    const bool own = (ch == 0) || pl.hi_rows;
-    const float* rows = reinterpret_cast<const float*>(ws + (own && ch == 1 ? pl.off_rows_hi
-                                                                               : pl.off_rows_qi));
-    const int src = own ? ch : 0;
-    const float* rowS = reinterpret_cast<const float*>(ws + pl.off_stats) + 2 * pl.H * W;   // from k_pool_reduce
-    for (int r = threadIdx.x; r < W; r += blockDim.x) {
-      float s;
-      if (use_rowsums) s = __ldcg(rowS + ch * W + r);
-      else s = sum_parts(rspart + (size_t)src * pl.rs_parts * W + r, pl.rs_parts, (size_t)W, 0, 1);
-      sRs[r] = fmaxf(s, 1e-8f);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int i = threadIdx.x; i < nchain * W; i += blockDim.x) {
+    const int ch = i / W, r = i % W;
+    const int src = (ch == 0 || pl.hi_rows) ? ch : 0;
+    const float s = use_rowsums ? __ldcg(rowS + ch * W + r)
+                                : sum_parts(rspart + (size_t)src * pl.rs_parts * W + r, pl.rs_parts, (size_t)W, 0, 1);
+    sRs[i] = fmaxf(s, 1e-8f);
+    sInv[i] = 1.0f / sRs[i];
+  }
+  __syncthreads();
+  const float* rows0 = reinterpret_cast<const float*>(ws + pl.off_rows_qi);
+  const float* rows1 = reinterpret_cast<const float*>(ws + (pl.hi_rows ? pl.off_rows_hi : pl.off_rows_qi));
+  const int R = nchain * W;                                   // (chain, row) pairs
+  for (int g0 = warp; g0 < R; g0 += 8 * nw) {
+    float v[8][kCols];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int g = g0 + u * nw, ch = g >= W ? 1 : 0, r = g - ch * W;
+      const float* src = (ch ? rows1 : rows0) + (size_t)r * pl.n_pad + pl.n_p;
+#pragma unroll
+      for (int q = 0; q < kCols; ++q) {
+        const int c = lane + 32 * q;
+        v[u][q] = (g < R && c < W) ? __ldcg(src + c) : 0.f;
+      }
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < W * W; i += blockDim.x) {
-      const int r = i / W, c = i % W;
-      float v = __ldcg(rows + (size_t)r * pl.n_pad + pl.n_p + c);
-      if (tempered) v = v > 0.f ? powf(v, invT) : 0.f;
-      sPw[i] = v / sRs[r];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int g = g0 + u * nw;
+      if (g < R) {
+        const float s = sRs[g];
+#pragma unroll
+        for (int q = 0; q < kCols; ++q) {
+          const int c = lane + 32 * q;
+          if (c < W) {
+            float x = v[u][q];
+            if (tempered) x = x > 0.f ? powf(x, invT) : 0.f;
+            sPw[(size_t)g * W + c] = div_rcp(x, s, sInv[g]);
+          }
+        }
+      }
     }
-    // start vector: the query one-hot (QI) or uniform 1/n_transient (HI)
-    const bool query_start = (ch == 0);
-    const float u = 1.0f / (float)(pl.n - pl.s);
-    for (int c = threadIdx.x; c < W; c += blockDim.x) sY[c] = query_start ? (c == W - 1 ? 1.f : 0.f) : u;
-    __syncthreads();
+  }
+  __syncthreads();
+  const int wpc = min(32, nw / nchain);                       // warps per chain
+  const int tpc = wpc * 32;
+  const int ch = warp / wpc;
+  if (ch < nchain) {
+    const int j = warp - ch * wpc;                            // row block of this warp
+    const int ct = threadIdx.x - ch * tpc;
+    const int rpw = (W + wpc - 1) / wpc;
+    const int r0 = min(W, j * rpw), r1 = min(W, r0 + rpw);
+    const float* Pw = sPw + (size_t)ch * W * W;
+    const float* rs = sRs + ch * W;
+    const float* inv = sInv + ch * W;
+    float* Y = sY + ch * 2 * W;
+    float* part = sPart + ch * 32 * kMaxWindow;
+    float* mxw = sMx + ch * 32;
+    auto chain_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + ch), "r"(tpc) : "memory"); };
+    const float u0 = 1.0f / (float)(pl.n - pl.s);
+    for (int c = ct; c < W; c += tpc) Y[c] = (ch == 0) ? (c == W - 1 ? 1.f : 0.f) : u0;
+    chain_sync();
     for (int k = 0; k <= K; ++k) {
-      float* cur = sY + (k & 1) * W;
-      float* nxt = sY + ((k + 1) & 1) * W;
-      for (int c = threadIdx.x; c < W; c += blockDim.x) {
-        yk[((size_t)ch * (K + 1) + k) * W + c] = cur[c];
-        if (k < K) wk[((size_t)ch * K + k) * W + c] = gam * cur[c] / sRs[c];
+      const float* cur = Y + (k & 1) * W;
+      float* nxt = Y + ((k + 1) & 1) * W;
+      if (k < K) {
+        float s[kCols];
+#pragma unroll
+        for (int q = 0; q < kCols; ++q) s[q] = 0.f;
+#pragma unroll 8
+        for (int r = r0; r < r1; ++r) {
+          const float yr = cur[r];
+#pragma unroll
+          for (int q = 0; q < kCols; ++q) {
+            const int c = lane + 32 * q;
+            if (c < W) s[q] = fmaf(Pw[r * W + c], yr, s[q]);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < kCols; ++q) {
+          const int c = lane + 32 * q;
+          if (c < W) part[j * W + c] = s[q];
+        }
       }
       float mx = 0.f;
-      for (int c = threadIdx.x; c < W; c += blockDim.x) mx = fmaxf(mx, fabsf(cur[c]));
-      mx = block_reduce<true>(mx, smem + W * W + 3 * W);
-      if (threadIdx.x == 0) ymax[ch * (K + 1) + k] = mx;
-      if (k < K) {
-        // y_{k+1}[c] = gamma * sum_{r >= c} Pw[r, c] y_k[r], four row groups per column
-        float* sPart = smem + W * W + 3 * W + 32;           // [4][W]
-        for (int idx = threadIdx.x; idx < 4 * W; idx += blockDim.x) {
-          const int c = idx % W, q = idx / W;
-          float s = 0.f;
-          for (int r = c + q; r < W; r += 4) s = fmaf(sPw[r * W + c], cur[r], s);
-          sPart[q * W + c] = s;
-        }
-        __syncthreads();
-        for (int c = threadIdx.x; c < W; c += blockDim.x)
-          nxt[c] = gam * ((sPart[c] + sPart[W + c]) + (sPart[2 * W + c] + sPart[3 * W + c]));
+      for (int c = ct; c < W; c += tpc) {
+        const float y = cur[c];
+        yk[((size_t)ch * (K + 1) + k) * W + c] = y;
+        if (k < K) wk[((size_t)ch * K + k) * W + c] = div_rcp(gam * y, rs[c], inv[c]);
+        mx = fmaxf(mx, fabsf(y));
       }
-      __syncthreads();
+      mx = warp_max(mx);
+      if (lane == 0) mxw[j] = mx;
+      chain_sync();
+      if (ct == 0) {
+        float m = 0.f;
+        for (int i = 0; i < wpc; ++i) m = fmaxf(m, mxw[i]);
+        ymax[ch * (K + 1) + k] = m;
+      }
+      if (k < K)
+        for (int c = ct; c < W; c += tpc) {
+          float t = 0.f;
+          for (int b = 0; b < wpc; ++b) t += part[b * W + c];
+          nxt[c] = gam * t;
+        }
+      chain_sync();
     }
-    __syncthreads();
   }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------
@@ -848,7 +948,7 @@ __global__ void __launch_bounds__(256) k_rows_chain(const Plan pl, const ckv_par
 
 cudaError_t launch_rows_prep(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st) {
   k_rows_prep<<<dim3(pl.ncol_tiles, pl.hi_rows ? 2 : 1), 256, 0, st>>>(pl, prm, ws);
-  const size_t sm = sizeof(float) * ((size_t)pl.W * pl.W + 9 * pl.W + 64);
+  const size_t sm = sizeof(float) * chains_smem_floats(pl.W);
   { const cudaError_t e = ensure_dynamic_smem((const void*)k_rows_chain, sm); if (e != cudaSuccess) return e; }
   k_rows_chain<<<1, 256, sm, st>>>(pl, prm, ws);
   return cudaGetLastError();
@@ -885,10 +985,9 @@ template <> CKV_DEV void round_pair<CKV_BF16>(float a, float b, float rs, float&
 // multiplying by the reciprocal (its CUDA scalar division) round apart often enough to
 // matter: fp16 divides.  (bf16: no difference in 1M sampled logits.)
 template <> CKV_DEV void round_pair<CKV_FP16>(float a, float b, float rs, float& x, float& y) {
-  const float sd = 11.313708305358887f;   // fp32(sqrt(128))
-  (void)rs;
-  x = __half2float(__float2half_rn(__fdiv_rn(__half2float(__float2half_rn(a)), sd)));
-  y = __half2float(__float2half_rn(__fdiv_rn(__half2float(__float2half_rn(b)), sd)));
+  const float sd = 11.313708305358887f;   // fp32(sqrt(128)); rs = RN(1 / sd)
+  x = __half2float(__float2half_rn(div_rcp(__half2float(__float2half_rn(a)), sd, rs)));
+  y = __half2float(__float2half_rn(div_rcp(__half2float(__float2half_rn(b)), sd, rs)));
 }
 
 template <int DT>
@@ -1175,6 +1274,7 @@ __global__ void __launch_bounds__(256, 1)
   const uint64_t qset = hdr->qi_heads, hset = hdr->hi_heads;
   const bool hmax = hdr->hi_mode == 1;
   const int nhi = hdr->n_hi;
+  const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
   const bool hi_rows = pl.hi_rows != 0;
   const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);
 
@@ -1358,7 +1458,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int k = 0; k < kRows; ++k) {
           const int rr = pr0 + 4 * k;
-          float v = c2 == 0 ? qacc[k] : (hmax ? hacc[k] : hacc[k] / (float)nhi);
+          float v = c2 == 0 ? qacc[k] : (hmax ? hacc[k] : hacc[k] * inv_nhi);
           if (j >= pl.n) v = 0.f;
           rows[(size_t)rr * pl.n_pad + j] = v;
           cs += v;
@@ -1488,8 +1588,8 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
 }
 
 size_t pool_reduce_smem(const Plan& pl) {
-  const size_t chains = (size_t)pl.W * pl.W + 5 * pl.W + 4 * pl.W + 64;
-  const size_t rows = (size_t)2 * pl.H * pl.W;
+  const size_t chains = chains_smem_floats(pl.W);
+  const size_t rows = (size_t)2 * pl.H * pl.W + 2 * pl.H;
   return sizeof(float) * (chains > rows ? chains : rows);
 }
 
