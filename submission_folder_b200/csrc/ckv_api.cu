@@ -118,7 +118,7 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.nscan = (pl.n_p + kScanChunk - 1) / kScanChunk;
   if (pl.nscan < 1) pl.nscan = 1;
   pl.tc_nclusters = pl.ncol_tiles < 148 ? pl.ncol_tiles : 148;   // CTAs of the tensor-core pooling pass
-  pl.e_parts = pl.tc_pool ? 2 * pl.tc_nclusters : pl.ncol_tiles;   // TC: one partial per (CTA, column half)
+  pl.e_parts = pl.tc_pool ? 4 * pl.tc_nclusters : pl.ncol_tiles;   // TC: one partial per (CTA, column quarter)
   pl.rs_parts = pl.ncol_tiles;
   pl.g_slice = kColTile;
   if (window_smem_bytes(pl, true) > 227 * 1024 || window_smem_bytes(pl, false) > 227 * 1024) {
@@ -132,8 +132,8 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
                          ? (size_t)pl.nstat_chunks * HW * 16 : (2 * HW + 2 * (size_t)pl.W) * 4);
   pl.off_lse = take(HW * 4);
   pl.off_spec = take((size_t)4 * H * 4);
-  pl.off_epart = take((size_t)2 * pl.ncol_tiles * HW * 4);
-  pl.off_mpart = take((size_t)2 * pl.ncol_tiles * HW * 4);
+  pl.off_epart = take((size_t)4 * pl.ncol_tiles * HW * 4);
+  pl.off_mpart = take((size_t)4 * pl.ncol_tiles * HW * 4);
   pl.off_rows_qi = take((size_t)pl.W * pl.n_pad * 4);
   pl.off_rows_hi = take((size_t)pl.W * pl.n_pad * 4);
   pl.off_colsum = take((size_t)2 * pl.n_pad * 4);

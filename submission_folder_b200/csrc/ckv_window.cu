@@ -1211,30 +1211,54 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
 // pass 2 on the tensor cores (W = 64, 4 query heads per KV group)
 // ---------------------------------------------------------------------------
 // Persistent CTAs (one per SM) walk 64-key column tiles; each tile is processed for
-// all KV groups in turn.  Per group, TMA streams the group's 256 window-query rows
-// and its K tile through a two-stage ring (the queries of the next group load
-// while this group computes), one thread issues the UMMAs (two m-tiles of 128 rows,
-// N = 64) into one of two TMEM buffers, and the epilogue runs with one thread per
-// TMEM lane and 32-column half: lane L of m-tile 0 holds (head 4g + L/64, row L%64),
-// lane L of m-tile 1 holds head 4g + 2 + L/64 for the same row, so each thread pools
-// its head pair in registers.  Pair partials go through shared memory; every thread
-// then folds the two pairs of 16 (row, column) elements into register accumulators
-// that run across the groups (QI max over selected heads, HI sum over HI heads).
-// Per tile the pooled rows, column sums, row-sum partials and g totals are written
-// exactly as by the SIMT pooling kernel; per row the exact clamped entropy and the
-// transient mass accumulate across the CTA's tiles in TMEM and are written once per
-// CTA and column half.  The last CTA of the grid
-// verifies the head sets and runs the window chain (window_pool_finish).
+// all KV groups in turn ((tile, group) steps).  A producer warp streams, per step,
+// the group's 256 window-query rows and the K tile through a two-stage ring (TMA)
+// and issues the UMMAs (two m-tiles of 128 rows, N = 64) into one of two TMEM
+// buffers.  The query map walks (dim, head, token) with the head inside the token,
+// so m-tile mt row 2t + e holds window row t of head 4g + 2mt + e: TMEM lanes 2t and
+// 2t + 1 carry two heads of one window row, and each thread holds two heads (one per
+// m-tile).  A lane pair pools the group's four heads with one shuffle per column
+// pair, each lane keeping alternate columns.  16 epilogue warps (TMEM lane group x
+// 16-column quarter) turn logits into exact probabilities, add each row's clamped
+// entropy and transient mass into TMEM running sums (one per (column quarter,
+// group, head pair)), and keep the QI max / HI sum of their columns across the
+// groups in registers.  After the last group of a tile the pooled rows go through
+// shared memory to coalesced writes of the rows, column sums, row-sum partials and
+// g totals (the SIMT kernel's layout).  mbarriers order the producer and the
+// epilogue (stage free, accumulator full, accumulator free); the epilogue warps
+// synchronise among themselves only around the per-tile writes.
+template <bool B> struct BoolTag { static constexpr bool value = B; };
+
 constexpr int kP2TN = 64;                 // keys per tile
 constexpr int kP2Stages = 2;              // (queries, K tile) stages
+constexpr int kP2EpiWarps = 16;           // epilogue warps
+constexpr int kP2Threads = 32 * (kP2EpiWarps + 1);
+constexpr int kP2Pitch = kP2TN + 1;       // staging row pitch (conflict-free column writes)
 
-size_t tc_pool_smem(const Plan& pl) {
-  const size_t R = (size_t)pl.G * pl.W;   // 256
-  return 1024 + (size_t)kP2Stages * (R * 256 + (size_t)kP2TN * 256) + (size_t)2 * 128 * kP2TN * 4;
+struct P2Smem {
+  size_t stage_bytes, off_stage, off_sq, off_sh, off_colpart, off_redrow, off_gsum, off_lse, total;
+};
+
+static __host__ __device__ P2Smem p2_layout(const Plan& pl) {
+  P2Smem L;
+  const size_t R = (size_t)pl.G * pl.W;
+  L.stage_bytes = R * 256 + (size_t)kP2TN * 256;
+  L.off_stage = 0;
+  size_t off = kP2Stages * L.stage_bytes;
+  L.off_sq = off; off += (size_t)64 * kP2Pitch * 4;
+  L.off_sh = off; off += (size_t)64 * kP2Pitch * 4;
+  L.off_colpart = off; off += (size_t)8 * kP2TN * 4;
+  L.off_redrow = off; off += (size_t)kP2EpiWarps * 8 * 4;
+  L.off_gsum = off; off += 16;
+  L.off_lse = off; off += (size_t)pl.H * pl.W * 4;
+  L.total = 1024 + off;   // + alignment of the stage ring to 1024 bytes
+  return L;
 }
 
+size_t tc_pool_smem(const Plan& pl) { return p2_layout(pl).total; }
+
 template <int DT>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kP2Threads, 1)
     k_tc_pool(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
   extern __shared__ char smem_raw[];
   const Plan& pl = a.pl;
@@ -1248,259 +1272,263 @@ __global__ void __launch_bounds__(256, 1)
   const int ngroups = pl.Hkv;
   const int my_tiles = (ntn - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // tiles b, b+grid, ...
   const int nsteps = max(0, my_tiles) * ngroups;                                       // (tile, group) steps
-  char* stg = align1024(smem_raw);
-  const int stage_bytes = R * 256 + TN * 256;
-  float* pq = reinterpret_cast<float*>(stg + S * stage_bytes);   // [128 lanes][64 cols] pair max
-  float* ph = pq + 128 * TN;                                     // [128 lanes][64 cols] pair sum
-  __shared__ __align__(8) uint64_t bar_ld[kP2Stages], bar_mma[2];
+  const P2Smem Ly = p2_layout(pl);
+  char* base = align1024(smem_raw);
+  char* stg = base + Ly.off_stage;
+  float* sQ = reinterpret_cast<float*>(base + Ly.off_sq);          // [64][kP2Pitch] QI pooled
+  float* sH = reinterpret_cast<float*>(base + Ly.off_sh);          // [64][kP2Pitch] HI pooled
+  float* colpart = reinterpret_cast<float*>(base + Ly.off_colpart);// [8][TN]
+  float* redrow = reinterpret_cast<float*>(base + Ly.off_redrow);  // [16][8]
+  float* gsum = reinterpret_cast<float*>(base + Ly.off_gsum);      // [2]
+  float* slse = reinterpret_cast<float*>(base + Ly.off_lse);       // [H][W]
+  __shared__ __align__(8) uint64_t bar_ld[kP2Stages], bar_sfree[kP2Stages], bar_full[2], bar_tfree[2];
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int abort_sh;
-  // columns [0, 256): two accumulator buffers of two m-tiles; [256, 384): per (column
-  // half, group) running entropy / mass sums of this thread's two heads
+  __shared__ volatile int abort_sh;
+  // TMEM columns [0, 256): two accumulator buffers of two m-tiles of N = 64; [256, 512):
+  // running entropy / mass sums, 64 columns per column quarter (4 per group)
   const uint32_t ncols = 512;
   if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) tc::mbar_init(&bar_ld[i], 1);
-    tc::mbar_init(&bar_mma[0], 1);
-    tc::mbar_init(&bar_mma[1], 1);
+    for (int i = 0; i < S; ++i) { tc::mbar_init(&bar_ld[i], 1); tc::mbar_init(&bar_sfree[i], 1); }
+    for (int i = 0; i < 2; ++i) { tc::mbar_init(&bar_full[i], 1); tc::mbar_init(&bar_tfree[i], kP2EpiWarps); }
     tc::fence_barrier_init();
     abort_sh = 0;
+  }
+  {
+    const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);
+    for (int i = threadIdx.x; i < pl.H * W; i += blockDim.x) slse[i] = __ldcg(lse + i);
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
-  const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
-  const uint64_t qset = hdr->qi_heads, hset = hdr->hi_heads;
-  const bool hmax = hdr->hi_mode == 1;
-  const int nhi = hdr->n_hi;
-  const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
-  const bool hi_rows = pl.hi_rows != 0;
-  const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);
-
-  // step s -> (tile, group)
   auto step_tile = [&](int s) { return (int)blockIdx.x + (s / ngroups) * (int)gridDim.x; };
-  auto load_step = [&](int s) {            // thread 0
-    const int st = s % S, t = step_tile(s), g = s % ngroups;
-    char* base = stg + st * stage_bytes;
-    tc::mbar_expect_tx(&bar_ld[st], (uint32_t)(R * 256 + TN * 256));
-    for (int hl = 0; hl < G; ++hl)
-      for (int p = 0; p < 2; ++p)
-        tc::tma_load_3d(base + p * R * 128 + hl * W * 128, &tmq, &bar_ld[st], p * 64, pl.n - W, g * G + hl);
-    for (int p = 0; p < 2; ++p)
-      tc::tma_load_3d(base + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, t * TN, g);
-  };
-  auto issue_step = [&](int s) {           // thread 0
-    const int st = s % S;
-    const char* base = stg + st * stage_bytes;
-    const uint32_t dcol = (uint32_t)((s & 1) * 2 * TN);
-    for (int mt = 0; mt < 2; ++mt) {
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int p = ks >> 2, koff = (ks & 3) * 32;
-        const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(base + p * R * 128 + mt * 128 * 128 + koff));
-        const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(base + R * 256 + p * TN * 128 + koff));
-        tc::umma_f16(tmem + dcol + mt * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
-      }
-    }
-    tc::umma_commit(&bar_mma[s & 1]);
-  };
-  if (nsteps > 0 && threadIdx.x == 0) {
-    for (int s = 0; s < min(S, nsteps); ++s) load_step(s);
-    if (tc::mbar_wait(&bar_ld[0], 0, status)) { tc::fence_after_sync(); issue_step(0); }
-    else abort_sh = 1;
-  }
 
-  // epilogue identity: TMEM lane group lg, column half ch; rows of m-tiles 0 and 1
-  const int lg = warp & 3, ch = warp >> 2;
-  const int L = 32 * lg + lane;                       // TMEM lane
-  const int r = L % W;
-  const int pair = L / W;                             // 0: heads (0, 2) of the group, 1: (1, 3)
-  const int lim = pl.n - W + r;
-  float* epart = reinterpret_cast<float*>(a.ws + pl.off_epart);   // [2 * ncol_tiles][H][W]
-  float* mpart = reinterpret_cast<float*>(a.ws + pl.off_mpart);
-  // pooling identity: column pc, rows pr0 + 4k
-  const int pc = threadIdx.x % TN, pr0 = threadIdx.x / TN;
-  constexpr int kRows = 16;                          // W / 4
-  float qacc[kRows], hacc[kRows];
-  const float rs = 1.0f / sqrtf((float)pl.D);
-  const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
-  const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
-  // running sums: column 256 + 64 ch + 4 g + {entropy a, entropy b, mass a, mass b}
-  const uint32_t acc_base = tmem + ((uint32_t)(32 * lg) << 16) + 256u + (uint32_t)(64 * ch);
-  {
-    const float z[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int g = 0; g < ngroups; ++g) tc::tmem_st4(acc_base + 4 * g, z);
-  }
-  __syncthreads();
-
-  for (int s = 0; s < nsteps; ++s) {
-    const bool alive = !abort_sh;
-    const int t = step_tile(s), g = s % ngroups;
-    const int j0 = t * TN;
-    if (g == 0) {
+  if (warp == kP2EpiWarps) {
+    // ---------------- producer: TMA loads and UMMA issue (one thread) ----------------
+    if (lane == 0 && nsteps > 0) {
+      const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
+      auto load_step = [&](int s) {
+        const int st = s % S, t = step_tile(s), g = s % ngroups;
+        char* sb = stg + st * Ly.stage_bytes;
+        tc::mbar_expect_tx(&bar_ld[st], (uint32_t)(R * 256 + TN * 256));
+        for (int mt = 0; mt < 2; ++mt)
+          for (int p = 0; p < 2; ++p)   // rows (token, head pair): head 4g + 2mt + e, token n - W + t
+            tc::tma_load_3d(sb + p * R * 128 + mt * 128 * 128, &tmq, &bar_ld[st], p * 64, g * G + 2 * mt, pl.n - W);
+        for (int p = 0; p < 2; ++p)
+          tc::tma_load_3d(sb + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, t * TN, g);
+      };
+      for (int s = 0; s < min(S, nsteps); ++s) load_step(s);
+      for (int s = 0; s < nsteps; ++s) {
+        const int st = s % S;
+        if (abort_sh) break;
+        if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        if (s >= 2 && !tc::mbar_wait(&bar_tfree[s & 1], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
+        tc::fence_after_sync();
+        const char* sb = stg + st * Ly.stage_bytes;
+        const uint32_t dcol = (uint32_t)((s & 1) * 2 * TN);
+        for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
-      for (int k = 0; k < kRows; ++k) { qacc[k] = 0.f; hacc[k] = 0.f; }
-    }
-    if (alive && threadIdx.x == 0 && s + 1 < nsteps) {
-      if (tc::mbar_wait(&bar_ld[(s + 1) % S], ((s + 1) / S) & 1, status)) { tc::fence_after_sync(); issue_step(s + 1); }
-      else abort_sh = 1;
-    }
-    if (alive && !tc::mbar_wait(&bar_mma[s & 1], (s >> 1) & 1, status)) abort_sh = 1;
-    tc::fence_after_sync();
-    if (alive && threadIdx.x == 0 && s + S < nsteps && !abort_sh) load_step(s + S);
-    // this thread's two heads: g*G + pair and g*G + 2 + pair
-    const int ha = g * G + pair, hb = ha + 2;
-    const bool qa = (qset >> ha) & 1ull, qb = (qset >> hb) & 1ull;
-    const bool hA = (hset >> ha) & 1ull, hB = (hset >> hb) & 1ull;
-    if (alive) {
-      float ent[2] = {0.f, 0.f}, mass[2] = {0.f, 0.f};   // this step's partials of the two heads
-      const float La = lse[ha * W + r], Lb = lse[hb * W + r];
-      float va[32], vb[32];
-      const uint32_t base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)((s & 1) * 2 * TN + ch * 32);
-      tc::tmem_ld32(base, va);
-      tc::tmem_ld32(base + TN, vb);
-      const int jb = j0 + ch * 32;
-      const bool interior = (jb + 31 <= lim) && (jb >= pl.s);
-      float qv[32], hv[32];
-#pragma unroll
-      for (int k = 0; k < 32; k += 2) {
-        float xa0, xa1, xb0, xb1;
-        round_pair<DT>(va[k], va[k + 1], rs, xa0, xa1);
-        round_pair<DT>(vb[k], vb[k + 1], rs, xb0, xb1);
-        va[k] = xa0; va[k + 1] = xa1; vb[k] = xb0; vb[k + 1] = xb1;
-      }
-      // head membership as 0/1 factors (p * 1 == p, p * 0 == 0 for finite p >= 0)
-      const float fqa = qa ? 1.f : 0.f, fqb = qb ? 1.f : 0.f;
-      const float fha = hA ? 1.f : 0.f, fhb = hB ? 1.f : 0.f;
-      if (interior) {
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float da = fmaf(va[k], kLog2e, -La), db = fmaf(vb[k], kLog2e, -Lb);
-          const float pa = ex2(da), pb = ex2(db);
-          ent[0] = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent[0]);
-          ent[1] = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent[1]);
-          mass[0] += pa;
-          mass[1] += pb;
-          qv[k] = fmaxf(pa * fqa, pb * fqb);
-          hv[k] = hmax ? fmaxf(pa * fha, pb * fhb) : fmaf(pa, fha, pb * fhb);
+          for (int ks = 0; ks < 8; ++ks) {
+            const int p = ks >> 2, koff = (ks & 3) * 32;
+            const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(sb + p * R * 128 + mt * 128 * 128 + koff));
+            const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(sb + R * 256 + p * TN * 128 + koff));
+            tc::umma_f16(tmem + dcol + mt * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
+          }
         }
-      } else {
+        tc::umma_commit(&bar_full[s & 1]);
+        tc::umma_commit(&bar_sfree[st]);
+        if (s + S < nsteps) {
+          if (!tc::mbar_wait(&bar_sfree[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+          load_step(s + S);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: 16 warps ----------------
+    const int lg = warp & 3, cq = warp >> 2;
+    const int L = 32 * lg + lane;                       // TMEM lane
+    const int t = L >> 1;                               // window row
+    const int e = lane & 1;                             // head within the m-tile pair
+    const int lim = pl.n - W + t;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
+    const uint32_t acc_base = lane_base + 256u + (uint32_t)(64 * cq);   // 4 columns per group, <= 16 groups
+    const uint64_t qset = hdr->qi_heads, hset = hdr->hi_heads;
+    const bool hmax = hdr->hi_mode == 1;
+    const int nhi = hdr->n_hi;
+    const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
+    const bool hi_rows = pl.hi_rows != 0;
+    const float rs = 1.0f / sqrtf((float)pl.D);
+    const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
+    const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
+    auto epi_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kP2EpiWarps) : "memory"); };
+    {
+      const float z[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int g = 0; g < ngroups; ++g) tc::tmem_st4(acc_base + 4 * g, z);
+    }
+    float qacc[8], hacc[8];                             // owned columns cq*16 + 2m + e
+    for (int s = 0; s < nsteps; ++s) {
+      const int tile = step_tile(s), g = s % ngroups;
+      const int j0 = tile * TN;
+      if (g == 0) {
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const int j = jb + k;
-          const float da = fmaf(va[k], kLog2e, -La), db = fmaf(vb[k], kLog2e, -Lb);
+        for (int m = 0; m < 8; ++m) { qacc[m] = 0.f; hacc[m] = 0.f; }
+      }
+      bool ok = !abort_sh;
+      if (ok && !tc::mbar_wait(&bar_full[s & 1], (s >> 1) & 1, status)) { abort_sh = 1; ok = false; }
+      if (__all_sync(0xffffffffu, ok)) {   // TMEM loads are warp-collective
+        tc::fence_after_sync();
+        uint32_t ra[16], rb[16];
+        const uint32_t col = (uint32_t)((s & 1) * 2 * TN + cq * 16);
+        tc::tmem_ld16_nowait(lane_base + col, ra);
+        tc::tmem_ld16_nowait(lane_base + col + TN, rb);
+        tc::tmem_wait_ld();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bar_tfree[s & 1]);
+        float va[16], vb[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          asm volatile("" : "+r"(ra[k]), "+r"(rb[k]));
+          va[k] = __uint_as_float(ra[k]);
+          vb[k] = __uint_as_float(rb[k]);
+        }
+        const int ha = g * G + e, hb = ha + 2;
+        const float La = slse[ha * W + t], Lb = slse[hb * W + t];
+        const float fqa = ((qset >> ha) & 1ull) ? 1.f : 0.f, fqb = ((qset >> hb) & 1ull) ? 1.f : 0.f;
+        const float fha = ((hset >> ha) & 1ull) ? 1.f : 0.f, fhb = ((hset >> hb) & 1ull) ? 1.f : 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; k += 2) {
+          float x0, x1, y0, y1;
+          round_pair<DT>(va[k], va[k + 1], rs, x0, x1);
+          round_pair<DT>(vb[k], vb[k + 1], rs, y0, y1);
+          va[k] = x0; va[k + 1] = x1; vb[k] = y0; vb[k + 1] = y1;
+        }
+        float ent0 = 0.f, ent1 = 0.f, mass0 = 0.f, mass1 = 0.f;
+        const int jb = j0 + cq * 16;
+        const bool interior = jb + 15 <= lim && jb >= pl.s;
+        // one logit pair (heads a, b at one column): probabilities, entropy, mass, own pool
+        auto logit2 = [&](auto itag, float xa, float xb, int j, float& qo, float& ho) {
+          const float da = fmaf(xa, kLog2e, -La), db = fmaf(xb, kLog2e, -Lb);
           float pa = ex2(da), pb = ex2(db);
-          if (j <= lim) {
-            ent[0] = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent[0]);
-            ent[1] = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent[1]);
-            if (j >= pl.s) { mass[0] += pa; mass[1] += pb; }
+          if constexpr (decltype(itag)::value) {
+            ent0 = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent0);
+            ent1 = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent1);
+            mass0 += pa;
+            mass1 += pb;
+          } else if (j <= lim) {
+            ent0 = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent0);
+            ent1 = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent1);
+            if (j >= pl.s) { mass0 += pa; mass1 += pb; }
           } else {
             pa = 0.f; pb = 0.f;
             if (j < pl.n) {   // masked: probability 0, clamped to 1e-8
-              ent[0] = fmaf(1e-8f, kLog2Eps, ent[0]);
-              ent[1] = fmaf(1e-8f, kLog2Eps, ent[1]);
+              ent0 = fmaf(1e-8f, kLog2Eps, ent0);
+              ent1 = fmaf(1e-8f, kLog2Eps, ent1);
             }
           }
-          qv[k] = fmaxf(pa * fqa, pb * fqb);
-          hv[k] = hmax ? fmaxf(pa * fha, pb * fhb) : fmaf(pa, fha, pb * fhb);
-        }
-      }
-      // exact entropy (log2 units) / mass: add this tile's sums to the running sums
-      {
-        float acc[4];
-        tc::tmem_ld4(acc_base + 4 * g, acc);
-        acc[0] += ent[0]; acc[1] += ent[1]; acc[2] += mass[0]; acc[3] += mass[1];
-        tc::tmem_st4(acc_base + 4 * g, acc);
-      }
-      // pair partials: [lane][column], 16-byte chunks XOR-swizzled by lane
+          qo = fmaxf(pa * fqa, pb * fqb);
+          ho = hmax ? fmaxf(pa * fha, pb * fhb) : fmaf(pa, fha, pb * fhb);
+        };
+        // per column pair: the partner lane holds the group's other two heads; each
+        // lane keeps one column of the pair (even lane: even, odd lane: odd)
+        auto pairs = [&](auto itag) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int cchunk = (ch * 8 + k) ^ (L & 15);
-        reinterpret_cast<float4*>(pq + L * TN)[cchunk] = make_float4(qv[4 * k], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3]);
-        reinterpret_cast<float4*>(ph + L * TN)[cchunk] = make_float4(hv[4 * k], hv[4 * k + 1], hv[4 * k + 2], hv[4 * k + 3]);
-      }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    // fold the two pairs of every (row, column) into the accumulators; the swizzled
-    // column of row rr depends on rr & 15, i.e. on k & 3 for rr = pr0 + 4k
-    {
-      int coff[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) coff[u] = (((pc >> 2) ^ ((pr0 + 4 * u) & 15)) << 2) + (pc & 3);
-#pragma unroll
-      for (int k = 0; k < kRows; ++k) {
-        const int rr = pr0 + 4 * k;
-        const int ia = rr * TN + coff[k & 3], ib = (rr + W) * TN + coff[k & 3];
-        const float q0 = pq[ia], q1 = pq[ib];
-        const float h0 = ph[ia], h1 = ph[ib];
-        qacc[k] = fmaxf(qacc[k], fmaxf(q0, q1));
-        hacc[k] = hmax ? fmaxf(hacc[k], fmaxf(h0, h1)) : hacc[k] + (h0 + h1);
-      }
-    }
-    __syncthreads();
-    if (g == ngroups - 1) {
-      // ---- the tile is complete: pooled rows and their sums (SIMT-kernel layout)
-      float* rows_qi = reinterpret_cast<float*>(a.ws + pl.off_rows_qi);
-      float* rows_hi = reinterpret_cast<float*>(a.ws + pl.off_rows_hi);
-      float* colsum = reinterpret_cast<float*>(a.ws + pl.off_colsum);
-      float* gtile = reinterpret_cast<float*>(a.ws + pl.off_gtile);
-      float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);
-      const int j = j0 + pc;
-      const int nch = hi_rows ? 2 : 1;
-      float (*colpart)[kP2TN] = reinterpret_cast<float (*)[kP2TN]>(pq);          // [4][TN] (pair area is free)
-      float (*redrow)[kP2TN] = reinterpret_cast<float (*)[kP2TN]>(pq + 4 * kP2TN);  // [8][TN]
-      float* gsum = pq + 12 * kP2TN;                                               // [2]
-      for (int c2 = 0; c2 < nch; ++c2) {
-        float* rows = c2 == 0 ? rows_qi : rows_hi;
-        float cs = 0.f;
-#pragma unroll
-        for (int k = 0; k < kRows; ++k) {
-          const int rr = pr0 + 4 * k;
-          float v = c2 == 0 ? qacc[k] : (hmax ? hacc[k] : hacc[k] * inv_nhi);
-          if (j >= pl.n) v = 0.f;
-          rows[(size_t)rr * pl.n_pad + j] = v;
-          cs += v;
-          float rv = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
-          rv = warp_sum(rv);
-          if (lane == 0) redrow[warp][k] = rv;     // warp covers 32 columns of row rr
-        }
-        colpart[pr0][pc] = cs;
-        __syncthreads();
-        if (threadIdx.x < W) {
-          const int rr = threadIdx.x, k = rr / 4, w0 = 2 * (rr % 4);
-          rspart[((size_t)c2 * pl.rs_parts + t) * W + rr] = redrow[w0][k] + redrow[w0 + 1][k];
-        }
-        if (threadIdx.x < TN) {
-          const int jj = j0 + threadIdx.x;
-          const float c = colpart[0][threadIdx.x] + colpart[1][threadIdx.x] + colpart[2][threadIdx.x] +
-                          colpart[3][threadIdx.x];
-          colsum[(size_t)c2 * pl.n_pad + jj] = c;
-          float gg = 0.f;
-          if (jj < pl.n_p) {
-            gg = fmaxf(c, 1e-6f);
-            if (tempered) gg = powf(gg, invT);
+          for (int m = 0; m < 8; ++m) {
+            float q0, h0, q1, h1;
+            logit2(itag, va[2 * m], vb[2 * m], jb + 2 * m, q0, h0);
+            logit2(itag, va[2 * m + 1], vb[2 * m + 1], jb + 2 * m + 1, q1, h1);
+            const float qr = __shfl_xor_sync(0xffffffffu, e ? q0 : q1, 1);
+            const float hr = __shfl_xor_sync(0xffffffffu, e ? h0 : h1, 1);
+            const float qm = e ? q1 : q0, hm = e ? h1 : h0;
+            qacc[m] = fmaxf(qacc[m], fmaxf(qm, qr));
+            hacc[m] = hmax ? fmaxf(hacc[m], fmaxf(hm, hr)) : hacc[m] + (hm + hr);
           }
-          gg = warp_sum(gg);
-          if (lane == 0) gsum[warp] = gg;
+        };
+        if (interior) pairs(BoolTag<true>{});
+        else pairs(BoolTag<false>{});
+        // exact entropy (log2 units) / mass running sums of the two heads
+        {
+          float acc[4];
+          tc::tmem_ld4(acc_base + 4 * g, acc);
+          acc[0] += ent0; acc[1] += ent1; acc[2] += mass0; acc[3] += mass1;
+          tc::tmem_st4(acc_base + 4 * g, acc);
         }
-        __syncthreads();
-        if (threadIdx.x == 0) gtile[(size_t)c2 * pl.ncol_tiles * 8 + t] = gsum[0] + gsum[1];
-        __syncthreads();
+      }
+      if (g == ngroups - 1) {
+        // ---- the tile is complete: pooled rows through shared memory
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int c = cq * 16 + 2 * m + e;
+          sQ[t * kP2Pitch + c] = qacc[m];
+          sH[t * kP2Pitch + c] = hacc[m];
+        }
+        epi_sync();
+        float* rows_qi = reinterpret_cast<float*>(a.ws + pl.off_rows_qi);
+        float* rows_hi = reinterpret_cast<float*>(a.ws + pl.off_rows_hi);
+        float* colsum = reinterpret_cast<float*>(a.ws + pl.off_colsum);
+        float* gtile = reinterpret_cast<float*>(a.ws + pl.off_gtile);
+        float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);
+        const int tid = threadIdx.x;                    // 0..511
+        const int pc = tid & 63, pr = tid >> 6;         // column, row group (rows pr + 8k)
+        const int j = j0 + pc;
+        const int nch = hi_rows ? 2 : 1;
+        for (int c2 = 0; c2 < nch; ++c2) {
+          float* rows = c2 == 0 ? rows_qi : rows_hi;
+          const float* sx = c2 == 0 ? sQ : sH;
+          float cs = 0.f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int rr = pr + 8 * k;
+            float v = sx[rr * kP2Pitch + pc];
+            if (c2 == 1 && !hmax) v = v * inv_nhi;
+            if (j >= pl.n) v = 0.f;
+            rows[(size_t)rr * pl.n_pad + j] = v;
+            cs += v;
+            float rv = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
+            rv = warp_sum(rv);
+            if (lane == 0) redrow[warp * 8 + k] = rv;   // this warp's 32 columns of row rr
+          }
+          colpart[pr * TN + pc] = cs;
+          epi_sync();
+          if (tid < W) {
+            const int rr = tid, k = rr >> 3, w0 = 2 * (rr & 7);
+            rspart[((size_t)c2 * pl.rs_parts + tile) * W + rr] = redrow[w0 * 8 + k] + redrow[(w0 + 1) * 8 + k];
+          }
+          if (tid < TN) {
+            const int jj = j0 + tid;
+            float c = 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) c += colpart[q * TN + tid];
+            colsum[(size_t)c2 * pl.n_pad + jj] = c;
+            float gg = 0.f;
+            if (jj < pl.n_p) {
+              gg = fmaxf(c, 1e-6f);
+              if (tempered) gg = powf(gg, invT);
+            }
+            gg = warp_sum(gg);
+            if (lane == 0) gsum[warp] = gg;
+          }
+          epi_sync();
+          if (tid == 0) gtile[(size_t)c2 * pl.ncol_tiles * 8 + tile] = gsum[0] + gsum[1];
+        }
+        epi_sync();
       }
     }
-  }
-  // one exact entropy / mass partial per (CTA, column half, head, row)
-  for (int g = 0; g < ngroups; ++g) {
-    float acc[4];
-    tc::tmem_ld4(acc_base + 4 * g, acc);
-    const int ha = g * G + pair, hb = ha + 2;
-    const size_t slot = (size_t)(blockIdx.x * 2 + ch) * pl.H;
-    epart[(slot + ha) * W + r] = -acc[0] * kLn2;
-    epart[(slot + hb) * W + r] = -acc[1] * kLn2;
-    mpart[(slot + ha) * W + r] = acc[2];
-    mpart[(slot + hb) * W + r] = acc[3];
+    // one exact entropy / mass partial per (CTA, column quarter, head, row)
+    float* epart = reinterpret_cast<float*>(a.ws + pl.off_epart);   // [e_parts][H][W]
+    float* mpart = reinterpret_cast<float*>(a.ws + pl.off_mpart);
+    for (int g = 0; g < ngroups; ++g) {
+      float acc[4];
+      tc::tmem_ld4(acc_base + 4 * g, acc);
+      const int ha = g * G + e, hb = ha + 2;
+      const size_t slot = (size_t)(blockIdx.x * 4 + cq) * pl.H;
+      epart[(slot + ha) * W + t] = -acc[0] * kLn2;
+      epart[(slot + hb) * W + t] = -acc[1] * kLn2;
+      mpart[(slot + ha) * W + t] = acc[2];
+      mpart[(slot + hb) * W + t] = acc[3];
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1508,20 +1536,36 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, ncols);
 }
 
+// [heads, n, 128] view -> a 3-D tiled map over (dim, head, token) with a (64 x 2 x rows)
+// box: consecutive smem rows alternate between two heads of one token.
+static bool make_tmap_pairs(CUtensorMap* m, const void* base, int dtype, int n, int heads, int64_t hs,
+                            int64_t ts, int rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)n};
+  const cuuint64_t strides[2] = {(cuuint64_t)hs * 2, (cuuint64_t)ts * 2};
+  const cuuint32_t box[3] = {64, 2, (cuuint32_t)rows};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, dtype == CKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int DT>
 static cudaError_t launch_tc_pool(const WinArgs& a0, cudaStream_t st) {
   WinArgs a = a0;
   const Plan& pl = a.pl;
   CUtensorMap tq, tk;
-  if (!make_tmap(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W) ||
+  if (!make_tmap_pairs(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W) ||
       !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kP2TN))
     return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
   const size_t smem = tc_pool_smem(pl);
   { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool<DT>, smem); if (e != cudaSuccess) return e; }
-  k_tc_pool<DT><<<pl.tc_nclusters, 256, smem, st>>>(tq, tk, a);
+  k_tc_pool<DT><<<pl.tc_nclusters, kP2Threads, smem, st>>>(tq, tk, a);
   return cudaGetLastError();
 }
-
 
 // ---------------------------------------------------------------------------
 // exact entropy / mass: reduce the pooling pass's partials, then (last CTA) verify
