@@ -30,11 +30,8 @@
 
 namespace ckv {
 
-__device__ void window_pool_finish(const WinArgs& a, char* smem);
 __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh);
 CKV_DEV float sum_parts(const float* base, int nparts, size_t stride, int first, int step);
-__device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem,
-                                  bool use_rowsums);
 
 constexpr float kGeps = 1.8420680743952367e-07f;   // -1e-8 * ln(1e-8): a clamped entry
 constexpr float kLog2Eps = -26.575424759098897f;     // log2(1e-8)
@@ -697,16 +694,241 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// window chains: the W x W block of the pooled rows (PU:2060-2206)
+// ---------------------------------------------------------------------------
+// Shared memory of the chain step, in floats: the raw then normalised window blocks
+// [2][W][W], row sums and their reciprocals [2][W] each, the fallback iteration's
+// vectors / partials / maxima, and (pooling finish only, before the chains) the row
+// entropies and masses [2][H*W] and the per-head means [2][H] in the same region.
+struct ChainSmem {
+  size_t pw, rs, inv, y, part, mx, rowe, head, total;
+};
+__host__ __device__ inline ChainSmem chain_smem(int W, int H) {
+  ChainSmem c;
+  size_t off = 0;
+  c.pw = off; off += (size_t)2 * W * W;
+  c.rs = off; off += (size_t)2 * W;
+  c.inv = off; off += (size_t)2 * W;
+  // the fallback iteration's scratch and the pooling finish's row statistics are
+  // never live together: they share one region
+  const size_t shared0 = off;
+  c.y = off; off += (size_t)4 * W;
+  c.part = off; off += (size_t)2 * 32 * kMaxWindow;
+  c.mx = off; off += 64;
+  const size_t end_fallback = off;
+  off = shared0;
+  c.rowe = off; off += (size_t)2 * H * W;
+  c.head = off; off += (size_t)2 * H;
+  c.total = off > end_fallback ? off : end_fallback;
+  return c;
+}
+
+CKV_DEV void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+
+// Start copying the window block of each chain's pooled rows (columns n_p .. n-1 of
+// its W rows) into shared memory; completes at cp_async_wait<0>().
+__device__ __forceinline__ void stage_window_block(const Plan& pl, const char* ws, float* smem) {
+  const ChainSmem cs = chain_smem(pl.W, pl.H);
+  const int W = pl.W, nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* rows0 = reinterpret_cast<const float*>(ws + pl.off_rows_qi);
+  const float* rows1 = reinterpret_cast<const float*>(ws + (pl.hi_rows ? pl.off_rows_hi : pl.off_rows_qi));
+  for (int g = warp; g < pl.nchains * W; g += nw) {
+    const int ch = g >= W ? 1 : 0, r = g - ch * W;
+    const float* src = (ch ? rows1 : rows0) + (size_t)r * pl.n_pad + pl.n_p;
+    for (int c = lane; c < W; c += 32) cp_async4(smem + cs.pw + (size_t)g * W + c, src + c);
+  }
+  cp_async_commit();
+}
+
+// One chain on one warp, W = 32 * KC: lane l holds y[l + 32 q]; the rows of Pww are
+// read from shared memory at fixed offsets and y[r] is broadcast by a shuffle.  Pww
+// is causal (Pww[r, c] = 0 for c > r), so summing every row in ascending order adds
+// exact zeros before row c and matches the triangular sum bit for bit.
+template <int KC>
+__device__ __forceinline__ void chain_warp(const float* Pw, const float* rs, const float* inv, int K, float gam,
+                                           float y0_uniform, bool query_start, float* yk, float* wk,
+                                           float* ymax) {
+  constexpr int W = 32 * KC;
+  const int lane = threadIdx.x & 31;
+  float y[KC];
+#pragma unroll
+  for (int q = 0; q < KC; ++q) {
+    const int c = lane + 32 * q;
+    y[q] = query_start ? (c == W - 1 ? 1.f : 0.f) : y0_uniform;
+  }
+  for (int k = 0; k <= K; ++k) {
+    float mx = 0.f;
+#pragma unroll
+    for (int q = 0; q < KC; ++q) {
+      const int c = lane + 32 * q;
+      yk[(size_t)k * W + c] = y[q];
+      if (k < K) wk[(size_t)k * W + c] = div_rcp(gam * y[q], rs[c], inv[c]);
+      mx = fmaxf(mx, fabsf(y[q]));
+    }
+    mx = warp_max(mx);
+    if (lane == 0) ymax[k] = mx;
+    if (k == K) break;
+    float s[KC];
+#pragma unroll
+    for (int q = 0; q < KC; ++q) s[q] = 0.f;
+#pragma unroll
+    for (int rq = 0; rq < KC; ++rq) {
+#pragma unroll
+      for (int l = 0; l < 32; ++l) {
+        const float yr = __shfl_sync(0xffffffffu, y[rq], l);
+        const int r = 32 * rq + l;
+#pragma unroll
+        for (int q = 0; q < KC; ++q) s[q] = fmaf(Pw[r * W + lane + 32 * q], yr, s[q]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < KC; ++q) y[q] = gam * s[q];
+  }
+}
+
+// Row sums (tempered) of the pooled rows and the W x W window chain of each
+// absorbing chain: y_0 (query one-hot or uniform), y_{k+1} = gamma * Pww^T y_k.
+// Writes y_k, the weights w_k = gamma * y_k / rowsum used by the prefix sweep,
+// and max_c y_k.  One CTA; the window block is being copied by stage_window_block.
+// W a multiple of 32 (<= 128): one warp per chain (chain_warp).  Otherwise the
+// chains run side by side on half of the warps each with a named barrier: warp j
+// sums its block of rows for every column and the partials are added in row order.
+__device__ __forceinline__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem,
+                                                  bool use_rowsums) {
+  const ChainSmem cs = chain_smem(pl.W, pl.H);
+  const int W = pl.W, K = pl.K;
+  const bool tempered = prm.neumann_temperature != 1.0f && prm.neumann_temperature > 0.f;
+  const float invT = tempered ? 1.0f / prm.neumann_temperature : 1.0f;
+  const float gam = prm.neumann_gamma;
+  const float* rspart = reinterpret_cast<const float*>(ws + pl.off_rspart);
+  const float* rowS = reinterpret_cast<const float*>(ws + pl.off_stats) + 2 * pl.H * W;   // from k_pool_reduce
+  float* wk = reinterpret_cast<float*>(ws + pl.off_wk);     // [2][K][W]
+  float* yk = reinterpret_cast<float*>(ws + pl.off_yk);     // [2][K+1][W]
+  float* ymax = reinterpret_cast<float*>(ws + pl.off_ymax); // [2][K+1]
+  float* sPw = smem + cs.pw;
+  float* sRs = smem + cs.rs;
+  float* sInv = smem + cs.inv;
+  const int nchain = pl.nchains;
+  for (int i = threadIdx.x; i < nchain * W; i += blockDim.x) {
+    const int ch = i / W, r = i % W;
+    const int src = (ch == 0 || pl.hi_rows) ? ch : 0;
+    const float s = use_rowsums ? __ldcg(rowS + ch * W + r)
+                                : sum_parts(rspart + (size_t)src * pl.rs_parts * W + r, pl.rs_parts, (size_t)W, 0, 1);
+    sRs[i] = fmaxf(s, 1e-8f);
+    sInv[i] = 1.0f / sRs[i];
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int i = threadIdx.x; i < nchain * W * W; i += blockDim.x) {
+    float x = sPw[i];
+    if (tempered) x = x > 0.f ? powf(x, invT) : 0.f;
+    const int g = i / W;
+    sPw[i] = div_rcp(x, sRs[g], sInv[g]);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const float u0 = 1.0f / (float)(pl.n - pl.s);
+  if (W % 32 == 0 && W <= kMaxWindow) {
+    if (warp < nchain) {
+      const int ch = warp;
+      const float* Pw = sPw + (size_t)ch * W * W;
+      float* yko = yk + (size_t)ch * (K + 1) * W;
+      float* wko = wk + (size_t)ch * K * W;
+      float* ymo = ymax + ch * (K + 1);
+      switch (W / 32) {
+        case 1: chain_warp<1>(Pw, sRs + ch * W, sInv + ch * W, K, gam, u0, ch == 0, yko, wko, ymo); break;
+        case 2: chain_warp<2>(Pw, sRs + ch * W, sInv + ch * W, K, gam, u0, ch == 0, yko, wko, ymo); break;
+        case 3: chain_warp<3>(Pw, sRs + ch * W, sInv + ch * W, K, gam, u0, ch == 0, yko, wko, ymo); break;
+        default: chain_warp<4>(Pw, sRs + ch * W, sInv + ch * W, K, gam, u0, ch == 0, yko, wko, ymo); break;
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  float* sY = smem + cs.y;                                    // [2][2][W]
+  float* sPart = smem + cs.part;                              // [2][32][W]
+  float* sMx = smem + cs.mx;                                  // [2][32]
+  const int wpc = min(32, nw / nchain);                       // warps per chain
+  const int tpc = wpc * 32;
+  const int ch = warp / wpc;
+  if (ch < nchain) {
+    const int j = warp - ch * wpc;                            // row block of this warp
+    const int ct = threadIdx.x - ch * tpc;
+    const int rpw = (W + wpc - 1) / wpc;
+    const int r0 = min(W, j * rpw), r1 = min(W, r0 + rpw);
+    const float* Pw = sPw + (size_t)ch * W * W;
+    const float* rs = sRs + ch * W;
+    const float* inv = sInv + ch * W;
+    float* Y = sY + ch * 2 * W;
+    float* part = sPart + ch * 32 * kMaxWindow;
+    float* mxw = sMx + ch * 32;
+    auto chain_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + ch), "r"(tpc) : "memory"); };
+    for (int c = ct; c < W; c += tpc) Y[c] = (ch == 0) ? (c == W - 1 ? 1.f : 0.f) : u0;
+    chain_sync();
+    for (int k = 0; k <= K; ++k) {
+      const float* cur = Y + (k & 1) * W;
+      float* nxt = Y + ((k + 1) & 1) * W;
+      if (k < K) {
+        float s[kMaxWindow / 32];
+#pragma unroll
+        for (int q = 0; q < kMaxWindow / 32; ++q) s[q] = 0.f;
+        for (int r = r0; r < r1; ++r) {
+          const float yr = cur[r];
+#pragma unroll
+          for (int q = 0; q < kMaxWindow / 32; ++q) {
+            const int c = lane + 32 * q;
+            if (c < W) s[q] = fmaf(Pw[r * W + c], yr, s[q]);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < kMaxWindow / 32; ++q) {
+          const int c = lane + 32 * q;
+          if (c < W) part[j * W + c] = s[q];
+        }
+      }
+      float mx = 0.f;
+      for (int c = ct; c < W; c += tpc) {
+        const float y = cur[c];
+        yk[((size_t)ch * (K + 1) + k) * W + c] = y;
+        if (k < K) wk[((size_t)ch * K + k) * W + c] = div_rcp(gam * y, rs[c], inv[c]);
+        mx = fmaxf(mx, fabsf(y));
+      }
+      mx = warp_max(mx);
+      if (lane == 0) mxw[j] = mx;
+      chain_sync();
+      if (ct == 0) {
+        float m = 0.f;
+        for (int i = 0; i < wpc; ++i) m = fmaxf(m, mxw[i]);
+        ymax[ch * (K + 1) + k] = m;
+      }
+      if (k < K)
+        for (int c = ct; c < W; c += tpc) {
+          float t = 0.f;
+          for (int b = 0; b < wpc; ++b) t += part[b * W + c];
+          nxt[c] = gam * t;
+        }
+      chain_sync();
+    }
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
 // last-CTA work of the pooling pass
 // ---------------------------------------------------------------------------
-__device__ void window_pool_finish(const WinArgs& a, char* smem) {
+__device__ __forceinline__ void window_pool_finish(const WinArgs& a, char* smem_c) {
   const Plan& pl = a.pl;
+  float* smem = reinterpret_cast<float*>(smem_c);
+  const ChainSmem cs = chain_smem(pl.W, pl.H);
+  stage_window_block(pl, a.ws, smem);   // overlaps the head selection below
   Header* hdr = reinterpret_cast<Header*>(a.ws);
   float* exact = reinterpret_cast<float*>(a.ws + pl.off_spec) + 2 * pl.H;   // [H] ent, [H] mass
   const float* rowE = reinterpret_cast<const float*>(a.ws + pl.off_stats);   // [H*W] (k_pool_reduce)
-  float* sE = reinterpret_cast<float*>(smem);       // [H*W] entropy, then [H*W] mass
+  float* sE = smem + cs.rowe;                        // [H*W] entropy, then [H*W] mass
   float* sM = sE + pl.H * pl.W;
-  float* sHead = sE + 2 * pl.H * pl.W;              // [H] entropy, [H] mass means
+  float* sHead = smem + cs.head;                     // [H] entropy, [H] mass means
   const int HW2 = 2 * pl.H * pl.W;                  // rowM follows rowE
   for (int base = threadIdx.x; base < HW2; base += 8 * blockDim.x) {
     float v[8];
@@ -756,148 +978,11 @@ __device__ void window_pool_finish(const WinArgs& a, char* smem) {
     hdr->cnt_pool = 0;
   }
   __syncthreads();
-  if (redo) return;   // the fixup launch redoes the pooling and this step
-
-  run_window_chains(a.pl, a.p, a.ws, reinterpret_cast<float*>(smem), true);
-}
-
-// Row sums (tempered) of the pooled rows and the W x W window chain of each
-// absorbing chain: y_0 (query one-hot or uniform), y_{k+1} = gamma * Pww^T y_k.
-// Writes y_k, the weights w_k = gamma * y_k / rowsum used by the prefix sweep,
-// and max_c y_k.  One CTA.  Staging: one warp per window row, lanes over columns,
-// 8 rows in flight per warp.  Iteration: the chains run side by side, each on
-// half of the warps with its own named barrier; warp j of a chain sums its block
-// of rows for every column, and the block partials are added in row order.
-// `smem` >= chains_smem_floats(W) floats.
-__host__ __device__ constexpr size_t chains_smem_floats(int W) { return (size_t)2 * W * W + 8 * W + 2 * 32 * kMaxWindow + 64; }
-
-__device__ void run_window_chains(const Plan& pl, const ckv_params& prm, char* ws, float* smem,
-                                  bool use_rowsums) {
-  constexpr int kCols = kMaxWindow / 32;                      // columns per lane
-  const int W = pl.W, K = pl.K;
-  const bool tempered = prm.neumann_temperature != 1.0f && prm.neumann_temperature > 0.f;
-  const float invT = tempered ? 1.0f / prm.neumann_temperature : 1.0f;
-  const float gam = prm.neumann_gamma;
-  const float* rspart = reinterpret_cast<const float*>(ws + pl.off_rspart);
-  const float* rowS = reinterpret_cast<const float*>(ws + pl.off_stats) + 2 * pl.H * W;   // from k_pool_reduce
-  float* wk = reinterpret_cast<float*>(ws + pl.off_wk);     // [2][K][W]
-  float* yk = reinterpret_cast<float*>(ws + pl.off_yk);     // [2][K+1][W]
-  float* ymax = reinterpret_cast<float*>(ws + pl.off_ymax); // [2][K+1]
-  float* sPw = smem;                                          // [2][W][W]
-  float* sRs = smem + 2 * W * W;                              // [2][W]
-  float* sY = sRs + 2 * W;                                    // [2][2][W]
-  float* sPart = sY + 4 * W;                                  // [2][32][W]
-  float* sMx = sPart + 2 * 32 * kMaxWindow;                   // [2][32]
-  float* sInv = sMx + 64;                                     // [2][W] reciprocal row sums
-  const int nchain = pl.nchains;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int i = threadIdx.x; i < nchain * W; i += blockDim.x) {
-    const int ch = i / W, r = i % W;
-    const int src = (ch == 0 || pl.hi_rows) ? ch : 0;
-    const float s = use_rowsums ? __ldcg(rowS + ch * W + r)
-                                : sum_parts(rspart + (size_t)src * pl.rs_parts * W + r, pl.rs_parts, (size_t)W, 0, 1);
-    sRs[i] = fmaxf(s, 1e-8f);
-    sInv[i] = 1.0f / sRs[i];
+  if (redo) {   // the fixup launch redoes the pooling and this step
+    cp_async_wait<0>();
+    return;
   }
-  __syncthreads();
-  const float* rows0 = reinterpret_cast<const float*>(ws + pl.off_rows_qi);
-  const float* rows1 = reinterpret_cast<const float*>(ws + (pl.hi_rows ? pl.off_rows_hi : pl.off_rows_qi));
-  const int R = nchain * W;                                   // (chain, row) pairs
-  for (int g0 = warp; g0 < R; g0 += 8 * nw) {
-    float v[8][kCols];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int g = g0 + u * nw, ch = g >= W ? 1 : 0, r = g - ch * W;
-      const float* src = (ch ? rows1 : rows0) + (size_t)r * pl.n_pad + pl.n_p;
-#pragma unroll
-      for (int q = 0; q < kCols; ++q) {
-        const int c = lane + 32 * q;
-        v[u][q] = (g < R && c < W) ? __ldcg(src + c) : 0.f;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int g = g0 + u * nw;
-      if (g < R) {
-        const float s = sRs[g];
-#pragma unroll
-        for (int q = 0; q < kCols; ++q) {
-          const int c = lane + 32 * q;
-          if (c < W) {
-            float x = v[u][q];
-            if (tempered) x = x > 0.f ? powf(x, invT) : 0.f;
-            sPw[(size_t)g * W + c] = div_rcp(x, s, sInv[g]);
-          }
-        }
-      }
-    }
-  }
-  __syncthreads();
-  const int wpc = min(32, nw / nchain);                       // warps per chain
-  const int tpc = wpc * 32;
-  const int ch = warp / wpc;
-  if (ch < nchain) {
-    const int j = warp - ch * wpc;                            // row block of this warp
-    const int ct = threadIdx.x - ch * tpc;
-    const int rpw = (W + wpc - 1) / wpc;
-    const int r0 = min(W, j * rpw), r1 = min(W, r0 + rpw);
-    const float* Pw = sPw + (size_t)ch * W * W;
-    const float* rs = sRs + ch * W;
-    const float* inv = sInv + ch * W;
-    float* Y = sY + ch * 2 * W;
-    float* part = sPart + ch * 32 * kMaxWindow;
-    float* mxw = sMx + ch * 32;
-    auto chain_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + ch), "r"(tpc) : "memory"); };
-    const float u0 = 1.0f / (float)(pl.n - pl.s);
-    for (int c = ct; c < W; c += tpc) Y[c] = (ch == 0) ? (c == W - 1 ? 1.f : 0.f) : u0;
-    chain_sync();
-    for (int k = 0; k <= K; ++k) {
-      const float* cur = Y + (k & 1) * W;
-      float* nxt = Y + ((k + 1) & 1) * W;
-      if (k < K) {
-        float s[kCols];
-#pragma unroll
-        for (int q = 0; q < kCols; ++q) s[q] = 0.f;
-#pragma unroll 8
-        for (int r = r0; r < r1; ++r) {
-          const float yr = cur[r];
-#pragma unroll
-          for (int q = 0; q < kCols; ++q) {
-            const int c = lane + 32 * q;
-            if (c < W) s[q] = fmaf(Pw[r * W + c], yr, s[q]);
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < kCols; ++q) {
-          const int c = lane + 32 * q;
-          if (c < W) part[j * W + c] = s[q];
-        }
-      }
-      float mx = 0.f;
-      for (int c = ct; c < W; c += tpc) {
-        const float y = cur[c];
-        yk[((size_t)ch * (K + 1) + k) * W + c] = y;
-        if (k < K) wk[((size_t)ch * K + k) * W + c] = div_rcp(gam * y, rs[c], inv[c]);
-        mx = fmaxf(mx, fabsf(y));
-      }
-      mx = warp_max(mx);
-      if (lane == 0) mxw[j] = mx;
-      chain_sync();
-      if (ct == 0) {
-        float m = 0.f;
-        for (int i = 0; i < wpc; ++i) m = fmaxf(m, mxw[i]);
-        ymax[ch * (K + 1) + k] = m;
-      }
-      if (k < K)
-        for (int c = ct; c < W; c += tpc) {
-          float t = 0.f;
-          for (int b = 0; b < wpc; ++b) t += part[b * W + c];
-          nxt[c] = gam * t;
-        }
-      chain_sync();
-    }
-  }
-  __syncthreads();
+  run_window_chains(a.pl, a.p, a.ws, smem, true);
 }
 
 // ---------------------------------------------------------------------------
@@ -943,12 +1028,13 @@ __global__ void __launch_bounds__(256) k_rows_prep(const Plan pl, const ckv_para
 
 __global__ void __launch_bounds__(256) k_rows_chain(const Plan pl, const ckv_params prm, char* ws) {
   extern __shared__ __align__(16) float fsmem[];
+  stage_window_block(pl, ws, fsmem);
   run_window_chains(pl, prm, ws, fsmem, false);
 }
 
 cudaError_t launch_rows_prep(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st) {
   k_rows_prep<<<dim3(pl.ncol_tiles, pl.hi_rows ? 2 : 1), 256, 0, st>>>(pl, prm, ws);
-  const size_t sm = sizeof(float) * chains_smem_floats(pl.W);
+  const size_t sm = sizeof(float) * chain_smem(pl.W, pl.H).total;
   { const cudaError_t e = ensure_dynamic_smem((const void*)k_rows_chain, sm); if (e != cudaSuccess) return e; }
   k_rows_chain<<<1, 256, sm, st>>>(pl, prm, ws);
   return cudaGetLastError();
@@ -1228,6 +1314,12 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
 // epilogue (stage free, accumulator full, accumulator free); the epilogue warps
 // synchronise among themselves only around the per-tile writes.
 template <bool B> struct BoolTag { static constexpr bool value = B; };
+template <int V> struct IntTag { static constexpr int value = V; };
+// HI pooling of the tensor-core pooling pass, fixed per launch
+constexpr int kHiMeanAll = 0;   // mean over every head (membership factors all 1)
+constexpr int kHiMean = 1;      // mean over a head subset
+constexpr int kHiMax = 2;       // max over a head subset
+constexpr int kHiNone = 3;      // no HI rows of its own (the HI chain reuses the QI rows)
 
 constexpr int kP2TN = 64;                 // keys per tile
 constexpr int kP2Stages = 2;              // (queries, K tile) stages
@@ -1359,6 +1451,8 @@ __global__ void __launch_bounds__(kP2Threads, 1)
     const int nhi = hdr->n_hi;
     const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
     const bool hi_rows = pl.hi_rows != 0;
+    const uint64_t all_heads = pl.H >= 64 ? ~0ull : ((1ull << pl.H) - 1);
+    const int hi_kind = !hi_rows ? kHiNone : (hmax ? kHiMax : (hset == all_heads ? kHiMeanAll : kHiMean));
     const float rs = 1.0f / sqrtf((float)pl.D);
     const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
     const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
@@ -1409,7 +1503,8 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         const int jb = j0 + cq * 16;
         const bool interior = jb + 15 <= lim && jb >= pl.s;
         // one logit pair (heads a, b at one column): probabilities, entropy, mass, own pool
-        auto logit2 = [&](auto itag, float xa, float xb, int j, float& qo, float& ho) {
+        auto logit2 = [&](auto itag, auto htag, float xa, float xb, int j, float& qo, float& ho) {
+          constexpr int HM = decltype(htag)::value;
           const float da = fmaf(xa, kLog2e, -La), db = fmaf(xb, kLog2e, -Lb);
           float pa = ex2(da), pb = ex2(db);
           if constexpr (decltype(itag)::value) {
@@ -1429,25 +1524,41 @@ __global__ void __launch_bounds__(kP2Threads, 1)
             }
           }
           qo = fmaxf(pa * fqa, pb * fqb);
-          ho = hmax ? fmaxf(pa * fha, pb * fhb) : fmaf(pa, fha, pb * fhb);
+          if constexpr (HM == kHiMeanAll) ho = pa + pb;
+          else if constexpr (HM == kHiMean) ho = fmaf(pa, fha, pb * fhb);
+          else if constexpr (HM == kHiMax) ho = fmaxf(pa * fha, pb * fhb);
+          else ho = 0.f;
         };
         // per column pair: the partner lane holds the group's other two heads; each
         // lane keeps one column of the pair (even lane: even, odd lane: odd)
-        auto pairs = [&](auto itag) {
+        auto pairs = [&](auto itag, auto htag) {
+          constexpr int HM = decltype(htag)::value;
 #pragma unroll
           for (int m = 0; m < 8; ++m) {
             float q0, h0, q1, h1;
-            logit2(itag, va[2 * m], vb[2 * m], jb + 2 * m, q0, h0);
-            logit2(itag, va[2 * m + 1], vb[2 * m + 1], jb + 2 * m + 1, q1, h1);
+            logit2(itag, htag, va[2 * m], vb[2 * m], jb + 2 * m, q0, h0);
+            logit2(itag, htag, va[2 * m + 1], vb[2 * m + 1], jb + 2 * m + 1, q1, h1);
             const float qr = __shfl_xor_sync(0xffffffffu, e ? q0 : q1, 1);
-            const float hr = __shfl_xor_sync(0xffffffffu, e ? h0 : h1, 1);
-            const float qm = e ? q1 : q0, hm = e ? h1 : h0;
+            const float qm = e ? q1 : q0;
             qacc[m] = fmaxf(qacc[m], fmaxf(qm, qr));
-            hacc[m] = hmax ? fmaxf(hacc[m], fmaxf(hm, hr)) : hacc[m] + (hm + hr);
+            if constexpr (HM != kHiNone) {
+              const float hr = __shfl_xor_sync(0xffffffffu, e ? h0 : h1, 1);
+              const float hm = e ? h1 : h0;
+              if constexpr (HM == kHiMax) hacc[m] = fmaxf(hacc[m], fmaxf(hm, hr));
+              else hacc[m] = hacc[m] + (hm + hr);
+            }
           }
         };
-        if (interior) pairs(BoolTag<true>{});
-        else pairs(BoolTag<false>{});
+        auto run = [&](auto htag) {
+          if (interior) pairs(BoolTag<true>{}, htag);
+          else pairs(BoolTag<false>{}, htag);
+        };
+        switch (hi_kind) {
+          case kHiMeanAll: run(IntTag<kHiMeanAll>{}); break;
+          case kHiMean: run(IntTag<kHiMean>{}); break;
+          case kHiMax: run(IntTag<kHiMax>{}); break;
+          default: run(IntTag<kHiNone>{}); break;
+        }
         // exact entropy (log2 units) / mass running sums of the two heads
         {
           float acc[4];
@@ -1632,9 +1743,7 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
 }
 
 size_t pool_reduce_smem(const Plan& pl) {
-  const size_t chains = chains_smem_floats(pl.W);
-  const size_t rows = (size_t)2 * pl.H * pl.W + 2 * pl.H;
-  return sizeof(float) * (chains > rows ? chains : rows);
+  return sizeof(float) * chain_smem(pl.W, pl.H).total;
 }
 
 // ---------------------------------------------------------------------------
