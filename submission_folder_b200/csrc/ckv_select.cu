@@ -194,6 +194,65 @@ __device__ void radix_select(cg::cluster_group& cl, const float* x, int b0, int 
   *take = remaining;
 }
 
+// Bitonic sort (descending) of buf[0, P2), P2 a power of two <= E * blockDim.x, with
+// the elements in registers: element i = warp * 32E + 32e + lane.  Compare distances
+// below 32 are lane shuffles, 32 .. 32E - 1 swaps inside a thread, and only distances
+// of 32E and more go through shared memory (two barriers each).  All threads.
+template <int E>
+__device__ void bitonic_desc(unsigned long long* buf, int P2) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long v[E];
+  int idx[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    idx[e] = warp * 32 * E + e * 32 + lane;
+    v[e] = idx[e] < P2 ? buf[idx[e]] : 0ull;
+  }
+  // new value of element i against partner value p at distance j within blocks of k
+  auto cmpx = [](unsigned long long own, unsigned long long p, int i, int j, int k) {
+    const bool desc = (i & k) == 0, lower = (i & j) == 0;
+    const bool take_max = desc == lower;
+    const bool own_gt = own > p;
+    return (take_max == own_gt) ? own : p;
+  };
+  for (int k = 2; k <= P2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32 * E) {
+        __syncthreads();   // the previous stage's readers are done
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (idx[e] < P2) buf[idx[e]] = v[e];
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (idx[e] < P2) v[e] = cmpx(v[e], buf[idx[e] ^ j], idx[e], j, k);
+      } else if (j >= 32) {
+        unsigned long long nv[E];
+#pragma unroll
+        for (int b = 1; b < E; b <<= 1) {
+          if ((j >> 5) == b) {
+#pragma unroll
+            for (int e = 0; e < E; ++e) nv[e] = cmpx(v[e], v[e ^ b], idx[e], j, k);
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = nv[e];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const unsigned long long p = __shfl_xor_sync(0xffffffffu, v[e], j);
+          v[e] = cmpx(v[e], p, idx[e], j, k);
+        }
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < E; ++e)
+    if (idx[e] < P2) buf[idx[e]] = v[e];
+  __syncthreads();
+}
+
 // The top-M (key, index) composites of the vector over [lo, hi), sorted descending,
 // in the leader CTA's sort buffer.  prefer_high: at the boundary key keep the highest
 // indices and rank a higher index higher (stable ascending ranks); otherwise the
@@ -247,18 +306,10 @@ __device__ void top_sorted(cg::cluster_group& cl, const float* x, int b0, int b1
     while (P2 < M) P2 <<= 1;
     for (int i = M + threadIdx.x; i < P2; i += blockDim.x) sh.sortbuf[i] = 0ull;
     __syncthreads();
-    for (int k = 2; k <= P2; k <<= 1) {
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        for (int i = threadIdx.x; i < P2; i += blockDim.x) {
-          const int l = i ^ j;
-          if (l > i) {
-            const unsigned long long a = sh.sortbuf[i], b = sh.sortbuf[l];
-            if (((i & k) == 0) ? (a < b) : (a > b)) { sh.sortbuf[i] = b; sh.sortbuf[l] = a; }
-          }
-        }
-        __syncthreads();
-      }
-    }
+    if (P2 <= kSelThreads) bitonic_desc<1>(sh.sortbuf, P2);
+    else if (P2 <= 2 * kSelThreads) bitonic_desc<2>(sh.sortbuf, P2);
+    else if (P2 <= 4 * kSelThreads) bitonic_desc<4>(sh.sortbuf, P2);
+    else bitonic_desc<8>(sh.sortbuf, P2);
   }
 }
 
