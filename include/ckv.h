@@ -147,12 +147,17 @@ int ckv_score_evict(const ckv_params* p, const ckv_layer* layer, void* workspace
                     size_t workspace_bytes, const ckv_outputs* out, ckv_stream_t stream);
 
 /* Many independent layers / sequences (each with batch-1 semantics, ragged n
- * allowed) in one call: equivalent to `count` ckv_score_evict calls whose
+ * allowed) in one call: the same results as `count` ckv_score_evict calls whose
  * workspaces are consecutive slices of `workspace` (each slice sized by
- * ckv_workspace_size for that layer, rounded up to 256 bytes). */
-int ckv_score_evict_batched(const ckv_params* p, const ckv_layer* layers, int32_t count,
-                            void* workspace, size_t workspace_bytes, const ckv_outputs* outs,
-                            ckv_stream_t stream);
+ * ckv_workspace_size for that layer, rounded up to 256 bytes).  `params` holds one
+ * struct shared by every layer (params_count 1) or one per layer (params_count ==
+ * count, e.g. per-layer budgets).  The layers run concurrently on internal streams
+ * forked from and joined back to `stream`; every output is complete when `stream`
+ * reaches the point of the call.  Arguments are validated before anything is
+ * enqueued. */
+int ckv_score_evict_batched(const ckv_params* params, int32_t params_count, const ckv_layer* layers,
+                            int32_t count, void* workspace, size_t workspace_bytes,
+                            const ckv_outputs* outs, ckv_stream_t stream);
 
 /* Reads (synchronising on `stream`) and clears the device status word of a
  * workspace: 0 when every kernel since the last read finished normally. */

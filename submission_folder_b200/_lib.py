@@ -109,7 +109,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "ckv_output_len": (i32, [P, i32, ctypes.POINTER(i32)]),
         "ckv_workspace_size": (i32, [P, i32, i32, i32, i32, ctypes.POINTER(sz)]),
         "ckv_score_evict": (i32, [P, L, vp, sz, O, vp]),
-        "ckv_score_evict_batched": (i32, [P, L, i32, vp, sz, O, vp]),
+        "ckv_score_evict_batched": (i32, [P, i32, L, i32, vp, sz, O, vp]),
         "ckv_read_status": (i32, [vp, vp, ctypes.POINTER(i32)]),
         "ckv_select_scores": (i32, [P, i32, vp, vp, vp, vp, sz, vp, vp, vp]),
         "ckv_select_scores_noalloc": (i32, [P, i32, vp, vp, vp, vp, vp, vp]),

@@ -7,7 +7,9 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "ckv_common.cuh"
 #include "ckv_gather.h"
@@ -186,7 +188,7 @@ static int launch_gather_layer(const Plan& pl, const ckv_layer* L, const ckv_out
 }
 
 static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* workspace,
-                           size_t ws_bytes, const ckv_outputs* out, cudaStream_t st) {
+                           size_t ws_bytes, const ckv_outputs* out, cudaStream_t st, bool marks = true) {
   if (!p || !out || !out->out_k || !out->out_v) return fail(CKV_ERR_ARG, "null params or outputs");
   int rc = check_layer(L);
   if (rc) return rc;
@@ -201,7 +203,7 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
   char* ws = static_cast<char*>(workspace);
   cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(Header), st);
   if (e != cudaSuccess) return cuda_fail(e, "workspace header reset");
-  g_stage_next = 0;
+  g_stage_next = marks ? 0 : g_stage_count;   // stage events only for single-layer calls
   stage_mark(st);
   WinArgs wa;
   wa.q = L->q; wa.qhs = L->q_head_stride; wa.qts = L->q_tok_stride;
@@ -295,24 +297,89 @@ int ckv_score_evict(const ckv_params* p, const ckv_layer* layer, void* workspace
   return score_evict_one(p, layer, workspace, workspace_bytes, out, (cudaStream_t)stream);
 }
 
-int ckv_score_evict_batched(const ckv_params* p, const ckv_layer* layers, int32_t count,
-                            void* workspace, size_t workspace_bytes, const ckv_outputs* outs,
-                            ckv_stream_t stream) {
-  if (!p || !layers || !outs || count < 0) return fail(CKV_ERR_ARG, "null argument");
+// Side streams of the batched entry point, per device: the layers are independent,
+// so their chains run concurrently on kLanes streams forked from and joined back to
+// the caller's stream (inside a stream capture this records parallel graph branches).
+// One layer's latency-bound steps (selection, reduction tails) then overlap another
+// layer's tensor-core passes.
+namespace {
+constexpr int kLanes = 4;
+constexpr int kMaxDevices = 64;
+struct Lanes {
+  cudaStream_t s[kLanes];
+  cudaEvent_t fork;
+  cudaEvent_t join[kLanes];
+  bool ready;
+};
+std::mutex g_lanes_mu;
+Lanes g_lanes[kMaxDevices];
+
+cudaError_t lanes_for_device(Lanes** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  Lanes& L = g_lanes[dev];
+  if (!L.ready) {
+    for (int i = 0; i < kLanes && e == cudaSuccess; ++i) e = cudaStreamCreateWithFlags(&L.s[i], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L.fork, cudaEventDisableTiming);
+    for (int i = 0; i < kLanes && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&L.join[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) return e;
+    L.ready = true;
+  }
+  *out = &L;
+  return cudaSuccess;
+}
+}  // namespace
+
+int ckv_score_evict_batched(const ckv_params* params, int32_t params_count, const ckv_layer* layers,
+                            int32_t count, void* workspace, size_t workspace_bytes,
+                            const ckv_outputs* outs, ckv_stream_t stream) {
+  if (!params || !layers || !outs || count < 0) return fail(CKV_ERR_ARG, "null argument");
+  if (params_count != 1 && params_count != count)
+    return fail(CKV_ERR_ARG, "params_count must be 1 or count");
+  auto par = [&](int i) { return params + (params_count == 1 ? 0 : i); };
   char* base = static_cast<char*>(workspace);
-  size_t used = 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  // validate every layer before anything is enqueued
+  std::vector<size_t> offs((size_t)count + 1, 0);
   for (int i = 0; i < count; ++i) {
     size_t need = 0;
-    int rc = ckv_workspace_size(p, layers[i].n, layers[i].num_heads, layers[i].num_kv_heads,
+    int rc = ckv_workspace_size(par(i), layers[i].n, layers[i].num_heads, layers[i].num_kv_heads,
                                 layers[i].head_dim, &need);
     if (rc) return rc;
-    need = align256(need);
-    if (used + need > workspace_bytes) return fail(CKV_ERR_WORKSPACE, "batched workspace too small");
-    rc = score_evict_one(p, &layers[i], base + used, need, &outs[i], (cudaStream_t)stream);
+    rc = check_layer(&layers[i]);
     if (rc) return rc;
-    used += need;
+    if (!outs[i].out_k || !outs[i].out_v || (layers[i].n >= par(i)->max_capacity_prompt && !outs[i].out_idx))
+      return fail(CKV_ERR_ARG, "null output pointer");
+    offs[i + 1] = offs[i] + align256(need);
+    if (offs[i + 1] > workspace_bytes) return fail(CKV_ERR_WORKSPACE, "batched workspace too small");
   }
-  return CKV_OK;
+  if (count == 0) return CKV_OK;
+  Lanes* lanes = nullptr;
+  if (count == 1 || lanes_for_device(&lanes) != cudaSuccess) {
+    cudaGetLastError();
+    for (int i = 0; i < count; ++i) {
+      const int rc = score_evict_one(par(i), &layers[i], base + offs[i], offs[i + 1] - offs[i], &outs[i], st);
+      if (rc) return rc;
+    }
+    return CKV_OK;
+  }
+  std::lock_guard<std::mutex> lock(g_lanes_mu);
+  const int nl = count < kLanes ? count : kLanes;
+  cudaError_t e = cudaEventRecord(lanes->fork, st);
+  for (int l = 0; l < nl && e == cudaSuccess; ++l) e = cudaStreamWaitEvent(lanes->s[l], lanes->fork, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "batched fork");
+  int rc = CKV_OK;
+  for (int i = 0; i < count && rc == CKV_OK; ++i)
+    rc = score_evict_one(par(i), &layers[i], base + offs[i], offs[i + 1] - offs[i], &outs[i], lanes->s[i % nl], false);
+  // join every lane back, also after a failure, so a stream capture stays well formed
+  for (int l = 0; l < nl; ++l) {
+    cudaError_t ej = cudaEventRecord(lanes->join[l], lanes->s[l]);
+    if (ej == cudaSuccess) ej = cudaStreamWaitEvent(st, lanes->join[l], 0);
+    if (ej != cudaSuccess && rc == CKV_OK) rc = cuda_fail(ej, "batched join");
+  }
+  return rc;
 }
 
 int ckv_read_status(void* workspace, ckv_stream_t stream, int32_t* device_status) {

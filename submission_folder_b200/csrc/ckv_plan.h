@@ -24,7 +24,8 @@ struct alignas(16) Header {
   int32_t n_hi;            // heads in the HI set
   int32_t steps;           // Neumann terms taken (early stop)
   int32_t kept;            // prefix positions kept (selection output count)
-  int32_t pad[52];
+  uint32_t tile_ctr[2];    // next column tile of the tensor-core pooling launch (pass, re-run)
+  int32_t pad[50];
   uint32_t cnt_group[64];  // arrival counters per head group of the stats kernel
 };
 static_assert(sizeof(Header) == 512, "header must be 512 bytes");

@@ -1296,8 +1296,10 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // pass 2 on the tensor cores (W = 64, 4 query heads per KV group)
 // ---------------------------------------------------------------------------
-// Persistent CTAs (one per SM) walk 64-key column tiles; each tile is processed for
-// all KV groups in turn ((tile, group) steps).  A producer warp streams, per step,
+// Persistent CTAs (one per SM) take 64-key column tiles from a counter in the
+// workspace header (so CTAs that start late, e.g. behind another layer's kernels,
+// simply take fewer tiles); each tile is processed for all KV groups in turn
+// ((tile, group) steps).  A producer warp streams, per step,
 // the group's 256 window-query rows and the K tile through a two-stage ring (TMA)
 // and issues the UMMAs (two m-tiles of 128 rows, N = 64) into one of two TMEM
 // buffers.  The query map walks (dim, head, token) with the head inside the token,
@@ -1362,8 +1364,6 @@ __global__ void __launch_bounds__(kP2Threads, 1)
   const int TN = kP2TN, S = kP2Stages;
   const int ntn = (pl.n + TN - 1) / TN;
   const int ngroups = pl.Hkv;
-  const int my_tiles = (ntn - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // tiles b, b+grid, ...
-  const int nsteps = max(0, my_tiles) * ngroups;                                       // (tile, group) steps
   const P2Smem Ly = p2_layout(pl);
   char* base = align1024(smem_raw);
   char* stg = base + Ly.off_stage;
@@ -1373,7 +1373,10 @@ __global__ void __launch_bounds__(kP2Threads, 1)
   float* redrow = reinterpret_cast<float*>(base + Ly.off_redrow);  // [16][8]
   float* gsum = reinterpret_cast<float*>(base + Ly.off_gsum);      // [2]
   float* slse = reinterpret_cast<float*>(base + Ly.off_lse);       // [H][W]
-  __shared__ __align__(8) uint64_t bar_ld[kP2Stages], bar_sfree[kP2Stages], bar_full[2], bar_tfree[2];
+  __shared__ __align__(8) uint64_t bar_ld[kP2Stages], bar_sfree[kP2Stages], bar_full[2], bar_tfree[2], bar_tile[2];
+  __shared__ __align__(8) uint64_t bar_epi;   // epilogue-wide barrier with bounded waits
+  __shared__ int stage_tile[kP2Stages];   // producer only: tile loaded into each stage (-1: none)
+  __shared__ int step_tile[2];            // tile of the step in each accumulator buffer (-1: done)
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
   // TMEM columns [0, 256): two accumulator buffers of two m-tiles of N = 64; [256, 512):
@@ -1382,7 +1385,12 @@ __global__ void __launch_bounds__(kP2Threads, 1)
   if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { tc::mbar_init(&bar_ld[i], 1); tc::mbar_init(&bar_sfree[i], 1); }
-    for (int i = 0; i < 2; ++i) { tc::mbar_init(&bar_full[i], 1); tc::mbar_init(&bar_tfree[i], kP2EpiWarps); }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bar_full[i], 1);
+      tc::mbar_init(&bar_tfree[i], kP2EpiWarps);
+      tc::mbar_init(&bar_tile[i], 1);
+    }
+    tc::mbar_init(&bar_epi, kP2EpiWarps);
     tc::fence_barrier_init();
     abort_sh = 0;
   }
@@ -1394,31 +1402,40 @@ __global__ void __launch_bounds__(kP2Threads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
-  auto step_tile = [&](int s) { return (int)blockIdx.x + (s / ngroups) * (int)gridDim.x; };
 
   if (warp == kP2EpiWarps) {
-    // ---------------- producer: TMA loads and UMMA issue (one thread) ----------------
-    if (lane == 0 && nsteps > 0) {
+    // ---------------- producer: tiles, TMA loads and UMMA issue (one thread) ----------------
+    if (lane == 0) {
       const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
+      uint32_t* ctr = &hdr->tile_ctr[a.fixup_pass ? 1 : 0];
+      int load_tile = -1;
+      // loads step s (tile fetched at the first group of each tile); false when no tile is left
       auto load_step = [&](int s) {
-        const int st = s % S, t = step_tile(s), g = s % ngroups;
+        const int st = s % S, g = s % ngroups;
+        if (g == 0) load_tile = (int)atomicAdd(ctr, 1u);
+        if (load_tile >= ntn) { stage_tile[st] = -1; return; }
+        stage_tile[st] = load_tile;
         char* sb = stg + st * Ly.stage_bytes;
         tc::mbar_expect_tx(&bar_ld[st], (uint32_t)(R * 256 + TN * 256));
         for (int mt = 0; mt < 2; ++mt)
           for (int p = 0; p < 2; ++p)   // rows (token, head pair): head 4g + 2mt + e, token n - W + t
             tc::tma_load_3d(sb + p * R * 128 + mt * 128 * 128, &tmq, &bar_ld[st], p * 64, g * G + 2 * mt, pl.n - W);
         for (int p = 0; p < 2; ++p)
-          tc::tma_load_3d(sb + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, t * TN, g);
+          tc::tma_load_3d(sb + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, load_tile * TN, g);
       };
-      for (int s = 0; s < min(S, nsteps); ++s) load_step(s);
-      for (int s = 0; s < nsteps; ++s) {
-        const int st = s % S;
+      for (int s = 0; s < S; ++s) load_step(s);
+      for (int s = 0;; ++s) {
+        const int st = s % S, b = s & 1;
         if (abort_sh) break;
+        if (s >= 2 && !tc::mbar_wait(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
+        const int tile = stage_tile[st];
+        step_tile[b] = tile;
+        tc::mbar_arrive(&bar_tile[b]);
+        if (tile < 0) { tc::mbar_arrive(&bar_full[b]); break; }   // no tile left: the epilogue stops
         if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
-        if (s >= 2 && !tc::mbar_wait(&bar_tfree[s & 1], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
         tc::fence_after_sync();
         const char* sb = stg + st * Ly.stage_bytes;
-        const uint32_t dcol = (uint32_t)((s & 1) * 2 * TN);
+        const uint32_t dcol = (uint32_t)(b * 2 * TN);
         for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
@@ -1428,12 +1445,10 @@ __global__ void __launch_bounds__(kP2Threads, 1)
             tc::umma_f16(tmem + dcol + mt * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
           }
         }
-        tc::umma_commit(&bar_full[s & 1]);
+        tc::umma_commit(&bar_full[b]);
         tc::umma_commit(&bar_sfree[st]);
-        if (s + S < nsteps) {
-          if (!tc::mbar_wait(&bar_sfree[st], (s / S) & 1, status)) { abort_sh = 1; break; }
-          load_step(s + S);
-        }
+        if (!tc::mbar_wait(&bar_sfree[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        load_step(s + S);
       }
     }
     __syncwarp();
@@ -1456,14 +1471,27 @@ __global__ void __launch_bounds__(kP2Threads, 1)
     const float rs = 1.0f / sqrtf((float)pl.D);
     const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
     const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
-    auto epi_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kP2EpiWarps) : "memory"); };
+    // epilogue barrier: one arrival per warp, bounded wait (a warp that left after a
+    // timeout cannot hang the others)
+    uint32_t epi_phase = 0;
+    auto epi_sync = [&]() {
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bar_epi);
+      if (!tc::mbar_wait(&bar_epi, epi_phase & 1, status)) abort_sh = 1;
+      ++epi_phase;
+      __syncwarp();
+    };
     {
       const float z[4] = {0.f, 0.f, 0.f, 0.f};
       for (int g = 0; g < ngroups; ++g) tc::tmem_st4(acc_base + 4 * g, z);
     }
     float qacc[8], hacc[8];                             // owned columns cq*16 + 2m + e
-    for (int s = 0; s < nsteps; ++s) {
-      const int tile = step_tile(s), g = s % ngroups;
+    for (int s = 0; s < ntn * ngroups; ++s) {
+      const int g = s % ngroups;
+      const bool got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile[s & 1], (s >> 1) & 1, status));
+      if (!got) { abort_sh = 1; break; }   // warp-uniform: the warp leaves together
+      const int tile = step_tile[s & 1];
+      if (tile < 0) break;
       const int j0 = tile * TN;
       if (g == 0) {
 #pragma unroll

@@ -103,6 +103,50 @@ def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return k_out, v_out, idx, scores
 
 
+def score_evict_batched(params, layers, want_scores: bool = False):
+    """Many independent layers / sequences in one call (ragged ``n`` allowed).
+
+    ``params``: one ``Params`` for every layer or a list with one per layer;
+    ``layers``: list of ``(q [H,n,D], k [Hkv,n,D], v [Hkv,n,D])``.  Returns a list of
+    ``score_evict`` results in the same order.  The layers run concurrently on the
+    library's internal streams; outputs are ready in stream order after the call.
+    """
+    plist = list(params) if isinstance(params, (list, tuple)) else [params]
+    if len(plist) not in (1, len(layers)):
+        raise ValueError("params: one struct or one per layer")
+    if not layers:
+        return []
+    dev = layers[0][0].device
+    Ls = (Layer * len(layers))()
+    Os = (Outputs * len(layers))()
+    results = []
+    total = 0
+    for i, (q, k, v) in enumerate(layers):
+        _require_cuda(q, k, v)
+        p = plist[0] if len(plist) == 1 else plist[i]
+        H, n, D = q.shape
+        Ls[i] = make_layer(q, k, v)
+        out_len = output_len(p, n)
+        k_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
+        v_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
+        idx = torch.empty(max(out_len - p.window_size, 1), dtype=torch.int32, device=dev)
+        scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
+        Os[i].out_k, Os[i].out_v, Os[i].out_idx, Os[i].out_scores = (k_out.data_ptr(), v_out.data_ptr(),
+                                                                     idx.data_ptr(), _ptr(scores))
+        results.append([k_out, v_out, idx, scores, n, p])
+        total += (workspace_size(p, n, H, k.shape[0], D) + 255) // 256 * 256
+    ws = workspace(total, dev)
+    P = (Params * len(plist))(*plist)
+    check(_lib.load().ckv_score_evict_batched(P, len(plist), Ls, len(layers), ctypes.c_void_p(ws.data_ptr()),
+                                              ws.numel(), Os, _stream(dev)), "ckv_score_evict_batched")
+    out = []
+    for k_out, v_out, idx, scores, n, p in results:
+        if n < p.max_capacity_prompt:
+            idx = torch.arange(max(n - p.window_size, 0), dtype=torch.int32, device=dev)
+        out.append((k_out, v_out, idx, scores))
+    return out
+
+
 def read_status(dev: torch.device) -> int:
     """Device status word of the cached workspace (synchronises)."""
     ws = _workspaces.get((dev.type, dev.index))

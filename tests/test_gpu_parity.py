@@ -219,6 +219,33 @@ def test_deterministic_and_batched():
         assert torch.equal(x, y)
 
 
+def test_batched_matches_single_calls():
+    """ckv_score_evict_batched (concurrent lanes, per-layer params, ragged n, mixed
+    dtypes, more layers than lanes) gives bit-identical results to one call per layer."""
+    dev = _cuda()
+    names = ["bf16_n2048_default", "fp16_n2048_w32", "cfg1_fp32_n4096", "bf16_w128", "bf16_hi_max",
+             "bf16_n2048_default"]
+    layers, params = [], []
+    for nm in names:
+        c = case(nm)
+        layers.append(tuple(x.to(dev) for x in inputs(c)))
+        params.append(_cluster(c).params(c["n"]))
+    single = [ops.score_evict(p, *lay, want_scores=True) for p, lay in zip(params, layers)]
+    batched = ops.score_evict_batched(params, layers, want_scores=True)
+    torch.cuda.synchronize()
+    for nm, a, b in zip(names, single, batched):
+        for x, y in zip(a, b):
+            assert torch.equal(x, y), nm
+    # one shared params struct for identical layers
+    c = case("bf16_n2048_default")
+    p = _cluster(c).params(c["n"])
+    shared = ops.score_evict_batched(p, [layers[0], layers[5]])
+    torch.cuda.synchronize()
+    for out in shared:
+        for x, y in zip(out[:3], single[0][:3]):
+            assert torch.equal(x, y)
+
+
 def test_short_sequence_returns_inputs():
     dev = _cuda()
     c = case("bf16_n2048_default")
