@@ -107,7 +107,9 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.nchains = (pl.mode == CKV_COMB_MAX || pl.mode == CKV_COMB_WEIGHTED) ? 1 : 2;
   pl.tc = (dtype != CKV_FP32 && (pl.G * pl.W) % 128 == 0 && pl.G * pl.W <= 512 && pl.W <= 128) ? 1 : 0;
   // tensor-core pooling pass: 4 query heads per KV group, window 64 (the Llama / Mistral shapes)
-  pl.tc_pool = (pl.tc && pl.G == 4 && pl.W == 64) ? 1 : 0;
+  // tensor-core pooling: 4 query heads per KV group, W = 64, and at least two KV groups
+  // (its per-tile handshake relies on a tile spanning two or more steps)
+  pl.tc_pool = (pl.tc && pl.G == 4 && pl.W == 64 && pl.Hkv >= 2) ? 1 : 0;
   pl.hi_rows = (pl.nchains == 2 && p.entropy_aware) ? 1 : 0;
   pl.ncol_tiles = (n + kColTile - 1) / kColTile;
   pl.n_pad = pl.ncol_tiles * kColTile;

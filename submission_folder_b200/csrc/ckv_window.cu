@@ -1373,10 +1373,10 @@ __global__ void __launch_bounds__(kP2Threads, 1)
   float* redrow = reinterpret_cast<float*>(base + Ly.off_redrow);  // [16][8]
   float* gsum = reinterpret_cast<float*>(base + Ly.off_gsum);      // [2]
   float* slse = reinterpret_cast<float*>(base + Ly.off_lse);       // [H][W]
-  __shared__ __align__(8) uint64_t bar_ld[kP2Stages], bar_sfree[kP2Stages], bar_full[2], bar_tfree[2], bar_tile[2];
-  __shared__ __align__(8) uint64_t bar_epi;   // epilogue-wide barrier with bounded waits
+  __shared__ __align__(8) uint64_t bar_ld[kP2Stages], bar_sfree[kP2Stages], bar_full[2], bar_tfree[2], bar_tile;
   __shared__ int stage_tile[kP2Stages];   // producer only: tile loaded into each stage (-1: none)
-  __shared__ int step_tile[2];            // tile of the step in each accumulator buffer (-1: done)
+  __shared__ int tile_slot[2];            // tile k of this CTA in slot k & 1 (-1: no tile left)
+  __shared__ volatile int epi_abort;      // written by epilogue warps only, read after a barrier
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
   // TMEM columns [0, 256): two accumulator buffers of two m-tiles of N = 64; [256, 512):
@@ -1388,9 +1388,9 @@ __global__ void __launch_bounds__(kP2Threads, 1)
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&bar_full[i], 1);
       tc::mbar_init(&bar_tfree[i], kP2EpiWarps);
-      tc::mbar_init(&bar_tile[i], 1);
     }
-    tc::mbar_init(&bar_epi, kP2EpiWarps);
+    tc::mbar_init(&bar_tile, 1);
+    epi_abort = 0;
     tc::fence_barrier_init();
     abort_sh = 0;
   }
@@ -1409,10 +1409,14 @@ __global__ void __launch_bounds__(kP2Threads, 1)
       const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
       uint32_t* ctr = &hdr->tile_ctr[a.fixup_pass ? 1 : 0];
       int load_tile = -1;
-      // loads step s (tile fetched at the first group of each tile); false when no tile is left
+      int next_tile = (int)atomicAdd(ctr, 1u);   // fetched one tile ahead: the atomic's latency hides
+      // loads step s (a new tile at the first group of each tile; -1 when none is left)
       auto load_step = [&](int s) {
         const int st = s % S, g = s % ngroups;
-        if (g == 0) load_tile = (int)atomicAdd(ctr, 1u);
+        if (g == 0) {
+          load_tile = next_tile;
+          if (load_tile < ntn) next_tile = (int)atomicAdd(ctr, 1u);
+        }
         if (load_tile >= ntn) { stage_tile[st] = -1; return; }
         stage_tile[st] = load_tile;
         char* sb = stg + st * Ly.stage_bytes;
@@ -1429,9 +1433,11 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         if (abort_sh) break;
         if (s >= 2 && !tc::mbar_wait(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
         const int tile = stage_tile[st];
-        step_tile[b] = tile;
-        tc::mbar_arrive(&bar_tile[b]);
-        if (tile < 0) { tc::mbar_arrive(&bar_full[b]); break; }   // no tile left: the epilogue stops
+        if (s % ngroups == 0) {   // a new tile (or none): publish it to the epilogue
+          tile_slot[(s / ngroups) & 1] = tile;
+          tc::mbar_arrive(&bar_tile);
+        }
+        if (tile < 0) break;      // no tile left: the epilogue stops at this tile boundary
         if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
         tc::fence_after_sync();
         const char* sb = stg + st * Ly.stage_bytes;
@@ -1471,35 +1477,39 @@ __global__ void __launch_bounds__(kP2Threads, 1)
     const float rs = 1.0f / sqrtf((float)pl.D);
     const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
     const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
-    // epilogue barrier: one arrival per warp, bounded wait (a warp that left after a
-    // timeout cannot hang the others)
-    uint32_t epi_phase = 0;
-    auto epi_sync = [&]() {
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bar_epi);
-      if (!tc::mbar_wait(&bar_epi, epi_phase & 1, status)) abort_sh = 1;
-      ++epi_phase;
-      __syncwarp();
-    };
+    // epilogue barrier (the 16 epilogue warps).  Every warp takes the same barriers:
+    // the loop ends only at a tile boundary, on a decision all warps read after a
+    // barrier (no tile left, or a wait that gave up in any epilogue warp).
+    auto epi_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kP2EpiWarps) : "memory"); };
     {
       const float z[4] = {0.f, 0.f, 0.f, 0.f};
       for (int g = 0; g < ngroups; ++g) tc::tmem_st4(acc_base + 4 * g, z);
     }
     float qacc[8], hacc[8];                             // owned columns cq*16 + 2m + e
+    int tile = -1;
     for (int s = 0; s < ntn * ngroups; ++s) {
       const int g = s % ngroups;
-      const bool got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile[s & 1], (s >> 1) & 1, status));
-      if (!got) { abort_sh = 1; break; }   // warp-uniform: the warp leaves together
-      const int tile = step_tile[s & 1];
-      if (tile < 0) break;
+      if (g == 0) {
+        const int k = s / ngroups;
+        if (!epi_abort) {
+          const bool got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile, k & 1, status));
+          if (!got && lane == 0) epi_abort = 1;
+        }
+        epi_sync();
+        if (epi_abort) { abort_sh = 1; break; }   // every epilogue warp reads the same flag here
+        tile = tile_slot[k & 1];
+        if (tile < 0) break;
+      }
       const int j0 = tile * TN;
       if (g == 0) {
 #pragma unroll
         for (int m = 0; m < 8; ++m) { qacc[m] = 0.f; hacc[m] = 0.f; }
       }
-      bool ok = !abort_sh;
-      if (ok && !tc::mbar_wait(&bar_full[s & 1], (s >> 1) & 1, status)) { abort_sh = 1; ok = false; }
-      if (__all_sync(0xffffffffu, ok)) {   // TMEM loads are warp-collective
+      bool ok = !epi_abort;
+      if (ok && !tc::mbar_wait(&bar_full[s & 1], (s >> 1) & 1, status)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) epi_abort = 1;   // the rest of the tile is skipped; the loop ends at its boundary
+      if (ok) {   // TMEM loads are warp-collective
         tc::fence_after_sync();
         uint32_t ra[16], rb[16];
         const uint32_t col = (uint32_t)((s & 1) * 2 * TN + cq * 16);
