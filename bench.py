@@ -177,6 +177,18 @@ def cpu_oracle_sample(args, seconds_cap=30.0):
                       f"reference path), median {t:.2f} s/layer"}
 
 
+def workload_config(args, world):
+    """The ``config`` object of both arms' JSON lines."""
+    bl = budgets(args)
+    return {"workload": "32-layer Llama-3-8B cache, 32 q / 8 kv heads, head_dim 128, bf16, "
+                        f"n={args.n}, window {args.window}, budget "
+                        f"{'pyramid 4096->512' if args.pyramid else bl[0]}",
+            "layers": args.layers, "n": args.n, "window": args.window,
+            "budget": "pyramid" if args.pyramid else bl[0],
+            "parallelism": f"layers of one cache per rank, {world} rank(s)",
+            "l2": "inputs larger than L2 (32 x 64 MiB distinct K per step)"}
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -184,9 +196,7 @@ def run_reference(args, rank):
     line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic", "config": {"workload": "one layer of the 32-layer Llama-3-8B cache",
-                                            "n": args.n, "window": args.window,
-                                            "budget": budgets(args)[0]},
+            "data": "synthetic", "config": workload_config(args, args.gpus),
             "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -391,11 +401,7 @@ def run_ours(args, rank, world):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "32-layer Llama-3-8B cache, 32 q / 8 kv heads, head_dim 128, bf16, "
-                               f"n={n}, window {W}, budget {'pyramid 4096->512' if args.pyramid else bl[0]}",
-                   "layers": L, "n": n, "window": W, "budget": "pyramid" if args.pyramid else bl[0],
-                   "parallelism": f"layers of one cache per rank, {world} rank(s)",
-                   "l2": "inputs larger than L2 (32 x 64 MiB distinct K per step)"},
+        "config": workload_config(args, world),
         "per_layer_us": ms * 1e3 / L,
         "serial_per_layer_us": serial_ms * 1e3 / L,
         "path_hbm_gbs": path_gbs, "path_hbm_frac": path_gbs / pk["hbm_gbs"],
