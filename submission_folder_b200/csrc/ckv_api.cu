@@ -68,7 +68,6 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
     return CKV_OK;
   }
   if (pl.per_head) { *why = "per_head_eviction is not built yet"; return CKV_ERR_UNSUPPORTED; }
-  if (pl.mode == CKV_COMB_WEIGHTED) { *why = "combination_mode 'weighted' is not built yet"; return CKV_ERR_UNSUPPORTED; }
   if (pl.W > kMaxWindow) { *why = "window_size must be <= 128"; return CKV_ERR_UNSUPPORTED; }
   pl.rows_per_warp = (dtype == CKV_FP32) ? 16 : 32;
   pl.rows_per_batch = kWarps * pl.rows_per_warp;
@@ -152,6 +151,8 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.off_cum = take((size_t)2 * (pl.K + 1) * pl.n_p * 4 + 4);
   pl.off_cmax = take((size_t)2 * pl.nscan * (kMaxIters + 1) * 4);
   pl.sel_bytes = (size_t)6 * n * 4 + (size_t)n * 4 + (size_t)n;
+  if (pl.mode == CKV_COMB_WEIGHTED)   // full-rank radix buffers [2][2][n] u64 and ranks [2][n]
+    pl.sel_bytes = (((size_t)29 * n + 15) & ~(size_t)15) + (size_t)40 * n;
   pl.off_sel = take(pl.sel_bytes);
   pl.off_ph = off;
   pl.total = off;
@@ -222,7 +223,8 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
   e = launch_sweep(pl, *p, ws, st);
   if (e != cudaSuccess) return cuda_fail(e, "sweep kernels");
   stage_mark(st);
-  if (pl.mode == CKV_COMB_MAX || (pl.mode == CKV_COMB_DIS && p->use_bridge_importance)) {
+  if (pl.mode == CKV_COMB_MAX || pl.mode == CKV_COMB_WEIGHTED ||
+      (pl.mode == CKV_COMB_DIS && p->use_bridge_importance)) {
     e = launch_aux(pl, *p, ws, st);
     if (e != cudaSuccess) return cuda_fail(e, "aux kernel");
   }

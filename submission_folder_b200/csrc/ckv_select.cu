@@ -43,7 +43,7 @@ constexpr int kSliceSmemMax = 16384;    // slice positions kept in shared memory
 struct SelLayout {
   int n, P, S, nchunk;
   bool smem_x;
-  size_t off_sort, off_x, off_cnt, off_misc, off_hx, off_xch, total;
+  size_t off_sort, off_x, off_cnt, off_misc, off_hx, off_xch, off_rk, total;
 };
 
 __host__ __device__ inline SelLayout sel_layout(int n, int P) {
@@ -62,6 +62,7 @@ __host__ __device__ inline SelLayout sel_layout(int n, int P) {
   L.off_misc = take(sizeof(int) * 256);
   L.off_hx = take(sizeof(int) * 2 * 256);
   L.off_xch = take(sizeof(float) * 16);
+  L.off_rk = take(sizeof(int) * 5 * 256);
   L.total = off;
   return L;
 }
@@ -75,6 +76,7 @@ struct SelSmem {
   int* hx;          // [2][256] this CTA's histogram, read by the vector's other CTAs
   float* xch;       // exchanged scalars: [0] total, [1] max; ints at [2..]
   int* ixch;
+  int* rk;          // [5][256] digit totals / below / bases / running / round totals (full ranks)
 };
 
 // ---------------------------------------------------------------------------
@@ -314,6 +316,109 @@ __device__ void top_sorted(cg::cluster_group& cl, const float* x, int b0, int b1
 }
 
 // ---------------------------------------------------------------------------
+// full stable ranks of one vector (weighted combination, PU:1865-1882)
+// ---------------------------------------------------------------------------
+// argsort(argsort(x)) with a stable sort, over the P CTAs that hold the vector's
+// slices: a 4-pass LSD radix sort of the 32-bit keys (float_key) carried with their
+// indices through two global buffers (L2-resident).  Each pass: per-CTA digit
+// histograms exchanged through distributed shared memory give every (digit, CTA)
+// its output base; inside a CTA, rounds of blockDim consecutive elements are ranked
+// stably with warp match_any and per-warp digit counts.  Stable passes over a
+// sequence that starts in index order leave equal keys in index order, so
+// rank[i] = the final position of element i.  All CTAs of the cluster call it.
+__device__ void full_ranks(cg::cluster_group& cl, const float* x, int b0, int b1, int vbase, int P, int part,
+                           unsigned long long* bufA, unsigned long long* bufB, int* rank, SelSmem& sh) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, bd = blockDim.x;
+  int* tot = sh.rk;              // [256] digit totals over the vector
+  int* below = sh.rk + 256;      // [256] digit counts of lower-ranked CTAs
+  int* base = sh.rk + 512;       // [256] output base of each digit for this CTA
+  int* run = sh.rk + 768;        // [256] elements of each digit placed so far
+  int* rtot = sh.rk + 1024;      // [256] per-round digit totals
+  int* wcnt = sh.hist;           // [32 warps][256] per-round warp digit counts
+  for (int j = b0 + tid; j < b1; j += bd)
+    bufA[j] = ((unsigned long long)float_key(x[j - b0]) << 32) | (uint32_t)j;
+  __syncthreads();
+  unsigned long long* in = bufA;
+  unsigned long long* out = bufB;
+  const int nrounds = (b1 - b0 + bd - 1) / bd;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 32 + 8 * pass;
+    int* hx = sh.hx + (pass & 1) * 256;
+    for (int i = tid; i < 256; i += bd) hx[i] = 0;
+    __syncthreads();
+    for (int r = 0; r < nrounds; ++r) {
+      const int pos = b0 + r * bd + tid;
+      const bool act = pos < b1;
+      const int d = act ? (int)((__ldcg(in + pos) >> shift) & 255u) : 256;
+      const unsigned peers = __match_any_sync(0xffffffffu, d);
+      if (act && lane == __ffs(peers) - 1) atomicAdd(&hx[d], __popc(peers));
+    }
+    cl.sync();
+    if (tid < 256) {
+      int t = 0, bl = 0;
+      for (int q = 0; q < P; ++q) {
+        const int c = cl.map_shared_rank(hx, vbase + q)[tid];
+        t += c;
+        if (q < part) bl += c;
+      }
+      tot[tid] = t;
+      below[tid] = bl;
+      run[tid] = 0;
+    }
+    __syncthreads();
+    if (wid < 8) {   // exclusive scan of the 256 digit totals
+      const int d = wid * 32 + lane;
+      int incl = tot[d];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      rtot[d] = incl;   // warp-inclusive; warp offsets below
+    }
+    __syncthreads();
+    if (tid < 256) {
+      int off = 0;
+      for (int q = 0; q < (tid >> 5); ++q) off += rtot[q * 32 + 31];
+      base[tid] = off + rtot[tid] - tot[tid] + below[tid];
+    }
+    __syncthreads();
+    for (int r = 0; r < nrounds; ++r) {
+      for (int i = tid; i < 32 * 256; i += bd) wcnt[i] = 0;
+      __syncthreads();
+      const int pos = b0 + r * bd + tid;
+      const bool act = pos < b1;
+      const unsigned long long e = act ? __ldcg(in + pos) : 0ull;
+      const int d = act ? (int)((e >> shift) & 255u) : 256;
+      const unsigned peers = __match_any_sync(0xffffffffu, d);
+      const int rk = __popc(peers & lanemask_lt());
+      if (act && rk == 0) wcnt[wid * 256 + d] = __popc(peers);
+      __syncthreads();
+      if (tid < 256) {   // exclusive prefix over warps, per digit
+        int s = 0;
+        for (int q = 0; q < (bd >> 5); ++q) {
+          const int c = wcnt[q * 256 + tid];
+          wcnt[q * 256 + tid] = s;
+          s += c;
+        }
+        rtot[tid] = s;
+      }
+      __syncthreads();
+      if (act) out[base[d] + run[d] + wcnt[wid * 256 + d] + rk] = e;
+      __syncthreads();
+      if (tid < 256) run[tid] += rtot[tid];
+      __syncthreads();
+    }
+    cl.sync();   // every element of the pass is placed
+    unsigned long long* t = in;
+    in = out;
+    out = t;
+  }
+  for (int j = b0 + tid; j < b1; j += bd) rank[(uint32_t)__ldcg(in + j)] = j;
+  cl.sync();
+}
+
+// ---------------------------------------------------------------------------
 // finished chain scores (PU:2186-2204)
 // ---------------------------------------------------------------------------
 __device__ int early_stop_steps(const Plan& pl, const char* ws) {
@@ -401,6 +506,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_select(SelArgs a) {
   sh.hx = reinterpret_cast<int*>(smraw + L.off_hx);
   sh.xch = reinterpret_cast<float*>(smraw + L.off_xch);
   sh.ixch = reinterpret_cast<int*>(sh.xch);
+  sh.rk = reinterpret_cast<int*>(smraw + L.off_rk);
   float* sc = reinterpret_cast<float*>(ws + pl.off_sel);               // [3][n] finished scores
   float* gx = sc + 3 * (size_t)n;                                      // [3][n] slices not held in smem
   int* gcomb = reinterpret_cast<int*>(gx + 3 * (size_t)n);             // [n] combined ranks
@@ -513,9 +619,33 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_select(SelArgs a) {
   int M;
   if (uni) M = (v == 0) ? min(qb, cand) : min(cand, hb + qb + kk);
   else M = Mx;
-  M = max(M, 1);
-  if (uni) top_sorted(cl, x, b0, b1, lo, hi, M, false, vbase, P, leader, sh);
-  else top_sorted(cl, x, b0, b1, 0, n, M, true, vbase, P, leader, sh);
+  const bool weighted = mode == CKV_COMB_WEIGHTED;
+  if (weighted) {
+    // full stable ranks of both vectors, then combined = w * rank(H2O) + (1 - w) * rank(influence)
+    // (PU:3237-3240); its top kk over the candidates, lowest index first at ties (PU:2616-2644)
+    char* wbase = reinterpret_cast<char*>(ws + pl.off_sel) + (((size_t)29 * n + 15) & ~(size_t)15);
+    unsigned long long* bufs = reinterpret_cast<unsigned long long*>(wbase);     // [2 vectors][2][n]
+    int* ranks = reinterpret_cast<int*>(bufs + (size_t)4 * n);                 // [2][n]
+    full_ranks(cl, x, b0, b1, vbase, P, part, bufs + (size_t)v * 2 * n, bufs + (size_t)v * 2 * n + n,
+               ranks + (size_t)v * n, sh);
+    const float wh = prm.h2o_weight, wi = (float)(1.0 - (double)prm.h2o_weight);
+    const float den = (float)(n - 1), iden = n > 1 ? 1.0f / den : 0.f;
+    for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) {
+      float ir = 1.f, hr = 1.f;
+      if (n > 1) {
+        ir = div_rcp((float)__ldcg(ranks + j), den, iden);       // influence (vector 0)
+        hr = div_rcp((float)__ldcg(ranks + n + j), den, iden);   // H2O (vector 1)
+      }
+      x[j - b0] = __fadd_rn(__fmul_rn(wh, hr), __fmul_rn(wi, ir));
+    }
+    __syncthreads();
+    M = max(min(kk, cand), 1);
+    top_sorted(cl, x, b0, b1, lo, hi, M, false, vbase, P, leader, sh);
+  } else if (uni) {
+    top_sorted(cl, x, b0, b1, lo, hi, M, false, vbase, P, leader, sh);
+  } else {
+    top_sorted(cl, x, b0, b1, 0, n, M, true, vbase, P, leader, sh);
+  }
   cl.sync();   // sorted lists ready
 
   // ---- phase 3: combination (PU:3177-3196 rank MAX; PU:2489-2589 union)
@@ -523,7 +653,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_select(SelArgs a) {
   const int nv = C / P;
   int live = 0;
   for (int u = 0; u < nv; ++u) live += zeroed(u) ? 0 : 1;
-  const bool rankmax = !uni && kk > 0 && live > 0;
+  const bool rankmax = !uni && !weighted && kk > 0 && live > 0;
   for (int i = g0 + threadIdx.x; i < min(g1, Mx); i += blockDim.x) gbins[i] = 0;
   if (rankmax) {
     // combined rank of every listed position: MAX over the vectors of n - 1 - list position
@@ -582,7 +712,14 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_select(SelArgs a) {
       const unsigned word = __ballot_sync(0xffffffffu, keep);
       if (lane == 0) gbits[i >> 5] = word;
     }
-  } else if (!uni && kk > 0) {
+  } else if (weighted && kk > 0 && rank == 0) {
+    // weighted: the kk best combined scores (vector 0's list)
+    const int m = min(kk, cand);
+    for (int q = threadIdx.x; q < m; q += blockDim.x) {
+      const int i = sorted_index(sh.sortbuf[q], false);
+      atomicOr(gbits + (i >> 5), 1u << (i & 31));
+    }
+  } else if (!uni && !weighted && kk > 0) {
     // every vector ablated: the first kk candidates
     for (int b = g0 + (int)threadIdx.x - lane; b < g1; b += blockDim.x) {
       const int i = b + lane;
@@ -867,6 +1004,10 @@ int select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const 
     return CKV_ERR_ARG;
   }
   if (n < p->max_capacity_prompt) { *why = "n < max_capacity_prompt: nothing to select"; return CKV_ERR_ARG; }
+  if (p->combination_mode == CKV_COMB_WEIGHTED) {
+    *why = "ckv_select_scores_noalloc: combination_mode 'weighted' needs ckv_select_scores (workspace)";
+    return CKV_ERR_UNSUPPORTED;
+  }
   Plan pl;
   int rc = make_plan(*p, n, 32, 8, 128, CKV_BF16, &pl, why);
   if (rc) return rc;

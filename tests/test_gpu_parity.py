@@ -33,7 +33,7 @@ def _cluster(c):
     return CircuitKVCluster(**c["kwargs"])
 
 
-SHARED = [c["name"] for c in cases() if "perhead" not in c["name"] and "weighted" not in c["name"]]
+SHARED = [c["name"] for c in cases() if "perhead" not in c["name"]]
 
 
 @pytest.mark.parametrize("name", ["bf16_n2048_default", "cfg1_fp32_n4096", "fp16_n2048_w32",
@@ -98,7 +98,7 @@ def test_neumann_rows_matches_oracle(name):
 @pytest.mark.parametrize("name", ["bf16_n2048_default", "cfg1_fp32_n4096", "fp16_n2048_w32",
                                   "bf16_ablate_qi", "bf16_ablate_hi", "bf16_boxcar5", "bf16_sink8",
                                   "bf16_w128", "bf16_n8192_cfg2", "bf16_union", "bf16_union_da",
-                                  "bf16_max", "bf16_bridge"])
+                                  "bf16_max", "bf16_bridge", "bf16_weighted"])
 def test_select_from_reference_scores(name):
     """Selection stage fed with the reference's own score vectors."""
     dev = _cuda()
@@ -111,7 +111,7 @@ def test_select_from_reference_scores(name):
     if mode in ("union", "union_da"):
         a, b = g["union_qi"], g["union_hi"]
         cvec = None
-    elif mode == "max":
+    elif mode in ("max", "weighted"):
         q, k, _ = inputs(c)
         at = O.window_attention(q.float().numpy(), k.float().numpy(), W, 4, c["dtype"])
         rq, _ = O.pool_rows(at, O.choose_heads(at, op))
@@ -244,6 +244,31 @@ def test_batched_matches_single_calls():
     for out in shared:
         for x, y in zip(out[:3], single[0][:3]):
             assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("n,budget,w", [(5000, 700, 0.5), (2048, 256, 0.3), (33000, 2048, 0.7)])
+def test_weighted_selection_exact(n, budget, w):
+    """Weighted combination (PU:3237-3240) from given influence / H2O vectors: full stable
+    ranks on the GPU (cluster radix sort), combined score, top-k with lowest-index ties --
+    the same kept set as the oracle, exactly.  Values repeat to exercise rank ties."""
+    dev = _cuda()
+    rng = np.random.default_rng(n)
+    infl = rng.integers(0, n // 4, n).astype(np.float32) / np.float32(n)   # many exact ties
+    h2o = rng.random(n).astype(np.float32)
+    h2o[rng.integers(0, n, n // 10)] = np.float32(0.25)
+    cl = CircuitKVCluster(window_size=64, max_capacity_prompt=budget, combination_mode="weighted",
+                          h2o_weight=w)
+    p = cl.params(n)
+    idx, sc = ops.select_scores(p, torch.from_numpy(infl).to(dev), torch.from_numpy(h2o).to(dev),
+                                want_scores=True)
+    torch.cuda.synchronize()
+    ir, hr = O.rank_normalize(infl), O.rank_normalize(h2o)
+    comb = (np.float32(w) * hr + np.float32(1 - w) * ir).astype(np.float32)
+    mask = O.keep_mask(comb, budget, n, 4, 64)
+    mask[n - 64:] = False
+    ref = np.nonzero(mask)[0]
+    got = idx.cpu().numpy()
+    np.testing.assert_array_equal(got, ref)
 
 
 def test_short_sequence_returns_inputs():
