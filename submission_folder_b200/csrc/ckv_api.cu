@@ -67,8 +67,10 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
     *out = pl;
     return CKV_OK;
   }
-  if (pl.per_head) { *why = "per_head_eviction is not built yet"; return CKV_ERR_UNSUPPORTED; }
   if (pl.W > kMaxWindow) { *why = "window_size must be <= 128"; return CKV_ERR_UNSUPPORTED; }
+  if (pl.per_head && n - pl.W > 65536) {
+    *why = "per_head_eviction supports n - window_size <= 65536"; return CKV_ERR_UNSUPPORTED;
+  }
   pl.rows_per_warp = (dtype == CKV_FP32) ? 16 : 32;
   pl.rows_per_batch = kWarps * pl.rows_per_warp;
   if (pl.W % pl.rows_per_warp != 0 || pl.rows_per_batch % pl.W != 0) {
@@ -155,6 +157,21 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
     pl.sel_bytes = (((size_t)29 * n + 15) & ~(size_t)15) + (size_t)40 * n;
   pl.off_sel = take(pl.sel_bytes);
   pl.off_ph = off;
+  if (pl.per_head) {
+    const size_t nw = (size_t)(n - pl.W), Hs = (size_t)H, nn = (size_t)n;
+    pl.ph_nw = n - pl.W;
+    pl.off_ph_q2w = take(Hs * pl.W * 4);
+    pl.off_ph_qrow = take(Hs * nn * 4);
+    pl.off_ph_two = take(Hs * nn * 4);
+    pl.off_ph_col = take(Hs * nn * 4);
+    pl.off_ph_ent = take((size_t)(pl.ncol_tiles + 1) * Hs * 4);   // + the per-head totals
+    pl.off_ph_vec = take(Hs * 2 * nw * 4);
+    pl.off_ph_ghi = take(nw * 4);
+    pl.off_ph_gbuf = take(nw * 2 * 8 + nw * 4);
+    pl.off_ph_bufs = take(Hs * 4 * nw * 8);
+    pl.off_ph_ranks = take(Hs * 2 * nw * 4);
+    pl.off_ph_bits = take(Hs * ((nw + 31) / 32) * 4);
+  }
   pl.total = off;
   *out = pl;
   return CKV_OK;
@@ -212,6 +229,19 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
   wa.q = L->q; wa.qhs = L->q_head_stride; wa.qts = L->q_tok_stride;
   wa.k = L->k; wa.khs = L->k_head_stride; wa.kts = L->k_tok_stride;
   wa.ws = ws; wa.fixup_pass = 0; wa.p = *p; wa.pl = pl;
+  if (pl.per_head) {   // PU:3296-3464: per-head importance and selection, per-head gather
+    e = launch_window_stage(wa, 0, st);
+    if (e != cudaSuccess) return cuda_fail(e, "window moments");
+    e = launch_ph_pass(wa, st);
+    if (e != cudaSuccess) return cuda_fail(e, "per-head pass");
+    PhArgs ph;
+    ph.pl = pl; ph.p = *p; ph.ws = ws; ph.out_idx = out->out_idx;
+    ph.eq = (float)pow((double)p->qi_gamma, pl.K / 2.0);
+    ph.eh = (float)pow((double)p->hi_gamma, pl.K / 2.0);
+    e = launch_ph_select(ph, st);
+    if (e != cudaSuccess) return cuda_fail(e, "per-head selection");
+    return launch_gather_layer(pl, L, out, out->out_idx, 0, st);
+  }
   for (int s = 0; s < 3; ++s) {
     e = launch_window_stage(wa, s, st);
     if (e != cudaSuccess) {
@@ -404,6 +434,8 @@ int ckv_select_scores(const ckv_params* p, int32_t n, const float* a, const floa
                       const float* c, void* workspace, size_t workspace_bytes, int32_t* out_idx,
                       float* out_scores, ckv_stream_t stream) {
   if (!p || !a || !b || !out_idx) return fail(CKV_ERR_ARG, "null argument");
+  if (p->per_head_eviction)
+    return fail(CKV_ERR_UNSUPPORTED, "per-head selection needs the window attention: use ckv_score_evict");
   Plan pl;
   const char* why = "";
   int rc = make_plan(*p, n, 32, 8, 128, CKV_BF16, &pl, &why);

@@ -63,6 +63,19 @@ struct Plan {
   size_t off_rows_qi, off_rows_hi, off_colsum, off_gtile, off_rspart;
   size_t off_wk, off_yk, off_ymax, off_bk, off_cg, off_agg, off_cum, off_cmax;
   size_t off_sel, off_ph;
+  // per-head eviction (PU:2208-2382, 3296-3464): only allocated in that mode
+  size_t off_ph_q2w;   // [H][W] query row -> window columns
+  size_t off_ph_qrow;  // [H][n] query row
+  size_t off_ph_two;   // [H][n] two-hop attention through the window rows
+  size_t off_ph_col;   // [H][n] column sums over the window rows
+  size_t off_ph_ent;   // [ncol_tiles][H] query-row entropy partials, then [H] totals
+  size_t off_ph_vec;   // [H][2][nw] finished, truncated, smoothed QI / HI (or H2O)
+  size_t off_ph_ghi;   // [nw] rank-normalised mean over heads of HI
+  size_t off_ph_gbuf;  // [2][nw] u64 + [nw] int: ranking scratch of the mean HI
+  size_t off_ph_bufs;  // [H][2][2][nw] u64: per-head ranking scratch
+  size_t off_ph_ranks; // [H][2][nw] int
+  size_t off_ph_bits;  // [H][ceil(nw / 32)] keep bits
+  int ph_nw;           // n - W
   size_t sel_bytes;
   size_t total;
 };

@@ -861,6 +861,253 @@ cudaError_t launch_select(const SelArgs& a0, cudaStream_t st) {
 }
 
 // ---------------------------------------------------------------------------
+// per-head eviction (PU:2208-2382 importance, PU:3296-3464 selection)
+// ---------------------------------------------------------------------------
+// k_ph_finish, one CTA per (head, vector): QI = query row + eq * two-hop, HI = query
+// row * (n_t - pos) / n_t * eh + query row (or the window column sums with
+// true_hub_hi) over [s, n); sinks = 0.01 * sum; divided by max(max, 1e-8); cut to
+// n - W and smoothed with the Gaussian kernel.  With both ablations the second
+// vector is the raw column sum (H2O).  CTA (h, 0) also totals the head's
+// query-row entropy.
+__global__ void __launch_bounds__(kSelThreads) k_ph_finish(PhArgs a) {
+  const Plan& pl = a.pl;
+  const ckv_params& prm = a.p;
+  const int h = blockIdx.x, v = blockIdx.y;
+  const int n = pl.n, s = pl.s, nw = pl.ph_nw;
+  const float* qrow = reinterpret_cast<const float*>(a.ws + pl.off_ph_qrow) + (size_t)h * n;
+  const float* two = reinterpret_cast<const float*>(a.ws + pl.off_ph_two) + (size_t)h * n;
+  const float* col = reinterpret_cast<const float*>(a.ws + pl.off_ph_col) + (size_t)h * n;
+  float* vec = reinterpret_cast<float*>(a.ws + pl.off_ph_vec) + ((size_t)h * 2 + v) * nw;
+  float* tmp = reinterpret_cast<float*>(a.ws + pl.off_ph_bufs) + (size_t)h * 8 * nw + (size_t)v * n;
+  __shared__ float red[64];
+  if (v == 0) {   // the head's query-row entropy: -sum_j p ln(p + 1e-10)
+    const float* entp = reinterpret_cast<const float*>(a.ws + pl.off_ph_ent);
+    float t = 0.f;
+    for (int i = threadIdx.x; i < pl.ncol_tiles; i += blockDim.x) t += __ldcg(entp + (size_t)i * pl.H + h);
+    t = block_reduce<false>(t, red);
+    if (threadIdx.x == 0)
+      reinterpret_cast<float*>(a.ws + pl.off_ph_ent)[(size_t)pl.ncol_tiles * pl.H + h] = -t;
+  }
+  if (v == 1 && prm.ablate_qi && prm.ablate_hi) {   // H2O per head: raw column sums
+    for (int j = threadIdx.x; j < nw; j += blockDim.x) vec[j] = __ldcg(col + j);
+    return;
+  }
+  const float nt = (float)(n - s), int_ = 1.0f / nt;
+  float tot = 0.f, mx = 0.f;
+  for (int j = s + threadIdx.x; j < n; j += blockDim.x) {
+    float r;
+    if (v == 0) {
+      r = __fadd_rn(__ldcg(qrow + j), __fmul_rn(a.eq, __ldcg(two + j)));
+    } else if (prm.true_hub_hi) {
+      r = __ldcg(col + j);
+    } else {
+      const float qt = __ldcg(qrow + j);
+      const float hw = div_rcp(nt - (float)(j - s), nt, int_);
+      r = __fadd_rn(__fmul_rn(__fmul_rn(qt, hw), a.eh), qt);
+    }
+    tmp[j] = r;
+    tot += r;
+    mx = fmaxf(mx, r);
+  }
+  tot = block_reduce<false>(tot, red);
+  mx = block_reduce<true>(mx, red);
+  const float sinkv = __fmul_rn(tot, 0.01f);
+  if (s > 0) mx = fmaxf(mx, sinkv);
+  mx = fmaxf(mx, 1e-8f);
+  const float imx = 1.0f / mx;
+  __syncthreads();
+  for (int j = threadIdx.x; j < nw; j += blockDim.x) tmp[j] = div_rcp(j < s ? sinkv : tmp[j], mx, imx);
+  __syncthreads();
+  const int ksz = prm.smoothing_kernel > 0 ? prm.smoothing_kernel : max(prm.qi_kernel_size, prm.hi_kernel_size);
+  if (ksz > 1 && nw > ksz) {
+    float wt[32];
+    const int kk = smooth_taps(ksz, true, prm.gaussian_sigma, wt);
+    const int pad = ksz / 2;
+    for (int j = threadIdx.x; j < nw; j += blockDim.x) {
+      float acc = 0.f;
+      for (int t = 0; t < kk; ++t) {
+        const int src = j + t - pad;
+        if (src >= 0 && src < nw) acc = fmaf(wt[t], __ldcg(tmp + src), acc);
+      }
+      vec[j] = acc;
+    }
+  } else {
+    for (int j = threadIdx.x; j < nw; j += blockDim.x) vec[j] = __ldcg(tmp + j);
+  }
+}
+
+// k_ph_ghi, one cluster: the mean over heads of the (smoothed) HI vectors and its
+// stable ranks, normalised by n - W - 1 (the global HI of PU:3400-3440).
+__global__ void __launch_bounds__(kSelThreads, 1) k_ph_ghi(PhArgs a) {
+  extern __shared__ __align__(16) char smraw[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int P = (int)cl.num_blocks(), part = (int)cl.block_rank();
+  const Plan& pl = a.pl;
+  const int nw = pl.ph_nw, H = pl.H;
+  const SelLayout L = sel_layout(nw, P);
+  SelSmem sh;
+  sh.sortbuf = reinterpret_cast<unsigned long long*>(smraw + L.off_sort);
+  sh.hist = reinterpret_cast<int*>(sh.sortbuf);
+  sh.cnt = reinterpret_cast<int*>(smraw + L.off_cnt);
+  sh.misc = reinterpret_cast<int*>(smraw + L.off_misc);
+  sh.fmisc = reinterpret_cast<float*>(sh.misc + 128);
+  sh.hx = reinterpret_cast<int*>(smraw + L.off_hx);
+  sh.xch = reinterpret_cast<float*>(smraw + L.off_xch);
+  sh.ixch = reinterpret_cast<int*>(sh.xch);
+  sh.rk = reinterpret_cast<int*>(smraw + L.off_rk);
+  const float* vec = reinterpret_cast<const float*>(a.ws + pl.off_ph_vec);
+  unsigned long long* gbuf = reinterpret_cast<unsigned long long*>(a.ws + pl.off_ph_gbuf);
+  int* granks = reinterpret_cast<int*>(gbuf + 2 * (size_t)nw);
+  float* ghi = reinterpret_cast<float*>(a.ws + pl.off_ph_ghi);
+  const int b0 = min(nw, part * L.S), b1 = min(nw, b0 + L.S);
+  float* x = L.smem_x ? reinterpret_cast<float*>(smraw + L.off_x) : ghi + b0;   // ghi doubles as scratch
+  const float fh = (float)H, ih = 1.0f / fh;
+  for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) {
+    float sum = 0.f;
+    for (int h = 0; h < H; ++h) sum += __ldcg(vec + ((size_t)h * 2 + 1) * nw + j);
+    x[j - b0] = div_rcp(sum, fh, ih);
+  }
+  __syncthreads();
+  full_ranks(cl, x, b0, b1, 0, P, part, gbuf, gbuf + nw, granks, sh);
+  const float den = (float)(nw - 1), iden = nw > 1 ? 1.0f / den : 0.f;
+  for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x)
+    ghi[j] = nw > 1 ? div_rcp((float)__ldcg(granks + j), den, iden) : 1.f;
+}
+
+// k_ph_select, one cluster of 8 CTAs per head (4 per vector): stable ranks of the
+// head's QI and HI vectors over [0, n - W), the per-head score of PU:3376-3440 (QI
+// rank only; global HI rank; H2O rank; entropy-adaptive mix; or MAX(QI rank,
+// global HI rank)), its top m over [s, n - W) with the lowest indices first at ties
+// (topk), and the kept positions, sinks first, ascending (PU:3442-3452).
+__global__ void __launch_bounds__(kSelThreads, 1) k_ph_select(PhArgs a) {
+  extern __shared__ __align__(16) char smraw[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  const int P = C / 2, v = rank / P, part = rank % P, vbase = v * P;
+  const bool leader = part == 0;
+  const int h = (int)blockIdx.x / C;
+  const Plan& pl = a.pl;
+  const ckv_params& prm = a.p;
+  const int nw = pl.ph_nw, s = pl.s, m = pl.kk, nk = pl.s + pl.kk;
+  const SelLayout L = sel_layout(nw, P);
+  SelSmem sh;
+  sh.sortbuf = reinterpret_cast<unsigned long long*>(smraw + L.off_sort);
+  sh.hist = reinterpret_cast<int*>(sh.sortbuf);
+  sh.cnt = reinterpret_cast<int*>(smraw + L.off_cnt);
+  sh.misc = reinterpret_cast<int*>(smraw + L.off_misc);
+  sh.fmisc = reinterpret_cast<float*>(sh.misc + 128);
+  sh.hx = reinterpret_cast<int*>(smraw + L.off_hx);
+  sh.xch = reinterpret_cast<float*>(smraw + L.off_xch);
+  sh.ixch = reinterpret_cast<int*>(sh.xch);
+  sh.rk = reinterpret_cast<int*>(smraw + L.off_rk);
+  const float* vec = reinterpret_cast<const float*>(a.ws + pl.off_ph_vec) + ((size_t)h * 2 + v) * nw;
+  unsigned long long* bufs = reinterpret_cast<unsigned long long*>(a.ws + pl.off_ph_bufs) + (size_t)h * 4 * nw;
+  int* ranks = reinterpret_cast<int*>(a.ws + pl.off_ph_ranks) + (size_t)h * 2 * nw;
+  const float* ghi = reinterpret_cast<const float*>(a.ws + pl.off_ph_ghi);
+  const int nwords = (nw + 31) / 32;
+  uint32_t* bits = reinterpret_cast<uint32_t*>(a.ws + pl.off_ph_bits) + (size_t)h * nwords;
+  const int b0 = min(nw, part * L.S), b1 = min(nw, b0 + L.S);
+  float* x = reinterpret_cast<float*>(smraw + L.off_x);   // the launcher guarantees slices in smem
+  const int T = (((nw + C - 1) / C) + 31) & ~31;
+  const int g0 = min(nw, rank * T), g1 = min(nw, g0 + T);
+  const int lane = threadIdx.x & 31;
+  for (int i = g0 / 32 + threadIdx.x; i < (g1 + 31) / 32; i += blockDim.x) bits[i] = 0u;
+  for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) x[j - b0] = __ldcg(vec + j);
+  __syncthreads();
+  full_ranks(cl, x, b0, b1, vbase, P, part, bufs + (size_t)v * 2 * nw, bufs + (size_t)v * 2 * nw + nw,
+             ranks + (size_t)v * nw, sh);
+  // per-head combined score of this slice (both vectors' CTAs compute it)
+  const bool aq = prm.ablate_qi, ah = prm.ablate_hi;
+  float wq = 0.5f;
+  if (!aq && !ah && prm.entropy_adaptive) {
+    const float* ent = reinterpret_cast<const float*>(a.ws + pl.off_ph_ent) + (size_t)pl.ncol_tiles * pl.H;
+    float lo = INFINITY, hi = -INFINITY;
+    for (int q = 0; q < pl.H; ++q) { const float e = __ldcg(ent + q); lo = fminf(lo, e); hi = fmaxf(hi, e); }
+    if (hi > lo) wq = __fsub_rn(1.0f, __fdiv_rn(__fsub_rn(__ldcg(ent + h), lo), __fsub_rn(hi, lo)));
+  }
+  const float den = (float)(nw - 1), iden = nw > 1 ? 1.0f / den : 0.f;
+  for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) {
+    const float qr = nw > 1 ? div_rcp((float)__ldcg(ranks + j), den, iden) : 1.f;
+    const float hr = nw > 1 ? div_rcp((float)__ldcg(ranks + nw + j), den, iden) : 1.f;
+    float sc;
+    if (ah && !aq) sc = qr;
+    else if (aq && !ah) sc = __ldcg(ghi + j);
+    else if (aq && ah) sc = hr;
+    else if (prm.entropy_adaptive) sc = __fadd_rn(__fmul_rn(wq, qr), __fmul_rn(__fsub_rn(1.0f, wq), hr));
+    else sc = fmaxf(qr, __ldcg(ghi + j));
+    x[j - b0] = sc;
+  }
+  __syncthreads();
+  top_sorted(cl, x, b0, b1, s, nw, max(m, 1), false, vbase, P, leader, sh);
+  cl.sync();
+  if (rank == 0 && m > 0)
+    for (int q = threadIdx.x; q < m; q += blockDim.x) {
+      const int i = sorted_index(sh.sortbuf[q], false);
+      atomicOr(bits + (i >> 5), 1u << (i & 31));
+    }
+  cl.sync();
+  // kept positions ascending: sinks, then the chosen
+  const int h1 = g1;
+  auto kept = [&](int i) { return i < h1 && (i < s || ((__ldcg(bits + (i >> 5)) >> (i & 31)) & 1u)); };
+  int mine = 0;
+  if (g0 < h1) {
+    chunk_counts(g0, h1, sh.cnt, kept);
+    mine = scan_counts(sh.cnt, (h1 - g0 + 31) / 32, sh.misc);
+  }
+  if (threadIdx.x == 0) sh.ixch[4] = mine;
+  cl.sync();
+  int base = 0;
+  for (int q = 0; q < rank; ++q) base += cl.map_shared_rank(sh.ixch, q)[4];
+  int32_t* out = a.out_idx + (size_t)h * nk;
+  for (int b = g0 + (int)threadIdx.x - lane; b < h1; b += blockDim.x) {
+    const int i = b + lane;
+    const bool kp = kept(i);
+    const unsigned bb = __ballot_sync(0xffffffffu, kp);
+    if (kp) {
+      const int r = base + chunk_rank(sh.cnt, g0, i, bb);
+      if (r < nk) out[r] = i;
+    }
+  }
+  cl.sync();
+}
+
+size_t ph_select_smem(int nw) { return sel_layout(nw, 4).total; }
+
+cudaError_t launch_ph_select(const PhArgs& a, cudaStream_t st) {
+  const Plan& pl = a.pl;
+  const int nw = pl.ph_nw;
+  if (sel_layout(nw, 4).smem_x == false || sel_layout(nw, 8).smem_x == false) return cudaErrorInvalidValue;
+  cudaError_t e = cudaSuccess;
+  k_ph_finish<<<dim3(pl.H, 2), kSelThreads, 0, st>>>(a);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  const bool need_ghi = (a.p.ablate_qi && !a.p.ablate_hi) || (!a.p.ablate_qi && !a.p.ablate_hi && !a.p.entropy_adaptive);
+  auto cluster_launch = [&](const void* fn, int grid, int cdim, size_t smem) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kSelThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cdim;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void* args[] = {const_cast<PhArgs*>(&a)};
+    return cudaLaunchKernelExC(&cfg, fn, args);
+  };
+  if (need_ghi) {
+    const size_t sm = sel_layout(nw, 8).total;
+    if ((e = ensure_dynamic_smem((const void*)k_ph_ghi, sm)) != cudaSuccess) return e;
+    if ((e = cluster_launch((const void*)k_ph_ghi, 8, 8, sm)) != cudaSuccess) return e;
+  }
+  const size_t sm = sel_layout(nw, 4).total;
+  if ((e = ensure_dynamic_smem((const void*)k_ph_select, sm)) != cudaSuccess) return e;
+  return cluster_launch((const void*)k_ph_select, pl.H * 8, 8, sm);
+}
+
+// ---------------------------------------------------------------------------
 // H2O column sums and bridge importance (one CTA)
 // ---------------------------------------------------------------------------
 // full_attn.sum(dim=0) (PU:3216) for pooled rows R:  colsum_R[j] + h[j] * E[j],
@@ -1004,6 +1251,10 @@ int select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const 
     return CKV_ERR_ARG;
   }
   if (n < p->max_capacity_prompt) { *why = "n < max_capacity_prompt: nothing to select"; return CKV_ERR_ARG; }
+  if (p->per_head_eviction) {
+    *why = "per-head selection needs the window attention: use ckv_score_evict";
+    return CKV_ERR_UNSUPPORTED;
+  }
   if (p->combination_mode == CKV_COMB_WEIGHTED) {
     *why = "ckv_select_scores_noalloc: combination_mode 'weighted' needs ckv_select_scores (workspace)";
     return CKV_ERR_UNSUPPORTED;

@@ -21,6 +21,16 @@ struct SelArgs {
   int parts;             // CTAs per score vector (set by launch_select)
 };
 
+// Per-head eviction: finishing, global HI ranks and the per-head selection.
+struct PhArgs {
+  Plan pl;
+  ckv_params p;
+  char* ws;
+  int32_t* out_idx;    // [H][s + kk]
+  float eq, eh;        // qi_gamma^(K/2), hi_gamma^(K/2)
+};
+cudaError_t launch_ph_select(const PhArgs& a, cudaStream_t st);
+
 size_t select_smem_bytes_n(int n);
 cudaError_t launch_select(const SelArgs& a, cudaStream_t st);
 // Selection stage with its scratch in a static device array (no workspace argument).

@@ -32,6 +32,7 @@ namespace ckv {
 
 __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh);
 CKV_DEV float sum_parts(const float* base, int nparts, size_t stride, int first, int step);
+template <int DT> size_t pool_smem(const Plan& pl);
 
 constexpr float kGeps = 1.8420680743952367e-07f;   // -1e-8 * ln(1e-8): a clamped entry
 constexpr float kLog2Eps = -26.575424759098897f;     // log2(1e-8)
@@ -691,6 +692,137 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
     __syncthreads();
   }
 
+}
+
+// ---------------------------------------------------------------------------
+// per-head eviction pass (PU:2208-2382)
+// ---------------------------------------------------------------------------
+// Exact window probabilities (as in the pooling pass) reduced per head and column:
+// the query row p[h, W-1, j], the two-hop term sum_r q2w[h, r] p[h, r, j] with
+// q2w[h, r] = p[h, W-1, n-W+r], the column sum over the window rows, and the
+// query row's entropy partial sum_j p ln(p + 1e-10) per tile.  The prelude launch
+// covers only the tiles holding the window columns and writes q2w from the same
+// MMA tiles, so both launches see bit-identical probabilities.
+template <int DT>
+__global__ void __launch_bounds__(256) k_ph_pass(WinArgs a, int prelude) {
+  using WT = WarpTile<DT>;
+  constexpr int MT = WT::MT;
+  extern __shared__ __align__(128) char smem[];
+  const Plan& pl = a.pl;
+  const int tile = prelude ? (pl.n_p / kColTile + (int)blockIdx.x) : (int)blockIdx.x;
+  const int j0 = tile * kColTile;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  char* sQ = smem;
+  char* sK = sQ + pl.rows_per_batch * row_bytes<DT>();
+  float* sP = reinterpret_cast<float*>(sK + pl.ktiles_per_batch * kColTile * row_bytes<DT>());
+  const char** srcs =
+      reinterpret_cast<const char**>(sP + pl.rows_per_batch * kStageStride) + 1;
+  __shared__ float sq2w[kWarps * 32];            // the batch's q2w rows (rows_per_batch <= 256)
+  __shared__ float part[2][4][kColTile];
+  __shared__ float entw[2];
+  const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);
+  float* q2w = reinterpret_cast<float*>(a.ws + pl.off_ph_q2w);
+  float* qrow = reinterpret_cast<float*>(a.ws + pl.off_ph_qrow);
+  float* two = reinterpret_cast<float*>(a.ws + pl.off_ph_two);
+  float* col = reinterpret_cast<float*>(a.ws + pl.off_ph_col);
+  float* entp = reinterpret_cast<float*>(a.ws + pl.off_ph_ent);
+  const float scale = sqrtf((float)pl.D);
+  const float inv_scale = 1.0f / scale;
+  const int pc = threadIdx.x % kColTile, pr0 = threadIdx.x / kColTile;
+  const int W = pl.W;
+  for (int b = 0; b < pl.nbatch; ++b) {
+    const BatchGeom bg = batch_geom(pl, b);
+    __syncthreads();
+    stage_q<DT>(a, bg, sQ, srcs);
+    stage_k<DT>(a, bg, j0, sK, srcs);
+    cp_async_commit();
+    if (!prelude)
+      for (int i = threadIdx.x; i < pl.heads_per_batch * W; i += blockDim.x) sq2w[i] = __ldcg(q2w + bg.h0 * W + i);
+    cp_async_wait<0>();
+    __syncthreads();
+    const int row0 = warp * pl.rows_per_warp;
+    const int hl = row0 / W;
+    const int kt = (bg.h0 + hl) / pl.G - bg.g0;
+    float acc[MT][8][4];
+    WT::compute(sQ, sK + kt * kColTile * row_bytes<DT>(), row0, acc);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int rl = row0 + mt * 16 + (lane >> 2) + 8 * hf;
+        const int h = bg.h0 + rl / W, r = rl % W;
+        const int lim = pl.n - W + r;
+        const float L = lse[h * W + r];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          float pv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = j0 + nt * 8 + 2 * (lane & 3) + e;
+            float p = 0.f;
+            if (j <= lim) p = ex2(logit_of<DT>(acc[mt][nt][2 * hf + e], scale, inv_scale) * kLog2e - L);
+            pv[e] = p;
+          }
+          *reinterpret_cast<float2*>(sP + rl * kStageStride + nt * 8 + 2 * (lane & 3)) =
+              make_float2(pv[0], pv[1]);
+        }
+      }
+    __syncthreads();
+    if (prelude) {
+      for (int i = threadIdx.x; i < pl.heads_per_batch * kColTile; i += blockDim.x) {
+        const int hh = i / kColTile, c = i % kColTile, j = j0 + c;
+        if (j >= pl.n_p && j < pl.n) q2w[(bg.h0 + hh) * W + (j - pl.n_p)] = sP[(hh * W + W - 1) * kStageStride + c];
+      }
+      continue;
+    }
+    for (int hh = 0; hh < pl.heads_per_batch; ++hh) {
+      const int h = bg.h0 + hh;
+      float s2 = 0.f, sc = 0.f;
+      for (int r = pr0; r < W; r += 4) {
+        const float p = sP[(hh * W + r) * kStageStride + pc];
+        s2 = fmaf(sq2w[hh * W + r], p, s2);
+        sc += p;
+      }
+      part[0][pr0][pc] = s2;
+      part[1][pr0][pc] = sc;
+      __syncthreads();
+      if (threadIdx.x < kColTile) {
+        const int j = j0 + threadIdx.x;
+        const float qa = sP[(hh * W + W - 1) * kStageStride + threadIdx.x];
+        if (j < pl.n) {
+          two[(size_t)h * pl.n + j] = (part[0][0][threadIdx.x] + part[0][1][threadIdx.x]) +
+                                      (part[0][2][threadIdx.x] + part[0][3][threadIdx.x]);
+          col[(size_t)h * pl.n + j] = (part[1][0][threadIdx.x] + part[1][1][threadIdx.x]) +
+                                      (part[1][2][threadIdx.x] + part[1][3][threadIdx.x]);
+          qrow[(size_t)h * pl.n + j] = qa;
+        }
+        const float t = j < pl.n ? qa * logf(qa + 1e-10f) : 0.f;
+        const float ws_ = warp_sum(t);
+        if (lane == 0) entw[warp] = ws_;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) entp[(size_t)tile * pl.H + h] = entw[0] + entw[1];
+    }
+  }
+}
+
+template <int DT>
+static cudaError_t launch_ph_pass_t(const WinArgs& a, cudaStream_t st) {
+  const Plan& pl = a.pl;
+  const size_t sm = pool_smem<DT>(pl);
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_ph_pass<DT>, sm); if (e != cudaSuccess) return e; }
+  const int t0 = pl.n_p / kColTile, t1 = (pl.n - 1) / kColTile;
+  k_ph_pass<DT><<<t1 - t0 + 1, 256, sm, st>>>(a, 1);
+  k_ph_pass<DT><<<pl.ncol_tiles, 256, sm, st>>>(a, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ph_pass(const WinArgs& a, cudaStream_t st) {
+  switch (a.pl.dtype) {
+    case CKV_BF16: return launch_ph_pass_t<CKV_BF16>(a, st);
+    case CKV_FP16: return launch_ph_pass_t<CKV_FP16>(a, st);
+    default: return launch_ph_pass_t<CKV_FP32>(a, st);
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -24,6 +24,8 @@ struct WinArgs {
 size_t window_smem_bytes(const Plan& pl, bool pool);
 cudaError_t launch_window(const WinArgs& a, cudaStream_t st);
 cudaError_t launch_window_stage(const WinArgs& a, int stage, cudaStream_t st);
+// Per-head eviction pass: query rows, two-hop terms, column sums, query-row entropy.
+cudaError_t launch_ph_pass(const WinArgs& a, cudaStream_t st);
 // Column sums / row sums / window chain of pooled rows already in the workspace.
 cudaError_t launch_rows_prep(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st);
 

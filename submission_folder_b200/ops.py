@@ -75,10 +75,19 @@ def make_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Layer:
     return L
 
 
+def _index_tensor(p: Params, heads: int, out_len: int, dev: torch.device) -> torch.Tensor:
+    """Kept-position output: ``[out_len - W]`` (shared) or ``[H, out_len - W]`` (per head)."""
+    nidx = max(out_len - p.window_size, 1)
+    if p.per_head_eviction:
+        return torch.empty(heads, nidx, dtype=torch.int32, device=dev)
+    return torch.empty(nidx, dtype=torch.int32, device=dev)
+
+
 def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 want_scores: bool = False) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor,
                                                      Optional[torch.Tensor]]:
-    """One layer: returns ``(k_out [H,B,D], v_out [H,B,D], keep_idx [B-W] int32, scores)``.
+    """One layer: returns ``(k_out [H,B,D], v_out [H,B,D], keep_idx, scores)``; ``keep_idx``
+    is ``[B-W]`` int32 (shared eviction) or ``[H, B-W]`` (per-head eviction).
 
     ``scores`` (when requested) is ``[2, n]`` fp32: the two vectors ranked by the
     selection (QI / HI after smoothing for "dis"; influence / H2O for "max").
@@ -90,8 +99,7 @@ def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     dev = q.device
     k_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
     v_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
-    nidx = max(out_len - p.window_size, 1)
-    idx = torch.empty(nidx, dtype=torch.int32, device=dev)
+    idx = _index_tensor(p, H, out_len, dev)
     scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
     ws = workspace(workspace_size(p, n, H, k.shape[0], D), dev)
     O = Outputs()
@@ -129,7 +137,7 @@ def score_evict_batched(params, layers, want_scores: bool = False):
         out_len = output_len(p, n)
         k_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
         v_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
-        idx = torch.empty(max(out_len - p.window_size, 1), dtype=torch.int32, device=dev)
+        idx = _index_tensor(p, H, out_len, dev)
         scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
         Os[i].out_k, Os[i].out_v, Os[i].out_idx, Os[i].out_scores = (k_out.data_ptr(), v_out.data_ptr(),
                                                                      idx.data_ptr(), _ptr(scores))

@@ -271,6 +271,74 @@ def test_weighted_selection_exact(n, budget, w):
     np.testing.assert_array_equal(got, ref)
 
 
+def _per_head_run(c, kwargs, dev):
+    q, k, v = inputs(c)
+    cl = CircuitKVCluster(**kwargs)
+    K, V = repeat_kv(k, 4).to(dev), repeat_kv(v, 4).to(dev)
+    ko, vo = cl.update_kv(K, q[None].to(dev), V, None, 4)
+    torch.cuda.synchronize()
+    idx = cl.last_keep_indices.cpu().numpy()
+    nk = idx.shape[1]
+    hk = torch.from_numpy(idx).long().to(dev)
+    for h in range(idx.shape[0]):
+        assert np.all(np.diff(idx[h]) > 0)
+        assert torch.equal(ko[0, h, :nk], K[0, h, hk[h]])
+        assert torch.equal(vo[0, h, :nk], V[0, h, hk[h]])
+        assert torch.equal(ko[0, h, nk:], K[0, h, c["n"] - c["window"]:])
+    return q, k, idx
+
+
+@pytest.mark.parametrize("name", ["bf16_perhead", "bf16_perhead_hub"])
+def test_per_head_matches_reference(name):
+    """Per-head eviction (PU:2208-2382, 3296-3464) end to end vs the reference's kept sets."""
+    dev = _cuda()
+    c = case(name)
+    g = load(name)
+    _, _, idx = _per_head_run(c, c["kwargs"], dev)
+    ref = g["keep_per_head"]
+    assert idx.shape == ref.shape
+    d = [len(set(idx[h].tolist()) ^ set(ref[h].tolist())) for h in range(ref.shape[0])]
+    assert max(d) <= 4 and np.mean(d) <= 1.0, d
+    assert ops.read_status(dev) == 0
+
+
+@pytest.mark.parametrize("extra", [dict(ablate_qi=True), dict(ablate_hi=True),
+                                   dict(ablate_qi=True, ablate_hi=True), dict(entropy_adaptive=False),
+                                   dict(smoothing_kernel=3), dict(true_hub_hi=True, entropy_adaptive=False)])
+def test_per_head_variants_match_oracle(extra):
+    dev = _cuda()
+    c = case("bf16_perhead")
+    kwargs = dict(c["kwargs"], **extra)
+    q, k, idx = _per_head_run(c, kwargs, dev)
+    op = oracle_params(dict(c, kwargs=kwargs))
+    attn = O.window_attention(q.float().numpy(), k.float().numpy(), c["window"], 4, c["dtype"])
+    oidx = O.per_head_select(attn, op, c["n"])
+    d = [len(set(idx[h].tolist()) ^ set(oidx[h].tolist())) for h in range(oidx.shape[0])]
+    assert max(d) <= 4 and np.mean(d) <= 1.0, (extra, d)
+
+
+def test_per_head_fp32_ragged():
+    """fp32 inputs, W = 32, n not a multiple of the column tile."""
+    dev = _cuda()
+    torch.manual_seed(3)
+    from submission_folder_b200.synth import make_layer
+    n, W = 3001, 32
+    q, k, v = make_layer(n, seed=5, window=W, dtype="fp32")
+    kwargs = dict(window_size=W, max_capacity_prompt=300, per_head_eviction=True, qi_kernel_size=3,
+                  hi_kernel_size=5, use_gaussian=True)
+    cl = CircuitKVCluster(**kwargs)
+    K, V = repeat_kv(k, 4).to(dev), repeat_kv(v, 4).to(dev)
+    ko, vo = cl.update_kv(K, q[None].to(dev), V, None, 4)
+    torch.cuda.synchronize()
+    idx = cl.last_keep_indices.cpu().numpy()
+    op = O.Params(**kwargs)
+    attn = O.window_attention(q.numpy(), k.numpy(), W, 4, "fp32")
+    oidx = O.per_head_select(attn, op, n)
+    d = [len(set(idx[h].tolist()) ^ set(oidx[h].tolist())) for h in range(32)]
+    assert max(d) <= 4 and np.mean(d) <= 1.0, d
+    assert ops.read_status(dev) == 0
+
+
 def test_short_sequence_returns_inputs():
     dev = _cuda()
     c = case("bf16_n2048_default")
