@@ -208,18 +208,51 @@ int ckv_window_pool(const ckv_params* p, const ckv_layer* layer, void* workspace
                     ckv_stream_t stream);
 
 /* ---- influence walker (legacy use_neumann=False path) ------------------------
- * Replaces CircuitGraph.update_and_step_influence_walker + get_influence_scores
- * (CircuitKV/csrc/pybind.cpp:263-300; circuit_manager.cpp:1190-1311;
- * influence_walker.cu:66-456) on the structured full_attn defined by pooled
- * window rows [W, n] fp32 (PU:3003-3027).  rng_mode 0 = Philox4x32-10
- * (counter-based; stream = (seed, walker id, step)), 1 = PCG-XSH-RR seeded as
- * the reference (seed + 3000 by CircuitGraph, per walker pcg_init(seed + id, id)).
- * Writes normalised scores [n] (and raw visit counts [n] if visits != NULL). */
-int ckv_influence_walk(const ckv_params* p, int32_t n, const float* rows, int32_t current_idx,
+ * Replaces CircuitGraph.update_and_step_influence_walker + get_influence_scores /
+ * get_influence_raw_visits (CircuitKV/csrc/pybind.cpp:263-300; circuit_manager.cpp:
+ * 1190-1311; influence_walker.cu:66-456).  Walkers step along full_attn rows; visits
+ * are counted per landing position, divided by sqrt(n - p + 1), normalised by their
+ * maximum (over the first min(n, 65536) positions, as the reference) and the sinks set
+ * to 1.  rng_mode CKV_RNG_PCG: PCG-XSH-RR, walker w seeded (seed, w) as the reference's
+ * init_rng_kernel (circuit_walker.cu:157-171; CircuitGraph passes its constructor
+ * seed + 3000); CKV_RNG_PHILOX: Philox4x64-10,
+ * key (seed, 0), counter (draw / 4, walker, call, 0).  rng_state: device uint64
+ * [2 * num_walkers] (PCG states; for Philox [0] counts the calls) kept by the caller
+ * across calls as the reference keeps its states, or NULL to seed on every call;
+ * init_state = 1 seeds it first.  Argument checks follow the reference
+ * (circuit_manager.cpp:1200-1226). */
+enum ckv_rng_mode { CKV_RNG_PHILOX = 0, CKV_RNG_PCG = 1 };
+
+/* Dense form: attn [n, n] fp32 row-major on the device (the reference's input). */
+int ckv_influence_walk_dense(const float* attn, int32_t n, int32_t current_idx, int32_t num_walkers,
+                             int32_t max_steps, int32_t sink_size, float temperature, float explore_temp,
+                             float explore_ratio, int32_t rng_mode, uint64_t seed, uint64_t* rng_state,
+                             int32_t init_state, float* visits, float* scores, ckv_stream_t stream);
+
+/* Structured form for the hook (PU:3244-3263): full_attn defined by pooled window rows
+ * rows [W, ld] fp32 (PU:3003-3034), never materialised, so n is not limited by n^2
+ * memory.  Also writes h2o [n] = full_attn column sums (PU:3253).  workspace:
+ * ckv_walk_workspace_size bytes, 256-byte aligned. */
+int ckv_walk_workspace_size(int32_t n, int32_t window, size_t* bytes);
+int ckv_influence_walk(const float* rows, int32_t W, int32_t ld, int32_t n, int32_t current_idx,
                        int32_t num_walkers, int32_t max_steps, int32_t sink_size, float temperature,
-                       float explore_temp, float explore_ratio, uint64_t seed, int32_t rng_mode,
-                       void* workspace, size_t workspace_bytes, float* scores, float* visits,
-                       ckv_stream_t stream);
+                       float explore_temp, float explore_ratio, int32_t rng_mode, uint64_t seed,
+                       uint64_t* rng_state, int32_t init_state, void* workspace, size_t workspace_bytes,
+                       float* visits, float* scores, float* h2o, ckv_stream_t stream);
+
+/* Raw generator output (no reference counterpart; tests and callers that reproduce a
+ * walk): CKV_RNG_PHILOX: out[i] = Philox4x64-10(key (seed, 0), counter (i / 4, stream_id,
+ * 0, 0))[i % 4]; CKV_RNG_PCG: out[i] = the i-th pcg32 output of the state seeded
+ * (seed, stream_id), i.e. pcg32_srandom_r(seed, stream_id). */
+int ckv_rng_fill(int32_t mode, uint64_t seed, uint64_t stream_id, int32_t count, uint64_t* out,
+                 ckv_stream_t stream);
+
+/* K / V compaction alone (PU:3496-3517 shared, PU:3448-3462 per head): the `kept`
+ * positions idx ([kept] or [H, kept] with per_head) then the last `window` rows, into
+ * [H, kept + window, D] outputs.  For callers that chose the positions themselves (the
+ * influence-walker path). */
+int ckv_gather(const ckv_layer* layer, int32_t window, const int32_t* idx, int32_t kept, int32_t per_head,
+               void* out_k, void* out_v, ckv_stream_t stream);
 
 /* Per-stage timing (no counterpart in the reference; for benchmarks): while
  * set, each ckv_score_evict call on this thread records events[0] before its

@@ -156,6 +156,8 @@ class CircuitKVCluster:
         # state of the last call (for callers that want the kept positions)
         self.last_keep_indices: Optional[torch.Tensor] = None
         self._graph = None
+        self._walk_rng = None         # influence-walker PCG states (use_neumann=False)
+        self._walk_rng_init = True
         self._device = None
 
     def reset(self, window_size: int = 64, max_capacity_prompt: int = 2048, kernel_size: int = 5,
@@ -188,10 +190,6 @@ class CircuitKVCluster:
         p.hi_gamma = float(self.hi_gamma)
         mode = self.combination_mode
         if mode not in ("dis", "union", "union_da"):
-            if not self.use_neumann:
-                raise NotImplementedError(
-                    "use_neumann=False (influence-walker scoring) is served by "
-                    "circuit_kv._C.CircuitGraph.update_and_step_influence_walker")
             mode = "weighted" if mode == "weighted" else "max"
         p.combination_mode = _lib.COMB_CODES[mode]
         p.h2o_weight = float(self.h2o_weight)
@@ -246,12 +244,34 @@ class CircuitKVCluster:
             q = qd
             k, v = _to_device_by_head(k, dev), _to_device_by_head(v, dev)
         p = self.params(q_len)
-        k_out, v_out, idx, _ = ops.score_evict(p, q, k, v)
+        if not self.use_neumann and self.combination_mode not in ("dis", "union", "union_da"):
+            k_out, v_out, idx = self._walker_path(p, q, k, v, q_len)
+        else:
+            k_out, v_out, idx, _ = ops.score_evict(p, q, k, v)
         self.last_keep_indices = idx
         k_out, v_out = k_out.unsqueeze(0), v_out.unsqueeze(0)
         if host:
             k_out, v_out = k_out.cpu(), v_out.cpu()
         return k_out, v_out
+
+    def _walker_path(self, p, q, k, v, q_len):
+        """use_neumann=False (PU:3244-3263): pooled window rows, the influence walker on
+        the structured full_attn (its PCG states kept across calls like the reference's
+        CircuitGraph, seeded once with 42 + 3000), H2O = full_attn column sums, rank MAX,
+        keep mask, gather."""
+        _, _, _, rows_qi, _ = ops.window_pool(p, q, k)
+        if self._walk_rng is None or self._walk_rng.device != q.device:
+            self._walk_rng = torch.zeros(2 * 10000, dtype=torch.int64, device=q.device)
+            self._walk_rng_init = True
+        scores, _, h2o = ops.influence_walk(rows_qi, q_len - 1, int(self.num_walkers), int(self.max_steps),
+                                            int(self.sink_size), rng_state=self._walk_rng,
+                                            init_state=self._walk_rng_init)
+        self._walk_rng_init = False
+        pm = self.params(q_len)
+        pm.combination_mode = _lib.COMB_CODES["max"]
+        idx, _ = ops.select_scores(pm, scores, h2o)
+        k_out, v_out = ops.gather(q, k, v, int(self.window_size), idx)
+        return k_out, v_out, idx
 
     @staticmethod
     def _views(query_states, key_states, value_states, groups, num_heads):

@@ -16,6 +16,7 @@
 #include "ckv_neumann.h"
 #include "ckv_plan.h"
 #include "ckv_select.h"
+#include "ckv_walker.h"
 #include "ckv_window.h"
 
 namespace ckv {
@@ -557,15 +558,114 @@ int ckv_window_pool(const ckv_params* p, const ckv_layer* layer, void* workspace
   return e == cudaSuccess ? CKV_OK : cuda_fail(e, "window stage");
 }
 
-int ckv_influence_walk(const ckv_params* p, int32_t n, const float* rows, int32_t current_idx,
+static int check_walk(int32_t n, int32_t current_idx, int32_t num_walkers, int32_t max_steps,
+                      int32_t sink_size, float temperature, float explore_temp, float explore_ratio,
+                      int32_t rng_mode) {
+  // the reference's argument checks (circuit_manager.cpp:1200-1226)
+  if (n < 1) return fail(CKV_ERR_ARG, "seq_len must be >= 1");
+  if (current_idx < 0 || current_idx >= n) return fail(CKV_ERR_ARG, "current_idx out of bounds");
+  if (num_walkers < 1) return fail(CKV_ERR_ARG, "num_walkers must be >= 1");
+  if (max_steps <= 0 || max_steps > 100) return fail(CKV_ERR_ARG, "max_steps must be in (0, 100]");
+  if (sink_size < 0 || sink_size >= n) return fail(CKV_ERR_ARG, "sink_size out of bounds");
+  if (!(temperature >= 0.1f && temperature <= 100.0f)) return fail(CKV_ERR_ARG, "temperature must be in [0.1, 100.0]");
+  if (!(explore_temp >= 0.1f && explore_temp <= 100.0f)) return fail(CKV_ERR_ARG, "explore_temp must be in [0.1, 100.0]");
+  if (!(explore_ratio >= 0.0f && explore_ratio <= 1.0f)) return fail(CKV_ERR_ARG, "explore_ratio must be in [0.0, 1.0]");
+  if (rng_mode != CKV_RNG_PHILOX && rng_mode != CKV_RNG_PCG) return fail(CKV_ERR_ARG, "unknown rng_mode");
+  return CKV_OK;
+}
+
+static WalkArgs walk_args(int32_t n, int32_t current_idx, int32_t num_walkers, int32_t max_steps,
+                          int32_t sink_size, float temperature, float explore_temp, float explore_ratio,
+                          int32_t rng_mode, uint64_t seed, uint64_t* rng_state, int32_t init_state,
+                          float* visits, float* scores) {
+  WalkArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n = n; a.current_idx = current_idx; a.num_walkers = num_walkers; a.max_steps = max_steps;
+  a.sink = sink_size;
+  a.inv_temp = 1.0f / fmaxf(temperature, 0.1f);
+  a.inv_explore_temp = 1.0f / fmaxf(explore_temp, 0.1f);
+  a.explore_ratio = explore_ratio;
+  a.rng_mode = rng_mode; a.seed = seed; a.rng_state = rng_state; a.init_state = init_state;
+  a.visits = visits; a.scores = scores;
+  return a;
+}
+
+int ckv_influence_walk_dense(const float* attn, int32_t n, int32_t current_idx, int32_t num_walkers,
+                             int32_t max_steps, int32_t sink_size, float temperature, float explore_temp,
+                             float explore_ratio, int32_t rng_mode, uint64_t seed, uint64_t* rng_state,
+                             int32_t init_state, float* visits, float* scores, ckv_stream_t stream) {
+  if (!attn || !visits || !scores) return fail(CKV_ERR_ARG, "null argument");
+  int rc = check_walk(n, current_idx, num_walkers, max_steps, sink_size, temperature, explore_temp,
+                      explore_ratio, rng_mode);
+  if (rc) return rc;
+  WalkArgs a = walk_args(n, current_idx, num_walkers, max_steps, sink_size, temperature, explore_temp,
+                         explore_ratio, rng_mode, seed, rng_state, init_state, visits, scores);
+  a.attn = attn;
+  const cudaError_t e = launch_walk_dense(a, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "influence walker (dense)");
+}
+
+static size_t walk_ws_bytes(int32_t n, int32_t W) {
+  const size_t n_p = n > W ? (size_t)(n - W) : 1;
+  return align256(n_p * 4) + align256(n_p * 4) + align256((n_p + 1) * 2 * 8);
+}
+
+int ckv_walk_workspace_size(int32_t n, int32_t window, size_t* bytes) {
+  if (!bytes || n < 1 || window < 1) return fail(CKV_ERR_ARG, "bad argument");
+  *bytes = walk_ws_bytes(n, window);
+  return CKV_OK;
+}
+
+int ckv_influence_walk(const float* rows, int32_t W, int32_t ld, int32_t n, int32_t current_idx,
                        int32_t num_walkers, int32_t max_steps, int32_t sink_size, float temperature,
-                       float explore_temp, float explore_ratio, uint64_t seed, int32_t rng_mode,
-                       void* workspace, size_t workspace_bytes, float* scores, float* visits,
-                       ckv_stream_t stream) {
-  (void)p; (void)n; (void)rows; (void)current_idx; (void)num_walkers; (void)max_steps;
-  (void)sink_size; (void)temperature; (void)explore_temp; (void)explore_ratio; (void)seed;
-  (void)rng_mode; (void)workspace; (void)workspace_bytes; (void)scores; (void)visits; (void)stream;
-  return fail(CKV_ERR_UNSUPPORTED, "influence walker is not built yet");
+                       float explore_temp, float explore_ratio, int32_t rng_mode, uint64_t seed,
+                       uint64_t* rng_state, int32_t init_state, void* workspace, size_t workspace_bytes,
+                       float* visits, float* scores, float* h2o, ckv_stream_t stream) {
+  if (!rows || !visits || !scores || !h2o || !workspace) return fail(CKV_ERR_ARG, "null argument");
+  if (W < 1 || W >= n || ld < n) return fail(CKV_ERR_ARG, "need 1 <= W < n and ld >= n");
+  int rc = check_walk(n, current_idx, num_walkers, max_steps, sink_size, temperature, explore_temp,
+                      explore_ratio, rng_mode);
+  if (rc) return rc;
+  if (workspace_bytes < walk_ws_bytes(n, W) || (uintptr_t)workspace % 256 != 0)
+    return fail(CKV_ERR_WORKSPACE, "walker workspace too small or not 256-byte aligned");
+  WalkArgs a = walk_args(n, current_idx, num_walkers, max_steps, sink_size, temperature, explore_temp,
+                         explore_ratio, rng_mode, seed, rng_state, init_state, visits, scores);
+  const size_t n_p = (size_t)(n - W);
+  char* ws = static_cast<char*>(workspace);
+  float* hbuf = reinterpret_cast<float*>(ws);
+  float* cinv = reinterpret_cast<float*>(ws + align256(n_p * 4));
+  double* pre = reinterpret_cast<double*>(ws + 2 * align256(n_p * 4));
+  a.rows = rows; a.W = W; a.ld = ld; a.pre = pre; a.cinv = cinv; a.h2o = h2o;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = launch_walk_prep(a, hbuf, cinv, pre, st);
+  if (e == cudaSuccess) e = launch_walk_rows(a, st);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "influence walker");
+}
+
+int ckv_rng_fill(int32_t mode, uint64_t seed, uint64_t stream_id, int32_t count, uint64_t* out,
+                 ckv_stream_t stream) {
+  if (!out || count < 0 || (mode != CKV_RNG_PHILOX && mode != CKV_RNG_PCG)) return fail(CKV_ERR_ARG, "bad argument");
+  if (count == 0) return CKV_OK;
+  const cudaError_t e = launch_rng_fill(mode, seed, stream_id, count, out, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "rng fill");
+}
+
+int ckv_gather(const ckv_layer* layer, int32_t window, const int32_t* idx, int32_t kept, int32_t per_head,
+               void* out_k, void* out_v, ckv_stream_t stream) {
+  int rc = check_layer(layer);
+  if (rc) return rc;
+  if (!idx || !out_k || !out_v || kept < 0 || window < 0 || window > layer->n)
+    return fail(CKV_ERR_ARG, "bad gather argument");
+  if (layer->num_heads % layer->num_kv_heads != 0) return fail(CKV_ERR_ARG, "num_heads % num_kv_heads != 0");
+  GatherArgs g;
+  g.k = layer->k; g.khs = layer->k_head_stride; g.kts = layer->k_tok_stride;
+  g.v = layer->v; g.vhs = layer->v_head_stride; g.vts = layer->v_tok_stride;
+  g.out_k = out_k; g.out_v = out_v; g.idx = idx;
+  g.n = layer->n; g.W = window; g.H = layer->num_heads; g.Hkv = layer->num_kv_heads;
+  g.G = layer->num_heads / layer->num_kv_heads; g.D = layer->head_dim;
+  g.out_len = kept + window; g.per_head = per_head ? 1 : 0; g.identity = 0;
+  const cudaError_t e = launch_gather(g, layer->dtype, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "gather");
 }
 
 int ckv_set_stage_events(void* const* events, int32_t count) {

@@ -220,3 +220,88 @@ def window_pool(p: Params, q: torch.Tensor, k: torch.Tensor):
                                       sets.data_ptr() + 8, rq.data_ptr(), rh.data_ptr(), _stream(dev)),
           "ckv_window_pool")
     return ent, mass, sets, rq, rh
+
+
+# ---------------------------------------------------------------------------
+# influence walker (legacy use_neumann=False path) and stand-alone gather
+# ---------------------------------------------------------------------------
+def walk_workspace_size(n: int, window: int) -> int:
+    out = ctypes.c_size_t()
+    check(_lib.load().ckv_walk_workspace_size(n, window, ctypes.byref(out)), "ckv_walk_workspace_size")
+    return out.value
+
+
+def _check_rng_state(rng_state: Optional[torch.Tensor], rng_mode: int, num_walkers: int) -> None:
+    if rng_state is None:
+        return
+    need = 2 * num_walkers if rng_mode == _lib.RNG_PCG else 1
+    if rng_state.dtype != torch.int64 or not rng_state.is_contiguous() or rng_state.numel() < need:
+        raise ValueError(f"rng_state must be a contiguous int64 tensor of at least {need} elements")
+
+
+def influence_walk(rows: torch.Tensor, current_idx: int, num_walkers: int = 10000, max_steps: int = 10,
+                   sink_size: int = 4, temperature: float = 2.0, explore_temp: float = 10.0,
+                   explore_ratio: float = 0.3, rng_mode: int = _lib.RNG_PCG, seed: int = 42 + 3000,
+                   rng_state: Optional[torch.Tensor] = None, init_state: bool = False):
+    """Walker on the full_attn defined by pooled window rows ``[W, n]`` fp32 (structured,
+    never materialised).  Returns ``(scores [n], visits [n], h2o [n])``."""
+    _require_cuda(rows, rng_state)
+    _check_rng_state(rng_state, rng_mode, num_walkers)
+    rows = rows.float().contiguous()
+    W, n = rows.shape
+    dev = rows.device
+    ws = torch.empty((walk_workspace_size(n, W) + 255) // 256 * 256 + 256, dtype=torch.uint8, device=dev)
+    base = (ws.data_ptr() + 255) // 256 * 256
+    scores = torch.empty(n, dtype=torch.float32, device=dev)
+    visits = torch.empty(n, dtype=torch.float32, device=dev)
+    h2o = torch.empty(n, dtype=torch.float32, device=dev)
+    check(_lib.load().ckv_influence_walk(rows.data_ptr(), W, n, n, current_idx, num_walkers, max_steps, sink_size,
+                                         temperature, explore_temp, explore_ratio, rng_mode, seed,
+                                         _ptr(rng_state), int(init_state), ctypes.c_void_p(base),
+                                         ws.numel() - (base - ws.data_ptr()), visits.data_ptr(),
+                                         scores.data_ptr(), h2o.data_ptr(), _stream(dev)),
+          "ckv_influence_walk")
+    return scores, visits, h2o
+
+
+def influence_walk_dense(attn: torch.Tensor, current_idx: int, num_walkers: int = 10000, max_steps: int = 10,
+                         sink_size: int = 4, temperature: float = 2.0, explore_temp: float = 10.0,
+                         explore_ratio: float = 0.3, rng_mode: int = _lib.RNG_PCG, seed: int = 42 + 3000,
+                         rng_state: Optional[torch.Tensor] = None, init_state: bool = False,
+                         visits: Optional[torch.Tensor] = None, scores: Optional[torch.Tensor] = None):
+    """Walker on a dense ``[n, n]`` fp32 attention matrix; returns ``(scores, visits)``."""
+    _require_cuda(attn, rng_state)
+    _check_rng_state(rng_state, rng_mode, num_walkers)
+    if attn.dtype != torch.float32 or attn.dim() != 2 or attn.shape[0] != attn.shape[1] or not attn.is_contiguous():
+        raise ValueError("attn must be a contiguous square float32 matrix")
+    n = attn.shape[0]
+    dev = attn.device
+    scores = torch.empty(n, dtype=torch.float32, device=dev) if scores is None else scores
+    visits = torch.empty(n, dtype=torch.float32, device=dev) if visits is None else visits
+    check(_lib.load().ckv_influence_walk_dense(attn.data_ptr(), n, current_idx, num_walkers, max_steps,
+                                               sink_size, temperature, explore_temp, explore_ratio, rng_mode,
+                                               seed, _ptr(rng_state), int(init_state), visits.data_ptr(),
+                                               scores.data_ptr(), _stream(dev)), "ckv_influence_walk_dense")
+    return scores, visits
+
+
+def rng_fill(mode: int, seed: int, stream_id: int, count: int, device: torch.device) -> torch.Tensor:
+    """Raw generator outputs (uint64 values in an int64 tensor)."""
+    out = torch.empty(max(count, 1), dtype=torch.int64, device=device)
+    check(_lib.load().ckv_rng_fill(mode, seed, stream_id, count, out.data_ptr(), _stream(device)), "ckv_rng_fill")
+    return out[:count]
+
+
+def gather(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window: int, idx: torch.Tensor):
+    """K / V of the kept positions ``idx`` (``[kept]`` or ``[H, kept]``) then the last
+    ``window`` rows: ``[H, kept + window, D]`` each."""
+    _require_cuda(q, k, v, idx)
+    H, n, D = q.shape
+    L = make_layer(q, k, v)
+    idx = idx.to(torch.int32).contiguous()
+    kept = idx.shape[-1]
+    k_out = torch.empty(H, kept + window, D, dtype=k.dtype, device=k.device)
+    v_out = torch.empty(H, kept + window, D, dtype=k.dtype, device=k.device)
+    check(_lib.load().ckv_gather(ctypes.byref(L), window, idx.data_ptr(), kept, int(idx.dim() == 2),
+                                 k_out.data_ptr(), v_out.data_ptr(), _stream(k.device)), "ckv_gather")
+    return k_out, v_out
