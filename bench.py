@@ -347,13 +347,10 @@ def run_ours(args, rank, world):
     # kept-index metadata of every rank (the only collective of the data path)
     gathered = None
     if pg:
-        meta = torch.cat([i.to(torch.int32) for i in idxs])
-        allm = [torch.empty_like(meta) for _ in range(world)]
-        dist.all_gather(allm, meta)
-        gathered = int(sum(x.numel() for x in allm))
-        tms = torch.tensor([ms], device=dev)
-        dist.all_reduce(tms, op=dist.ReduceOp.MAX)
-        ms = float(tms.item())
+        from submission_folder_b200 import sharding
+        ms = sharding.max_over_ranks(ms, device=dev)
+        allk = sharding.gather_kept({rank * L + l: idxs[l] for l in range(L)}, device=dev)
+        gathered = int(sum(t.numel() for t in allk.values()))
 
     # device status of every layer's workspace slice (outside the timed region)
     st = ctypes.c_int32()
@@ -465,9 +462,8 @@ def e2e(args, rank, world, dev, bl, CircuitKVCluster, cli_cluster_kwargs, make_l
     torch.cuda.synchronize()
     sec = (time.perf_counter() - t) / args.e2e_steps
     if pg:
-        ts = torch.tensor([sec], device=dev)
-        dist.all_reduce(ts, op=dist.ReduceOp.MAX)
-        sec = float(ts.item())
+        from submission_folder_b200 import sharding
+        sec = sharding.max_over_ranks(sec, device=dev)
     return {"value": L * n * world / sec, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "s_per_step": sec,
             "api": "CircuitKVCluster.update_kv on pinned host tensors"}

@@ -124,7 +124,7 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.nscan = (pl.n_p + kScanChunk - 1) / kScanChunk;
   if (pl.nscan < 1) pl.nscan = 1;
   pl.tc_nclusters = pl.ncol_tiles < 148 ? pl.ncol_tiles : 148;   // CTAs of the tensor-core pooling pass
-  pl.e_parts = pl.tc_pool ? 4 * pl.tc_nclusters : pl.ncol_tiles;   // TC: one partial per (CTA, column quarter)
+  pl.e_parts = pl.tc_pool ? pl.tc_nclusters : pl.ncol_tiles;   // TC: one partial per CTA
   pl.rs_parts = pl.ncol_tiles;
   pl.g_slice = kColTile;
   if (window_smem_bytes(pl, true) > 227 * 1024 || window_smem_bytes(pl, false) > 227 * 1024) {
@@ -137,9 +137,10 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.off_stats = take(((size_t)pl.nstat_chunks * HW * 16 > (2 * HW + 2 * (size_t)pl.W) * 4)
                          ? (size_t)pl.nstat_chunks * HW * 16 : (2 * HW + 2 * (size_t)pl.W) * 4);
   pl.off_lse = take(HW * 4);
-  pl.off_spec = take((size_t)4 * H * 4);
-  pl.off_epart = take((size_t)4 * pl.ncol_tiles * HW * 4);
-  pl.off_mpart = take((size_t)4 * pl.ncol_tiles * HW * 4);
+  pl.off_spec = take((size_t)5 * H * 4);   // [H] ent, [H] mass (speculated), [H] ent, [H] mass (final), [H] bound
+  pl.off_minx = take((size_t)pl.nstat_chunks * HW * 4);
+  pl.off_epart = take((size_t)pl.e_parts * HW * 4);
+  pl.off_mpart = take((size_t)pl.e_parts * HW * 4);
   pl.off_rows_qi = take((size_t)pl.W * pl.n_pad * 4);
   pl.off_rows_hi = take((size_t)pl.W * pl.n_pad * 4);
   pl.off_colsum = take((size_t)2 * pl.n_pad * 4);
@@ -230,6 +231,7 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
   wa.q = L->q; wa.qhs = L->q_head_stride; wa.qts = L->q_tok_stride;
   wa.k = L->k; wa.khs = L->k_head_stride; wa.kts = L->k_tok_stride;
   wa.ws = ws; wa.fixup_pass = 0; wa.p = *p; wa.pl = pl;
+  wa.tc_min = 0; wa.force_exact = 0;
   if (pl.per_head) {   // PU:3296-3464: per-head importance and selection, per-head gather
     e = launch_window_stage(wa, 0, st);
     if (e != cudaSuccess) return cuda_fail(e, "window moments");
@@ -536,6 +538,7 @@ int ckv_window_pool(const ckv_params* p, const ckv_layer* layer, void* workspace
   wa.q = layer->q; wa.qhs = layer->q_head_stride; wa.qts = layer->q_tok_stride;
   wa.k = layer->k; wa.khs = layer->k_head_stride; wa.kts = layer->k_tok_stride;
   wa.ws = ws; wa.fixup_pass = 0; wa.p = q; wa.pl = pl;
+  wa.tc_min = 0; wa.force_exact = 1;   // the entropies and masses are outputs here
   for (int s = 0; s < 3 && e == cudaSuccess; ++s) {
     e = launch_window_stage(wa, s, st);
     if (e != cudaSuccess) {

@@ -25,7 +25,8 @@ struct alignas(16) Header {
   int32_t steps;           // Neumann terms taken (early stop)
   int32_t kept;            // prefix positions kept (selection output count)
   uint32_t tile_ctr[2];    // next column tile of the tensor-core pooling launch (pass, re-run)
-  int32_t pad[50];
+  int32_t need_exact;      // 1: the pooling pass recomputes the clamped entropy / mass exactly
+  int32_t pad[49];
   uint32_t cnt_group[64];  // arrival counters per head group of the stats kernel
 };
 static_assert(sizeof(Header) == 512, "header must be 512 bytes");
@@ -60,6 +61,7 @@ struct Plan {
   int nscan;          // ceil(n_p / kScanChunk)
   // workspace offsets (bytes from the layer workspace base)
   size_t off_stats, off_lse, off_lastlogit, off_spec, off_epart, off_mpart;
+  size_t off_minx;    // [nstat_chunks][H][W] row minimum of the rounded logits (tensor-core moments)
   size_t off_rows_qi, off_rows_hi, off_colsum, off_gtile, off_rspart;
   size_t off_wk, off_yk, off_ymax, off_bk, off_cg, off_agg, off_cum, off_cmax;
   size_t off_sel, off_ph;

@@ -255,6 +255,62 @@ __device__ void select_heads(const ckv_params& p, int H, const float* ent, const
   __syncthreads();
 }
 
+// Whether the head sets chosen from the moments pass's entropies and masses are the
+// ones the exact values would give (one thread).  The exact entropy of head h lies in
+// [ent[h], ent[h] + bnd[h]] (the clamp at 1e-8 only raises it; bnd bounds the raise),
+// up to rounding; the exact mass equals the moments pass's up to rounding.  A decision
+// is certain when every margin it depends on exceeds the bound plus a rounding slack
+// of 1e-5 relative; otherwise the pooling pass recomputes both exactly (and, if the
+// sets change, re-runs).  The slack is orders of magnitude above the fp32 rounding of
+// either computation.
+CKV_DEV float certainty_slack(float a, float b) { return 1e-5f * fmaxf(fabsf(a), fabsf(b)) + 1e-6f; }
+
+__device__ bool selection_certain(const ckv_params& p, int H, const float* ent, const float* mass,
+                                  const float* bnd, uint64_t qs) {
+  if (!p.entropy_aware) return true;
+  const int k = min(p.top_k_heads, H);
+  if (k < H) {
+    if (p.head_selection_mode == 1) {   // QI: the k heads of largest mass
+      float lo_in = INFINITY, hi_out = -INFINITY;
+      for (int h = 0; h < H; ++h) {
+        if ((qs >> h) & 1ull) lo_in = fminf(lo_in, mass[h]);
+        else hi_out = fmaxf(hi_out, mass[h]);
+      }
+      if (!(lo_in - hi_out > certainty_slack(lo_in, hi_out))) return false;
+    } else {                            // QI: the k heads of smallest entropy
+      float hi_in = -INFINITY, lo_out = INFINITY;
+      for (int h = 0; h < H; ++h) {
+        if ((qs >> h) & 1ull) hi_in = fmaxf(hi_in, ent[h] + bnd[h]);
+        else lo_out = fminf(lo_out, ent[h]);
+      }
+      if (!(lo_out - hi_in > certainty_slack(hi_in, lo_out))) return false;
+    }
+  }
+  if (p.hi_pooling_mode == 1) return true;   // HI: every head
+  if (p.hi_mass_cdf > 0.f || p.hi_top_k_heads > 0) {
+    // masses in descending order with clear gaps, and clear CDF crossings
+    float prev = INFINITY, cum = 0.f, total = 0.f;
+    for (int h = 0; h < H; ++h) total += mass[h];
+    uint64_t used = 0;
+    for (int i = 0; i < H; ++i) {
+      int best = -1;
+      for (int h = 0; h < H; ++h)
+        if (!((used >> h) & 1ull) && (best < 0 || mass[h] > mass[best])) best = h;
+      used |= 1ull << best;
+      const float m = mass[best];
+      if (i > 0 && !(prev - m > certainty_slack(prev, m))) return false;
+      prev = m;
+      cum += m;
+      if (p.hi_mass_cdf > 0.f && total > 0.f && !(fabsf(cum / total - p.hi_mass_cdf) > 1e-5f)) return false;
+    }
+    return true;
+  }
+  if (p.hi_mass_threshold > 0.f)
+    for (int h = 0; h < H; ++h)
+      if (!(fabsf(mass[h] - p.hi_mass_threshold) > certainty_slack(mass[h], p.hi_mass_threshold))) return false;
+  return true;
+}
+
 // ---------------------------------------------------------------------------
 // common per-CTA setup of the window kernels
 // ---------------------------------------------------------------------------
@@ -448,10 +504,12 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
   if (!last) return;
   __threadfence();
   float* lse = reinterpret_cast<float*>(a.ws + pl.off_lse);
-  float* spec = reinterpret_cast<float*>(a.ws + pl.off_spec);   // [H] entropy, [H] mass
+  float* spec = reinterpret_cast<float*>(a.ws + pl.off_spec);   // [H] entropy, [H] mass; [4H..5H) bounds
+  const float* minx = reinterpret_cast<const float*>(a.ws + pl.off_minx);
   const int nrows = nh * pl.W, i0 = h0 * pl.W;
   float* rowE = reinterpret_cast<float*>(smem);                  // [nrows]
   float* rowM = rowE + nrows;
+  float* rowB = rowM + nrows;
   // tpr consecutive lanes share a row; each merges every tpr-th chunk, 8 loads in flight
   int tpr = 1;
   while (tpr < 8 && tpr * 2 * nrows <= (int)blockDim.x) tpr *= 2;
@@ -460,6 +518,7 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
     const int li = (base + threadIdx.x) / tpr;
     const bool valid = li < nrows;
     Moments M{-INFINITY, 0.f, 0.f, 0.f};
+    float xmin = INFINITY;
     if (valid) {
       for (int c0 = sub; c0 < pl.nstat_chunks; c0 += 8 * tpr) {
         float4 v[8];
@@ -469,6 +528,10 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           if (c0 + u * tpr < pl.nstat_chunks) M = merge(M, Moments{v[u].x, v[u].y, v[u].z, v[u].w});
+        if (a.tc_min)
+          for (int u = 0; u < 8; ++u)
+            if (c0 + u * tpr < pl.nstat_chunks)
+              xmin = fminf(xmin, __ldcg(minx + (size_t)(c0 + u * tpr) * pl.H * pl.W + i0 + li));
       }
     }
     for (int o = 1; o < tpr; o <<= 1) {   // lanes of one row are consecutive within a warp
@@ -478,27 +541,37 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
       O.t = __shfl_xor_sync(0xffffffffu, M.t, o);
       O.s = __shfl_xor_sync(0xffffffffu, M.s, o);
       M = merge(M, O);
+      xmin = fminf(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
     }
     if (valid && sub == 0) {
       const float l2z = log2f(M.z);
       const float iz = 1.0f / M.z;
-      lse[i0 + li] = M.m + l2z;
+      const float L = M.m + l2z;
+      lse[i0 + li] = L;
       const int r = li % pl.W;
       rowE[li] = l2z * kLn2 - kLn2 * div_rcp(M.t, M.z, iz) + (float)(pl.W - 1 - r) * kGeps;
       rowM[li] = 1.f - div_rcp(M.s, M.z, iz);
+      // the clamp at 1e-8 adds at most kGeps per visible entry to the row's entropy; a
+      // row whose smallest probability is above the clamp (with margin) adds nothing
+      const bool clamp_free = a.tc_min && fmaf(xmin, kLog2e, -L) >= kLog2Eps + 1e-3f;
+      rowB[li] = clamp_free ? 0.f : (float)(pl.n - pl.W + r + 1) * kGeps;
     }
   }
   __syncthreads();
   {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (int hl = warp; hl < nh; hl += nw) {
-      float e = 0.f, m = 0.f;
-      for (int r = lane; r < pl.W; r += 32) { e += rowE[hl * pl.W + r]; m += rowM[hl * pl.W + r]; }
+      float e = 0.f, m = 0.f, b = 0.f;
+      for (int r = lane; r < pl.W; r += 32) {
+        e += rowE[hl * pl.W + r]; m += rowM[hl * pl.W + r]; b += rowB[hl * pl.W + r];
+      }
       e = warp_sum(e);
       m = warp_sum(m);
+      b = warp_sum(b);
       if (lane == 0) {
         spec[h0 + hl] = e / (float)pl.W;
         spec[pl.H + h0 + hl] = m / (float)pl.W;
+        spec[4 * pl.H + h0 + hl] = a.tc_min ? b / (float)pl.W : INFINITY;
       }
     }
   }
@@ -512,8 +585,9 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  float* sSpec = rowE;                                           // [2H]
+  float* sSpec = rowE;                                           // [2H] + [H] bounds
   for (int h = threadIdx.x; h < 2 * pl.H; h += blockDim.x) sSpec[h] = __ldcg(spec + h);
+  for (int h = threadIdx.x; h < pl.H; h += blockDim.x) sSpec[2 * pl.H + h] = __ldcg(spec + 4 * pl.H + h);
   __syncthreads();
   uint64_t qs, hs;
   int hm, nhi;
@@ -525,6 +599,8 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
     hdr->n_hi = nhi;
     hdr->fixup = 0;
     hdr->cnt_stats = 0;
+    hdr->need_exact = (a.force_exact || !pl.tc_pool ||
+                       !selection_certain(a.p, pl.H, sSpec, sSpec + pl.H, sSpec + 2 * pl.H, qs)) ? 1 : 0;
   }
 }
 
@@ -1061,6 +1137,15 @@ __device__ __forceinline__ void window_pool_finish(const WinArgs& a, char* smem_
   float* sE = smem + cs.rowe;                        // [H*W] entropy, then [H*W] mass
   float* sM = sE + pl.H * pl.W;
   float* sHead = smem + cs.head;                     // [H] entropy, [H] mass means
+  if (!hdr->need_exact) {
+    // the head sets of the moments pass are certain: its entropies and masses stand
+    const float* spec = reinterpret_cast<const float*>(a.ws + pl.off_spec);
+    for (int h = threadIdx.x; h < 2 * pl.H; h += blockDim.x) exact[h] = __ldcg(spec + h);
+    if (threadIdx.x == 0) hdr->cnt_pool = 0;
+    __syncthreads();
+    run_window_chains(a.pl, a.p, a.ws, smem, true);
+    return;
+  }
   const int HW2 = 2 * pl.H * pl.W;                  // rowM follows rowE
   for (int base = threadIdx.x; base < HW2; base += 8 * blockDim.x) {
     float v[8];
@@ -1190,14 +1275,56 @@ CKV_DEV char* align1024(char* p) {
 }
 
 // Round a pair of fp32 accumulators as the reference rounds a 16-bit logit.
+// bf16: RN_bf16(RN_f32(r * rs)) for a bf16 product r and rs = RN_f32(1 / sqrt(128))
+// equals RN_bf16(r * kRsHi + RN_bf16(r * kRsLo)), rs split into two bf16 parts: the
+// result depends only on r's 7-bit mantissa (the exponent scales every term alike) and
+// all 128 mantissas agree (checked exhaustively in exact rational arithmetic), so the
+// second rounding runs on packed bf16 pairs.  Head dim 128 only (the plan enforces it).
+constexpr uint32_t kRsHi2 = 0x3db53db5u;   // bf16(rs) in both halves
+constexpr uint32_t kRsLo2 = 0x371e371eu;   // bf16(rs - bf16(rs)) in both halves
 template <int DT> CKV_DEV void round_pair(float a, float b, float rs, float& x, float& y);
 template <> CKV_DEV void round_pair<CKV_BF16>(float a, float b, float rs, float& x, float& y) {
-  uint32_t p;
+  uint32_t p, t;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(b), "f"(a));
-  float u = __uint_as_float(p << 16) * rs, v = __uint_as_float(p & 0xffff0000u) * rs;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v), "f"(u));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t) : "r"(p), "r"(kRsLo2));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(p) : "r"(p), "r"(kRsHi2), "r"(t));
   x = __uint_as_float(p << 16);
   y = __uint_as_float(p & 0xffff0000u);
+}
+// The same, also returning the two rounded logits packed as a 16-bit pair (exact), for
+// packed max / min.
+template <int DT> CKV_DEV uint32_t round_pack(float a, float b, float rs, float& x, float& y);
+template <> CKV_DEV uint32_t round_pack<CKV_BF16>(float a, float b, float rs, float& x, float& y) {
+  uint32_t p, t;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(b), "f"(a));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t) : "r"(p), "r"(kRsLo2));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(p) : "r"(p), "r"(kRsHi2), "r"(t));
+  x = __uint_as_float(p << 16);
+  y = __uint_as_float(p & 0xffff0000u);
+  return p;
+}
+template <int DT> CKV_DEV uint32_t pmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (DT == CKV_BF16) asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <int DT> CKV_DEV uint32_t pmin2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (DT == CKV_BF16) asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// The larger / smaller of the two halves of a packed pair, as fp32.
+template <int DT> CKV_DEV float phalf_max(uint32_t p) {
+  if constexpr (DT == CKV_BF16) return fmaxf(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
+  else return fmaxf(__half2float(__ushort_as_half((unsigned short)(p & 0xffffu))),
+                    __half2float(__ushort_as_half((unsigned short)(p >> 16))));
+}
+template <int DT> CKV_DEV float phalf_min(uint32_t p) {
+  if constexpr (DT == CKV_BF16) return fminf(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
+  else return fminf(__half2float(__ushort_as_half((unsigned short)(p & 0xffffu))),
+                    __half2float(__ushort_as_half((unsigned short)(p >> 16))));
 }
 // fp16 keeps 3 more mantissa bits than bf16, so dividing (the reference on CPU) and
 // multiplying by the reciprocal (its CUDA scalar division) round apart often enough to
@@ -1206,6 +1333,11 @@ template <> CKV_DEV void round_pair<CKV_FP16>(float a, float b, float rs, float&
   const float sd = 11.313708305358887f;   // fp32(sqrt(128)); rs = RN(1 / sd)
   x = __half2float(__float2half_rn(div_rcp(__half2float(__float2half_rn(a)), sd, rs)));
   y = __half2float(__float2half_rn(div_rcp(__half2float(__float2half_rn(b)), sd, rs)));
+}
+template <> CKV_DEV uint32_t round_pack<CKV_FP16>(float a, float b, float rs, float& x, float& y) {
+  round_pair<CKV_FP16>(a, b, rs, x, y);
+  const __half2 h = __floats2half2_rn(x, y);   // exact: x, y are fp16 values
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 template <int DT>
@@ -1285,6 +1417,7 @@ __global__ void __launch_bounds__(512, 1)
   const int r = row % pl.W;
   const int lim = pl.n - pl.W + r;                     // last visible key of this window row
   Moments M{-INFINITY, 0.f, 0.f, 0.f};
+  float xmin = INFINITY;                               // smallest visible rounded logit of the row
   const float rs = 1.0f / sqrtf((float)pl.D);
   __syncthreads();
 
@@ -1304,17 +1437,31 @@ __global__ void __launch_bounds__(512, 1)
       __syncwarp();
       tc::tmem_ld32(base + c, v);
       const int jb = t * TN + c;
+      // a chunk past the row's last visible key adds nothing (after the warp-wide load);
+      // folding it in would seed the running max with the mask value when it comes first
+      if (jb > lim) continue;
       float x[32];
+      uint32_t px = 0, pn = 0;   // packed running max / min of the chunk's rounded logits
 #pragma unroll
-      for (int k = 0; k < 32; k += 2) round_pair<DT>(v[k], v[k + 1], rs, x[k], x[k + 1]);
-      if (jb + 31 > lim) {   // the masked / out-of-range tail of the row (last tiles only)
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (jb + k > lim) x[k] = -1e30f;
+      for (int k = 0; k < 32; k += 2) {
+        const uint32_t pk = round_pack<DT>(v[k], v[k + 1], rs, x[k], x[k + 1]);
+        px = k == 0 ? pk : pmax2<DT>(px, pk);
+        pn = k == 0 ? pk : pmin2<DT>(pn, pk);
       }
-      float cm = x[0];
+      float cm, cmin;
+      if (jb + 31 > lim) {   // the masked / out-of-range tail of the row (last tiles only)
+        cmin = INFINITY;
+        cm = -INFINITY;
 #pragma unroll
-      for (int k = 1; k < 32; ++k) cm = fmaxf(cm, x[k]);
+        for (int k = 0; k < 32; ++k) {
+          if (jb + k > lim) x[k] = -1e30f;
+          else { cmin = fminf(cmin, x[k]); cm = fmaxf(cm, x[k]); }
+        }
+      } else {
+        cm = phalf_max<DT>(px);
+        cmin = phalf_min<DT>(pn);
+      }
+      xmin = fminf(xmin, cmin);
       const float cm2 = cm * kLog2e;
       if (cm2 > M.m) {
         if (M.m != -INFINITY) {
@@ -1354,15 +1501,19 @@ __global__ void __launch_bounds__(512, 1)
   tc::fence_before_sync();
   __syncthreads();
   float4* msh = reinterpret_cast<float4*>(sB);        // K stages are free now: [nsplit][R]
+  float* mnsh = reinterpret_cast<float*>(msh + nsplit * R);
   msh[sp * R + row] = make_float4(M.m, M.z, M.t, M.s);
+  mnsh[sp * R + row] = xmin;
   __syncthreads();
   if (sp == 0) {
     for (int q = 1; q < nsplit; ++q) {
       const float4 o = msh[q * R + row];
       M = merge(M, Moments{o.x, o.y, o.z, o.w});
+      xmin = fminf(xmin, mnsh[q * R + row]);
     }
     const int h = g * pl.G + row / pl.W;
     part[((size_t)chunk * pl.H + h) * pl.W + r] = make_float4(M.m, M.z, M.t, M.s);
+    reinterpret_cast<float*>(a.ws + pl.off_minx)[((size_t)chunk * pl.H + h) * pl.W + r] = xmin;
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1412,6 +1563,7 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
   const int m_tiles = pl.G * pl.W / 128;
   a.tc_tn = m_tiles <= 2 ? 128 : 64;
   a.tc_stages = 4;
+  a.tc_min = 1;
   const int ntn = (pl.n + a.tc_tn - 1) / a.tc_tn;
   a.tc_tpc = (ntn + pl.nstat_chunks - 1) / pl.nstat_chunks;
   CUtensorMap tq, tk;
@@ -1606,6 +1758,13 @@ __global__ void __launch_bounds__(kP2Threads, 1)
     const bool hi_rows = pl.hi_rows != 0;
     const uint64_t all_heads = pl.H >= 64 ? ~0ull : ((1ull << pl.H) - 1);
     const int hi_kind = !hi_rows ? kHiNone : (hmax ? kHiMax : (hset == all_heads ? kHiMeanAll : kHiMean));
+    // this lane's heads 4g + e (bit g) and 4g + 2 + e (bit 16 + g) in the QI / HI sets
+    uint32_t qbits = 0, hbits = 0;
+    for (int g = 0; g < ngroups && g < 16; ++g) {
+      const int ha = g * G + e, hb = ha + 2;
+      qbits |= (uint32_t)((qset >> ha) & 1ull) << g | (uint32_t)((qset >> hb) & 1ull) << (16 + g);
+      hbits |= (uint32_t)((hset >> ha) & 1ull) << g | (uint32_t)((hset >> hb) & 1ull) << (16 + g);
+    }
     const float rs = 1.0f / sqrtf((float)pl.D);
     const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
     const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
@@ -1613,11 +1772,15 @@ __global__ void __launch_bounds__(kP2Threads, 1)
     // the loop ends only at a tile boundary, on a decision all warps read after a
     // barrier (no tile left, or a wait that gave up in any epilogue warp).
     auto epi_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kP2EpiWarps) : "memory"); };
-    {
+    // exact clamped entropy / mass only when the moments pass could not settle the head sets
+    const bool exact = *reinterpret_cast<volatile int32_t*>(&hdr->need_exact) != 0;
+    if (exact) {
       const float z[4] = {0.f, 0.f, 0.f, 0.f};
       for (int g = 0; g < ngroups; ++g) tc::tmem_st4(acc_base + 4 * g, z);
     }
-    float qacc[8], hacc[8];                             // owned columns cq*16 + 2m + e
+    // pooled values of this lane's two heads (4g + e, 4g + 2 + e) over the groups so far,
+    // per column of the quarter; the lane pair combines its four heads once per tile
+    float qown[16], hown[16];
     int tile = -1;
     for (int s = 0; s < ntn * ngroups; ++s) {
       const int g = s % ngroups;
@@ -1635,7 +1798,7 @@ __global__ void __launch_bounds__(kP2Threads, 1)
       const int j0 = tile * TN;
       if (g == 0) {
 #pragma unroll
-        for (int m = 0; m < 8; ++m) { qacc[m] = 0.f; hacc[m] = 0.f; }
+        for (int c = 0; c < 16; ++c) { qown[c] = 0.f; hown[c] = 0.f; }
       }
       bool ok = !epi_abort;
       if (ok && !tc::mbar_wait(&bar_full[s & 1], (s >> 1) & 1, status)) ok = false;
@@ -1660,8 +1823,8 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         }
         const int ha = g * G + e, hb = ha + 2;
         const float La = slse[ha * W + t], Lb = slse[hb * W + t];
-        const float fqa = ((qset >> ha) & 1ull) ? 1.f : 0.f, fqb = ((qset >> hb) & 1ull) ? 1.f : 0.f;
-        const float fha = ((hset >> ha) & 1ull) ? 1.f : 0.f, fhb = ((hset >> hb) & 1ull) ? 1.f : 0.f;
+        const float fqa = ((qbits >> g) & 1u) ? 1.f : 0.f, fqb = ((qbits >> (16 + g)) & 1u) ? 1.f : 0.f;
+        const float fha = ((hbits >> g) & 1u) ? 1.f : 0.f, fhb = ((hbits >> (16 + g)) & 1u) ? 1.f : 0.f;
 #pragma unroll
         for (int k = 0; k < 16; k += 2) {
           float x0, x1, y0, y1;
@@ -1672,65 +1835,57 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         float ent0 = 0.f, ent1 = 0.f, mass0 = 0.f, mass1 = 0.f;
         const int jb = j0 + cq * 16;
         const bool interior = jb + 15 <= lim && jb >= pl.s;
-        // one logit pair (heads a, b at one column): probabilities, entropy, mass, own pool
-        auto logit2 = [&](auto itag, auto htag, float xa, float xb, int j, float& qo, float& ho) {
+        // one logit pair (heads a, b at column c of the quarter): probabilities, the
+        // exact entropy / mass terms when asked for, this lane's pooled values
+        auto logit2 = [&](auto xtag, auto itag, auto htag, float xa, float xb, int j, int c) {
+          constexpr bool EX = decltype(xtag)::value;
           constexpr int HM = decltype(htag)::value;
           const float da = fmaf(xa, kLog2e, -La), db = fmaf(xb, kLog2e, -Lb);
           float pa = ex2(da), pb = ex2(db);
           if constexpr (decltype(itag)::value) {
-            ent0 = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent0);
-            ent1 = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent1);
-            mass0 += pa;
-            mass1 += pb;
+            if constexpr (EX) {
+              ent0 = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent0);
+              ent1 = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent1);
+              mass0 += pa;
+              mass1 += pb;
+            }
           } else if (j <= lim) {
-            ent0 = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent0);
-            ent1 = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent1);
-            if (j >= pl.s) { mass0 += pa; mass1 += pb; }
+            if constexpr (EX) {
+              ent0 = fmaf(fmaxf(pa, 1e-8f), fmaxf(da, kLog2Eps), ent0);
+              ent1 = fmaf(fmaxf(pb, 1e-8f), fmaxf(db, kLog2Eps), ent1);
+              if (j >= pl.s) { mass0 += pa; mass1 += pb; }
+            }
           } else {
             pa = 0.f; pb = 0.f;
-            if (j < pl.n) {   // masked: probability 0, clamped to 1e-8
-              ent0 = fmaf(1e-8f, kLog2Eps, ent0);
-              ent1 = fmaf(1e-8f, kLog2Eps, ent1);
+            if constexpr (EX) {
+              if (j < pl.n) {   // masked: probability 0, clamped to 1e-8
+                ent0 = fmaf(1e-8f, kLog2Eps, ent0);
+                ent1 = fmaf(1e-8f, kLog2Eps, ent1);
+              }
             }
           }
-          qo = fmaxf(pa * fqa, pb * fqb);
-          if constexpr (HM == kHiMeanAll) ho = pa + pb;
-          else if constexpr (HM == kHiMean) ho = fmaf(pa, fha, pb * fhb);
-          else if constexpr (HM == kHiMax) ho = fmaxf(pa * fha, pb * fhb);
-          else ho = 0.f;
+          qown[c] = fmaxf(qown[c], fmaxf(pa * fqa, pb * fqb));
+          if constexpr (HM == kHiMean) hown[c] += fmaf(pa, fha, pb * fhb);
+          else if constexpr (HM == kHiMax) hown[c] = fmaxf(hown[c], fmaxf(pa * fha, pb * fhb));
         };
-        // per column pair: the partner lane holds the group's other two heads; each
-        // lane keeps one column of the pair (even lane: even, odd lane: odd)
-        auto pairs = [&](auto itag, auto htag) {
-          constexpr int HM = decltype(htag)::value;
+        auto cols = [&](auto xtag, auto itag, auto htag) {
 #pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            float q0, h0, q1, h1;
-            logit2(itag, htag, va[2 * m], vb[2 * m], jb + 2 * m, q0, h0);
-            logit2(itag, htag, va[2 * m + 1], vb[2 * m + 1], jb + 2 * m + 1, q1, h1);
-            const float qr = __shfl_xor_sync(0xffffffffu, e ? q0 : q1, 1);
-            const float qm = e ? q1 : q0;
-            qacc[m] = fmaxf(qacc[m], fmaxf(qm, qr));
-            if constexpr (HM != kHiNone) {
-              const float hr = __shfl_xor_sync(0xffffffffu, e ? h0 : h1, 1);
-              const float hm = e ? h1 : h0;
-              if constexpr (HM == kHiMax) hacc[m] = fmaxf(hacc[m], fmaxf(hm, hr));
-              else hacc[m] = hacc[m] + (hm + hr);
-            }
-          }
+          for (int c = 0; c < 16; ++c) logit2(xtag, itag, htag, va[c], vb[c], jb + c, c);
         };
-        auto run = [&](auto htag) {
-          if (interior) pairs(BoolTag<true>{}, htag);
-          else pairs(BoolTag<false>{}, htag);
+        auto run = [&](auto xtag, auto htag) {
+          if (interior) cols(xtag, BoolTag<true>{}, htag);
+          else cols(xtag, BoolTag<false>{}, htag);
         };
-        switch (hi_kind) {
-          case kHiMeanAll: run(IntTag<kHiMeanAll>{}); break;
-          case kHiMean: run(IntTag<kHiMean>{}); break;
-          case kHiMax: run(IntTag<kHiMax>{}); break;
-          default: run(IntTag<kHiNone>{}); break;
+        auto run_x = [&](auto htag) {
+          if (exact) run(BoolTag<true>{}, htag);
+          else run(BoolTag<false>{}, htag);
+        };
+        switch (hi_kind) {   // a mean over every head is a mean with all factors 1
+          case kHiMeanAll: case kHiMean: run_x(IntTag<kHiMean>{}); break;
+          case kHiMax: run_x(IntTag<kHiMax>{}); break;
+          default: run_x(IntTag<kHiNone>{}); break;
         }
-        // exact entropy (log2 units) / mass running sums of the two heads
-        {
+        if (exact) {   // exact entropy (log2 units) / mass running sums of the two heads
           float acc[4];
           tc::tmem_ld4(acc_base + 4 * g, acc);
           acc[0] += ent0; acc[1] += ent1; acc[2] += mass0; acc[3] += mass1;
@@ -1738,12 +1893,21 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         }
       }
       if (g == ngroups - 1) {
-        // ---- the tile is complete: pooled rows through shared memory
+        // ---- the tile is complete: the lane pair's four heads (lane e keeps the columns
+        // 2m + e of the quarter), then pooled rows through shared memory
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
+          const float qk = e ? qown[2 * m + 1] : qown[2 * m];
+          const float qr = __shfl_xor_sync(0xffffffffu, e ? qown[2 * m] : qown[2 * m + 1], 1);
+          float hv = 0.f;
+          if (hi_kind != kHiNone) {
+            const float hk = e ? hown[2 * m + 1] : hown[2 * m];
+            const float hr = __shfl_xor_sync(0xffffffffu, e ? hown[2 * m] : hown[2 * m + 1], 1);
+            hv = hi_kind == kHiMax ? fmaxf(hk, hr) : hk + hr;
+          }
           const int c = cq * 16 + 2 * m + e;
-          sQ[t * kP2Pitch + c] = qacc[m];
-          sH[t * kP2Pitch + c] = hacc[m];
+          sQ[t * kP2Pitch + c] = fmaxf(qk, qr);
+          sH[t * kP2Pitch + c] = hv;
         }
         epi_sync();
         float* rows_qi = reinterpret_cast<float*>(a.ws + pl.off_rows_qi);
@@ -1797,18 +1961,33 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         epi_sync();
       }
     }
-    // one exact entropy / mass partial per (CTA, column quarter, head, row)
-    float* epart = reinterpret_cast<float*>(a.ws + pl.off_epart);   // [e_parts][H][W]
-    float* mpart = reinterpret_cast<float*>(a.ws + pl.off_mpart);
-    for (int g = 0; g < ngroups; ++g) {
-      float acc[4];
-      tc::tmem_ld4(acc_base + 4 * g, acc);
-      const int ha = g * G + e, hb = ha + 2;
-      const size_t slot = (size_t)(blockIdx.x * 4 + cq) * pl.H;
-      epart[(slot + ha) * W + t] = -acc[0] * kLn2;
-      epart[(slot + hb) * W + t] = -acc[1] * kLn2;
-      mpart[(slot + ha) * W + t] = acc[2];
-      mpart[(slot + hb) * W + t] = acc[3];
+    if (exact) {
+      // one exact entropy / mass partial per (CTA, head, row): the four column quarters
+      // of a TMEM lane are summed through shared memory (the staging rows are free now)
+      float* epart = reinterpret_cast<float*>(a.ws + pl.off_epart);   // [e_parts][H][W]
+      float* mpart = reinterpret_cast<float*>(a.ws + pl.off_mpart);
+      float4* red = reinterpret_cast<float4*>(sQ);                    // [4 quarters][128 lanes]
+      for (int g = 0; g < ngroups; ++g) {
+        float acc[4];
+        tc::tmem_ld4(acc_base + 4 * g, acc);
+        red[cq * 128 + L] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        epi_sync();
+        if (cq == 0) {
+          float4 sum4 = red[L];
+#pragma unroll
+          for (int q2 = 1; q2 < 4; ++q2) {
+            const float4 o = red[q2 * 128 + L];
+            sum4.x += o.x; sum4.y += o.y; sum4.z += o.z; sum4.w += o.w;
+          }
+          const int ha = g * G + e, hb = ha + 2;
+          const size_t slot = (size_t)blockIdx.x * pl.H;
+          epart[(slot + ha) * W + t] = -sum4.x * kLn2;
+          epart[(slot + hb) * W + t] = -sum4.y * kLn2;
+          mpart[(slot + ha) * W + t] = sum4.z;
+          mpart[(slot + hb) * W + t] = sum4.w;
+        }
+        epi_sync();
+      }
     }
   }
   tc::fence_before_sync();
@@ -1885,11 +2064,12 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
   const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
   const int row = blockIdx.x * 32 + lane;
   __shared__ float sp[kReduceStreams][32];
+  const bool exact = hdr->need_exact != 0;   // else the moments pass's values stand
   float e = 0.f;
   if (row < HW) {
-    e = sum_parts(epart + row, pl.e_parts, (size_t)HW, q, kReduceStreams);
+    if (exact) e = sum_parts(epart + row, pl.e_parts, (size_t)HW, q, kReduceStreams);
   } else if (row < 2 * HW) {
-    e = sum_parts(mpart + (row - HW), pl.e_parts, (size_t)HW, q, kReduceStreams);
+    if (exact) e = sum_parts(mpart + (row - HW), pl.e_parts, (size_t)HW, q, kReduceStreams);
   } else if (row < nrows) {
     const int ch = (row - 2 * HW) / pl.W, rr = (row - 2 * HW) % pl.W;
     const int src = (ch == 1 && pl.hi_rows) ? 1 : 0;

@@ -17,6 +17,8 @@ struct WinArgs {
   int tc_tn;         // tensor-core path: key columns per MMA tile
   int tc_tpc;        // tensor-core path: tiles per column chunk of the moments pass
   int tc_stages;     // tensor-core path: K-tile stages in shared memory
+  int tc_min;        // moments pass: the tensor-core kernel wrote row minima (clamp bounds)
+  int force_exact;   // pooling pass: always recompute the clamped entropy / mass
   ckv_params p;
   Plan pl;
 };

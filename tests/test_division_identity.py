@@ -75,3 +75,40 @@ def test_markstein_division_is_correctly_rounded(seed):
         if q != e:
             bad.append((float(a), float(b), float(q), float(e)))
     assert not bad, bad[:5]
+
+
+def rn_bits(x: Fraction, bits: int) -> Fraction:
+    """Round an exact rational to `bits` significant bits, nearest, ties to even."""
+    if x == 0:
+        return x
+    sgn, x = (1, x) if x > 0 else (-1, -x)
+    e = x.numerator.bit_length() - x.denominator.bit_length()
+    while Fraction(2) ** e > x:
+        e -= 1
+    while Fraction(2) ** (e + 1) <= x:
+        e += 1
+    ulp = Fraction(2) ** (e - bits + 1)
+    q = x / ulp
+    fl = q.numerator // q.denominator
+    rem = q - fl
+    if rem > Fraction(1, 2) or (rem == Fraction(1, 2) and fl % 2 == 1):
+        fl += 1
+    return sgn * fl * ulp
+
+
+def test_bf16_logit_scaling_by_split_constant():
+    """The tensor-core passes scale a bf16 logit r by rs = RN_f32(1 / sqrt(128)) as
+    RN_bf16(r * hi + RN_bf16(r * lo)) (hi = bf16(rs) = 0x3db5, lo = bf16(rs - hi) =
+    0x371e, packed bf16 multiply and FMA) instead of RN_bf16(RN_f32(r * rs)); the two
+    agree for every bf16 mantissa (the exponent scales every term alike)."""
+    sd = np.float32(np.sqrt(np.float32(128.0)))
+    rs = np.float32(np.float32(1.0) / sd)
+    hi = Fraction(float(np.array([0x3db50000], np.uint32).view(np.float32)[0]))
+    lo = Fraction(float(np.array([0x371e0000], np.uint32).view(np.float32)[0]))
+    assert hi == rn_bits(Fraction(float(rs)), 8) and lo == rn_bits(Fraction(float(rs)) - hi, 8)
+    for e in (-20, 0, 7):
+        for f in range(128):
+            for sign in (1, -1):
+                r = sign * (1 + Fraction(f, 128)) * Fraction(2) ** e
+                ref = rn_bits(Fraction(float(rn32(r * Fraction(float(rs))))), 8)
+                assert rn_bits(r * hi + rn_bits(r * lo, 8), 8) == ref, (e, f, sign)

@@ -54,3 +54,46 @@ def test_full_size_layer(n, W, B, planted):
         got = sc.cpu().numpy()
         assert np.max(np.abs(got[0] - r.qi)) / np.abs(r.qi).max() < 1e-3
         assert np.max(np.abs(got[1] - r.hi)) / np.abs(r.hi).max() < 1e-3
+
+
+def test_ragged_batch_of_sequences():
+    """A ragged batch of 16 sequences, n_i ~ U[2048, 32768] (seeded), window 32, budget
+    int(0.1 n_i), bf16, as independent units in one batched call: bit-identical to one
+    call per sequence, valid kept sets, and the two shortest against the structured oracle."""
+    from submission_folder_b200 import sharding
+    dev = _cuda()
+    rng = np.random.default_rng(2024)
+    lengths = rng.integers(2048, 32769, size=16).tolist()
+    W = 32
+    layers, params, cpu = [], [], []
+    for i, n in enumerate(lengths):
+        q, k, v = make_layer(n, seed=500 + i, window=W, planted=16, dtype="bf16", device="cpu")
+        cpu.append((q, k, v))
+        layers.append((q.to(dev), k.to(dev), v.to(dev)))
+        params.append(CircuitKVCluster(**cli_cluster_kwargs(W, int(0.1 * n))).params(n))
+    batched = ops.score_evict_batched(params, layers, want_scores=True)
+    # the units one rank of eight would own: its slice of the batch alone gives the same results
+    mine = sharding.sequences_for_rank(lengths, 3, 8)
+    part = ops.score_evict_batched([params[i] for i in mine], [layers[i] for i in mine])
+    torch.cuda.synchronize()
+    assert ops.read_status(dev) == 0
+    for j, i in enumerate(mine):
+        assert torch.equal(part[j][2], batched[i][2])
+    for i, n in enumerate(lengths):
+        ko, vo, idx, sc = batched[i]
+        assert torch.isfinite(sc).all(), (i, n)
+        one = ops.score_evict(params[i], *layers[i], want_scores=True)
+        for x, y in zip(one, batched[i]):
+            assert torch.equal(x, y), i
+        B = int(0.1 * n)
+        ii = idx.cpu().numpy()
+        assert len(ii) == B - W and np.all(np.diff(ii) > 0) and np.all(ii[:4] == np.arange(4)) and ii[-1] < n - W
+        kd = layers[i][1]
+        assert torch.equal(ko[0, : B - W], kd[0, idx.long()]) and torch.equal(ko[31, B - W:], kd[7, n - W:])
+    for i in sorted(range(16), key=lambda i: lengths[i])[:2]:
+        n, (q, k, v) = lengths[i], cpu[i]
+        r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4,
+                        O.Params(window_size=W, max_capacity_prompt=int(0.1 * n)), dtype="bf16")
+        ii = batched[i][2].cpu().numpy()
+        nd, ok = compare_keep(ii, r.keep_idx, r.combined, 4, n - W, int(0.1 * n) - W - 4, margin=16.0 / (n - 1))
+        assert ok, (i, n, nd)

@@ -339,6 +339,28 @@ def test_per_head_fp32_ragged():
     assert ops.read_status(dev) == 0
 
 
+@pytest.mark.parametrize("n,W", [(4460, 64), (11554, 64), (4466, 32)])
+def test_moments_chunk_of_one_masked_tile(n, W):
+    """Lengths where a moments-pass CTA gets only the last, partly masked key tile:
+    finite scores and the oracle's kept set (up to near-ties)."""
+    from submission_folder_b200.cluster import cli_cluster_kwargs
+    from submission_folder_b200.synth import make_layer
+    dev = _cuda()
+    B = n // 8
+    q, k, v = make_layer(n, seed=n, window=W, planted=16, dtype="bf16", device="cpu")
+    p = CircuitKVCluster(**cli_cluster_kwargs(W, B)).params(n)
+    ent, mass, _, rq, rh = ops.window_pool(p, q.to(dev), k.to(dev))
+    ko, vo, idx, sc = ops.score_evict(p, q.to(dev), k.to(dev), v.to(dev), want_scores=True)
+    torch.cuda.synchronize()
+    for t in (ent, mass, rq, rh, sc):
+        assert torch.isfinite(t).all()
+    r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4,
+                    O.Params(window_size=W, max_capacity_prompt=B), dtype="bf16")
+    np.testing.assert_allclose(mass.cpu().numpy(), r.choice.mass, rtol=1e-4, atol=1e-5)
+    nd, ok = compare_keep(idx.cpu().numpy(), r.keep_idx, r.combined, 4, n - W, B - W - 4, margin=16.0 / (n - 1))
+    assert ok, nd
+
+
 def test_short_sequence_returns_inputs():
     dev = _cuda()
     c = case("bf16_n2048_default")
