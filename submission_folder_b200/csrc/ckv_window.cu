@@ -1340,8 +1340,11 @@ template <> CKV_DEV uint32_t round_pack<CKV_FP16>(float a, float b, float rs, fl
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+constexpr int kStatsEpiWarps = 16;                       // epilogue warps of the moments pass
+constexpr int kStatsThreads = 32 * (kStatsEpiWarps + 1);  // + one producer warp
+
 template <int DT>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(kStatsThreads, 1)
     k_tc_stats(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
   extern __shared__ char smem_raw[];
   const Plan& pl = a.pl;
@@ -1357,60 +1360,25 @@ __global__ void __launch_bounds__(512, 1)
   const int ntile = max(0, t1 - t0);
   char* sA = align1024(smem_raw);
   char* sB = sA + 2 * R * 128;
-  __shared__ __align__(8) uint64_t bar_q, bar_k[4], bar_mma[2];
+  // K stage full / free, accumulator buffer full / free (16 epilogue warps arrive)
+  __shared__ __align__(8) uint64_t bar_q, bar_k[4], bar_kfree[4], bar_full[2], bar_tfree[2];
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int abort_sh;
   const uint32_t ncols = (2 * m_tiles * TN <= 256) ? 256u : 512u;
   if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
   if (threadIdx.x == 0) {
     tc::mbar_init(&bar_q, 1);
-    for (int i = 0; i < 4; ++i) tc::mbar_init(&bar_k[i], 1);
-    tc::mbar_init(&bar_mma[0], 1);
-    tc::mbar_init(&bar_mma[1], 1);
+    for (int i = 0; i < 4; ++i) { tc::mbar_init(&bar_k[i], 1); tc::mbar_init(&bar_kfree[i], 1); }
+    for (int i = 0; i < 2; ++i) { tc::mbar_init(&bar_full[i], 1); tc::mbar_init(&bar_tfree[i], kStatsEpiWarps); }
     tc::fence_barrier_init();
-    abort_sh = 0;
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
-  const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
 
-  auto issue_tile = [&](int i) {   // thread 0: UMMAs of local tile i into buffer i & 1
-    const int s = i % S;
-    const uint32_t dcol = (uint32_t)((i & 1) * m_tiles * TN);
-    for (int mt = 0; mt < m_tiles; ++mt) {
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int p = ks >> 2, koff = (ks & 3) * 32;
-        const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(sA + p * R * 128 + mt * 128 * 128 + koff));
-        const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(sB + (s * 2 + p) * TN * 128 + koff));
-        tc::umma_f16(tmem + dcol + mt * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
-      }
-    }
-    tc::umma_commit(&bar_mma[i & 1]);
-  };
-  auto load_tile = [&](int i) {    // thread 0: TMA of local tile i into stage i % S
-    const int s = i % S;
-    tc::mbar_expect_tx(&bar_k[s], (uint32_t)TN * 256u);
-    for (int p = 0; p < 2; ++p)
-      tc::tma_load_3d(sB + (s * 2 + p) * TN * 128, &tmk, &bar_k[s], p * 64, (t0 + i) * TN, g);
-  };
-
-  if (ntile > 0 && threadIdx.x == 0) {
-    tc::mbar_expect_tx(&bar_q, (uint32_t)R * 256u);
-    for (int hl = 0; hl < pl.G; ++hl)
-      for (int p = 0; p < 2; ++p)
-        tc::tma_load_3d(sA + p * R * 128 + hl * pl.W * 128, &tmq, &bar_q, p * 64, pl.n - pl.W, g * pl.G + hl);
-    for (int i = 0; i < min(S, ntile); ++i) load_tile(i);
-    bool ok = tc::mbar_wait(&bar_q, 0, status) && tc::mbar_wait(&bar_k[0], 0, status);
-    if (ok) { tc::fence_after_sync(); issue_tile(0); }
-    else abort_sh = 1;
-  }
-
-  // 16 warps: TMEM lane group lg, m-tile mt, column split sp of nsplit
+  // 16 epilogue warps: TMEM lane group lg, m-tile mt, column split sp of nsplit
   const int lg = warp & 3;
-  const int nsplit = 16 / (4 * m_tiles);               // 4, 2 or 1
+  const int nsplit = kStatsEpiWarps / (4 * m_tiles);   // 4, 2 or 1
   const int mt = (warp >> 2) % m_tiles, sp = (warp >> 2) / m_tiles;
   const int cw = TN / nsplit;                          // columns per thread per tile (>= 32)
   const int row = mt * 128 + 32 * lg + lane;
@@ -1418,82 +1386,132 @@ __global__ void __launch_bounds__(512, 1)
   const int lim = pl.n - pl.W + r;                     // last visible key of this window row
   Moments M{-INFINITY, 0.f, 0.f, 0.f};
   float xmin = INFINITY;                               // smallest visible rounded logit of the row
-  const float rs = 1.0f / sqrtf((float)pl.D);
-  __syncthreads();
 
-  for (int i = 0; i < ntile; ++i) {
-    if (abort_sh) break;
-    const int t = t0 + i;
-    if (threadIdx.x == 0 && i + 1 < ntile) {
-      if (tc::mbar_wait(&bar_k[(i + 1) % S], ((i + 1) / S) & 1, status)) { tc::fence_after_sync(); issue_tile(i + 1); }
-      else abort_sh = 1;
-    }
-    if (!tc::mbar_wait(&bar_mma[i & 1], (i >> 1) & 1, status)) abort_sh = 1;
-    tc::fence_after_sync();
-    if (threadIdx.x == 0 && i + S < ntile && !abort_sh) load_tile(i + S);
-    const uint32_t base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)((i & 1) * m_tiles * TN + mt * TN);
-    for (int c = sp * cw; c < (sp + 1) * cw; c += 32) {
-      float v[32];
-      __syncwarp();
-      tc::tmem_ld32(base + c, v);
-      const int jb = t * TN + c;
-      // a chunk past the row's last visible key adds nothing (after the warp-wide load);
-      // folding it in would seed the running max with the mask value when it comes first
-      if (jb > lim) continue;
-      float x[32];
-      uint32_t px = 0, pn = 0;   // packed running max / min of the chunk's rounded logits
+  if (warp == kStatsEpiWarps) {
+    // ---------------- producer: TMA ring of K tiles and the UMMAs (one thread) ----------------
+    if (lane == 0 && ntile > 0) {
+      const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
+      auto load_tile = [&](int i) {   // K tile i of this chunk into stage i % S
+        const int st = i % S;
+        tc::mbar_expect_tx(&bar_k[st], (uint32_t)TN * 256u);
+        for (int p = 0; p < 2; ++p)
+          tc::tma_load_3d(sB + (st * 2 + p) * TN * 128, &tmk, &bar_k[st], p * 64, (t0 + i) * TN, g);
+      };
+      tc::mbar_expect_tx(&bar_q, (uint32_t)R * 256u);
+      for (int hl = 0; hl < pl.G; ++hl)
+        for (int p = 0; p < 2; ++p)
+          tc::tma_load_3d(sA + p * R * 128 + hl * pl.W * 128, &tmq, &bar_q, p * 64, pl.n - pl.W, g * pl.G + hl);
+      int issued = min(S, ntile), consumed = 0, mmas = 0;
+      for (int i = 0; i < issued; ++i) load_tile(i);
+      bool ok = tc::mbar_wait(&bar_q, 0, status);
+      for (int i = 0; ok && i < ntile; ++i) {
+        const int st = i % S, b = i & 1;
+        if (i >= 2 && !tc::mbar_wait(&bar_tfree[b], ((i - 2) >> 1) & 1, status)) { ok = false; break; }
+        if (!tc::mbar_wait(&bar_k[st], (i / S) & 1, status)) { ok = false; break; }
+        consumed = i + 1;
+        tc::fence_after_sync();
+        const uint32_t dcol = (uint32_t)(b * m_tiles * TN);
+        for (int m = 0; m < m_tiles; ++m) {
 #pragma unroll
-      for (int k = 0; k < 32; k += 2) {
-        const uint32_t pk = round_pack<DT>(v[k], v[k + 1], rs, x[k], x[k + 1]);
-        px = k == 0 ? pk : pmax2<DT>(px, pk);
-        pn = k == 0 ? pk : pmin2<DT>(pn, pk);
-      }
-      float cm, cmin;
-      if (jb + 31 > lim) {   // the masked / out-of-range tail of the row (last tiles only)
-        cmin = INFINITY;
-        cm = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          if (jb + k > lim) x[k] = -1e30f;
-          else { cmin = fminf(cmin, x[k]); cm = fmaxf(cm, x[k]); }
+          for (int ks = 0; ks < 8; ++ks) {
+            const int p = ks >> 2, koff = (ks & 3) * 32;
+            const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(sA + p * R * 128 + m * 128 * 128 + koff));
+            const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(sB + (st * 2 + p) * TN * 128 + koff));
+            tc::umma_f16(tmem + dcol + m * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
+          }
         }
-      } else {
-        cm = phalf_max<DT>(px);
-        cmin = phalf_min<DT>(pn);
-      }
-      xmin = fminf(xmin, cmin);
-      const float cm2 = cm * kLog2e;
-      if (cm2 > M.m) {
-        if (M.m != -INFINITY) {
-          const float d = cm2 - M.m;
-          const float sc = ex2(-d);
-          M.t = sc * (M.t - d * M.z);
-          M.z *= sc;
-          M.s *= sc;
+        tc::umma_commit(&bar_full[b]);
+        tc::umma_commit(&bar_kfree[st]);
+        mmas = i + 1;
+        if (i + S < ntile) {
+          if (!tc::mbar_wait(&bar_kfree[st], (i / S) & 1, status)) { ok = false; break; }
+          load_tile(i + S);
+          issued = i + S + 1;
         }
-        M.m = cm2;
       }
-      const float nm = -M.m;
-      float z0 = 0.f, z1 = 0.f, t0a = 0.f, t1a = 0.f;
-#pragma unroll
-      for (int k = 0; k < 32; k += 2) {
-        const float d0 = fmaf(x[k], kLog2e, nm), d1 = fmaf(x[k + 1], kLog2e, nm);
-        const float e0 = ex2(d0), e1 = ex2(d1);
-        z0 += e0;
-        z1 += e1;
-        t0a = fmaf(e0, d0, t0a);
-        t1a = fmaf(e1, d1, t1a);
-      }
-      M.z += z0 + z1;
-      M.t += t0a + t1a;
-      if (jb < pl.s) {
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (jb + k < pl.s) M.s += ex2(fmaf(x[k], kLog2e, nm));
+      if (!ok) {
+        // gave up: let the copies and MMAs already issued land before the CTA frees its
+        // shared memory and TMEM (each wait bounded again)
+        for (int i = consumed; i < issued; ++i) tc::mbar_wait(&bar_k[i % S], (i / S) & 1, status);
+        if (mmas > 0) tc::mbar_wait(&bar_kfree[(mmas - 1) % S], ((mmas - 1) / S) & 1, status);
       }
     }
-    tc::fence_before_sync();
-    __syncthreads();
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: running moments of this thread's row ----------------
+    const float rs = 1.0f / sqrtf((float)pl.D);
+    for (int i = 0; i < ntile; ++i) {
+      const int b = i & 1;
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&bar_full[b], (i >> 1) & 1, status))) break;
+      tc::fence_after_sync();
+      const int t = t0 + i;
+      const uint32_t base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)(b * m_tiles * TN + mt * TN);
+      for (int c = sp * cw; c < (sp + 1) * cw; c += 32) {
+        float v[32];
+        __syncwarp();
+        tc::tmem_ld32(base + c, v);
+        if (c + 32 >= (sp + 1) * cw) {   // this warp's last load of the tile: release the buffer
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bar_tfree[b]);
+        }
+        const int jb = t * TN + c;
+        // a chunk past the row's last visible key adds nothing (after the warp-wide load);
+        // folding it in would seed the running max with the mask value when it comes first
+        if (jb > lim) continue;
+        float x[32];
+        uint32_t px = 0, pn = 0;   // packed running max / min of the chunk's rounded logits
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const uint32_t pk = round_pack<DT>(v[k], v[k + 1], rs, x[k], x[k + 1]);
+          px = k == 0 ? pk : pmax2<DT>(px, pk);
+          pn = k == 0 ? pk : pmin2<DT>(pn, pk);
+        }
+        float cm, cmin;
+        if (jb + 31 > lim) {   // the masked / out-of-range tail of the row (last tiles only)
+          cmin = INFINITY;
+          cm = -INFINITY;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            if (jb + k > lim) x[k] = -1e30f;
+            else { cmin = fminf(cmin, x[k]); cm = fmaxf(cm, x[k]); }
+          }
+        } else {
+          cm = phalf_max<DT>(px);
+          cmin = phalf_min<DT>(pn);
+        }
+        xmin = fminf(xmin, cmin);
+        const float cm2 = cm * kLog2e;
+        if (cm2 > M.m) {
+          if (M.m != -INFINITY) {
+            const float d = cm2 - M.m;
+            const float sc = ex2(-d);
+            M.t = sc * (M.t - d * M.z);
+            M.z *= sc;
+            M.s *= sc;
+          }
+          M.m = cm2;
+        }
+        const float nm = -M.m;
+        float z0 = 0.f, z1 = 0.f, t0a = 0.f, t1a = 0.f;
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const float d0 = fmaf(x[k], kLog2e, nm), d1 = fmaf(x[k + 1], kLog2e, nm);
+          const float e0 = ex2(d0), e1 = ex2(d1);
+          z0 += e0;
+          z1 += e1;
+          t0a = fmaf(e0, d0, t0a);
+          t1a = fmaf(e1, d1, t1a);
+        }
+        M.z += z0 + z1;
+        M.t += t0a + t1a;
+        if (jb < pl.s) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (jb + k < pl.s) M.s += ex2(fmaf(x[k], kLog2e, nm));
+        }
+      }
+    }
   }
 
   // merge the column splits of each row, then write this chunk's partial moments
@@ -1502,10 +1520,12 @@ __global__ void __launch_bounds__(512, 1)
   __syncthreads();
   float4* msh = reinterpret_cast<float4*>(sB);        // K stages are free now: [nsplit][R]
   float* mnsh = reinterpret_cast<float*>(msh + nsplit * R);
-  msh[sp * R + row] = make_float4(M.m, M.z, M.t, M.s);
-  mnsh[sp * R + row] = xmin;
+  if (warp < kStatsEpiWarps) {
+    msh[sp * R + row] = make_float4(M.m, M.z, M.t, M.s);
+    mnsh[sp * R + row] = xmin;
+  }
   __syncthreads();
-  if (sp == 0) {
+  if (warp < kStatsEpiWarps && sp == 0) {
     for (int q = 1; q < nsplit; ++q) {
       const float4 o = msh[q * R + row];
       M = merge(M, Moments{o.x, o.y, o.z, o.w});
@@ -1572,7 +1592,7 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
     return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
   const size_t smem = tc_stats_smem(pl, a.tc_tn, a.tc_stages);
   { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_stats<DT>, smem); if (e != cudaSuccess) return e; }
-  k_tc_stats<DT><<<dim3(pl.nstat_chunks, pl.Hkv), 512, smem, st>>>(tq, tk, a);
+  k_tc_stats<DT><<<dim3(pl.nstat_chunks, pl.Hkv), kStatsThreads, smem, st>>>(tq, tk, a);
   return cudaGetLastError();
 }
 

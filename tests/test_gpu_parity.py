@@ -361,6 +361,43 @@ def test_moments_chunk_of_one_masked_tile(n, W):
     assert ok, nd
 
 
+def test_both_pooling_branches_are_exercised():
+    """The pooling pass skips the exact entropy / mass recomputation when the moments
+    pass settles the head sets (header word need_exact = 0) and redoes it otherwise;
+    the golden cases that reach the tensor-core pooling pass must cover both, so the
+    parity tests above check both branches against the reference."""
+    dev = _cuda()
+    seen = {}
+    for c in cases():
+        if c["dtype"] != "bf16" or c["window"] != 64 or "perhead" in c["name"]:
+            continue
+        q, k, v = (x.to(dev) for x in inputs(c))
+        p = _cluster(c).params(c["n"])
+        ops.score_evict(p, q, k, v)
+        torch.cuda.synchronize()
+        ws = ops._workspaces[(dev.type, dev.index)]
+        seen[c["name"]] = int(ws[56:60].cpu().view(torch.int32).item())   # Header.need_exact
+    assert 0 in seen.values(), seen
+    # the four query heads of each KV group identical: their entropies tie, so the 10-head
+    # selection boundary falls inside a tied group and the exact branch must run
+    c = case("bf16_n2048_default")
+    q, k, v = inputs(c)
+    q = q.reshape(8, 4, *q.shape[1:])[:, :1].expand(8, 4, *q.shape[1:]).reshape(q.shape).contiguous()
+    p = _cluster(c).params(c["n"])
+    ko, vo, idx, sc = ops.score_evict(p, q.to(dev), k.to(dev), v.to(dev), want_scores=True)
+    torch.cuda.synchronize()
+    ws = ops._workspaces[(dev.type, dev.index)]
+    assert int(ws[56:60].cpu().view(torch.int32).item()) == 1
+    r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4, oracle_params(c),
+                    dtype=c["dtype"])
+    n, W, B = c["n"], c["window"], c["kwargs"]["max_capacity_prompt"]
+    nd, ok = compare_keep(idx.cpu().numpy(), r.keep_idx, r.combined, 4, n - W, B - W - 4, margin=8.0 / (n - 1))
+    assert ok, nd
+    got = sc.cpu().numpy()
+    assert np.max(np.abs(got[0] - r.qi)) / np.abs(r.qi).max() < SCORE_RTOL
+    assert np.max(np.abs(got[1] - r.hi)) / np.abs(r.hi).max() < SCORE_RTOL
+
+
 def test_short_sequence_returns_inputs():
     dev = _cuda()
     c = case("bf16_n2048_default")
