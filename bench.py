@@ -443,7 +443,9 @@ def e2e(args, rank, world, dev, bl, CircuitKVCluster, cli_cluster_kwargs, make_l
         host.append(tuple(x.cpu().pin_memory() for x in (q[None], repeat_kv(k, G), repeat_kv(v, G))))
         del q, k, v
     clusters = [CircuitKVCluster(**cli_cluster_kwargs(W, b)) for b in bl]
-    h2d = sum(2 * (32 * W * 128 + 2 * 8 * n * 128) for _ in range(L))
+    # host -> device per layer: the window queries and K are copied; the gather reads V's
+    # kept rows (8 KV heads x budget rows) from the pinned host tensor in place
+    h2d = sum(2 * (32 * W * 128 + 8 * n * 128 + 8 * b * 128) for b in bl)
     d2h = sum(2 * 2 * 32 * b * 128 for b in bl)
 
     def one_step():

@@ -247,6 +247,13 @@ int ckv_influence_walk(const float* rows, int32_t W, int32_t ld, int32_t n, int3
 int ckv_rng_fill(int32_t mode, uint64_t seed, uint64_t stream_id, int32_t count, uint64_t* out,
                  ckv_stream_t stream);
 
+/* Whether the current device can read `ptr` in place (no reference counterpart): device
+ * memory of the current device, managed memory, or page-locked host memory mapped at the
+ * same address.  The hook uses it to let the final gather read V rows straight from a
+ * caller's pinned host tensor instead of copying all of V to the device first.  Sets
+ * *accessible to 0 for pageable host memory and unknown pointers. */
+int ckv_device_accessible(const void* ptr, int32_t* accessible);
+
 /* K / V compaction alone (PU:3496-3517 shared, PU:3448-3462 per head): the `kept`
  * positions idx ([kept] or [H, kept] with per_head) then the last `window` rows, into
  * [H, kept + window, D] outputs.  For callers that chose the positions themselves (the

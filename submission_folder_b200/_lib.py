@@ -22,7 +22,8 @@ EXPORTED = (
     "ckv_score_evict_batched", "ckv_read_status", "ckv_select_scores", "ckv_select_scores_noalloc",
     "ckv_neumann_rows",
     "ckv_window_pool", "ckv_influence_walk", "ckv_influence_walk_dense", "ckv_walk_workspace_size",
-    "ckv_rng_fill", "ckv_gather", "ckv_set_stage_events", "ckv_last_error_string", "ckv_version",
+    "ckv_rng_fill", "ckv_gather", "ckv_device_accessible", "ckv_set_stage_events", "ckv_last_error_string",
+    "ckv_version",
 )
 RNG_PHILOX, RNG_PCG = 0, 1
 
@@ -123,6 +124,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "ckv_walk_workspace_size": (i32, [i32, i32, ctypes.POINTER(sz)]),
         "ckv_rng_fill": (i32, [i32, u64, u64, i32, vp, vp]),
         "ckv_gather": (i32, [L, i32, vp, i32, i32, vp, vp, vp]),
+        "ckv_device_accessible": (i32, [vp, ctypes.POINTER(i32)]),
         "ckv_set_stage_events": (i32, [ctypes.POINTER(vp), i32]),
         "ckv_last_error_string": (ctypes.c_char_p, []),
         "ckv_version": (ctypes.c_char_p, []),

@@ -242,7 +242,11 @@ class CircuitKVCluster:
             for h in range(q.shape[0]):
                 qd[h, q_len - W:].copy_(q[h, q_len - W:], non_blocking=True)
             q = qd
-            k, v = _to_device_by_head(k, dev), _to_device_by_head(v, dev)
+            k = _to_device_by_head(k, dev)
+            # V is read only by the final gather (the kept rows): from a page-locked host
+            # tensor the device reads those rows in place instead of copying all of V
+            if not ops.device_readable(v):
+                v = _to_device_by_head(v, dev)
         p = self.params(q_len)
         if not self.use_neumann and self.combination_mode not in ("dis", "union", "union_da"):
             k_out, v_out, idx = self._walker_path(p, q, k, v, q_len)
@@ -251,7 +255,14 @@ class CircuitKVCluster:
         self.last_keep_indices = idx
         k_out, v_out = k_out.unsqueeze(0), v_out.unsqueeze(0)
         if host:
-            k_out, v_out = k_out.cpu(), v_out.cpu()
+            # one pass over the link each way at full rate: pinned outputs (torch's caching
+            # host allocator), asynchronous copies, one wait
+            kh = torch.empty(k_out.shape, dtype=k_out.dtype, pin_memory=True)
+            vh = torch.empty(v_out.shape, dtype=v_out.dtype, pin_memory=True)
+            kh.copy_(k_out, non_blocking=True)
+            vh.copy_(v_out, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            k_out, v_out = kh, vh
         return k_out, v_out
 
     def _walker_path(self, p, q, k, v, q_len):

@@ -671,6 +671,21 @@ int ckv_gather(const ckv_layer* layer, int32_t window, const int32_t* idx, int32
   return e == cudaSuccess ? CKV_OK : cuda_fail(e, "gather");
 }
 
+int ckv_device_accessible(const void* ptr, int32_t* accessible) {
+  if (!accessible) return fail(CKV_ERR_ARG, "null argument");
+  *accessible = 0;
+  if (!ptr) return CKV_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return CKV_OK; }
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) { cudaGetLastError(); return CKV_OK; }
+  if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged)
+    *accessible = at.device == dev ? 1 : 0;
+  else if (at.type == cudaMemoryTypeHost)   // page-locked: mapped at the same address under UVA
+    *accessible = at.devicePointer == ptr ? 1 : 0;
+  return CKV_OK;
+}
+
 int ckv_set_stage_events(void* const* events, int32_t count) {
   if (count < 0 || (count > 0 && !events)) return fail(CKV_ERR_ARG, "bad stage event list");
   g_stage_events = count ? reinterpret_cast<cudaEvent_t*>(const_cast<void**>(events)) : nullptr;

@@ -51,6 +51,27 @@ def output_len(p: Params, n: int) -> int:
     return out.value
 
 
+def device_readable(t: torch.Tensor) -> bool:
+    """Whether the current CUDA device can read ``t`` in place (its own memory, or
+    page-locked host memory mapped at the same address)."""
+    if t.is_cuda:
+        return True
+    if not t.is_pinned() or not torch.cuda.is_available():
+        return False
+    ok = ctypes.c_int32(0)
+    check(_lib.load().ckv_device_accessible(ctypes.c_void_p(t.data_ptr()), ctypes.byref(ok)), "ckv_device_accessible")
+    return ok.value == 1
+
+
+def _require_readable(v: torch.Tensor) -> None:
+    """V is read only by the final gather: device memory, or page-locked host memory the
+    device reads in place."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("the CircuitKV B200 kernels need a CUDA device; none is available")
+    if not device_readable(v):
+        raise RuntimeError("v must be on the CUDA device or in page-locked host memory it can read")
+
+
 def _require_cuda(*ts: torch.Tensor) -> None:
     if not torch.cuda.is_available():
         raise RuntimeError("the CircuitKV B200 kernels need a CUDA device; none is available")
@@ -92,7 +113,8 @@ def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     ``scores`` (when requested) is ``[2, n]`` fp32: the two vectors ranked by the
     selection (QI / HI after smoothing for "dis"; influence / H2O for "max").
     """
-    _require_cuda(q, k, v)
+    _require_cuda(q, k)
+    _require_readable(v)
     H, n, D = q.shape
     L = make_layer(q, k, v)
     out_len = output_len(p, n)
@@ -295,7 +317,8 @@ def rng_fill(mode: int, seed: int, stream_id: int, count: int, device: torch.dev
 def gather(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window: int, idx: torch.Tensor):
     """K / V of the kept positions ``idx`` (``[kept]`` or ``[H, kept]``) then the last
     ``window`` rows: ``[H, kept + window, D]`` each."""
-    _require_cuda(q, k, v, idx)
+    _require_cuda(q, k, idx)
+    _require_readable(v)
     H, n, D = q.shape
     L = make_layer(q, k, v)
     idx = idx.to(torch.int32).contiguous()

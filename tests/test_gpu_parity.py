@@ -421,3 +421,14 @@ def test_host_tensors_round_trip():
     nd, ok = compare_keep(idx, g["keep"], g["combined"], 4, c["n"] - c["window"], len(g["keep"]) - 4,
                           margin=8.0 / (c["n"] - 1))
     assert ok
+    # pinned host tensors: K is copied, V's kept rows are read in place by the gather; the
+    # outputs equal those of device-resident inputs exactly
+    dev = torch.device("cuda", 0)
+    K, Q, V = repeat_kv(k, 4), q[None], repeat_kv(v, 4)
+    kp, qp, vp = K.pin_memory(), Q.pin_memory(), V.pin_memory()
+    assert ops.device_readable(vp[0]) and not ops.device_readable(V[0])
+    kd, vd = _cluster(c).update_kv(K.to(dev), Q.to(dev), V.to(dev), None, 4)
+    kh, vh = _cluster(c).update_kv(kp, qp, vp, None, 4)
+    assert kh.is_pinned() and vh.is_pinned()
+    assert torch.equal(kh, kd.cpu()) and torch.equal(vh, vd.cpu())
+    assert torch.equal(ko, kd.cpu()) and torch.equal(vo, vd.cpu())
