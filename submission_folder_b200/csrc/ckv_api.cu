@@ -152,6 +152,7 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.off_bk = take((size_t)2 * pl.K * pl.n_p * 4 + 4);
   pl.off_cg = take((size_t)2 * pl.n_p * 8 + 8);
   pl.off_agg = take((size_t)2 * pl.nscan * 2 * kMaxIters * 4);
+  pl.off_sin = take((size_t)2 * pl.nscan * kMaxIters * 4);   // incoming carry of each chunk
   pl.off_cum = take((size_t)2 * (pl.K + 1) * pl.n_p * 4 + 4);
   pl.off_cmax = take((size_t)2 * pl.nscan * (kMaxIters + 1) * 4);
   pl.sel_bytes = (size_t)6 * n * 4 + (size_t)n * 4 + (size_t)n;
@@ -340,7 +341,7 @@ int ckv_score_evict(const ckv_params* p, const ckv_layer* layer, void* workspace
 // One layer's latency-bound steps (selection, reduction tails) then overlap another
 // layer's tensor-core passes.
 namespace {
-constexpr int kLanes = 4;
+constexpr int kLanes = 16;
 constexpr int kMaxDevices = 64;
 struct Lanes {
   cudaStream_t s[kLanes];

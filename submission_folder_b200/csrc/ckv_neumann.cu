@@ -11,10 +11,15 @@
 // All K steps are carried together in ONE reverse sweep over positions: the
 // per-position update of the carry S = (S_0..S_{K-1}) is the affine map
 //     S' = (I + c_j gamma g_j N) S + c_j (x0_j, b_0[j], ..., b_{K-2}[j]),
-// N the shift; these maps are polynomials in N, so a chunk of positions
-// composes into one (K coefficients, K offsets) map and chunks combine in a
-// tree.  k_sweep_chunks builds b_k, c, g and the chunk maps; k_sweep_apply
-// folds the maps of all later chunks into its incoming carry, scans its own
+// N the shift; these maps are polynomials in N, so a run of positions
+// composes into one (K coefficients, K offsets) map.  Applying or composing a
+// single position's map costs O(K) (it is 1 + alpha N plus an offset); two
+// composed runs cost O(K^2).  So each thread sweeps a run of kSweepRun
+// consecutive positions in O(K) per position, and only run / warp / chunk
+// aggregates are composed densely (warp shuffles, then across warps).
+// k_sweep_chunks builds b_k, c, g and each chunk's map; its last CTA per chain
+// composes the chunk maps from the top and stores every chunk's incoming carry.
+// k_sweep_apply turns that carry into each run's incoming carry, sweeps its
 // positions and writes the running sums of x_0..x_K plus per-chunk maxima (the
 // early stop of PU:2183 needs the max of every term).
 #include "ckv_common.cuh"
@@ -109,36 +114,74 @@ __device__ float block_exclusive_scan_f(float v, float* scratch, float* total) {
 // reference's attention_for_hi is None, PU:2135-2146).
 CKV_DEV int row_source(const Plan& pl, int ch) { return (ch == 1 && pl.hi_rows) ? 1 : 0; }
 
-// Per-position map of position j (identity outside the transient prefix).
-template <int KM>
-CKV_DEV Map<KM> position_map(const Plan& pl, int ch, int j, float c, float g, const float* bk,
-                             float gamma, float x0) {
-  Map<KM> m;
-  map_identity(m);
-  if (j < pl.s || j >= pl.n_p) return m;
-  if (KM > 1) m.a[1] = c * gamma * g;
-  m.u[0] = c * x0;
-#pragma unroll
-  for (int k = 1; k < KM; ++k) m.u[k] = (k < pl.K) ? c * bk[k - 1] : 0.f;
-  return m;
-}
-
 CKV_DEV float start_value(const Plan& pl, int ch, int j) {
   // HI chain starts uniform over the transient states, QI from the query one-hot (a window position)
   return (ch == 1 && j >= pl.s && j < pl.n_p) ? 1.0f / (float)(pl.n - pl.s) : 0.f;
 }
 
+// Position j's map composed onto M (M covers higher positions and is applied first):
+// a <- (1 + alpha N) a, u <- (1 + alpha N) u + u_j, truncated at degree KM - 1.
+template <int KM>
+CKV_DEV void push_position(Map<KM>& M, float alpha, const float* uj) {
+#pragma unroll
+  for (int k = KM - 1; k >= 1; --k) {
+    M.a[k] = fmaf(alpha, M.a[k - 1], M.a[k]);
+    M.u[k] = fmaf(alpha, M.u[k - 1], M.u[k]) + uj[k];
+  }
+  M.u[0] += uj[0];
+}
+
+// Inclusive suffix composition within a warp: lane l ends with A_l o A_{l+1} o ... o A_31.
+template <int KM>
+CKV_DEV Map<KM> warp_suffix_compose(Map<KM> A) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    Map<KM> B;
+#pragma unroll
+    for (int i = 0; i < KM; ++i) {
+      B.a[i] = __shfl_down_sync(0xffffffffu, A.a[i], d);
+      B.u[i] = __shfl_down_sync(0xffffffffu, A.u[i], d);
+    }
+    if (lane + d < 32) A = compose(A, B);
+  }
+  return A;
+}
+
+// The map of lane l + 1's inclusive suffix (identity for the last lane).
+template <int KM>
+CKV_DEV Map<KM> next_lane_map(const Map<KM>& A) {
+  Map<KM> B;
+#pragma unroll
+  for (int i = 0; i < KM; ++i) {
+    B.a[i] = __shfl_down_sync(0xffffffffu, A.a[i], 1);
+    B.u[i] = __shfl_down_sync(0xffffffffu, A.u[i], 1);
+  }
+  if ((threadIdx.x & 31) == 31) map_identity(B);
+  return B;
+}
+
+// c, g and the per-position offsets u_j of thread's run (positions j0 .. j0 + kSweepRun - 1).
+static_assert(kSweepRun == 4, "the row loads below read one float4 per run");
+
+struct RunIn {
+  float c[kSweepRun], g[kSweepRun];
+};
+
 // ---------------------------------------------------------------------------
-// kernel 1: b_k, c, g and the chunk maps
+// kernel 1: b_k, c, g and the chunk maps; the last CTA of a chain stores the
+// incoming carry of every chunk
 // ---------------------------------------------------------------------------
 template <int KM>
-__global__ void __launch_bounds__(kScanChunk) k_sweep_chunks(const Plan pl, const ckv_params prm,
-                                                             char* ws) {
+__global__ void __launch_bounds__(kSweepThreads) k_sweep_chunks(const Plan pl, const ckv_params prm,
+                                                                char* ws) {
+  constexpr int KW = (KM + 3) / 4 * 4;       // w_k padded to whole float4s
   extern __shared__ __align__(16) float sm[];
   const int chunk = blockIdx.x, ch = blockIdx.y;
   const int src = row_source(pl, ch);
-  const int j = chunk * kScanChunk + threadIdx.x;
   const int K = pl.K;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int j0 = chunk * kScanChunk + threadIdx.x * kSweepRun;
   const bool tempered = prm.neumann_temperature != 1.0f && prm.neumann_temperature > 0.f;
   const float invT = tempered ? 1.0f / prm.neumann_temperature : 1.0f;
   const float gamma = prm.neumann_gamma;
@@ -150,10 +193,13 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_chunks(const Plan pl, cons
   float2* cg_out = reinterpret_cast<float2*>(ws + pl.off_cg) + (size_t)ch * pl.n_p;
   float* agg = reinterpret_cast<float*>(ws + pl.off_agg) + ((size_t)ch * pl.nscan) * 2 * KM;
 
-  float* sW = sm;                            // [K][W]
-  float* sMaps = sW + K * pl.W;              // [kScanChunk][2*KM+1]
-  float* scratch = sMaps + kScanChunk * map_stride<KM>();   // 32 floats
-  for (int i = threadIdx.x; i < K * pl.W; i += blockDim.x) sW[i] = wk[i];
+  float* sW = sm;                                        // [W][KW]: w_k of window row r
+  float* sWarp = sW + pl.W * KW;                         // [8 warps][2*KM+1]
+  float* scratch = sWarp + (kSweepThreads / 32) * map_stride<KM>();   // 32 floats
+  for (int i = threadIdx.x; i < pl.W * KW; i += blockDim.x) {
+    const int r = i / KW, k = i % KW;
+    sW[i] = k < K ? wk[k * pl.W + r] : 0.f;
+  }
 
   // G offset of this chunk: sum of g over all earlier positions (partial totals of
   // g_slice columns each)
@@ -162,185 +208,280 @@ __global__ void __launch_bounds__(kScanChunk) k_sweep_chunks(const Plan pl, cons
   for (int t = threadIdx.x; t < tiles_before; t += blockDim.x) off += gtile[t];
   off = block_reduce<false>(off, scratch);
 
-  float g = 0.f;
-  if (j < pl.n_p) {
-    g = fmaxf(colsum[j], 1e-6f);
-    if (tempered) g = powf(g, invT);
+  RunIn ri;
+  float run_tot = 0.f, pre[kSweepRun];
+#pragma unroll
+  for (int p = 0; p < kSweepRun; ++p) {
+    const int j = j0 + p;
+    float g = 0.f;
+    if (j < pl.n_p) {
+      g = fmaxf(colsum[j], 1e-6f);
+      if (tempered) g = powf(g, invT);
+    }
+    ri.g[p] = g;
+    pre[p] = run_tot;
+    run_tot += g;
   }
-  const float excl = block_exclusive_scan_f(g, scratch, nullptr);
-  const float Gprev = off + excl;              // G[j-1]
-  const float c = (j >= 1 && Gprev > 0.f) ? 1.0f / Gprev : 0.f;
+  const float excl = block_exclusive_scan_f(run_tot, scratch, nullptr);
+#pragma unroll
+  for (int p = 0; p < kSweepRun; ++p) {
+    const int j = j0 + p;
+    const float Gprev = off + excl + pre[p];           // G[j-1]
+    ri.c[p] = (j >= 1 && Gprev > 0.f) ? 1.0f / Gprev : 0.f;
+  }
+  __syncthreads();   // sW is complete
 
-  float bk[KM];
+  // b_k[j] = sum_r rows[r][j] w_k[r] for the run (rows are L2-resident)
+  float bk[kSweepRun][KM];
 #pragma unroll
-  for (int k = 0; k < KM; ++k) bk[k] = 0.f;
-  if (j < pl.n_p && j >= pl.s) {
-    // 16 independent row loads in flight per batch (the rows are L2-resident)
-    for (int r0 = 0; r0 < pl.W; r0 += 16) {
-      float v[16];
+  for (int p = 0; p < kSweepRun; ++p)
 #pragma unroll
-      for (int u = 0; u < 16; ++u) v[u] = __ldcg(rows + (size_t)(r0 + u) * pl.n_pad + j);
+    for (int k = 0; k < KM; ++k) bk[p][k] = 0.f;
+  if (j0 < pl.n_p && j0 + kSweepRun > pl.s) {
+    const bool full = j0 + kSweepRun <= pl.n_p;
+    constexpr int kRowBatch = 8;   // rows in flight per thread (W is a multiple of 8)
+    for (int r0 = 0; r0 < pl.W; r0 += kRowBatch) {
+      float4 xb[kRowBatch];
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        float x = v[u];
-        if (tempered) x = x > 0.f ? powf(x, invT) : 0.f;
+      for (int u = 0; u < kRowBatch; ++u) {
+        const float* rr = rows + (size_t)(r0 + u) * pl.n_pad + j0;
+        if (full) {
+          xb[u] = __ldcg(reinterpret_cast<const float4*>(rr));
+        } else {
+          xb[u].x = (j0 < pl.n_p) ? __ldcg(rr) : 0.f;
+          xb[u].y = (j0 + 1 < pl.n_p) ? __ldcg(rr + 1) : 0.f;
+          xb[u].z = (j0 + 2 < pl.n_p) ? __ldcg(rr + 2) : 0.f;
+          xb[u].w = (j0 + 3 < pl.n_p) ? __ldcg(rr + 3) : 0.f;
+        }
+      }
 #pragma unroll
-        for (int k = 0; k < KM; ++k)
-          if (k < K) bk[k] = fmaf(x, sW[k * pl.W + r0 + u], bk[k]);
+      for (int u = 0; u < kRowBatch; ++u) {
+        float x[kSweepRun] = {xb[u].x, xb[u].y, xb[u].z, xb[u].w};
+        if (tempered) {
+#pragma unroll
+          for (int p = 0; p < kSweepRun; ++p) x[p] = x[p] > 0.f ? powf(x[p], invT) : 0.f;
+        }
+        float w[KW];
+#pragma unroll
+        for (int q = 0; q < KW; q += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(sW + (r0 + u) * KW + q);
+          w[q] = v.x; w[q + 1] = v.y; w[q + 2] = v.z; w[q + 3] = v.w;
+        }
+#pragma unroll
+        for (int p = 0; p < kSweepRun; ++p)
+#pragma unroll
+          for (int k = 0; k < KM; ++k) bk[p][k] = fmaf(x[p], w[k], bk[p][k]);
       }
     }
   }
-  if (j < pl.n_p) {
+  // outside the transient prefix the position map is the identity
 #pragma unroll
-    for (int k = 0; k < KM; ++k)
-      if (k < K) bk_out[(size_t)k * pl.n_p + j] = bk[k];
-    cg_out[j] = make_float2(c, g);
-  }
-  Map<KM> m = position_map<KM>(pl, ch, j, c, g, bk, gamma, start_value(pl, ch, j));
-  store_map(sMaps + threadIdx.x * map_stride<KM>(), m);
-  __syncthreads();
-  for (int d = 1; d < kScanChunk; d <<= 1) {
-    if ((threadIdx.x % (2 * d)) == 0) {
-      const Map<KM> L = load_map<KM>(sMaps + threadIdx.x * map_stride<KM>());
-      const Map<KM> R = load_map<KM>(sMaps + (threadIdx.x + d) * map_stride<KM>());
-      store_map(sMaps + threadIdx.x * map_stride<KM>(), compose(L, R));
+  for (int p = 0; p < kSweepRun; ++p) {
+    const int j = j0 + p;
+    if (j < pl.s || j >= pl.n_p)
+#pragma unroll
+      for (int k = 0; k < KM; ++k) bk[p][k] = 0.f;
+    if (j < pl.n_p) {
+#pragma unroll
+      for (int k = 0; k < KM; ++k)
+        if (k < K) bk_out[(size_t)k * pl.n_p + j] = bk[p][k];
+      cg_out[j] = make_float2(ri.c[p], ri.g[p]);
     }
-    __syncthreads();
   }
-  if (threadIdx.x < 2 * KM) agg[(size_t)chunk * 2 * KM + threadIdx.x] = sMaps[threadIdx.x];
+
+  // this run's map (positions from the top of the run down), then the chunk's
+  Map<KM> A;
+  map_identity(A);
+#pragma unroll
+  for (int p = kSweepRun - 1; p >= 0; --p) {
+    const int j = j0 + p;
+    if (j < pl.s || j >= pl.n_p) continue;
+    float uj[KM];
+    uj[0] = ri.c[p] * start_value(pl, ch, j);
+#pragma unroll
+    for (int k = 1; k < KM; ++k) uj[k] = (k < K) ? ri.c[p] * bk[p][k - 1] : 0.f;
+    push_position(A, KM > 1 ? ri.c[p] * gamma * ri.g[p] : 0.f, uj);
+  }
+  A = warp_suffix_compose(A);
+  if (lane == 0) store_map(sWarp + wid * map_stride<KM>(), A);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Map<KM> M = load_map<KM>(sWarp + (kSweepThreads / 32 - 1) * map_stride<KM>());
+    for (int w = kSweepThreads / 32 - 2; w >= 0; --w) M = compose(load_map<KM>(sWarp + w * map_stride<KM>()), M);
+    store_map(agg + (size_t)chunk * 2 * KM, M);
+  }
+
+  // the last CTA of this chain: incoming carry of every chunk = u of (A_{c+1} o ... o A_top)
+  Header* hdr = reinterpret_cast<Header*>(ws);
+  __shared__ bool last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(&hdr->cnt_sweep[ch], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last || wid != 0) return;
+  __threadfence();
+  float* sin = reinterpret_cast<float*>(ws + pl.off_sin) + ((size_t)ch * pl.nscan) * kMaxIters;
+  Map<KM> acc;   // composition of the chunks above the current group of 32
+  map_identity(acc);
+  for (int hi = pl.nscan; hi > 0; hi -= 32) {
+    const int lo = hi - 32;
+    const int c = lo + lane;
+    Map<KM> m;
+    if (c >= 0) {
+#pragma unroll
+      for (int i = 0; i < KM; ++i) {
+        m.a[i] = __ldcg(agg + (size_t)c * 2 * KM + i);
+        m.u[i] = __ldcg(agg + (size_t)c * 2 * KM + KM + i);
+      }
+    } else {
+      map_identity(m);
+    }
+    const Map<KM> incl = warp_suffix_compose(m);
+    const Map<KM> excl = compose(next_lane_map(incl), acc);   // chunks c+1 .. top
+    if (c >= 0)
+#pragma unroll
+      for (int k = 0; k < KM; ++k) sin[(size_t)c * kMaxIters + k] = excl.u[k];
+    Map<KM> top;
+#pragma unroll
+    for (int i = 0; i < KM; ++i) {
+      top.a[i] = __shfl_sync(0xffffffffu, incl.a[i], 0);
+      top.u[i] = __shfl_sync(0xffffffffu, incl.u[i], 0);
+    }
+    acc = compose(top, acc);
+  }
+  if (lane == 0) hdr->cnt_sweep[ch] = 0;
 }
 
 // ---------------------------------------------------------------------------
-// kernel 2: incoming carry, in-chunk suffix scan, terms x_0..x_K
+// kernel 2: incoming carry of each run, the run's sweep, terms x_0..x_K
 // ---------------------------------------------------------------------------
 template <int KM>
-__global__ void __launch_bounds__(kScanChunk) k_sweep_apply(const Plan pl, const ckv_params prm,
-                                                            char* ws) {
-  extern __shared__ __align__(16) float sm[];
+__global__ void __launch_bounds__(kSweepThreads) k_sweep_apply(const Plan pl, const ckv_params prm,
+                                                               char* ws) {
   const int chunk = blockIdx.x, ch = blockIdx.y;
-  const int j = chunk * kScanChunk + threadIdx.x;
   const int K = pl.K;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int j0 = chunk * kScanChunk + threadIdx.x * kSweepRun;
   const float gamma = prm.neumann_gamma;
-  const float* agg = reinterpret_cast<const float*>(ws + pl.off_agg) + ((size_t)ch * pl.nscan) * 2 * KM;
+  const float* sin = reinterpret_cast<const float*>(ws + pl.off_sin) + ((size_t)ch * pl.nscan + chunk) * kMaxIters;
   const float* bk_in = reinterpret_cast<const float*>(ws + pl.off_bk) + (size_t)ch * K * pl.n_p;
   const float2* cg_in = reinterpret_cast<const float2*>(ws + pl.off_cg) + (size_t)ch * pl.n_p;
   float* cum = reinterpret_cast<float*>(ws + pl.off_cum) + (size_t)ch * (K + 1) * pl.n_p;
   float* cmax = reinterpret_cast<float*>(ws + pl.off_cmax) + ((size_t)ch * pl.nscan + chunk) * (kMaxIters + 1);
+  __shared__ float sWarp[kSweepThreads / 32][2 * KM + 1];
+  __shared__ float sCarry[kSweepThreads / 32][KM];
+  __shared__ float sMax[kSweepThreads / 32][kMaxIters + 1];
 
-  float* bufA = sm;                               // [kScanChunk][2*KM+1]
-  float* bufB = bufA + kScanChunk * map_stride<KM>();   // [kScanChunk][2*KM+1]
-  float* scratch = bufB + kScanChunk * map_stride<KM>();   // (kScanChunk/32) * (kMaxIters+1) floats
-
-  // 1) fold the maps of all later chunks (tree over at most kScanChunk maps per round)
-  float Sin[KM];
+  float c[kSweepRun], g[kSweepRun], bk[kSweepRun][KM];
 #pragma unroll
-  for (int k = 0; k < KM; ++k) Sin[k] = 0.f;
-  {
-    // process later chunks from the far end in rounds of kScanChunk maps
-    Map<KM> acc;   // composition of the chunks already folded (they are higher)
-    map_identity(acc);
-    const int first = chunk + 1, last = pl.nscan;   // [first, last)
-    for (int hi = last; hi > first; hi -= kScanChunk) {
-      const int lo = max(first, hi - kScanChunk);
-      const int cnt = hi - lo;
-      Map<KM> m;
-      if ((int)threadIdx.x < cnt) m = load_map<KM>(agg + (size_t)(lo + threadIdx.x) * 2 * KM);
-      else map_identity(m);
-      store_map(bufA + threadIdx.x * map_stride<KM>(), m);
-      __syncthreads();
-      for (int d = 1; d < kScanChunk; d <<= 1) {
-        if ((threadIdx.x % (2 * d)) == 0) {
-          const Map<KM> L = load_map<KM>(bufA + threadIdx.x * map_stride<KM>());
-          const Map<KM> R = load_map<KM>(bufA + (threadIdx.x + d) * map_stride<KM>());
-          store_map(bufA + threadIdx.x * map_stride<KM>(), compose(L, R));
-        }
-        __syncthreads();
-      }
-      acc = compose(load_map<KM>(bufA), acc);
-      __syncthreads();
-    }
-    const float zero[KM] = {};
-    apply(acc, zero, Sin);
+  for (int p = 0; p < kSweepRun; ++p) {
+    const int j = j0 + p;
+    const bool in = j < pl.n_p;
+    const float2 v = in ? cg_in[j] : make_float2(0.f, 0.f);
+    c[p] = v.x; g[p] = v.y;
+#pragma unroll
+    for (int k = 0; k < KM; ++k) bk[p][k] = (in && k < K && j >= pl.s) ? bk_in[(size_t)k * pl.n_p + j] : 0.f;
   }
-
-  // 2) per-position maps of this chunk, inclusive suffix scan (Hillis-Steele)
-  float c = 0.f, g = 0.f, bk[KM];
+  auto offsets = [&](int p, float* uj) {
+    const int j = j0 + p;
+    uj[0] = c[p] * start_value(pl, ch, j);
 #pragma unroll
-  for (int k = 0; k < KM; ++k) bk[k] = 0.f;
-  if (j < pl.n_p) {
-    const float2 v = cg_in[j];
-    c = v.x; g = v.y;
+    for (int k = 1; k < KM; ++k) uj[k] = (k < K) ? c[p] * bk[p][k - 1] : 0.f;
+  };
+  // this run's map, the suffix within the warp, the carry into each warp
+  Map<KM> A;
+  map_identity(A);
 #pragma unroll
-    for (int k = 0; k < KM; ++k)
-      if (k < K) bk[k] = bk_in[(size_t)k * pl.n_p + j];
+  for (int p = kSweepRun - 1; p >= 0; --p) {
+    const int j = j0 + p;
+    if (j < pl.s || j >= pl.n_p) continue;
+    float uj[KM];
+    offsets(p, uj);
+    push_position(A, KM > 1 ? c[p] * gamma * g[p] : 0.f, uj);
   }
-  const float x0 = start_value(pl, ch, j);
-  store_map(bufA + threadIdx.x * map_stride<KM>(), position_map<KM>(pl, ch, j, c, g, bk, gamma, x0));
+  const Map<KM> incl = warp_suffix_compose(A);
+  if (lane == 0) store_map(&sWarp[wid][0], incl);
   __syncthreads();
-  float* src = bufA;
-  float* dst = bufB;
-  for (int d = 1; d < kScanChunk; d <<= 1) {
-    Map<KM> m = load_map<KM>(src + threadIdx.x * map_stride<KM>());
-    if (threadIdx.x + d < kScanChunk) m = compose(m, load_map<KM>(src + (threadIdx.x + d) * map_stride<KM>()));
-    store_map(dst + threadIdx.x * map_stride<KM>(), m);
-    __syncthreads();
-    float* t = src; src = dst; dst = t;
-  }
-  // carry after all positions > j
-  float S[KM];
-  if (threadIdx.x + 1 < kScanChunk) apply(load_map<KM>(src + (threadIdx.x + 1) * map_stride<KM>()), Sin, S);
-  else {
+  if (threadIdx.x == 0) {
+    float S[KM], T[KM];
 #pragma unroll
-    for (int k = 0; k < KM; ++k) S[k] = Sin[k];
-  }
-
-  // 3) terms x_0..x_K of this position, running sums and per-chunk maxima
-  const bool valid = (j >= pl.s && j < pl.n_p);
-  float x = x0, run = x0;
-  float mx[kMaxIters + 1];
+    for (int k = 0; k < KM; ++k) S[k] = sin[k];
+    for (int w = kSweepThreads / 32 - 1; w >= 0; --w) {
 #pragma unroll
-  for (int k = 0; k <= kMaxIters; ++k) mx[k] = 0.f;
-  if (valid) cum[j] = run;
+      for (int k = 0; k < KM; ++k) sCarry[w][k] = S[k];
+      apply(load_map<KM>(&sWarp[w][0]), S, T);
 #pragma unroll
-  for (int k = 0; k < KM; ++k) {
-    if (k < K) {
-      x = fmaf(gamma * g, S[k], bk[k]);
-      run += x;
-      if (valid) {
-        cum[(size_t)(k + 1) * pl.n_p + j] = run;
-        mx[k + 1] = fabsf(x);
-      }
+      for (int k = 0; k < KM; ++k) S[k] = T[k];
     }
   }
-  // block max of every term index: warp shuffles, one barrier
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  float S[KM];
+  {
+    float Cw[KM];
+#pragma unroll
+    for (int k = 0; k < KM; ++k) Cw[k] = sCarry[wid][k];
+    apply(next_lane_map(incl), Cw, S);   // carry after every position above this run
+  }
+
+  // the run's positions from the top: terms from the incoming carry, then the update
+  float mx[KM + 1];
+#pragma unroll
+  for (int k = 0; k <= KM; ++k) mx[k] = 0.f;
+#pragma unroll
+  for (int p = kSweepRun - 1; p >= 0; --p) {
+    const int j = j0 + p;
+    if (j >= pl.n_p) continue;
+    const bool valid = j >= pl.s;
+    const float x0 = start_value(pl, ch, j);
+    float xs[KM];
+#pragma unroll
+    for (int k = 0; k < KM; ++k) xs[k] = 0.f;
+    float run = x0;
+    if (valid) cum[j] = run;
+#pragma unroll
+    for (int k = 0; k < KM; ++k) {
+      if (k < K) {
+        const float x = fmaf(gamma * g[p], S[k], bk[p][k]);
+        xs[k] = x;
+        run += x;
+        if (valid) {
+          cum[(size_t)(k + 1) * pl.n_p + j] = run;
+          mx[k + 1] = fmaxf(mx[k + 1], fabsf(x));
+        }
+      }
+    }
+    if (valid) {   // S_k += c_j x_k[j] (x_0 = start, x_k for k >= 1 from the old carry)
+#pragma unroll
+      for (int k = KM - 1; k >= 1; --k) S[k] = fmaf(c[p], xs[k - 1], S[k]);
+      S[0] = fmaf(c[p], x0, S[0]);
+    }
+  }
+  // block max of every term index
 #pragma unroll
   for (int k = 1; k <= KM; ++k) {
-    float v = (valid && k <= K) ? mx[k] : 0.f;
-    v = warp_max(v);
-    if (lane == 0) scratch[wid * (kMaxIters + 1) + k] = v;
+    const float v = warp_max(k <= K ? mx[k] : 0.f);
+    if (lane == 0) sMax[wid][k] = v;
   }
   __syncthreads();
   if (threadIdx.x >= 1 && threadIdx.x <= K) {
     float v = 0.f;
-    for (int w = 0; w < kScanChunk / 32; ++w) v = fmaxf(v, scratch[w * (kMaxIters + 1) + threadIdx.x]);
+    for (int w = 0; w < kSweepThreads / 32; ++w) v = fmaxf(v, sMax[w][threadIdx.x]);
     cmax[threadIdx.x] = v;
   }
 }
 
 template <int KM>
 static cudaError_t launch_sweep_t(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st) {
-  const size_t s1 = sizeof(float) * ((size_t)pl.K * pl.W + kScanChunk * map_stride<KM>() + 64);
-  const size_t s2 = sizeof(float) * (2 * (size_t)kScanChunk * map_stride<KM>() + (kScanChunk / 32) * (kMaxIters + 1) + 64);
+  constexpr int KW = (KM + 3) / 4 * 4;
+  const size_t s1 = sizeof(float) * ((size_t)pl.W * KW + (kSweepThreads / 32) * map_stride<KM>() + 64);
   {
-    cudaError_t e = ensure_dynamic_smem((const void*)k_sweep_chunks<KM>, s1);
-    if (e == cudaSuccess) e = ensure_dynamic_smem((const void*)k_sweep_apply<KM>, s2);
+    const cudaError_t e = ensure_dynamic_smem((const void*)k_sweep_chunks<KM>, s1);
     if (e != cudaSuccess) return e;
   }
   const dim3 grid(pl.nscan, pl.nchains);
-  k_sweep_chunks<KM><<<grid, kScanChunk, s1, st>>>(pl, prm, ws);
+  k_sweep_chunks<KM><<<grid, kSweepThreads, s1, st>>>(pl, prm, ws);
   stage_mark(st);
-  k_sweep_apply<KM><<<grid, kScanChunk, s2, st>>>(pl, prm, ws);
+  k_sweep_apply<KM><<<grid, kSweepThreads, 0, st>>>(pl, prm, ws);
   return cudaGetLastError();
 }
 

@@ -9,7 +9,9 @@
 namespace ckv {
 
 constexpr int kColTile = 64;        // key columns per MMA tile
-constexpr int kScanChunk = 256;     // prefix positions per sweep chunk (one CTA)
+constexpr int kScanChunk = 1024;    // prefix positions per sweep chunk (one CTA)
+constexpr int kSweepThreads = 256;  // threads per sweep CTA
+constexpr int kSweepRun = kScanChunk / kSweepThreads;   // consecutive positions per thread
 constexpr int kWarps = 8;           // warps of the window kernels
 
 // Workspace header (first 512 bytes of every layer workspace).
@@ -26,7 +28,8 @@ struct alignas(16) Header {
   int32_t kept;            // prefix positions kept (selection output count)
   uint32_t tile_ctr[2];    // next column tile of the tensor-core pooling launch (pass, re-run)
   int32_t need_exact;      // 1: the pooling pass recomputes the clamped entropy / mass exactly
-  int32_t pad[49];
+  uint32_t cnt_sweep[2];   // arrival counters of the sweep's chunk kernel, per chain
+  int32_t pad[47];
   uint32_t cnt_group[64];  // arrival counters per head group of the stats kernel
 };
 static_assert(sizeof(Header) == 512, "header must be 512 bytes");
@@ -63,7 +66,7 @@ struct Plan {
   size_t off_stats, off_lse, off_lastlogit, off_spec, off_epart, off_mpart;
   size_t off_minx;    // [nstat_chunks][H][W] row minimum of the rounded logits (tensor-core moments)
   size_t off_rows_qi, off_rows_hi, off_colsum, off_gtile, off_rspart;
-  size_t off_wk, off_yk, off_ymax, off_bk, off_cg, off_agg, off_cum, off_cmax;
+  size_t off_wk, off_yk, off_ymax, off_bk, off_cg, off_agg, off_sin, off_cum, off_cmax;
   size_t off_sel, off_ph;
   // per-head eviction (PU:2208-2382, 3296-3464): only allocated in that mode
   size_t off_ph_q2w;   // [H][W] query row -> window columns
