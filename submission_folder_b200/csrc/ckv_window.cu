@@ -1460,12 +1460,21 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
         // folding it in would seed the running max with the mask value when it comes first
         if (jb > lim) continue;
         float x[32];
-        uint32_t px = 0, pn = 0;   // packed running max / min of the chunk's rounded logits
+        uint32_t pk[16];
 #pragma unroll
-        for (int k = 0; k < 32; k += 2) {
-          const uint32_t pk = round_pack<DT>(v[k], v[k + 1], rs, x[k], x[k + 1]);
-          px = k == 0 ? pk : pmax2<DT>(px, pk);
-          pn = k == 0 ? pk : pmin2<DT>(pn, pk);
+        for (int k = 0; k < 32; k += 2) pk[k >> 1] = round_pack<DT>(v[k], v[k + 1], rs, x[k], x[k + 1]);
+        // packed max / min of the chunk's rounded logits: trees of depth 4
+        uint32_t px, pn;
+        {
+          uint32_t mx[8], mn[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) { mx[i] = pmax2<DT>(pk[i], pk[i + 8]); mn[i] = pmin2<DT>(pk[i], pk[i + 8]); }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) { mx[i] = pmax2<DT>(mx[i], mx[i + 4]); mn[i] = pmin2<DT>(mn[i], mn[i + 4]); }
+#pragma unroll
+          for (int i = 0; i < 2; ++i) { mx[i] = pmax2<DT>(mx[i], mx[i + 2]); mn[i] = pmin2<DT>(mn[i], mn[i + 2]); }
+          px = pmax2<DT>(mx[0], mx[1]);
+          pn = pmin2<DT>(mn[0], mn[1]);
         }
         float cm, cmin;
         if (jb + 31 > lim) {   // the masked / out-of-range tail of the row (last tiles only)
@@ -1493,18 +1502,21 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
           M.m = cm2;
         }
         const float nm = -M.m;
-        float z0 = 0.f, z1 = 0.f, t0a = 0.f, t1a = 0.f;
+        // even / odd columns in the two halves of packed pairs (the same sums as two
+        // scalar accumulators)
+        const F2 l2e = f2(kLog2e, kLog2e), nm2 = f2(nm, nm);
+        F2 z2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)}, t2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};   // 4 chains each
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
-          const float d0 = fmaf(x[k], kLog2e, nm), d1 = fmaf(x[k + 1], kLog2e, nm);
-          const float e0 = ex2(d0), e1 = ex2(d1);
-          z0 += e0;
-          z1 += e1;
-          t0a = fmaf(e0, d0, t0a);
-          t1a = fmaf(e1, d1, t1a);
+          const F2 d2 = fma2(f2(x[k], x[k + 1]), l2e, nm2);
+          const F2 e2 = f2(ex2(f2lo(d2)), ex2(f2hi(d2)));
+          const int q = (k >> 1) & 1;
+          z2[q] = add2(z2[q], e2);
+          t2[q] = fma2(e2, d2, t2[q]);
         }
-        M.z += z0 + z1;
-        M.t += t0a + t1a;
+        const F2 zs = add2(z2[0], z2[1]), ts = add2(t2[0], t2[1]);
+        M.z += f2lo(zs) + f2hi(zs);
+        M.t += f2lo(ts) + f2hi(ts);
         if (jb < pl.s) {
 #pragma unroll
           for (int k = 0; k < 32; ++k)
