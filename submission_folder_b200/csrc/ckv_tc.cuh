@@ -117,6 +117,12 @@ CKV_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 CKV_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 8 consecutive fp32 columns of this thread's TMEM lane into r[0..7] (no wait).
+CKV_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 
 // One arrival on an mbarrier (no transaction bytes).
 CKV_DEV void mbar_arrive(uint64_t* bar) {

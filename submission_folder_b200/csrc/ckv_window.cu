@@ -1838,35 +1838,42 @@ __global__ void __launch_bounds__(kP2Threads, 1)
       if (!ok && lane == 0) epi_abort = 1;   // the rest of the tile is skipped; the loop ends at its boundary
       if (ok) {   // TMEM loads are warp-collective
         tc::fence_after_sync();
+        // two halves of 8 columns: the second half's TMEM loads are in flight while the
+        // first half is processed
         uint32_t ra[16], rb[16];
         const uint32_t col = (uint32_t)((s & 1) * 2 * TN + cq * 16);
-        tc::tmem_ld16_nowait(lane_base + col, ra);
-        tc::tmem_ld16_nowait(lane_base + col + TN, rb);
+        tc::tmem_ld8_nowait(lane_base + col, ra);
+        tc::tmem_ld8_nowait(lane_base + col + TN, rb);
         tc::tmem_wait_ld();
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bar_tfree[s & 1]);
+        tc::tmem_ld8_nowait(lane_base + col + 8, ra + 8);
+        tc::tmem_ld8_nowait(lane_base + col + TN + 8, rb + 8);
         float va[16], vb[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          asm volatile("" : "+r"(ra[k]), "+r"(rb[k]));
-          va[k] = __uint_as_float(ra[k]);
-          vb[k] = __uint_as_float(rb[k]);
-        }
         const int ha = g * G + e, hb = ha + 2;
         const float La = slse[ha * W + t], Lb = slse[hb * W + t];
         const float fqa = ((qbits >> g) & 1u) ? 1.f : 0.f, fqb = ((qbits >> (16 + g)) & 1u) ? 1.f : 0.f;
         const float fha = ((hbits >> g) & 1u) ? 1.f : 0.f, fhb = ((hbits >> (16 + g)) & 1u) ? 1.f : 0.f;
+        // the loaded half [h0, h0 + 8): into floats, rounded as the reference rounds a logit
+        auto take_half = [&](int h0) {
 #pragma unroll
-        for (int k = 0; k < 16; k += 2) {
-          float x0, x1, y0, y1;
-          round_pair<DT>(va[k], va[k + 1], rs, x0, x1);
-          round_pair<DT>(vb[k], vb[k + 1], rs, y0, y1);
-          va[k] = x0; va[k + 1] = x1; vb[k] = y0; vb[k + 1] = y1;
-        }
+          for (int k = h0; k < h0 + 8; ++k) {
+            asm volatile("" : "+r"(ra[k]), "+r"(rb[k]));
+            va[k] = __uint_as_float(ra[k]);
+            vb[k] = __uint_as_float(rb[k]);
+          }
+#pragma unroll
+          for (int k = h0; k < h0 + 8; k += 2) {
+            float x0, x1, y0, y1;
+            round_pair<DT>(va[k], va[k + 1], rs, x0, x1);
+            round_pair<DT>(vb[k], vb[k + 1], rs, y0, y1);
+            va[k] = x0; va[k + 1] = x1; vb[k] = y0; vb[k + 1] = y1;
+          }
+        };
+        take_half(0);
         float ent0 = 0.f, ent1 = 0.f, mass0 = 0.f, mass1 = 0.f;
         const int jb = j0 + cq * 16;
-        const bool interior = jb + 15 <= lim && jb >= pl.s;
+        // warp-uniform (the TMEM wait inside `cols` is warp-collective): a warp with any
+        // lane at the masked edge takes the general path
+        const bool interior = __all_sync(0xffffffffu, jb + 15 <= lim && jb >= pl.s);
         // one logit pair (heads a, b at column c of the quarter): probabilities, the
         // exact entropy / mass terms when asked for, this lane's pooled values
         auto logit2 = [&](auto xtag, auto itag, auto htag, float xa, float xb, int j, int c) {
@@ -1902,7 +1909,15 @@ __global__ void __launch_bounds__(kP2Threads, 1)
         };
         auto cols = [&](auto xtag, auto itag, auto htag) {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) logit2(xtag, itag, htag, va[c], vb[c], jb + c, c);
+          for (int c = 0; c < 8; ++c) logit2(xtag, itag, htag, va[c], vb[c], jb + c, c);
+          __syncwarp();
+          tc::tmem_wait_ld();   // the second half; then the accumulator buffer is free
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bar_tfree[s & 1]);
+          take_half(8);
+#pragma unroll
+          for (int c = 8; c < 16; ++c) logit2(xtag, itag, htag, va[c], vb[c], jb + c, c);
         };
         auto run = [&](auto xtag, auto htag) {
           if (interior) cols(xtag, BoolTag<true>{}, htag);
