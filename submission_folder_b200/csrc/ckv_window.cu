@@ -1674,6 +1674,8 @@ __global__ void __launch_bounds__(kP2Threads, 1)
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
   if (a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->fixup) == 0) return;
+  // the branch without the exact recomputation runs in k_tc_pool_t
+  if (!a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->need_exact) == 0) return;
   int32_t* status = &hdr->status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int W = pl.W, G = pl.G, R = G * W;          // 64, 4, 256
@@ -2046,12 +2048,12 @@ __global__ void __launch_bounds__(kP2Threads, 1)
 // [heads, n, 128] view -> a 3-D tiled map over (dim, head, token) with a (64 x 2 x rows)
 // box: consecutive smem rows alternate between two heads of one token.
 static bool make_tmap_pairs(CUtensorMap* m, const void* base, int dtype, int n, int heads, int64_t hs,
-                            int64_t ts, int rows) {
+                            int64_t ts, int rows, int hbox = 2) {
   auto enc = get_encode();
   if (!enc) return false;
   const cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)n};
   const cuuint64_t strides[2] = {(cuuint64_t)hs * 2, (cuuint64_t)ts * 2};
-  const cuuint32_t box[3] = {64, 2, (cuuint32_t)rows};
+  const cuuint32_t box[3] = {64, (cuuint32_t)hbox, (cuuint32_t)rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = enc(m, dtype == CKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                          3, const_cast<void*>(base), dims, strides, box, estr,
@@ -2071,6 +2073,314 @@ static cudaError_t launch_tc_pool(const WinArgs& a0, cudaStream_t st) {
   const size_t smem = tc_pool_smem(pl);
   { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool<DT>, smem); if (e != cudaSuccess) return e; }
   k_tc_pool<DT><<<pl.tc_nclusters, kP2Threads, smem, st>>>(tq, tk, a);
+  return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------------------
+// pooling pass with keys on the TMEM lanes (the branch without the exact recomputation)
+// ---------------------------------------------------------------------------
+// When the moments pass settled the head sets, the pooling pass only turns logits into
+// probabilities and pools them.  This form puts a tile of 128 keys on the UMMA's M side
+// (A operand) and the KV group's 256 window-query rows on its N side (B operand; a
+// (dim, head, token) tensor map with a 4-head box orders them (window row, head)), so
+// 8 UMMAs of N = 256 cover a 128 x 256 block: half the operand traffic per logit of the
+// head-pair form and half as many pipeline steps.  A thread owns one key (its TMEM lane)
+// and a quarter of the columns (16 window rows x the group's 4 heads): pooling over the
+// heads is in-thread, and its rows' pooled values accumulate over the KV groups in
+// registers until the tile's rows, column sums, row-sum partials and g totals are written
+// (the head-pair form's layout, per 64-key half).
+constexpr int kPTTN = 128;                 // keys per tile
+constexpr int kPTStages = 2;               // (queries, K tile) stages
+constexpr int kPTEpiWarps = 16;
+constexpr int kPTThreads = 32 * (kPTEpiWarps + 1);
+
+struct PTSmem {
+  size_t stage_bytes, off_lse, off_colpart, off_rowpart, off_gsum, total;
+};
+
+static __host__ __device__ PTSmem pt_layout(const Plan& pl) {
+  PTSmem L;
+  const size_t R = (size_t)pl.G * pl.W;
+  L.stage_bytes = R * 256 + (size_t)kPTTN * 256;
+  size_t off = kPTStages * L.stage_bytes;
+  L.off_lse = off; off += (size_t)pl.H * pl.W * 4;       // [group][row][head of the group]
+  L.off_colpart = off; off += (size_t)4 * kPTTN * 4;     // [quarter][key]
+  L.off_rowpart = off; off += (size_t)4 * pl.W * 4;      // [lane group][row]
+  L.off_gsum = off; off += 16 * 4;
+  L.total = 1024 + off;
+  return L;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kPTThreads, 1)
+    k_tc_pool_t(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
+  extern __shared__ char smem_raw[];
+  const Plan& pl = a.pl;
+  Header* hdr = reinterpret_cast<Header*>(a.ws);
+  if (*reinterpret_cast<volatile int32_t*>(&hdr->need_exact) != 0) return;   // the head-pair form runs
+  int32_t* status = &hdr->status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = pl.W, G = pl.G, R = G * W;          // 64, 4, 256
+  const int TN = kPTTN, S = kPTStages;
+  const int ntn = (pl.n + TN - 1) / TN;
+  const int ngroups = pl.Hkv;
+  const PTSmem Ly = pt_layout(pl);
+  char* base = align1024(smem_raw);
+  char* stg = base;
+  const float4* slse4 = reinterpret_cast<const float4*>(base + Ly.off_lse);
+  float* colpart = reinterpret_cast<float*>(base + Ly.off_colpart);
+  float* rowpart = reinterpret_cast<float*>(base + Ly.off_rowpart);
+  float* gsum = reinterpret_cast<float*>(base + Ly.off_gsum);
+  __shared__ __align__(8) uint64_t bar_ld[kPTStages], bar_sfree[kPTStages], bar_full[2], bar_tfree[2], bar_tile;
+  __shared__ int stage_tile[kPTStages];   // producer only: tile loaded into each stage (-1: none)
+  __shared__ int tile_slot[2];            // tile k of this CTA in slot k & 1 (-1: no tile left)
+  __shared__ volatile int epi_abort;      // written by epilogue warps only, read after a barrier
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+  const uint32_t ncols = 512;             // two accumulator buffers of N = 256
+  if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) { tc::mbar_init(&bar_ld[i], 1); tc::mbar_init(&bar_sfree[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bar_full[i], 1);
+      tc::mbar_init(&bar_tfree[i], kPTEpiWarps);
+    }
+    tc::mbar_init(&bar_tile, 1);
+    epi_abort = 0;
+    tc::fence_barrier_init();
+    abort_sh = 0;
+  }
+  {   // log-sum-exp re-laid as [group][window row][head of the group] (one float4 per row)
+    const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);   // [H][W]
+    float* sl = reinterpret_cast<float*>(base + Ly.off_lse);
+    for (int i = threadIdx.x; i < pl.H * W; i += blockDim.x) {
+      const int h = i / W, r = i % W;
+      sl[((h / G) * W + r) * G + (h % G)] = __ldcg(lse + i);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == kPTEpiWarps) {
+    // ---------------- producer: tiles, TMA loads and UMMA issue (one thread) ----------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, 256);
+      uint32_t* ctr = &hdr->tile_ctr[0];
+      int load_tile = -1;
+      int next_tile = (int)atomicAdd(ctr, 1u);   // fetched one tile ahead: the atomic's latency hides
+      auto load_step = [&](int s) {
+        const int st = s % S, g = s % ngroups;
+        if (g == 0) {
+          load_tile = next_tile;
+          if (load_tile < ntn) next_tile = (int)atomicAdd(ctr, 1u);
+        }
+        if (load_tile >= ntn) { stage_tile[st] = -1; return; }
+        stage_tile[st] = load_tile;
+        char* sb = stg + st * Ly.stage_bytes;
+        tc::mbar_expect_tx(&bar_ld[st], (uint32_t)(R * 256 + TN * 256));
+        for (int p = 0; p < 2; ++p)   // rows (window row, head) of group g: heads 4g .. 4g + 3, tokens n - W ..
+          tc::tma_load_3d(sb + p * R * 128, &tmq, &bar_ld[st], p * 64, g * G, pl.n - W);
+        for (int p = 0; p < 2; ++p)   // the K tile: 128 keys of KV head g
+          tc::tma_load_3d(sb + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, load_tile * TN, g);
+      };
+      for (int s = 0; s < S; ++s) load_step(s);
+      static_assert(kPTStages == 2, "one descriptor base per stage below");
+      const uint64_t base0 = tc::sw128_kmajor_desc(tc::smem_addr(stg));
+      const uint64_t base1 = tc::sw128_kmajor_desc(tc::smem_addr(stg + Ly.stage_bytes));
+      for (int s = 0;; ++s) {
+        const int st = s % S, b = s & 1;
+        if (abort_sh) break;
+        if (s >= 2 && !tc::mbar_wait(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
+        const int tile = stage_tile[st];
+        if (s % ngroups == 0) {   // a new tile (or none): publish it to the epilogue
+          tile_slot[(s / ngroups) & 1] = tile;
+          tc::mbar_arrive(&bar_tile);
+        }
+        if (tile < 0) break;      // no tile left: the epilogue stops at this tile boundary
+        if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        tc::fence_after_sync();
+        const uint64_t sbase = st == 0 ? base0 : base1;   // descriptors: base + (offset >> 4)
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int p = ks >> 2, koff = (ks & 3) * 32;
+          const uint64_t ad = sbase + (uint64_t)((R * 256 + p * TN * 128 + koff) >> 4);   // keys (M)
+          const uint64_t bd = sbase + (uint64_t)((p * R * 128 + koff) >> 4);              // query rows (N)
+          tc::umma_f16(tmem + (uint32_t)(b * 256), ad, bd, idesc, ks > 0 ? 1u : 0u);
+        }
+        tc::umma_commit(&bar_full[b]);
+        tc::umma_commit(&bar_sfree[st]);
+        if (!tc::mbar_wait(&bar_sfree[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        load_step(s + S);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: 16 warps ----------------
+    const int lg = warp & 3, q = warp >> 2;             // TMEM lane group (32 keys), column quarter
+    const int key = 32 * lg + lane;                     // this thread's key within the tile
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
+    const uint64_t qset = hdr->qi_heads, hset = hdr->hi_heads;
+    const bool hmax = hdr->hi_mode == 1;
+    const int nhi = hdr->n_hi;
+    const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
+    const bool hi_rows = pl.hi_rows != 0;
+    const int hi_kind = !hi_rows ? kHiNone : (hmax ? kHiMax : kHiMean);
+    const float rs = 1.0f / sqrtf((float)pl.D);
+    const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
+    const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
+    auto epi_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kPTEpiWarps) : "memory"); };
+    float qacc[16], hacc[16];                           // rows 16 q + i of this thread's key
+    int tile = -1;
+    for (int s = 0; s < ntn * ngroups; ++s) {
+      const int g = s % ngroups;
+      if (g == 0) {
+        const int k = s / ngroups;
+        if (!epi_abort) {
+          const bool got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile, k & 1, status));
+          if (!got && lane == 0) epi_abort = 1;
+        }
+        epi_sync();
+        if (epi_abort) { abort_sh = 1; break; }   // every epilogue warp reads the same flag here
+        tile = tile_slot[k & 1];
+        if (tile < 0) break;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { qacc[i] = 0.f; hacc[i] = 0.f; }
+      }
+      const int j = tile * TN + key;
+      bool ok = !epi_abort;
+      if (ok && !tc::mbar_wait(&bar_full[s & 1], (s >> 1) & 1, status)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) epi_abort = 1;   // the rest of the tile is skipped; the loop ends at its boundary
+      if (ok) {   // TMEM loads are warp-collective
+        tc::fence_after_sync();
+        float fq[4], fh[4];
+#pragma unroll
+        for (int hl = 0; hl < 4; ++hl) {
+          fq[hl] = ((qset >> (g * G + hl)) & 1ull) ? 1.f : 0.f;
+          fh[hl] = ((hset >> (g * G + hl)) & 1ull) ? 1.f : 0.f;
+        }
+        const uint32_t col0 = (uint32_t)((s & 1) * 256 + 64 * q);
+        auto chunks = [&](auto htag) {
+          constexpr int HM = decltype(htag)::value;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {   // 16 columns: window rows 16 q + 4 c + i, heads 0..3
+            uint32_t r16[16];
+            __syncwarp();
+            tc::tmem_ld16_nowait(lane_base + col0 + 16 * c, r16);
+            tc::tmem_wait_ld();
+            if (c == 3) {   // the last load of the step: the accumulator buffer is free
+              tc::fence_before_sync();
+              __syncwarp();
+              if (lane == 0) tc::mbar_arrive(&bar_tfree[s & 1]);
+            }
+            float x[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              asm volatile("" : "+r"(r16[k]));
+              x[k] = __uint_as_float(r16[k]);
+            }
+#pragma unroll
+            for (int k = 0; k < 16; k += 2) {
+              float x0, x1;
+              round_pair<DT>(x[k], x[k + 1], rs, x0, x1);
+              x[k] = x0; x[k + 1] = x1;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = 16 * q + 4 * c + i;
+              const float4 L4 = slse4[g * W + r];
+              float p0 = ex2(fmaf(x[4 * i], kLog2e, -L4.x)), p1 = ex2(fmaf(x[4 * i + 1], kLog2e, -L4.y));
+              float p2 = ex2(fmaf(x[4 * i + 2], kLog2e, -L4.z)), p3 = ex2(fmaf(x[4 * i + 3], kLog2e, -L4.w));
+              if (j > pl.n - W + r) { p0 = 0.f; p1 = 0.f; p2 = 0.f; p3 = 0.f; }   // causal mask (and keys past n)
+              const int u = 4 * c + i;
+              qacc[u] = fmaxf(qacc[u], fmaxf(fmaxf(p0 * fq[0], p1 * fq[1]), fmaxf(p2 * fq[2], p3 * fq[3])));
+              if constexpr (HM == kHiMean)
+                hacc[u] += fmaf(p0, fh[0], p1 * fh[1]) + fmaf(p2, fh[2], p3 * fh[3]);
+              else if constexpr (HM == kHiMax)
+                hacc[u] = fmaxf(hacc[u], fmaxf(fmaxf(p0 * fh[0], p1 * fh[1]), fmaxf(p2 * fh[2], p3 * fh[3])));
+            }
+          }
+        };
+        switch (hi_kind) {
+          case kHiMean: chunks(IntTag<kHiMean>{}); break;
+          case kHiMax: chunks(IntTag<kHiMax>{}); break;
+          default: chunks(IntTag<kHiNone>{}); break;
+        }
+      }
+      if (g == ngroups - 1) {
+        // ---- the tile is complete: rows, column sums, row-sum partials, g totals
+        float* rows_qi = reinterpret_cast<float*>(a.ws + pl.off_rows_qi);
+        float* rows_hi = reinterpret_cast<float*>(a.ws + pl.off_rows_hi);
+        float* colsum = reinterpret_cast<float*>(a.ws + pl.off_colsum);
+        float* gtile = reinterpret_cast<float*>(a.ws + pl.off_gtile);
+        float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);
+        const int tid = threadIdx.x;                    // 0..511
+        const int nch = hi_rows ? 2 : 1;
+        for (int c2 = 0; c2 < nch; ++c2) {
+          float* rows = c2 == 0 ? rows_qi : rows_hi;
+          float cs = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int r = 16 * q + i;
+            float v = c2 == 0 ? qacc[i] : hacc[i];
+            if (c2 == 1 && !hmax) v = v * inv_nhi;
+            if (j >= pl.n) v = 0.f;
+            if (j < pl.n_pad) rows[(size_t)r * pl.n_pad + j] = v;
+            cs += v;
+            float rv = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
+            rv = warp_sum(rv);                          // this lane group's 32 keys
+            if (lane == 0) rowpart[lg * W + r] = rv;
+          }
+          colpart[q * TN + key] = cs;
+          epi_sync();
+          if (tid < TN) {                               // column sums of the tile's keys
+            const int jj = tile * TN + tid;
+            const float c = (colpart[tid] + colpart[TN + tid]) + (colpart[2 * TN + tid] + colpart[3 * TN + tid]);
+            if (jj < pl.n_pad) colsum[(size_t)c2 * pl.n_pad + jj] = c;
+            float gg = 0.f;
+            if (jj < pl.n_p) {
+              gg = fmaxf(c, 1e-6f);
+              if (tempered) gg = powf(gg, invT);
+            }
+            gg = warp_sum(gg);
+            if (lane == 0) gsum[tid >> 5] = gg;
+          } else if (tid < TN + 2 * W) {                // row sums of each 64-key half
+            const int u = tid - TN, half = u / W, r = u % W;
+            const int t64 = tile * 2 + half;
+            if (t64 < pl.ncol_tiles)
+              rspart[((size_t)c2 * pl.rs_parts + t64) * W + r] = rowpart[(2 * half) * W + r] + rowpart[(2 * half + 1) * W + r];
+          }
+          epi_sync();
+          if (tid < 2) {                                // g totals of each 64-key half
+            const int t64 = tile * 2 + tid;
+            if (t64 < pl.ncol_tiles) gtile[(size_t)c2 * pl.ncol_tiles * 8 + t64] = gsum[2 * tid] + gsum[2 * tid + 1];
+          }
+        }
+        epi_sync();
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 0) tc::tmem_dealloc(tmem, ncols);
+}
+
+template <int DT>
+static cudaError_t launch_tc_pool_t(const WinArgs& a0, cudaStream_t st) {
+  WinArgs a = a0;
+  const Plan& pl = a.pl;
+  CUtensorMap tq, tk;
+  if (!make_tmap_pairs(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W, pl.G) ||
+      !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kPTTN))
+    return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
+  const size_t smem = pt_layout(pl).total;
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool_t<DT>, smem); if (e != cudaSuccess) return e; }
+  const int ntn = (pl.n + kPTTN - 1) / kPTTN;
+  k_tc_pool_t<DT><<<ntn < 148 ? ntn : 148, kPTThreads, smem, st>>>(tq, tk, a);
   return cudaGetLastError();
 }
 
@@ -2185,8 +2495,9 @@ static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st)
     b.fixup_pass = stage == 2 ? 1 : 0;
     bool launched = false;
     if constexpr (DT != CKV_FP32) {
-      if (pl.tc_pool) {
-        const cudaError_t e = launch_tc_pool<DT>(b, st);
+      if (pl.tc_pool) {   // each returns at once unless its branch (exact recomputation or not) runs
+        cudaError_t e = launch_tc_pool<DT>(b, st);
+        if (e == cudaSuccess && stage == 1) e = launch_tc_pool_t<DT>(b, st);
         if (e != cudaSuccess) return e;
         launched = true;
       }
