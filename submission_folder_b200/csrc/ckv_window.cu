@@ -2256,15 +2256,14 @@ __global__ void __launch_bounds__(kPTThreads, 1)
       if (!ok && lane == 0) epi_abort = 1;   // the rest of the tile is skipped; the loop ends at its boundary
       if (ok) {   // TMEM loads are warp-collective
         tc::fence_after_sync();
-        float fq[4], fh[4];
-#pragma unroll
-        for (int hl = 0; hl < 4; ++hl) {
-          fq[hl] = ((qset >> (g * G + hl)) & 1ull) ? 1.f : 0.f;
-          fh[hl] = ((hset >> (g * G + hl)) & 1ull) ? 1.f : 0.f;
-        }
+        const uint32_t qb = (uint32_t)(qset >> (g * G)) & 0xFu, hb = (uint32_t)(hset >> (g * G)) & 0xFu;
+        auto fbit = [](uint32_t m, int hl) { return ((m >> hl) & 1u) ? 1.f : 0.f; };
         const uint32_t col0 = (uint32_t)((s & 1) * 256 + 64 * q);
-        auto chunks = [&](auto htag) {
+        // the causal mask only touches the tile that reaches the window (warp-uniform)
+        const bool edge = tile * TN + TN - 1 > pl.n - W;
+        auto chunks = [&](auto htag, auto etag) {
           constexpr int HM = decltype(htag)::value;
+          constexpr bool EDGE = decltype(etag)::value;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {   // 16 columns: window rows 16 q + 4 c + i, heads 0..3
             uint32_t r16[16];
@@ -2294,20 +2293,28 @@ __global__ void __launch_bounds__(kPTThreads, 1)
               const float4 L4 = slse4[g * W + r];
               float p0 = ex2(fmaf(x[4 * i], kLog2e, -L4.x)), p1 = ex2(fmaf(x[4 * i + 1], kLog2e, -L4.y));
               float p2 = ex2(fmaf(x[4 * i + 2], kLog2e, -L4.z)), p3 = ex2(fmaf(x[4 * i + 3], kLog2e, -L4.w));
-              if (j > pl.n - W + r) { p0 = 0.f; p1 = 0.f; p2 = 0.f; p3 = 0.f; }   // causal mask (and keys past n)
+              if constexpr (EDGE) {
+                if (j > pl.n - W + r) { p0 = 0.f; p1 = 0.f; p2 = 0.f; p3 = 0.f; }   // causal mask (and keys past n)
+              }
               const int u = 4 * c + i;
-              qacc[u] = fmaxf(qacc[u], fmaxf(fmaxf(p0 * fq[0], p1 * fq[1]), fmaxf(p2 * fq[2], p3 * fq[3])));
+              qacc[u] = fmaxf(qacc[u], fmaxf(fmaxf(p0 * fbit(qb, 0), p1 * fbit(qb, 1)),
+                                             fmaxf(p2 * fbit(qb, 2), p3 * fbit(qb, 3))));
               if constexpr (HM == kHiMean)
-                hacc[u] += fmaf(p0, fh[0], p1 * fh[1]) + fmaf(p2, fh[2], p3 * fh[3]);
+                hacc[u] += fmaf(p0, fbit(hb, 0), p1 * fbit(hb, 1)) + fmaf(p2, fbit(hb, 2), p3 * fbit(hb, 3));
               else if constexpr (HM == kHiMax)
-                hacc[u] = fmaxf(hacc[u], fmaxf(fmaxf(p0 * fh[0], p1 * fh[1]), fmaxf(p2 * fh[2], p3 * fh[3])));
+                hacc[u] = fmaxf(hacc[u], fmaxf(fmaxf(p0 * fbit(hb, 0), p1 * fbit(hb, 1)),
+                                               fmaxf(p2 * fbit(hb, 2), p3 * fbit(hb, 3))));
             }
           }
         };
+        auto run = [&](auto htag) {
+          if (edge) chunks(htag, BoolTag<true>{});
+          else chunks(htag, BoolTag<false>{});
+        };
         switch (hi_kind) {
-          case kHiMean: chunks(IntTag<kHiMean>{}); break;
-          case kHiMax: chunks(IntTag<kHiMax>{}); break;
-          default: chunks(IntTag<kHiNone>{}); break;
+          case kHiMean: run(IntTag<kHiMean>{}); break;
+          case kHiMax: run(IntTag<kHiMax>{}); break;
+          default: run(IntTag<kHiNone>{}); break;
         }
       }
       if (g == ngroups - 1) {
