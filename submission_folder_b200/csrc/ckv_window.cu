@@ -30,7 +30,7 @@
 
 namespace ckv {
 
-__device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh);
+__device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh, int gidx, int per_group, int ngroups);
 CKV_DEV float sum_parts(const float* base, int nparts, size_t stride, int first, int step);
 template <int DT> size_t pool_smem(const Plan& pl);
 
@@ -485,21 +485,21 @@ __global__ void __launch_bounds__(256) k_window_stats(WinArgs a) {
       }
     }
 
-  stats_finish(a, smem, bg.h0, pl.heads_per_batch);
+  stats_finish(a, smem, bg.h0, pl.heads_per_batch, blockIdx.y, gridDim.x, gridDim.y);
 }
 
 // Last-CTA steps of the moments pass (PU:2905-2999).  The last CTA of each head
 // group merges the chunk partials of the group's rows into their log-sum-exp, the
 // unclamped entropy and the transient mass, and writes the group's per-head means;
 // the last group then speculates the head sets from them.
-__device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
+__device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh, int gidx, int per_group, int ngroups) {
   const Plan& pl = a.pl;
   const float4* part = reinterpret_cast<const float4*>(a.ws + pl.off_stats);
   Header* hdr = reinterpret_cast<Header*>(a.ws);
   __shared__ bool last;
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(&hdr->cnt_group[blockIdx.y], 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) last = atomicAdd(&hdr->cnt_group[gidx], 1u) == (unsigned)per_group - 1;
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -579,8 +579,8 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh) {
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    hdr->cnt_group[blockIdx.y] = 0;
-    last = atomicAdd(&hdr->cnt_stats, 1u) == gridDim.y - 1;
+    hdr->cnt_group[gidx] = 0;
+    last = atomicAdd(&hdr->cnt_stats, 1u) == (unsigned)ngroups - 1;
   }
   __syncthreads();
   if (!last) return;
@@ -1350,20 +1350,21 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
   int32_t* status = &hdr->status;
-  const int chunk = blockIdx.x, g = blockIdx.y;
+  const int m_tiles = (pl.G * pl.W) / 128;            // 128-row m-tiles of a KV group
+  const int chunk = blockIdx.x, g = blockIdx.y / m_tiles, mtc = blockIdx.y % m_tiles;
+  const int hpm = 128 / pl.W;                          // heads per m-tile
+  const int hfirst = g * pl.G + mtc * hpm;             // first head of this CTA's m-tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int R = pl.G * pl.W;                 // window-query rows of the group
-  const int m_tiles = R / 128;
   const int TN = a.tc_tn, S = a.tc_stages;
   const int ntn = (pl.n + TN - 1) / TN;
   const int t0 = chunk * a.tc_tpc, t1 = min(t0 + a.tc_tpc, ntn);
   const int ntile = max(0, t1 - t0);
-  char* sA = align1024(smem_raw);
-  char* sB = sA + 2 * R * 128;
+  char* sA = align1024(smem_raw);                      // the m-tile's 128 window-query rows
+  char* sB = sA + 2 * 128 * 128;                       // K stages
   // K stage full / free, accumulator buffer full / free (16 epilogue warps arrive)
   __shared__ __align__(8) uint64_t bar_q, bar_k[4], bar_kfree[4], bar_full[2], bar_tfree[2];
   __shared__ uint32_t tmem_base_sh;
-  const uint32_t ncols = (2 * m_tiles * TN <= 256) ? 256u : 512u;
+  const uint32_t ncols = (2 * TN <= 256) ? 256u : 512u;   // two accumulator buffers of N = TN
   if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
   if (threadIdx.x == 0) {
     tc::mbar_init(&bar_q, 1);
@@ -1376,12 +1377,12 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
 
-  // 16 epilogue warps: TMEM lane group lg, m-tile mt, column split sp of nsplit
+  // 16 epilogue warps: TMEM lane group lg (32 rows of the m-tile), column split sp of 4
   const int lg = warp & 3;
-  const int nsplit = kStatsEpiWarps / (4 * m_tiles);   // 4, 2 or 1
-  const int mt = (warp >> 2) % m_tiles, sp = (warp >> 2) / m_tiles;
+  constexpr int nsplit = kStatsEpiWarps / 4;
+  const int sp = warp >> 2;
   const int cw = TN / nsplit;                          // columns per thread per tile (>= 32)
-  const int row = mt * 128 + 32 * lg + lane;
+  const int row = 32 * lg + lane;
   const int r = row % pl.W;
   const int lim = pl.n - pl.W + r;                     // last visible key of this window row
   Moments M{-INFINITY, 0.f, 0.f, 0.f};
@@ -1397,10 +1398,10 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
         for (int p = 0; p < 2; ++p)
           tc::tma_load_3d(sB + (st * 2 + p) * TN * 128, &tmk, &bar_k[st], p * 64, (t0 + i) * TN, g);
       };
-      tc::mbar_expect_tx(&bar_q, (uint32_t)R * 256u);
-      for (int hl = 0; hl < pl.G; ++hl)
+      tc::mbar_expect_tx(&bar_q, 128u * 256u);
+      for (int hl = 0; hl < hpm; ++hl)
         for (int p = 0; p < 2; ++p)
-          tc::tma_load_3d(sA + p * R * 128 + hl * pl.W * 128, &tmq, &bar_q, p * 64, pl.n - pl.W, g * pl.G + hl);
+          tc::tma_load_3d(sA + p * 128 * 128 + hl * pl.W * 128, &tmq, &bar_q, p * 64, pl.n - pl.W, hfirst + hl);
       int issued = min(S, ntile), consumed = 0, mmas = 0;
       for (int i = 0; i < issued; ++i) load_tile(i);
       bool ok = tc::mbar_wait(&bar_q, 0, status);
@@ -1410,15 +1411,13 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
         if (!tc::mbar_wait(&bar_k[st], (i / S) & 1, status)) { ok = false; break; }
         consumed = i + 1;
         tc::fence_after_sync();
-        const uint32_t dcol = (uint32_t)(b * m_tiles * TN);
-        for (int m = 0; m < m_tiles; ++m) {
+        const uint32_t dcol = (uint32_t)(b * TN);
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const int p = ks >> 2, koff = (ks & 3) * 32;
-            const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(sA + p * R * 128 + m * 128 * 128 + koff));
-            const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(sB + (st * 2 + p) * TN * 128 + koff));
-            tc::umma_f16(tmem + dcol + m * TN, ad, bd, idesc, ks > 0 ? 1u : 0u);
-          }
+        for (int ks = 0; ks < 8; ++ks) {   // M = 128 query rows, N = TN keys, K = 128 in 8 steps
+          const int p = ks >> 2, koff = (ks & 3) * 32;
+          const uint64_t ad = tc::sw128_kmajor_desc(tc::smem_addr(sA + p * 128 * 128 + koff));
+          const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_addr(sB + (st * 2 + p) * TN * 128 + koff));
+          tc::umma_f16(tmem + dcol, ad, bd, idesc, ks > 0 ? 1u : 0u);
         }
         tc::umma_commit(&bar_full[b]);
         tc::umma_commit(&bar_kfree[st]);
@@ -1445,7 +1444,7 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
       if (!__all_sync(0xffffffffu, tc::mbar_wait(&bar_full[b], (i >> 1) & 1, status))) break;
       tc::fence_after_sync();
       const int t = t0 + i;
-      const uint32_t base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)(b * m_tiles * TN + mt * TN);
+      const uint32_t base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)(b * TN);
       for (int c = sp * cw; c < (sp + 1) * cw; c += 32) {
         float v[32];
         __syncwarp();
@@ -1530,20 +1529,20 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
   float4* part = reinterpret_cast<float4*>(a.ws + pl.off_stats);
   tc::fence_before_sync();
   __syncthreads();
-  float4* msh = reinterpret_cast<float4*>(sB);        // K stages are free now: [nsplit][R]
-  float* mnsh = reinterpret_cast<float*>(msh + nsplit * R);
+  float4* msh = reinterpret_cast<float4*>(sB);        // K stages are free now: [nsplit][128]
+  float* mnsh = reinterpret_cast<float*>(msh + nsplit * 128);
   if (warp < kStatsEpiWarps) {
-    msh[sp * R + row] = make_float4(M.m, M.z, M.t, M.s);
-    mnsh[sp * R + row] = xmin;
+    msh[sp * 128 + row] = make_float4(M.m, M.z, M.t, M.s);
+    mnsh[sp * 128 + row] = xmin;
   }
   __syncthreads();
   if (warp < kStatsEpiWarps && sp == 0) {
     for (int q = 1; q < nsplit; ++q) {
-      const float4 o = msh[q * R + row];
+      const float4 o = msh[q * 128 + row];
       M = merge(M, Moments{o.x, o.y, o.z, o.w});
-      xmin = fminf(xmin, mnsh[q * R + row]);
+      xmin = fminf(xmin, mnsh[q * 128 + row]);
     }
-    const int h = g * pl.G + row / pl.W;
+    const int h = hfirst + row / pl.W;
     part[((size_t)chunk * pl.H + h) * pl.W + r] = make_float4(M.m, M.z, M.t, M.s);
     reinterpret_cast<float*>(a.ws + pl.off_minx)[((size_t)chunk * pl.H + h) * pl.W + r] = xmin;
   }
@@ -1551,7 +1550,7 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == 0) tc::tmem_dealloc(tmem, ncols);
-  stats_finish(a, smem_raw, (int)blockIdx.y * pl.G, pl.G);
+  stats_finish(a, smem_raw, g * pl.G, pl.G, g, (int)gridDim.x * m_tiles, pl.Hkv);
 }
 
 // ---- TMA descriptors (host) -------------------------------------------------
@@ -1585,7 +1584,8 @@ static bool make_tmap(CUtensorMap* m, const void* base, int dtype, int n, int he
 }
 
 size_t tc_stats_smem(const Plan& pl, int TN, int S) {
-  return 1024 + (size_t)2 * pl.G * pl.W * 128 + (size_t)S * 2 * TN * 128;
+  (void)pl;
+  return 1024 + (size_t)2 * 128 * 128 + (size_t)S * 2 * TN * 128;
 }
 
 template <int DT>
@@ -1593,8 +1593,8 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
   WinArgs a = a0;
   const Plan& pl = a.pl;
   const int m_tiles = pl.G * pl.W / 128;
-  a.tc_tn = m_tiles <= 2 ? 128 : 64;
-  a.tc_stages = 4;
+  a.tc_tn = 256;        // keys per tile: UMMA N = 256 over one 128-row m-tile
+  a.tc_stages = 3;
   a.tc_min = 1;
   const int ntn = (pl.n + a.tc_tn - 1) / a.tc_tn;
   a.tc_tpc = (ntn + pl.nstat_chunks - 1) / pl.nstat_chunks;
@@ -1604,7 +1604,7 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
     return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
   const size_t smem = tc_stats_smem(pl, a.tc_tn, a.tc_stages);
   { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_stats<DT>, smem); if (e != cudaSuccess) return e; }
-  k_tc_stats<DT><<<dim3(pl.nstat_chunks, pl.Hkv), kStatsThreads, smem, st>>>(tq, tk, a);
+  k_tc_stats<DT><<<dim3(pl.nstat_chunks, pl.Hkv * m_tiles), kStatsThreads, smem, st>>>(tq, tk, a);
   return cudaGetLastError();
 }
 
