@@ -267,6 +267,7 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
   SelArgs sa;
   memset(&sa, 0, sizeof(sa));
   sa.pl = pl; sa.p = *p; sa.ws = ws; sa.out_idx = out->out_idx; sa.out_scores = out->out_scores;
+  sa.narrow = marks ? 0 : 1;   // concurrent layers: the smaller cluster
   e = launch_select(sa, st);
   if (e != cudaSuccess) return cuda_fail(e, "select kernel");
   stage_mark(st);

@@ -534,25 +534,39 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_select(SelArgs a) {
     for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) mysc[j] = g[j];
   } else if (chain) {
     steps = early_stop_steps(pl, ws);
-    float tot = 0.f, mx = 0.f;
-    for (int j = max(b0, pl.s) + threadIdx.x; j < b1; j += blockDim.x) {
-      const float r = raw_result(pl, ws, v, j, steps);
-      mysc[j] = r;
-      tot += r;
-      mx = fmaxf(mx, r);
+    // sums of 32-position blocks (the slices are 32-aligned), so that the total below
+    // does not depend on how many CTAs share the vector
+    float* bsum = gx + (size_t)v * n;   // [ceil(n / 32)]; free until the smoothing phase
+    const int wid = threadIdx.x >> 5;
+    float mx = 0.f;
+    for (int jb = b0 + 32 * wid; jb < b1; jb += 32 * kSelWarps) {
+      const int j = jb + lane;
+      float r = 0.f;
+      if (j < b1 && j >= pl.s) {
+        r = raw_result(pl, ws, v, j, steps);
+        mysc[j] = r;
+        mx = fmaxf(mx, r);
+      }
+      const float bs = warp_sum(r);
+      if (lane == 0) bsum[jb >> 5] = bs;
     }
-    tot = block_reduce<false>(tot, sh.fmisc);
     mx = block_reduce<true>(mx, sh.fmisc);
-    if (threadIdx.x == 0) { sh.xch[0] = tot; sh.xch[1] = mx; }
+    if (threadIdx.x == 0) sh.xch[1] = mx;
   }
   cl.sync();
   if (chain) {
-    float tot = 0.f, mx = 0.f;
-    for (int q = 0; q < P; ++q) {
-      const float* r = cl.map_shared_rank(sh.xch, vbase + q);
-      tot += r[0];
-      mx = fmaxf(mx, r[1]);
+    float mx = 0.f;
+    for (int q = 0; q < P; ++q) mx = fmaxf(mx, cl.map_shared_rank(sh.xch, vbase + q)[1]);
+    // the total of the block sums in a fixed order (one warp; the same in every CTA)
+    if (threadIdx.x < 32) {
+      const float* bsum = gx + (size_t)v * n;
+      float t = 0.f;
+      for (int k = lane; k < (n + 31) / 32; k += 32) t += __ldcg(bsum + k);
+      t = warp_sum(t);
+      if (lane == 0) sh.fmisc[64] = t;
     }
+    __syncthreads();
+    const float tot = sh.fmisc[64];
     const float sinkv = tot * 0.01f;
     mx = fmaxf(mx, pl.s > 0 ? sinkv : 0.f);
     const float* colsum = reinterpret_cast<const float*>(ws + pl.off_colsum);
@@ -800,7 +814,8 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_select(SelArgs a) {
 
 // CTAs per score vector: up to 16 CTAs per cluster where the device schedules that
 // cluster size, else the portable 8.
-static int select_parts(int nv, size_t smem, cudaStream_t st) {
+static int select_parts(int nv, size_t smem, cudaStream_t st, bool narrow) {
+  if (narrow) return 8 / nv;
   static std::mutex mu;
   static int cached[64][4] = {};
   int dev = 0;
@@ -843,7 +858,7 @@ cudaError_t launch_select(const SelArgs& a0, cudaStream_t st) {
   // the shared memory layout depends on the slice length, hence on the CTAs per vector
   const size_t s8 = sel_layout(pl.n, 8 / nv).total, s16 = sel_layout(pl.n, 16 / nv).total;
   { const cudaError_t e = ensure_dynamic_smem((const void*)k_select, s8 > s16 ? s8 : s16); if (e != cudaSuccess) return e; }
-  a.parts = select_parts(nv, s16, st);
+  a.parts = select_parts(nv, s16, st, a.narrow != 0);
   const size_t smem = sel_layout(pl.n, a.parts).total;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nv * a.parts, 1, 1);

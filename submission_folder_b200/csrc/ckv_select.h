@@ -19,6 +19,8 @@ struct SelArgs {
   const float* gc;
   int finish_only;       // 1: stop after the finished chain scores (written to out_scores)
   int parts;             // CTAs per score vector (set by launch_select)
+  int narrow;            // 1: the portable 8-CTA cluster (layers run concurrently, so fewer SMs
+                         //    per selection outweigh its longer latency)
 };
 
 // Per-head eviction: finishing, global HI ranks and the per-head selection.
