@@ -86,6 +86,14 @@ CKV_DEV F2 mul2(F2 a, F2 b) {
   return r;
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max.f32).
+CKV_DEV float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+CKV_DEV F2 ex2_2(F2 a) { return f2(ex2(f2lo(a)), ex2(f2hi(a))); }
+
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -115,6 +123,25 @@ CKV_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+// Sixteen warp sums at once (transpose reduction): returns, in lane l, the sum over
+// the 32 lanes of v[idx], idx = ((l >> 4) & 1) * 8 + ((l >> 3) & 1) * 4 + ((l >> 2) & 1) * 2
+// + ((l >> 1) & 1).  Each round halves the values a lane holds: it keeps the half
+// selected by its lane bit and adds the partner's copy of that half: 16 shuffles and
+// adds in place of 16 x 5.  v is clobbered.
+CKV_DEV float warp_sum16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16, m = 8; o >= 2; o >>= 1, m >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int k = 0; k < m; ++k) {
+      const float keep = up ? v[m + k] : v[k];
+      const float send = up ? v[k] : v[m + k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 CKV_DEV float warp_max(float v) {
 #pragma unroll

@@ -1291,6 +1291,18 @@ template <> CKV_DEV void round_pair<CKV_BF16>(float a, float b, float rs, float&
   x = __uint_as_float(p << 16);
   y = __uint_as_float(p & 0xffff0000u);
 }
+// The same, returning the two rounded logits as a packed fp32 pair.
+template <int DT> CKV_DEV F2 round_f2(float a, float b, float rs);
+template <> CKV_DEV F2 round_f2<CKV_BF16>(float a, float b, float rs) {
+  uint32_t p, t;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(b), "f"(a));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t) : "r"(p), "r"(kRsLo2));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(p) : "r"(p), "r"(kRsHi2), "r"(t));
+  F2 r;
+  asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xffff0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+      : "=l"(r.v) : "r"(p));
+  return r;
+}
 // The same, also returning the two rounded logits packed as a 16-bit pair (exact), for
 // packed max / min.
 template <int DT> CKV_DEV uint32_t round_pack(float a, float b, float rs, float& x, float& y);
@@ -1338,6 +1350,11 @@ template <> CKV_DEV uint32_t round_pack<CKV_FP16>(float a, float b, float rs, fl
   round_pair<CKV_FP16>(a, b, rs, x, y);
   const __half2 h = __floats2half2_rn(x, y);   // exact: x, y are fp16 values
   return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <> CKV_DEV F2 round_f2<CKV_FP16>(float a, float b, float rs) {
+  float x, y;
+  round_pair<CKV_FP16>(a, b, rs, x, y);
+  return f2(x, y);
 }
 
 constexpr int kStatsEpiWarps = 16;                       // epilogue warps of the moments pass
@@ -2128,7 +2145,7 @@ __global__ void __launch_bounds__(kPTThreads, 1)
   const PTSmem Ly = pt_layout(pl);
   char* base = align1024(smem_raw);
   char* stg = base;
-  const float4* slse4 = reinterpret_cast<const float4*>(base + Ly.off_lse);
+  const float4* snlse4 = reinterpret_cast<const float4*>(base + Ly.off_lse);
   float* colpart = reinterpret_cast<float*>(base + Ly.off_colpart);
   float* rowpart = reinterpret_cast<float*>(base + Ly.off_rowpart);
   float* gsum = reinterpret_cast<float*>(base + Ly.off_gsum);
@@ -2151,12 +2168,12 @@ __global__ void __launch_bounds__(kPTThreads, 1)
     tc::fence_barrier_init();
     abort_sh = 0;
   }
-  {   // log-sum-exp re-laid as [group][window row][head of the group] (one float4 per row)
+  {   // negated log-sum-exp re-laid as [group][window row][head of the group] (one float4 per row)
     const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);   // [H][W]
     float* sl = reinterpret_cast<float*>(base + Ly.off_lse);
     for (int i = threadIdx.x; i < pl.H * W; i += blockDim.x) {
       const int h = i / W, r = i % W;
-      sl[((h / G) * W + r) * G + (h % G)] = __ldcg(lse + i);
+      sl[((h / G) * W + r) * G + (h % G)] = -__ldcg(lse + i);
     }
   }
   tc::fence_before_sync();
@@ -2258,12 +2275,18 @@ __global__ void __launch_bounds__(kPTThreads, 1)
         tc::fence_after_sync();
         const uint32_t qb = (uint32_t)(qset >> (g * G)) & 0xFu, hb = (uint32_t)(hset >> (g * G)) & 0xFu;
         auto fbit = [](uint32_t m, int hl) { return ((m >> hl) & 1u) ? 1.f : 0.f; };
+        // head membership factors (1 in the set, 0 outside) as pairs (heads 0 1, 2 3)
+        const F2 qm01 = f2(fbit(qb, 0), fbit(qb, 1)), qm23 = f2(fbit(qb, 2), fbit(qb, 3));
+        const F2 hm01 = f2(fbit(hb, 0), fbit(hb, 1)), hm23 = f2(fbit(hb, 2), fbit(hb, 3));
+        const F2 l2e = f2(kLog2e, kLog2e);
         const uint32_t col0 = (uint32_t)((s & 1) * 256 + 64 * q);
         // the causal mask only touches the tile that reaches the window (warp-uniform)
         const bool edge = tile * TN + TN - 1 > pl.n - W;
-        auto chunks = [&](auto htag, auto etag) {
+        // QANY: some head of the group is in the QI set (else its max-pooling is skipped)
+        auto chunks = [&](auto htag, auto etag, auto qtag) {
           constexpr int HM = decltype(htag)::value;
           constexpr bool EDGE = decltype(etag)::value;
+          constexpr bool QANY = decltype(qtag)::value;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {   // 16 columns: window rows 16 q + 4 c + i, heads 0..3
             uint32_t r16[16];
@@ -2275,41 +2298,36 @@ __global__ void __launch_bounds__(kPTThreads, 1)
               __syncwarp();
               if (lane == 0) tc::mbar_arrive(&bar_tfree[s & 1]);
             }
-            float x[16];
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              asm volatile("" : "+r"(r16[k]));
-              x[k] = __uint_as_float(r16[k]);
-            }
-#pragma unroll
-            for (int k = 0; k < 16; k += 2) {
-              float x0, x1;
-              round_pair<DT>(x[k], x[k + 1], rs, x0, x1);
-              x[k] = x0; x[k + 1] = x1;
-            }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int r = 16 * q + 4 * c + i;
-              const float4 L4 = slse4[g * W + r];
-              float p0 = ex2(fmaf(x[4 * i], kLog2e, -L4.x)), p1 = ex2(fmaf(x[4 * i + 1], kLog2e, -L4.y));
-              float p2 = ex2(fmaf(x[4 * i + 2], kLog2e, -L4.z)), p3 = ex2(fmaf(x[4 * i + 3], kLog2e, -L4.w));
+              const float4 nL = snlse4[g * W + r];   // -log2-sum-exp of (row, head 0..3)
+              const F2 x01 = round_f2<DT>(__uint_as_float(r16[4 * i]), __uint_as_float(r16[4 * i + 1]), rs);
+              const F2 x23 = round_f2<DT>(__uint_as_float(r16[4 * i + 2]), __uint_as_float(r16[4 * i + 3]), rs);
+              F2 p01 = ex2_2(fma2(x01, l2e, f2(nL.x, nL.y)));
+              F2 p23 = ex2_2(fma2(x23, l2e, f2(nL.z, nL.w)));
               if constexpr (EDGE) {
-                if (j > pl.n - W + r) { p0 = 0.f; p1 = 0.f; p2 = 0.f; p3 = 0.f; }   // causal mask (and keys past n)
+                if (j > pl.n - W + r) { p01 = f2(0.f, 0.f); p23 = p01; }   // causal mask (and keys past n)
               }
               const int u = 4 * c + i;
-              qacc[u] = fmaxf(qacc[u], fmaxf(fmaxf(p0 * fbit(qb, 0), p1 * fbit(qb, 1)),
-                                             fmaxf(p2 * fbit(qb, 2), p3 * fbit(qb, 3))));
-              if constexpr (HM == kHiMean)
-                hacc[u] += fmaf(p0, fbit(hb, 0), p1 * fbit(hb, 1)) + fmaf(p2, fbit(hb, 2), p3 * fbit(hb, 3));
-              else if constexpr (HM == kHiMax)
-                hacc[u] = fmaxf(hacc[u], fmaxf(fmaxf(p0 * fbit(hb, 0), p1 * fbit(hb, 1)),
-                                               fmaxf(p2 * fbit(hb, 2), p3 * fbit(hb, 3))));
+              if constexpr (QANY) {
+                const F2 a = mul2(p01, qm01), b = mul2(p23, qm23);
+                qacc[u] = max3f(max3f(qacc[u], f2lo(a), f2hi(a)), f2lo(b), f2hi(b));
+              }
+              if constexpr (HM == kHiMean) {
+                const F2 t = fma2(p23, hm23, mul2(p01, hm01));
+                hacc[u] += f2lo(t) + f2hi(t);
+              } else if constexpr (HM == kHiMax) {
+                const F2 a = mul2(p01, hm01), b = mul2(p23, hm23);
+                hacc[u] = max3f(max3f(hacc[u], f2lo(a), f2hi(a)), f2lo(b), f2hi(b));
+              }
             }
           }
         };
         auto run = [&](auto htag) {
-          if (edge) chunks(htag, BoolTag<true>{});
-          else chunks(htag, BoolTag<false>{});
+          if (edge) chunks(htag, BoolTag<true>{}, BoolTag<true>{});
+          else if (qb != 0) chunks(htag, BoolTag<false>{}, BoolTag<true>{});
+          else chunks(htag, BoolTag<false>{}, BoolTag<false>{});
         };
         switch (hi_kind) {
           case kHiMean: run(IntTag<kHiMean>{}); break;
@@ -2328,7 +2346,7 @@ __global__ void __launch_bounds__(kPTThreads, 1)
         const int nch = hi_rows ? 2 : 1;
         for (int c2 = 0; c2 < nch; ++c2) {
           float* rows = c2 == 0 ? rows_qi : rows_hi;
-          float cs = 0.f;
+          float cs = 0.f, rv[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int r = 16 * q + i;
@@ -2337,9 +2355,11 @@ __global__ void __launch_bounds__(kPTThreads, 1)
             if (j >= pl.n) v = 0.f;
             if (j < pl.n_pad) rows[(size_t)r * pl.n_pad + j] = v;
             cs += v;
-            float rv = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
-            rv = warp_sum(rv);                          // this lane group's 32 keys
-            if (lane == 0) rowpart[lg * W + r] = rv;
+            rv[i] = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
+          }
+          {   // row sums over this lane group's 32 keys: row 16 q + ((lane >> 1) & 15) in lane pairs
+            const float t = warp_sum16(rv);
+            if ((lane & 1) == 0) rowpart[lg * W + 16 * q + ((lane >> 1) & 15)] = t;
           }
           colpart[q * TN + key] = cs;
           epi_sync();
