@@ -126,7 +126,7 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   if (pl.nscan < 1) pl.nscan = 1;
   pl.tc_nclusters = pl.ncol_tiles < 148 ? pl.ncol_tiles : 148;   // CTAs of the tensor-core pooling pass
   pl.e_parts = pl.tc_pool ? pl.tc_nclusters : pl.ncol_tiles;   // TC: one partial per CTA
-  pl.rs_parts = pl.ncol_tiles;
+  pl.rs_parts = pl.tc_pool ? 2 * pl.ncol_tiles : pl.ncol_tiles;
   pl.g_slice = kColTile;
   if (window_smem_bytes(pl, true) > 227 * 1024 || window_smem_bytes(pl, false) > 227 * 1024) {
     *why = "window tile does not fit in shared memory"; return CKV_ERR_UNSUPPORTED;
@@ -147,6 +147,7 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.off_colsum = take((size_t)2 * pl.n_pad * 4);
   pl.off_gtile = take((size_t)2 * pl.ncol_tiles * 8 * 4);
   pl.off_rspart = take((size_t)2 * pl.ncol_tiles * 8 * pl.W * 4);
+  pl.off_colpart = take(pl.tc_pool ? (size_t)2 * 4 * pl.n_pad * 4 : 0);
   pl.off_wk = take((size_t)2 * pl.K * pl.W * 4);
   pl.off_yk = take((size_t)2 * (pl.K + 1) * pl.W * 4);
   pl.off_ymax = take((size_t)2 * (pl.K + 1) * 4);

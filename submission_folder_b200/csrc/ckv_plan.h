@@ -47,7 +47,7 @@ struct Plan {
   int tc_pool;        // 1: pooling pass on tcgen05 with one cluster CTA per KV group
   int tc_nclusters;   // clusters of the tensor-core pooling pass
   int e_parts;        // exact entropy / mass partials per row
-  int rs_parts;       // row-sum partials per chain
+  int rs_parts;       // row-sum partials per chain (tensor-core pooling: one per 32 keys)
   int g_slice;        // columns per g-total partial (64 or 8)
   int hi_rows;        // 1 when the HI chain has its own pooled rows
   // window tiling
@@ -66,6 +66,7 @@ struct Plan {
   size_t off_stats, off_lse, off_lastlogit, off_spec, off_epart, off_mpart;
   size_t off_minx;    // [nstat_chunks][H][W] row minimum of the rounded logits (tensor-core moments)
   size_t off_rows_qi, off_rows_hi, off_colsum, off_gtile, off_rspart;
+  size_t off_colpart;  // [2][4][n_pad] column-sum partials of the keys-on-lanes pooling pass (4 row blocks)
   size_t off_wk, off_yk, off_ymax, off_bk, off_cg, off_agg, off_sin, off_cum, off_cmax;
   size_t off_sel, off_ph;
   // per-head eviction (PU:2208-2382, 3296-3464): only allocated in that mode

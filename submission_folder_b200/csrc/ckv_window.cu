@@ -2003,9 +2003,9 @@ __global__ void __launch_bounds__(kP2Threads, 1)
           }
           colpart[pr * TN + pc] = cs;
           epi_sync();
-          if (tid < W) {
-            const int rr = tid, k = rr >> 3, w0 = 2 * (rr & 7);
-            rspart[((size_t)c2 * pl.rs_parts + tile) * W + rr] = redrow[w0 * 8 + k] + redrow[(w0 + 1) * 8 + k];
+          if (tid < 2 * W) {   // row sums of each 32-key half of the tile (one partial per 32 keys)
+            const int rr = tid % W, e = tid / W, k = rr >> 3, w0 = 2 * (rr & 7);
+            rspart[((size_t)c2 * pl.rs_parts + 2 * tile + e) * W + rr] = redrow[(w0 + e) * 8 + k];
           }
           if (tid < TN) {
             const int jj = j0 + tid;
@@ -2113,7 +2113,7 @@ constexpr int kPTEpiWarps = 16;
 constexpr int kPTThreads = 32 * (kPTEpiWarps + 1);
 
 struct PTSmem {
-  size_t stage_bytes, off_lse, off_colpart, off_rowpart, off_gsum, total;
+  size_t stage_bytes, off_lse, total;
 };
 
 static __host__ __device__ PTSmem pt_layout(const Plan& pl) {
@@ -2122,9 +2122,6 @@ static __host__ __device__ PTSmem pt_layout(const Plan& pl) {
   L.stage_bytes = R * 256 + (size_t)kPTTN * 256;
   size_t off = kPTStages * L.stage_bytes;
   L.off_lse = off; off += (size_t)pl.H * pl.W * 4;       // [group][row][head of the group]
-  L.off_colpart = off; off += (size_t)4 * kPTTN * 4;     // [quarter][key]
-  L.off_rowpart = off; off += (size_t)4 * pl.W * 4;      // [lane group][row]
-  L.off_gsum = off; off += 16 * 4;
   L.total = 1024 + off;
   return L;
 }
@@ -2146,9 +2143,6 @@ __global__ void __launch_bounds__(kPTThreads, 1)
   char* base = align1024(smem_raw);
   char* stg = base;
   const float4* snlse4 = reinterpret_cast<const float4*>(base + Ly.off_lse);
-  float* colpart = reinterpret_cast<float*>(base + Ly.off_colpart);
-  float* rowpart = reinterpret_cast<float*>(base + Ly.off_rowpart);
-  float* gsum = reinterpret_cast<float*>(base + Ly.off_gsum);
   __shared__ __align__(8) uint64_t bar_ld[kPTStages], bar_sfree[kPTStages], bar_full[2], bar_tfree[2], bar_tile;
   __shared__ int stage_tile[kPTStages];   // producer only: tile loaded into each stage (-1: none)
   __shared__ int tile_slot[2];            // tile k of this CTA in slot k & 1 (-1: no tile left)
@@ -2248,19 +2242,21 @@ __global__ void __launch_bounds__(kPTThreads, 1)
     const float rs = 1.0f / sqrtf((float)pl.D);
     const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
     const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
-    auto epi_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kPTEpiWarps) : "memory"); };
     float qacc[16], hacc[16];                           // rows 16 q + i of this thread's key
     int tile = -1;
     for (int s = 0; s < ntn * ngroups; ++s) {
       const int g = s % ngroups;
       if (g == 0) {
+        // no barrier among the epilogue warps: the producer's wait for all of them to free
+        // a TMEM buffer keeps them within a step of one another, so the tile slot and the
+        // tile barrier's phase of the current tile are still the ones each warp reads
         const int k = s / ngroups;
-        if (!epi_abort) {
-          const bool got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile, k & 1, status));
-          if (!got && lane == 0) epi_abort = 1;
+        bool got = __shfl_sync(0xffffffffu, epi_abort == 0, 0);   // warp-uniform
+        if (got) got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile, k & 1, status));
+        if (!got) {
+          if (lane == 0) { epi_abort = 1; abort_sh = 1; }
+          break;
         }
-        epi_sync();
-        if (epi_abort) { abort_sh = 1; break; }   // every epilogue warp reads the same flag here
         tile = tile_slot[k & 1];
         if (tile < 0) break;
 #pragma unroll
@@ -2336,13 +2332,13 @@ __global__ void __launch_bounds__(kPTThreads, 1)
         }
       }
       if (g == ngroups - 1) {
-        // ---- the tile is complete: rows, column sums, row-sum partials, g totals
+        // ---- the tile is complete: rows, then partial sums that the reduction kernel
+        // completes (no barrier: each warp writes its own partials)
         float* rows_qi = reinterpret_cast<float*>(a.ws + pl.off_rows_qi);
         float* rows_hi = reinterpret_cast<float*>(a.ws + pl.off_rows_hi);
-        float* colsum = reinterpret_cast<float*>(a.ws + pl.off_colsum);
-        float* gtile = reinterpret_cast<float*>(a.ws + pl.off_gtile);
-        float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);
-        const int tid = threadIdx.x;                    // 0..511
+        float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);     // [2][rs_parts][W]
+        float* colpart = reinterpret_cast<float*>(a.ws + pl.off_colpart);   // [2][4][n_pad]
+        const int t32 = tile * 4 + lg;                  // 32-key row-sum partial of this lane group
         const int nch = hi_rows ? 2 : 1;
         for (int c2 = 0; c2 < nch; ++c2) {
           float* rows = c2 == 0 ? rows_qi : rows_hi;
@@ -2357,36 +2353,13 @@ __global__ void __launch_bounds__(kPTThreads, 1)
             cs += v;
             rv[i] = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
           }
-          {   // row sums over this lane group's 32 keys: row 16 q + ((lane >> 1) & 15) in lane pairs
-            const float t = warp_sum16(rv);
-            if ((lane & 1) == 0) rowpart[lg * W + 16 * q + ((lane >> 1) & 15)] = t;
-          }
-          colpart[q * TN + key] = cs;
-          epi_sync();
-          if (tid < TN) {                               // column sums of the tile's keys
-            const int jj = tile * TN + tid;
-            const float c = (colpart[tid] + colpart[TN + tid]) + (colpart[2 * TN + tid] + colpart[3 * TN + tid]);
-            if (jj < pl.n_pad) colsum[(size_t)c2 * pl.n_pad + jj] = c;
-            float gg = 0.f;
-            if (jj < pl.n_p) {
-              gg = fmaxf(c, 1e-6f);
-              if (tempered) gg = powf(gg, invT);
-            }
-            gg = warp_sum(gg);
-            if (lane == 0) gsum[tid >> 5] = gg;
-          } else if (tid < TN + 2 * W) {                // row sums of each 64-key half
-            const int u = tid - TN, half = u / W, r = u % W;
-            const int t64 = tile * 2 + half;
-            if (t64 < pl.ncol_tiles)
-              rspart[((size_t)c2 * pl.rs_parts + t64) * W + r] = rowpart[(2 * half) * W + r] + rowpart[(2 * half + 1) * W + r];
-          }
-          epi_sync();
-          if (tid < 2) {                                // g totals of each 64-key half
-            const int t64 = tile * 2 + tid;
-            if (t64 < pl.ncol_tiles) gtile[(size_t)c2 * pl.ncol_tiles * 8 + t64] = gsum[2 * tid] + gsum[2 * tid + 1];
-          }
+          // row sums over this lane group's 32 keys: row 16 q + ((lane >> 1) & 15) in lane pairs
+          const float t = warp_sum16(rv);
+          if ((lane & 1) == 0 && t32 < pl.rs_parts)
+            rspart[((size_t)c2 * pl.rs_parts + t32) * W + 16 * q + ((lane >> 1) & 15)] = t;
+          // column sum of this key over the row block's 16 rows
+          if (j < pl.n_pad) colpart[((size_t)c2 * 4 + q) * pl.n_pad + j] = cs;
         }
-        epi_sync();
       }
     }
   }
@@ -2458,6 +2431,35 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
     const int ch = (row - 2 * HW) / pl.W, rr = (row - 2 * HW) % pl.W;
     const int src = (ch == 1 && pl.hi_rows) ? 1 : 0;
     e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, pl.rs_parts, (size_t)pl.W, q, kReduceStreams);
+  }
+  if (pl.tc_pool && !exact) {
+    // column sums and g totals behind the keys-on-lanes pooling pass: four row-block
+    // partials per key, one 64-key slice per warp (added in the order that pass used)
+    const float* colpart = reinterpret_cast<const float*>(a.ws + pl.off_colpart);   // [2][4][n_pad]
+    float* colsum = reinterpret_cast<float*>(a.ws + pl.off_colsum);
+    float* gtile = reinterpret_cast<float*>(a.ws + pl.off_gtile);
+    const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
+    const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
+    const int nslice = (pl.hi_rows ? 2 : 1) * pl.ncol_tiles;
+    const int nwarps = (int)(gridDim.x * (blockDim.x >> 5));
+    for (int sl = (int)blockIdx.x * (int)(blockDim.x >> 5) + q; sl < nslice; sl += nwarps) {
+      const int c2 = sl / pl.ncol_tiles, t = sl % pl.ncol_tiles;
+      float gh[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int jj = t * 64 + 32 * h + lane;   // < n_pad
+        const float* cp = colpart + (size_t)c2 * 4 * pl.n_pad + jj;
+        const float c = (__ldcg(cp) + __ldcg(cp + pl.n_pad)) + (__ldcg(cp + 2 * (size_t)pl.n_pad) + __ldcg(cp + 3 * (size_t)pl.n_pad));
+        colsum[(size_t)c2 * pl.n_pad + jj] = c;
+        float gg = 0.f;
+        if (jj < pl.n_p) {
+          gg = fmaxf(c, 1e-6f);
+          if (tempered) gg = powf(gg, invT);
+        }
+        gh[h] = warp_sum(gg);
+      }
+      if (lane == 0) gtile[(size_t)c2 * pl.ncol_tiles * 8 + t] = gh[0] + gh[1];
+    }
   }
   sp[q][lane] = e;
   __syncthreads();
