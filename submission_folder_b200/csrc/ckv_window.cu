@@ -2162,6 +2162,12 @@ __global__ void __launch_bounds__(kPTThreads, 1)
     tc::fence_barrier_init();
     abort_sh = 0;
   }
+  __shared__ float4 smask[2 * kMaxHeads / 4];   // per KV group: QI, HI membership factors of its 4 heads
+  if (threadIdx.x < 2 * ngroups) {
+    const int g = threadIdx.x >> 1;
+    const uint32_t m = (uint32_t)(((threadIdx.x & 1) ? hdr->hi_heads : hdr->qi_heads) >> (g * G)) & 0xFu;
+    smask[threadIdx.x] = make_float4((m & 1u) ? 1.f : 0.f, (m & 2u) ? 1.f : 0.f, (m & 4u) ? 1.f : 0.f, (m & 8u) ? 1.f : 0.f);
+  }
   {   // negated log-sum-exp re-laid as [group][window row][head of the group] (one float4 per row)
     const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);   // [H][W]
     float* sl = reinterpret_cast<float*>(base + Ly.off_lse);
@@ -2182,8 +2188,10 @@ __global__ void __launch_bounds__(kPTThreads, 1)
       uint32_t* ctr = &hdr->tile_ctr[0];
       int load_tile = -1;
       int next_tile = (int)atomicAdd(ctr, 1u);   // fetched one tile ahead: the atomic's latency hides
+      int ld_g = 0;                              // KV group of the next step to load (steps load in order)
       auto load_step = [&](int s) {
-        const int st = s % S, g = s % ngroups;
+        const int st = s % S, g = ld_g;
+        ld_g = ld_g + 1 == ngroups ? 0 : ld_g + 1;
         if (g == 0) {
           load_tile = next_tile;
           if (load_tile < ntn) next_tile = (int)atomicAdd(ctr, 1u);
@@ -2201,15 +2209,16 @@ __global__ void __launch_bounds__(kPTThreads, 1)
       static_assert(kPTStages == 2, "one descriptor base per stage below");
       const uint64_t base0 = tc::sw128_kmajor_desc(tc::smem_addr(stg));
       const uint64_t base1 = tc::sw128_kmajor_desc(tc::smem_addr(stg + Ly.stage_bytes));
-      for (int s = 0;; ++s) {
+      for (int s = 0, g = 0, k = 0;; ++s) {   // g: KV group of step s, k: this CTA's tile count
         const int st = s % S, b = s & 1;
         if (abort_sh) break;
         if (s >= 2 && !tc::mbar_wait(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
         const int tile = stage_tile[st];
-        if (s % ngroups == 0) {   // a new tile (or none): publish it to the epilogue
-          tile_slot[(s / ngroups) & 1] = tile;
+        if (g == 0) {   // a new tile (or none): publish it to the epilogue
+          tile_slot[k & 1] = tile;
           tc::mbar_arrive(&bar_tile);
         }
+        if (++g == ngroups) { g = 0; ++k; }
         if (tile < 0) break;      // no tile left: the epilogue stops at this tile boundary
         if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
         tc::fence_after_sync();
@@ -2233,7 +2242,7 @@ __global__ void __launch_bounds__(kPTThreads, 1)
     const int lg = warp & 3, q = warp >> 2;             // TMEM lane group (32 keys), column quarter
     const int key = 32 * lg + lane;                     // this thread's key within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
-    const uint64_t qset = hdr->qi_heads, hset = hdr->hi_heads;
+    const uint64_t qset = hdr->qi_heads;
     const bool hmax = hdr->hi_mode == 1;
     const int nhi = hdr->n_hi;
     const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
@@ -2244,13 +2253,12 @@ __global__ void __launch_bounds__(kPTThreads, 1)
     const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
     float qacc[16], hacc[16];                           // rows 16 q + i of this thread's key
     int tile = -1;
-    for (int s = 0; s < ntn * ngroups; ++s) {
-      const int g = s % ngroups;
+    // s: step, g: its KV group, k: tiles this warp has started (no integer division per step)
+    for (int s = 0, g = 0, k = 0; s < ntn * ngroups; ++s, g = g + 1 == ngroups ? 0 : g + 1) {
       if (g == 0) {
         // no barrier among the epilogue warps: the producer's wait for all of them to free
         // a TMEM buffer keeps them within a step of one another, so the tile slot and the
         // tile barrier's phase of the current tile are still the ones each warp reads
-        const int k = s / ngroups;
         bool got = __shfl_sync(0xffffffffu, epi_abort == 0, 0);   // warp-uniform
         if (got) got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile, k & 1, status));
         if (!got) {
@@ -2258,6 +2266,7 @@ __global__ void __launch_bounds__(kPTThreads, 1)
           break;
         }
         tile = tile_slot[k & 1];
+        ++k;
         if (tile < 0) break;
 #pragma unroll
         for (int i = 0; i < 16; ++i) { qacc[i] = 0.f; hacc[i] = 0.f; }
@@ -2269,11 +2278,11 @@ __global__ void __launch_bounds__(kPTThreads, 1)
       if (!ok && lane == 0) epi_abort = 1;   // the rest of the tile is skipped; the loop ends at its boundary
       if (ok) {   // TMEM loads are warp-collective
         tc::fence_after_sync();
-        const uint32_t qb = (uint32_t)(qset >> (g * G)) & 0xFu, hb = (uint32_t)(hset >> (g * G)) & 0xFu;
-        auto fbit = [](uint32_t m, int hl) { return ((m >> hl) & 1u) ? 1.f : 0.f; };
+        const uint32_t qb = (uint32_t)(qset >> (g * G)) & 0xFu;
         // head membership factors (1 in the set, 0 outside) as pairs (heads 0 1, 2 3)
-        const F2 qm01 = f2(fbit(qb, 0), fbit(qb, 1)), qm23 = f2(fbit(qb, 2), fbit(qb, 3));
-        const F2 hm01 = f2(fbit(hb, 0), fbit(hb, 1)), hm23 = f2(fbit(hb, 2), fbit(hb, 3));
+        const float4 q4 = smask[2 * g], h4 = smask[2 * g + 1];
+        const F2 qm01 = f2(q4.x, q4.y), qm23 = f2(q4.z, q4.w);
+        const F2 hm01 = f2(h4.x, h4.y), hm23 = f2(h4.z, h4.w);
         const F2 l2e = f2(kLog2e, kLog2e);
         const uint32_t col0 = (uint32_t)((s & 1) * 256 + 64 * q);
         // the causal mask only touches the tile that reaches the window (warp-uniform)
