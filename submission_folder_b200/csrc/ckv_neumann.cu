@@ -281,11 +281,25 @@ __global__ void __launch_bounds__(kSweepThreads) k_sweep_chunks(const Plan pl, c
     if (j < pl.s || j >= pl.n_p)
 #pragma unroll
       for (int k = 0; k < KM; ++k) bk[p][k] = 0.f;
-    if (j < pl.n_p) {
+  }
+  if ((pl.n_p & 3) == 0 && j0 + kSweepRun <= pl.n_p) {   // whole run, 16-byte aligned: vector stores
 #pragma unroll
-      for (int k = 0; k < KM; ++k)
-        if (k < K) bk_out[(size_t)k * pl.n_p + j] = bk[p][k];
-      cg_out[j] = make_float2(ri.c[p], ri.g[p]);
+    for (int k = 0; k < KM; ++k)
+      if (k < K)
+        *reinterpret_cast<float4*>(bk_out + (size_t)k * pl.n_p + j0) = make_float4(bk[0][k], bk[1][k], bk[2][k], bk[3][k]);
+    float4* cg4 = reinterpret_cast<float4*>(cg_out + j0);
+    cg4[0] = make_float4(ri.c[0], ri.g[0], ri.c[1], ri.g[1]);
+    cg4[1] = make_float4(ri.c[2], ri.g[2], ri.c[3], ri.g[3]);
+  } else {
+#pragma unroll
+    for (int p = 0; p < kSweepRun; ++p) {
+      const int j = j0 + p;
+      if (j < pl.n_p) {
+#pragma unroll
+        for (int k = 0; k < KM; ++k)
+          if (k < K) bk_out[(size_t)k * pl.n_p + j] = bk[p][k];
+        cg_out[j] = make_float2(ri.c[p], ri.g[p]);
+      }
     }
   }
 

@@ -1357,6 +1357,11 @@ template <> CKV_DEV F2 round_f2<CKV_FP16>(float a, float b, float rs) {
   return f2(x, y);
 }
 
+// v^e for v > 0, else 0 (the tempered pooled rows), out of line: the temperature is
+// rarely set, and sixteen inlined copies of powf in a tile's row loop would spread the
+// hot epilogue code over many more instruction-cache lines.
+__device__ __noinline__ float pow_pos(float v, float e) { return v > 0.f ? powf(v, e) : 0.f; }
+
 constexpr int kStatsEpiWarps = 16;                       // epilogue warps of the moments pass
 constexpr int kStatsThreads = 32 * (kStatsEpiWarps + 1);  // + one producer warp
 
@@ -1997,7 +2002,7 @@ __global__ void __launch_bounds__(kP2Threads, 1)
             if (j >= pl.n) v = 0.f;
             rows[(size_t)rr * pl.n_pad + j] = v;
             cs += v;
-            float rv = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
+            float rv = tempered ? pow_pos(v, invT) : v;
             rv = warp_sum(rv);
             if (lane == 0) redrow[warp * 8 + k] = rv;   // this warp's 32 columns of row rr
           }
@@ -2163,6 +2168,9 @@ __global__ void __launch_bounds__(kPTThreads, 1)
     abort_sh = 0;
   }
   __shared__ float4 smask[2 * kMaxHeads / 4];   // per KV group: QI, HI membership factors of its 4 heads
+  __shared__ int s_hi_kind;                      // kHiMean / kHiMax / kHiNone
+  if (threadIdx.x == 0)
+    s_hi_kind = pl.hi_rows == 0 ? kHiNone : (hdr->hi_mode == 1 ? kHiMax : kHiMean);
   if (threadIdx.x < 2 * ngroups) {
     const int g = threadIdx.x >> 1;
     const uint32_t m = (uint32_t)(((threadIdx.x & 1) ? hdr->hi_heads : hdr->qi_heads) >> (g * G)) & 0xFu;
@@ -2242,15 +2250,8 @@ __global__ void __launch_bounds__(kPTThreads, 1)
     const int lg = warp & 3, q = warp >> 2;             // TMEM lane group (32 keys), column quarter
     const int key = 32 * lg + lane;                     // this thread's key within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
-    const uint64_t qset = hdr->qi_heads;
-    const bool hmax = hdr->hi_mode == 1;
-    const int nhi = hdr->n_hi;
-    const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
-    const bool hi_rows = pl.hi_rows != 0;
-    const int hi_kind = !hi_rows ? kHiNone : (hmax ? kHiMax : kHiMean);
+    // (values used once per tile are re-read there, not held in registers across the steps)
     const float rs = 1.0f / sqrtf((float)pl.D);
-    const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
-    const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
     float qacc[16], hacc[16];                           // rows 16 q + i of this thread's key
     int tile = -1;
     // s: step, g: its KV group, k: tiles this warp has started (no integer division per step)
@@ -2278,9 +2279,9 @@ __global__ void __launch_bounds__(kPTThreads, 1)
       if (!ok && lane == 0) epi_abort = 1;   // the rest of the tile is skipped; the loop ends at its boundary
       if (ok) {   // TMEM loads are warp-collective
         tc::fence_after_sync();
-        const uint32_t qb = (uint32_t)(qset >> (g * G)) & 0xFu;
         // head membership factors (1 in the set, 0 outside) as pairs (heads 0 1, 2 3)
         const float4 q4 = smask[2 * g], h4 = smask[2 * g + 1];
+        const bool qany = (q4.x + q4.y) + (q4.z + q4.w) > 0.f;
         const F2 qm01 = f2(q4.x, q4.y), qm23 = f2(q4.z, q4.w);
         const F2 hm01 = f2(h4.x, h4.y), hm23 = f2(h4.z, h4.w);
         const F2 l2e = f2(kLog2e, kLog2e);
@@ -2331,10 +2332,10 @@ __global__ void __launch_bounds__(kPTThreads, 1)
         };
         auto run = [&](auto htag) {
           if (edge) chunks(htag, BoolTag<true>{}, BoolTag<true>{});
-          else if (qb != 0) chunks(htag, BoolTag<false>{}, BoolTag<true>{});
+          else if (qany) chunks(htag, BoolTag<false>{}, BoolTag<true>{});
           else chunks(htag, BoolTag<false>{}, BoolTag<false>{});
         };
-        switch (hi_kind) {
+        switch (s_hi_kind) {
           case kHiMean: run(IntTag<kHiMean>{}); break;
           case kHiMax: run(IntTag<kHiMax>{}); break;
           default: run(IntTag<kHiNone>{}); break;
@@ -2348,27 +2349,36 @@ __global__ void __launch_bounds__(kPTThreads, 1)
         float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);     // [2][rs_parts][W]
         float* colpart = reinterpret_cast<float*>(a.ws + pl.off_colpart);   // [2][4][n_pad]
         const int t32 = tile * 4 + lg;                  // 32-key row-sum partial of this lane group
+        const bool hi_rows = pl.hi_rows != 0, hmax = s_hi_kind == kHiMax;
         const int nch = hi_rows ? 2 : 1;
-        for (int c2 = 0; c2 < nch; ++c2) {
+        const int nhi = hdr->n_hi;
+        const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
+        const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
+        const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
+        // one accumulator set at a time, its registers reused for the row-sum terms (the
+        // accumulators start again at zero with the next tile)
+        auto flush = [&](float (&acc)[16], int c2) {
           float* rows = c2 == 0 ? rows_qi : rows_hi;
-          float cs = 0.f, rv[16];
+          float* rp = rows + (size_t)(16 * q) * pl.n_pad + j;
+          float cs = 0.f;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int r = 16 * q + i;
-            float v = c2 == 0 ? qacc[i] : hacc[i];
+            float v = acc[i];
             if (c2 == 1 && !hmax) v = v * inv_nhi;
             if (j >= pl.n) v = 0.f;
-            if (j < pl.n_pad) rows[(size_t)r * pl.n_pad + j] = v;
+            if (j < pl.n_pad) rp[(size_t)i * pl.n_pad] = v;
             cs += v;
-            rv[i] = tempered ? (v > 0.f ? powf(v, invT) : 0.f) : v;
+            acc[i] = tempered ? pow_pos(v, invT) : v;
           }
           // row sums over this lane group's 32 keys: row 16 q + ((lane >> 1) & 15) in lane pairs
-          const float t = warp_sum16(rv);
+          const float t = warp_sum16(acc);
           if ((lane & 1) == 0 && t32 < pl.rs_parts)
             rspart[((size_t)c2 * pl.rs_parts + t32) * W + 16 * q + ((lane >> 1) & 15)] = t;
           // column sum of this key over the row block's 16 rows
           if (j < pl.n_pad) colpart[((size_t)c2 * 4 + q) * pl.n_pad + j] = cs;
-        }
+        };
+        flush(qacc, 0);
+        if (nch == 2) flush(hacc, 1);
       }
     }
   }
@@ -2541,6 +2551,7 @@ static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st)
       }
     }
     if (!launched) k_window_pool<DT><<<pl.ncol_tiles, 256, pool_smem<DT>(pl), st>>>(b);
+    if (stage == 1) stage_mark(st);   // pooling kernels | reduction (timing only)
     const size_t rsm = pool_reduce_smem(pl);
     { const cudaError_t e = ensure_dynamic_smem((const void*)k_pool_reduce, rsm); if (e != cudaSuccess) return e; }
     k_pool_reduce<<<(2 * pl.H * pl.W + 2 * pl.W + 31) / 32, 32 * kReduceStreams, rsm, st>>>(b);

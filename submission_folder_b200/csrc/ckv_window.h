@@ -26,6 +26,9 @@ struct WinArgs {
 size_t window_smem_bytes(const Plan& pl, bool pool);
 cudaError_t launch_window(const WinArgs& a, cudaStream_t st);
 cudaError_t launch_window_stage(const WinArgs& a, int stage, cudaStream_t st);
+// Records the next per-stage timing event, if any are set (ckv_set_stage_events); the
+// pooling stage marks the boundary between its pooling kernels and their reduction.
+void stage_mark(cudaStream_t st);
 // Per-head eviction pass: query rows, two-hop terms, column sums, query-row entropy.
 cudaError_t launch_ph_pass(const WinArgs& a, cudaStream_t st);
 // Column sums / row sums / window chain of pooled rows already in the workspace.
