@@ -1690,8 +1690,7 @@ static __host__ __device__ P2Smem p2_layout(const Plan& pl) {
 size_t tc_pool_smem(const Plan& pl) { return p2_layout(pl).total; }
 
 template <int DT>
-__global__ void __launch_bounds__(kP2Threads, 1)
-    k_tc_pool(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
+__device__ __forceinline__ void tc_pool_body(const CUtensorMap& tmq, const CUtensorMap& tmk, const WinArgs& a) {
   extern __shared__ char smem_raw[];
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
@@ -2084,6 +2083,14 @@ static bool make_tmap_pairs(CUtensorMap* m, const void* base, int dtype, int n, 
   return r == CUDA_SUCCESS;
 }
 
+// The re-run with the exact head sets (returns at once unless the reduction flagged it).
+template <int DT>
+__global__ void __launch_bounds__(kP2Threads, 1)
+    k_tc_pool(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+              const __grid_constant__ WinArgs a) {
+  tc_pool_body<DT>(tmq, tmk, a);
+}
+
 template <int DT>
 static cudaError_t launch_tc_pool(const WinArgs& a0, cudaStream_t st) {
   WinArgs a = a0;
@@ -2132,8 +2139,7 @@ static __host__ __device__ PTSmem pt_layout(const Plan& pl) {
 }
 
 template <int DT>
-__global__ void __launch_bounds__(kPTThreads, 1)
-    k_tc_pool_t(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
+__device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUtensorMap& tmk, const WinArgs& a) {
   extern __shared__ char smem_raw[];
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
@@ -2388,18 +2394,39 @@ __global__ void __launch_bounds__(kPTThreads, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, ncols);
 }
 
+// The pooling pass is one launch that takes its branch on the device: the head-pair form
+// when the moments pass left the head sets unsettled (need_exact), the keys-on-lanes form
+// otherwise.  A second kernel for the branch not taken would cost every layer a launch of
+// 148 CTAs that return at once (about 3% of the batched step).  The keys-on-lanes form,
+// the usual one, comes first: with the head-pair form's code laid out ahead of it, its loop
+// missed the instruction cache about 2.5 times as often (64 instead of 55 us).
+static_assert(kP2Threads == kPTThreads, "both pooling forms run in one launch");
 template <int DT>
-static cudaError_t launch_tc_pool_t(const WinArgs& a0, cudaStream_t st) {
+__global__ void __launch_bounds__(kPTThreads, 1)
+    k_tc_pool_any(const __grid_constant__ CUtensorMap tmq2, const __grid_constant__ CUtensorMap tmk2,
+                  const __grid_constant__ CUtensorMap tmq4, const __grid_constant__ CUtensorMap tmk4,
+                  const __grid_constant__ WinArgs a) {
+  const Header* hdr = reinterpret_cast<const Header*>(a.ws);
+  if (*reinterpret_cast<const volatile int32_t*>(&hdr->need_exact) == 0) tc_pool_t_body<DT>(tmq4, tmk4, a);
+  else tc_pool_body<DT>(tmq2, tmk2, a);
+}
+
+template <int DT>
+static cudaError_t launch_tc_pool_any(const WinArgs& a0, cudaStream_t st) {
   WinArgs a = a0;
   const Plan& pl = a.pl;
-  CUtensorMap tq, tk;
-  if (!make_tmap_pairs(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W, pl.G) ||
-      !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kPTTN))
+  CUtensorMap tq2, tk2, tq4, tk4;
+  if (!make_tmap_pairs(&tq2, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W) ||
+      !make_tmap(&tk2, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kP2TN) ||
+      !make_tmap_pairs(&tq4, a.q, DT, pl.n, pl.H, a.qhs, a.qts, pl.W, pl.G) ||
+      !make_tmap(&tk4, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kPTTN))
     return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
-  const size_t smem = pt_layout(pl).total;
-  { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool_t<DT>, smem); if (e != cudaSuccess) return e; }
-  const int ntn = (pl.n + kPTTN - 1) / kPTTN;
-  k_tc_pool_t<DT><<<ntn < 148 ? ntn : 148, kPTThreads, smem, st>>>(tq, tk, a);
+  const size_t s2 = tc_pool_smem(pl), s4 = pt_layout(pl).total;
+  const size_t smem = s2 > s4 ? s2 : s4;
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool_any<DT>, smem); if (e != cudaSuccess) return e; }
+  // grid: one CTA per exact-branch partial (tc_nclusters >= the keys-on-lanes tile count
+  // up to 148; surplus CTAs of that branch find no tile and return)
+  k_tc_pool_any<DT><<<pl.tc_nclusters, kPTThreads, smem, st>>>(tq2, tk2, tq4, tk4, a);
   return cudaGetLastError();
 }
 
@@ -2544,8 +2571,7 @@ static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st)
     bool launched = false;
     if constexpr (DT != CKV_FP32) {
       if (pl.tc_pool) {   // each returns at once unless its branch (exact recomputation or not) runs
-        cudaError_t e = launch_tc_pool<DT>(b, st);
-        if (e == cudaSuccess && stage == 1) e = launch_tc_pool_t<DT>(b, st);
+        const cudaError_t e = stage == 1 ? launch_tc_pool_any<DT>(b, st) : launch_tc_pool<DT>(b, st);
         if (e != cudaSuccess) return e;
         launched = true;
       }
