@@ -2361,30 +2361,28 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         const float inv_nhi = 1.0f / (float)(nhi > 0 ? nhi : 1);   // mean = sum * (1 / count)
         const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
         const float invT = tempered ? 1.0f / a.p.neumann_temperature : 1.0f;
-        // one accumulator set at a time, its registers reused for the row-sum terms (the
-        // accumulators start again at zero with the next tile)
-        auto flush = [&](float (&acc)[16], int c2) {
-          float* rows = c2 == 0 ? rows_qi : rows_hi;
-          float* rp = rows + (size_t)(16 * q) * pl.n_pad + j;
+        // one accumulator set at a time (one copy of this code: a loop, not unrolled); the QI
+        // registers take each set's row-sum terms (both sets start again at zero next tile)
+#pragma unroll 1
+        for (int c2 = 0; c2 < nch; ++c2) {
+          float* rp = (c2 == 0 ? rows_qi : rows_hi) + (size_t)(16 * q) * pl.n_pad + j;
           float cs = 0.f;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float v = acc[i];
+            float v = c2 == 0 ? qacc[i] : hacc[i];
             if (c2 == 1 && !hmax) v = v * inv_nhi;
             if (j >= pl.n) v = 0.f;
             if (j < pl.n_pad) rp[(size_t)i * pl.n_pad] = v;
             cs += v;
-            acc[i] = tempered ? pow_pos(v, invT) : v;
+            qacc[i] = tempered ? pow_pos(v, invT) : v;
           }
           // row sums over this lane group's 32 keys: row 16 q + ((lane >> 1) & 15) in lane pairs
-          const float t = warp_sum16(acc);
+          const float t = warp_sum16(qacc);
           if ((lane & 1) == 0 && t32 < pl.rs_parts)
             rspart[((size_t)c2 * pl.rs_parts + t32) * W + 16 * q + ((lane >> 1) & 15)] = t;
           // column sum of this key over the row block's 16 rows
           if (j < pl.n_pad) colpart[((size_t)c2 * 4 + q) * pl.n_pad + j] = cs;
-        };
-        flush(qacc, 0);
-        if (nch == 2) flush(hacc, 1);
+        }
       }
     }
   }
