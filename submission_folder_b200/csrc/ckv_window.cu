@@ -1695,7 +1695,7 @@ __device__ __forceinline__ void tc_pool_body(const CUtensorMap& tmq, const CUten
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
   if (a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->fixup) == 0) return;
-  // the branch without the exact recomputation runs in k_tc_pool_t
+  // the branch without the exact recomputation is the keys-on-lanes form (tc_pool_t_body)
   if (!a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->need_exact) == 0) return;
   int32_t* status = &hdr->status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
