@@ -432,3 +432,85 @@ def test_host_tensors_round_trip():
     assert kh.is_pinned() and vh.is_pinned()
     assert torch.equal(kh, kd.cpu()) and torch.equal(vh, vd.cpu())
     assert torch.equal(ko, kd.cpu()) and torch.equal(vo, vd.cpu())
+
+
+def _flip_case(n=4096, W=64, H=32, Hkv=8, D=128, seed=11):
+    """Window queries whose speculated QI head set is wrong.
+
+    The moments pass ranks heads by their unclamped entropy; the reference clamps
+    probabilities at 1e-8 inside the entropy (PU:1452-1477), which can only raise it.
+    Head 1 puts its mass on 20 keys and leaves every other key ~30 logits lower (below
+    the clamp), so clamping raises its entropy by ~7.5e-4; head 12 has Gaussian logits
+    whose scale is searched so that its unclamped entropy lies just above head 1's and
+    its clamped entropy just below.  Nine heads are far more peaked, the rest far
+    flatter, so heads 1 and 12 share the 10th place of the 10-head QI set: the pass-1
+    choice takes head 1, the exact one head 12, and the pooling pass must re-run.
+    """
+    G = H // Hkv
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((H, n, D)).astype(np.float32)
+    k = rng.standard_normal((Hkv, n, D)).astype(np.float32)
+    v = rng.standard_normal((Hkv, n, D)).astype(np.float32)
+    bf = lambda x: torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(torch.bfloat16).float().numpy()
+    X, Y = 1, 12
+    P = rng.choice(np.arange(100, n - W - 100), size=20, replace=False)
+    k[X // G, :, 0] = 0.0
+    k[X // G, P, 0] = 10.0
+    q[X, n - W:, :] = 0.0
+    q[X, n - W:, 0] = 34.0
+    q[20:29, n - W:] *= 8.0
+    q, k, v = bf(q), bf(k), bf(v)
+
+    def entropy(qh, kg):
+        att = O.window_attention(qh[None], kg[None], W, 1, "bf16")[0].astype(np.float64)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            un = float(np.where(att > 0, -att * np.log(att), 0.0).sum(-1).mean())
+        return un, float(O.head_entropy(att[None].astype(np.float32))[0])
+
+    unX, clX = entropy(q[X], k[X // G])
+    base = q[Y, n - W:].copy()
+
+    def scaled(s):
+        qq = q[Y].copy()
+        qq[n - W:] = bf(base * s)
+        return qq
+
+    lo, hi = 1.0, 8.0   # the entropy falls as the scale grows: bisect to the window's middle
+    for _ in range(16):
+        mid = 0.5 * (lo + hi)
+        if entropy(scaled(mid), k[Y // G])[0] > 0.5 * (unX + clX):
+            lo = mid
+        else:
+            hi = mid
+    # the logits' 16-bit rounding makes the entropy a staircase of ~1e-3 steps there:
+    # scan nearby scales for one that lands inside the window with margins
+    for d in sorted(np.arange(-0.02, 0.02, 5e-5), key=abs):
+        qq = scaled(lo + d)
+        un, cl = entropy(qq, k[Y // G])
+        if unX + 1.5e-4 < un and cl < clX - 1.5e-4:
+            q[Y] = qq
+            return q, k, v
+    pytest.skip("no scale of head 12 lands between head 1's entropies")
+
+
+def test_speculated_head_set_wrong_reruns_pooling():
+    """The re-run path: pass 1's head set differs from the exact one (header words
+    need_exact = 1 and fixup = 1 after the call), and the pooling pass re-runs with the
+    exact sets, so the kept positions follow the reference's (clamped) head choice."""
+    from submission_folder_b200.cluster import cli_cluster_kwargs
+    dev = _cuda()
+    n, W, B = 4096, 64, 512
+    q, k, v = _flip_case(n=n, W=W)
+    kw = cli_cluster_kwargs(W, B)
+    p = CircuitKVCluster(**kw).params(n)
+    to = lambda x: torch.from_numpy(x).to(torch.bfloat16).to(dev)
+    ko, vo, idx, sc = ops.score_evict(p, to(q), to(k), to(v), want_scores=True)
+    torch.cuda.synchronize()
+    ws = ops._workspaces[(dev.type, dev.index)]
+    assert int(ws[56:60].cpu().view(torch.int32).item()) == 1   # Header.need_exact
+    assert int(ws[12:16].cpu().view(torch.int32).item()) == 1   # Header.fixup
+    r = O.update_kv(q, k, v, 4, O.Params(**{a: b for a, b in kw.items() if a in O.Params.__dataclass_fields__}),
+                    dtype="bf16")
+    assert 12 in r.choice.qi_heads and 1 not in r.choice.qi_heads
+    nd, ok = compare_keep(idx.cpu().numpy(), r.keep_idx, r.combined, 4, n - W, B - W - 4, margin=8.0 / (n - 1))
+    assert ok, nd
