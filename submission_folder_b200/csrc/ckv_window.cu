@@ -2463,18 +2463,31 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
   const int HW = pl.H * pl.W;
   const int nrows = 2 * HW + 2 * pl.W;
   const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
-  const int row = blockIdx.x * 32 + lane;
   __shared__ float sp[kReduceStreams][32];
   const bool exact = hdr->need_exact != 0;   // else the moments pass's values stand
-  float e = 0.f;
-  if (row < HW) {
-    if (exact) e = sum_parts(epart + row, pl.e_parts, (size_t)HW, q, kReduceStreams);
-  } else if (row < 2 * HW) {
-    if (exact) e = sum_parts(mpart + (row - HW), pl.e_parts, (size_t)HW, q, kReduceStreams);
-  } else if (row < nrows) {
-    const int ch = (row - 2 * HW) / pl.W, rr = (row - 2 * HW) % pl.W;
-    const int src = (ch == 1 && pl.hi_rows) ? 1 : 0;
-    e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, pl.rs_parts, (size_t)pl.W, q, kReduceStreams);
+  // blocks of 32 rows, strided over the grid (the re-run launches a few CTAs: it returns at
+  // once unless the head sets changed, and then speed matters less than launch cost)
+  const int nblk = (nrows + 31) / 32;
+  for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const int row = blk * 32 + lane;
+    float e = 0.f;
+    if (row < HW) {
+      if (exact) e = sum_parts(epart + row, pl.e_parts, (size_t)HW, q, kReduceStreams);
+    } else if (row < 2 * HW) {
+      if (exact) e = sum_parts(mpart + (row - HW), pl.e_parts, (size_t)HW, q, kReduceStreams);
+    } else if (row < nrows) {
+      const int ch = (row - 2 * HW) / pl.W, rr = (row - 2 * HW) % pl.W;
+      const int src = (ch == 1 && pl.hi_rows) ? 1 : 0;
+      e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, pl.rs_parts, (size_t)pl.W, q, kReduceStreams);
+    }
+    sp[q][lane] = e;
+    __syncthreads();
+    if (threadIdx.x < 32 && row < nrows) {
+      float t = 0.f;
+      for (int k = 0; k < kReduceStreams; ++k) t += sp[k][threadIdx.x];
+      out[row] = t;
+    }
+    __syncthreads();   // sp is reused by the next block
   }
   if (pl.tc_pool && !exact) {
     // column sums and g totals behind the keys-on-lanes pooling pass: four row-block
@@ -2504,13 +2517,6 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
       }
       if (lane == 0) gtile[(size_t)c2 * pl.ncol_tiles * 8 + t] = gh[0] + gh[1];
     }
-  }
-  sp[q][lane] = e;
-  __syncthreads();
-  if (threadIdx.x < 32 && row < nrows) {
-    float t = 0.f;
-    for (int k = 0; k < kReduceStreams; ++k) t += sp[k][threadIdx.x];
-    out[row] = t;
   }
   __shared__ bool last;
   __threadfence();
@@ -2578,7 +2584,8 @@ static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st)
     if (stage == 1) stage_mark(st);   // pooling kernels | reduction (timing only)
     const size_t rsm = pool_reduce_smem(pl);
     { const cudaError_t e = ensure_dynamic_smem((const void*)k_pool_reduce, rsm); if (e != cudaSuccess) return e; }
-    k_pool_reduce<<<(2 * pl.H * pl.W + 2 * pl.W + 31) / 32, 32 * kReduceStreams, rsm, st>>>(b);
+    const int nblk = (2 * pl.H * pl.W + 2 * pl.W + 31) / 32;
+    k_pool_reduce<<<stage == 2 ? (nblk < 8 ? nblk : 8) : nblk, 32 * kReduceStreams, rsm, st>>>(b);
   }
   return cudaGetLastError();
 }
