@@ -1,27 +1,43 @@
 #!/usr/bin/env python3
 """Benchmark of the CircuitKV prefill scoring + eviction path on B200.
 
-Workload (one "step"): score and evict every layer of a Llama-3-8B-shaped
-prefill cache -- 32 layers x 32 query / 8 KV heads, head_dim 128, bf16,
-32768 tokens, observation window 64, budget 2048 per layer (``--pyramid``: the
-budget falls linearly from 4096 at layer 0 to 512 at layer 31).  The timed step
-is one ``ckv_score_evict_batched`` call over the 32 layers (each layer with the
-semantics of CircuitKVCluster.update_kv; the library runs the layers on four
-concurrent lanes) on device-resident inputs, captured in one CUDA graph.  The
-per-stage breakdown and the roofline of the dominant kernel come from the serial
-form of the step (one ``ckv_score_evict`` call per layer), timed separately.
-Inputs are seeded synthetic tensors (``submission_folder_b200.synth``).
+Workloads (``--config``; one "step" scores and evicts every unit of the workload):
 
-``value`` = tokens scored per second over all ranks (layers x tokens per step /
-step time, max over ranks).  ``e2e`` = the same metric through the public hook
-(``CircuitKVCluster.update_kv``) with pinned host buffers: the host->device copy
-of each layer's window queries and distinct K / V heads and the device->host copy
-of the compressed K / V are inside its timed region.
+1. one layer, fp32, n = 4096, window 32, budget 512, 16 planted keys;
+2. a 32-layer Llama-3-8B cache (32 query / 8 KV heads, head_dim 128), bf16, n = 8192,
+   window 64, budget 1024, 64 planted keys per head;
+3. (default) the same shape at n = 32768, window 64, budget 2048 (``--pyramid``: the
+   budget falls linearly from 4096 at layer 0 to 512 at layer 31);
+4. a 32-layer Mistral-7B-shaped cache, n = 131072, window 128, budget 4096, 256 planted
+   keys, locality band 1024;
+5. a serving batch of 16 sequences, n_i ~ U[2048, 32768] (seeded), window 32, budget
+   int(0.1 n_i), 32 layers each.
 
-Multi-GPU: one process per GPU (torchrun); every rank scores its own 32-layer
-cache (weak scaling), then the kept-index metadata of all ranks is all-gathered
-over NCCL (the only collective).  ``--impl reference`` times the CPU oracle port
-of the reference's path on the host cores (rank 0 only).
+A unit is one ``update_kv`` call (one layer of one sequence).  The timed step is one
+``ckv_score_evict_batched`` call over the rank's units (each with the semantics of
+CircuitKVCluster.update_kv; the library runs them on concurrent lanes), captured in a
+CUDA graph, on device-resident inputs; with N > 1 ranks the kept positions of every unit
+are then all-gathered over NCCL inside the timed region (one fixed-size
+all_gather_into_tensor, ``sharding.KeptExchange``).
+
+``--scaling strong`` (default): the units of ONE workload are split over the ranks
+(layers round-robin; config 5: sequences, longest first to the least-loaded rank).
+``--scaling weak``: every rank scores its own full workload (different seeds).
+
+``value`` = tokens scored per second over all ranks (unit tokens per step / step time,
+max over ranks).  Timing: W warm-up replays, then repeated blocks of exactly K steps, each
+bracketed by a barrier and a synchronise and timed with CUDA events on the replay stream,
+until about ``--min-timed-s`` seconds have been timed; ``ms_per_step`` is the median block
+(max over ranks); clocks are sampled over all blocks.  Inputs are larger than L2 (32 MiB
+and more of distinct K per unit, hundreds of MiB per step).  ``e2e`` = the same metric
+through the public hook (``CircuitKVCluster.update_kv``) on pinned host tensors, with the
+host->device copies of the window queries and the distinct K heads (V's kept rows are read
+in place from pinned memory) and the device->host copy of the compressed K / V inside the
+timed region.
+
+``--impl reference`` times the CPU oracle port of the reference's path (the numpy
+restatement under ``oracle/``) on the host cores, rank 0 only.  Inputs are seeded synthetic
+tensors (``submission_folder_b200.synth``).
 """
 
 from __future__ import annotations
@@ -35,7 +51,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -43,9 +58,23 @@ sys.path.insert(0, ROOT)
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-METRIC = "tokens scored/s (per-layer CircuitKV scoring+eviction, 32-layer Llama-3-8B cache, 32k ctx)"
 STAGES = ["window_moments", "window_pool", "pool_reduce", "window_pool_rerun", "sweep_maps",
           "sweep_terms", "aux", "select", "gather"]
+H, HKV, D, G = 32, 8, 128, 4
+
+CONFIGS = {
+    1: dict(name="1 layer, fp32, n=4096, window 32, budget 512", layers=1, n=4096, window=32, budget=512,
+            dtype="fp32", planted=16, band=256),
+    2: dict(name="32-layer Llama-3-8B cache, bf16, n=8192, window 64, budget 1024", layers=32, n=8192,
+            window=64, budget=1024, dtype="bf16", planted=64, band=256),
+    3: dict(name="32-layer Llama-3-8B cache, bf16, n=32768, window 64, budget 2048", layers=32, n=32768,
+            window=64, budget=2048, dtype="bf16", planted=64, band=256),
+    4: dict(name="32-layer Mistral-7B cache, bf16, n=131072, window 128, budget 4096, locality band 1024",
+            layers=32, n=131072, window=128, budget=4096, dtype="bf16", planted=256, band=1024),
+    5: dict(name="serving batch of 16 sequences x 32 layers, bf16, n_i ~ U[2048, 32768], window 32, "
+                 "budget int(0.1 n_i)", layers=32, n=None, window=32, budget=None, dtype="bf16", planted=16,
+            band=256, batch=16),
+}
 
 
 def parse():
@@ -54,14 +83,17 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--n", type=int, default=32768)
-    ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--window", type=int, default=64)
-    ap.add_argument("--budget", type=int, default=2048)
-    ap.add_argument("--pyramid", action="store_true")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=3)
+    ap.add_argument("--layers", type=int, default=None, help="override the workload's layer count")
+    ap.add_argument("--pyramid", action="store_true", help="config 3: budget 4096 -> 512 over the layers")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong")
+    ap.add_argument("--qk", choices=["unit", "literal"], default="unit",
+                    help="Q/K component scale: unit (logits ~ N(0,1)) or literal N(0,1)/sqrt(128)")
+    ap.add_argument("--min-timed-s", type=float, default=1.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-stages", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=2)
     return ap.parse_args()
 
 
@@ -79,17 +111,80 @@ def peaks():
         return d
 
 
-def budgets(args):
-    if args.pyramid:
-        L = args.layers
-        return [int(round(4096 - 3584 * l / max(1, L - 1))) for l in range(L)]
-    return [args.budget] * args.layers
+# ---------------------------------------------------------------------------
+# workload: units (one update_kv call each) and their assignment to ranks
+# ---------------------------------------------------------------------------
+class Unit:
+    def __init__(self, uid, seq, layer, n, window, budget, dtype, seed):
+        self.uid, self.seq, self.layer = uid, seq, layer
+        self.n, self.window, self.budget, self.dtype, self.seed = n, window, budget, dtype, seed
 
 
-def layer_bytes(n, W, B, e=2, H=32, Hkv=8, D=128):
-    """Algorithmic bytes of one layer call: K read once (distinct heads), window Q,
-    kept K/V read, compacted K/V written."""
-    return e * (Hkv * n * D + H * W * D + 2 * Hkv * B * D + 2 * H * B * D)
+def workload(args, rank, world):
+    """(all units, units of this rank, owner map, description)."""
+    from submission_folder_b200 import sharding
+    c = CONFIGS[args.config]
+    L = args.layers or c["layers"]
+    units = []
+    if args.config == 5:
+        from submission_folder_b200.synth import ragged_lengths
+        lengths = ragged_lengths(c["batch"], 2048, 32768, seed=2025)
+        for i, n in enumerate(lengths):
+            for l in range(L):
+                units.append(Unit(len(units), i, l, n, c["window"], int(0.1 * n), c["dtype"], 700 + i))
+        seq_owner = {}
+        for r in range(world):
+            for i in sharding.sequences_for_rank(lengths, r, world):
+                seq_owner[i] = r
+        owner = {u.uid: seq_owner[u.seq] for u in units}
+    else:
+        for l in range(L):
+            b = c["budget"]
+            if args.pyramid:
+                b = int(round(4096 - 3584 * l / max(1, L - 1)))
+            units.append(Unit(l, 0, l, c["n"], c["window"], b, c["dtype"], 1))
+        owner = {}
+        for r in range(world):
+            for l in sharding.layers_for_rank(L, r, world):
+                owner[l] = r
+    if args.scaling == "weak":
+        # every rank scores its own copy of the whole workload (seeded per rank)
+        mine = []
+        for u in units:
+            mine.append(Unit(u.uid + rank * len(units), u.seq, u.layer, u.n, u.window, u.budget, u.dtype,
+                             u.seed + 1000 * rank))
+        allu = [Unit(u.uid + r * len(units), u.seq, u.layer, u.n, u.window, u.budget, u.dtype, u.seed)
+                for r in range(world) for u in units]
+        owner = {u.uid: u.uid // len(units) for u in allu}
+        return allu, mine, owner
+    mine = [u for u in units if owner[u.uid] == rank]
+    return units, mine, owner
+
+
+def unit_bytes(u, e):
+    """Algorithmic bytes of one unit: K read once (distinct heads), window Q, kept K/V
+    read, compacted K/V written."""
+    return e * (HKV * u.n * D + H * u.window * D + 2 * HKV * u.budget * D + 2 * H * u.budget * D)
+
+
+def config_obj(args, world, units):
+    c = CONFIGS[args.config]
+    L = args.layers or c["layers"]
+    cfg = {"workload": c["name"] + (" (pyramid budget 4096 -> 512)" if args.pyramid else ""),
+           "config": args.config, "layers": L, "units": len(units) // (world if args.scaling == "weak" else 1),
+           "window": c["window"], "dtype": c["dtype"],
+           "qk_scale": "N(0,1)/sqrt(128) (literal)" if args.qk == "literal" else "N(0,1) (unit-variance logits)",
+           "parallelism": (f"{'layers' if args.config != 5 else 'sequences'} of one workload split over "
+                           f"{world} rank(s)" if args.scaling == "strong" else
+                           f"every rank scores its own workload ({world} rank(s))"),
+           "l2": "inputs larger than L2 (>= 32 MiB of distinct K per unit, every unit's K read each step)"}
+    if args.config == 5:
+        cfg["sequence_lengths"] = sorted({u.n for u in units})
+        cfg["inputs"] = "distinct K / V heads per (sequence, layer); window queries shared by a sequence's layers"
+    else:
+        cfg["n"] = units[0].n
+        cfg["budget"] = "pyramid" if args.pyramid else units[0].budget
+    return cfg
 
 
 class ClockSampler:
@@ -151,52 +246,53 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU oracle (baseline / reference arm)
 # ---------------------------------------------------------------------------
-def cpu_oracle_sample(args, seconds_cap=30.0):
-    """The oracle port on the host cores: one full layer of the workload per sample."""
+def cpu_oracle_sample(args, u, samples=3, seconds_cap=30.0):
+    """The oracle port on the host cores: one unit of the workload per sample."""
     import numpy as np
     import torch
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import ckv_oracle as O
     from submission_folder_b200.synth import make_layer
+    c = CONFIGS[args.config]
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    q, k, v = make_layer(args.n, seed=0, window=args.window, planted=64, dtype="bf16")
+    q, k, v = make_layer(u.n, seed=u.seed, window=u.window, planted=c["planted"], locality=c["band"],
+                         qk_scale=qk_scale(args), dtype=u.dtype)
     qn, kn, vn = (x.float().numpy() for x in (q, k, v))
-    p = O.Params(window_size=args.window, max_capacity_prompt=budgets(args)[0])
+    p = O.Params(window_size=u.window, max_capacity_prompt=u.budget)
     times = []
     t_all = time.perf_counter()
     while True:
         t0 = time.perf_counter()
-        O.update_kv(qn, kn, vn, 4, p, dtype="bf16", solver="structured")
+        O.update_kv(qn, kn, vn, G, p, dtype=u.dtype, solver="structured")
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_all > seconds_cap or len(times) >= 3:
+        if time.perf_counter() - t_all > seconds_cap or len(times) >= samples:
             break
     t = statistics.median(times)
-    return {"value": args.n / t, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{len(times)} x one {args.n}-token layer (structured numpy restatement of the "
-                      f"reference path), median {t:.2f} s/layer"}
+    return {"value": u.n / t, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{len(times)} x one {u.n}-token unit (structured numpy restatement of the "
+                      f"reference path, {u.dtype}), median {t:.2f} s per unit"}
 
 
-def workload_config(args, world):
-    """The ``config`` object of both arms' JSON lines."""
-    bl = budgets(args)
-    return {"workload": "32-layer Llama-3-8B cache, 32 q / 8 kv heads, head_dim 128, bf16, "
-                        f"n={args.n}, window {args.window}, budget "
-                        f"{'pyramid 4096->512' if args.pyramid else bl[0]}",
-            "layers": args.layers, "n": args.n, "window": args.window,
-            "budget": "pyramid" if args.pyramid else bl[0],
-            "parallelism": f"layers of one cache per rank, {world} rank(s)",
-            "l2": "inputs larger than L2 (32 x 64 MiB distinct K per step)"}
+def qk_scale(args):
+    return 1.0 / math.sqrt(D) if args.qk == "literal" else 1.0
 
 
-def run_reference(args, rank):
+def metric_name(args):
+    c = CONFIGS[args.config]
+    return f"tokens scored/s (per-layer CircuitKV scoring+eviction; {c['name']})"
+
+
+def run_reference(args, rank, world):
     if rank != 0:
         return
-    cpu = cpu_oracle_sample(args)
-    line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tokens/s",
+    units, _, _ = workload(args, 0, 1)
+    u = max(units, key=lambda x: x.n) if args.config == 5 else units[0]
+    cpu = cpu_oracle_sample(args, u, samples=max(1, min(args.steps, 3)))
+    line = {"impl": "reference", "metric": metric_name(args), "value": cpu["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic", "config": workload_config(args, args.gpus),
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": config_obj(args, world, units),
             "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -209,7 +305,7 @@ def run_reference(args, rank):
 def run_ours(args, rank, world):
     import torch
     import torch.distributed as dist
-    from submission_folder_b200 import _lib, ops
+    from submission_folder_b200 import _lib, ops, sharding
     from submission_folder_b200.cluster import CircuitKVCluster, cli_cluster_kwargs
     from submission_folder_b200.synth import make_layer, repeat_kv
 
@@ -217,71 +313,59 @@ def run_ours(args, rank, world):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     lib = _lib.load()
-    n, W, L = args.n, args.window, args.layers
-    bl = budgets(args)
-    H, Hkv, D, G = 32, 8, 128, 4
+    c = CONFIGS[args.config]
+    pg = dist.is_initialized()
+    units, mine, owner = workload(args, rank, world)
+    e = 4 if c["dtype"] == "fp32" else 2
+    tdt = {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[c["dtype"]]
 
-    # ---- inputs: the caller's layout ([1,32,n,128] Q and repeat_kv'd K / V) ----
-    Q, K, V = [], [], []
-    for l in range(L):
-        q, k, v = make_layer(n, seed=1000 * rank + 1, layer=l, window=W, planted=64, dtype="bf16",
-                             device=str(dev))
-        Q.append(q[None])
-        K.append(repeat_kv(k, G))
-        V.append(repeat_kv(v, G))
+    # ---- inputs on the device.  Configs 1-4: the caller's layout ([1, 32, n, 128] Q and
+    # repeat_kv'd K / V, read as the distinct heads); config 5: distinct K / V heads per
+    # unit and one Q per sequence (its layers share the window queries).
+    Qs, Ks, Vs = [], [], []
+    seq_q = {}
+    for u in mine:
+        q, k, v = make_layer(u.n, seed=u.seed, layer=u.layer, window=u.window, planted=c["planted"],
+                             locality=c["band"], qk_scale=qk_scale(args), dtype=u.dtype, device=str(dev))
+        if args.config == 5:
+            if u.seq not in seq_q:
+                seq_q[u.seq] = q
+            Qs.append(seq_q[u.seq])
+            Ks.append(k)
+            Vs.append(v)
+        else:
+            Qs.append(q[None])
+            Ks.append(repeat_kv(k, G)[0, ::G])
+            Vs.append(repeat_kv(v, G)[0, ::G])
         del q, k, v
     torch.cuda.synchronize()
 
-    params, structs, outs, idxs = [], [], [], []
-    ws_size, ws_total = 0, 0
-    for l in range(L):
-        cl = CircuitKVCluster(**cli_cluster_kwargs(W, bl[l]))
-        p = cl.params(n)
+    exch = sharding.KeptExchange({u.uid: (u.budget - u.window,) for u in units}, owner, rank, world, device=dev)
+    params, structs, outs, ws_sizes = [], [], [], []
+    for u in mine:
+        p = CircuitKVCluster(**cli_cluster_kwargs(u.window, u.budget)).params(u.n)
         params.append(p)
-        one = ops.workspace_size(p, n, H, Hkv, D)
-        ws_size = max(ws_size, one)
-        ws_total += (one + 255) // 256 * 256
-    # one workspace slice per layer: the batched call runs the layers concurrently
-    ws = torch.empty(ws_total, dtype=torch.uint8, device=dev)
-    for l in range(L):
-        lay = ops.make_layer(Q[l][0], K[l][0, ::G], V[l][0, ::G])
-        olen = ops.output_len(params[l], n)
-        ko = torch.empty(H, olen, D, dtype=torch.bfloat16, device=dev)
-        vo = torch.empty(H, olen, D, dtype=torch.bfloat16, device=dev)
-        idx = torch.empty(olen - W, dtype=torch.int32, device=dev)
+        ws_sizes.append((ops.workspace_size(p, u.n, H, HKV, D) + 255) // 256 * 256)
+    ws = torch.empty(max(1, sum(ws_sizes)), dtype=torch.uint8, device=dev)
+    for i, u in enumerate(mine):
+        q = Qs[i][0] if args.config != 5 else Qs[i]
+        lay = ops.make_layer(q, Ks[i], Vs[i])
+        olen = ops.output_len(params[i], u.n)
+        ko = torch.empty(H, olen, D, dtype=tdt, device=dev)
+        vo = torch.empty(H, olen, D, dtype=tdt, device=dev)
+        idx = exch.out(u.uid)
         o = _lib.Outputs()
         o.out_k, o.out_v, o.out_idx, o.out_scores = ko.data_ptr(), vo.data_ptr(), idx.data_ptr(), None
         structs.append(lay)
         outs.append((o, ko, vo))
-        idxs.append(idx)
+    L = len(mine)
     wsp = ctypes.c_void_p(ws.data_ptr())
-
-    nev = len(STAGES) + 1
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(L)]
-    for row in events:
-        for e in row:
-            e.record()
-    torch.cuda.synchronize()
-    ev_arrays = [(ctypes.c_void_p * nev)(*[e.cuda_event for e in row]) for row in events]
-
     P_arr = (_lib.Params * L)(*params)
     L_arr = (_lib.Layer * L)(*structs)
     O_arr = (_lib.Outputs * L)(*[o[0] for o in outs])
 
-    def step_serial(with_events=True):
-        """One ckv_score_evict call per layer; per-stage event records (graph capture only)."""
-        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-        for l in range(L):
-            if with_events:
-                lib.ckv_set_stage_events(ev_arrays[l], nev)
-            rc = lib.ckv_score_evict(ctypes.byref(params[l]), ctypes.byref(structs[l]), wsp, ws_size,
-                                     ctypes.byref(outs[l][0]), st)
-            if rc != 0:
-                raise RuntimeError(lib.ckv_last_error_string().decode())
-        lib.ckv_set_stage_events(None, 0)
-
     def step():
-        """The timed step: every layer in one batched call (concurrent lanes)."""
+        """The timed step's kernels: every local unit in one batched call (concurrent lanes)."""
         st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         rc = lib.ckv_score_evict_batched(P_arr, L, L_arr, L, wsp, ws.numel(), O_arr, st)
         if rc != 0:
@@ -298,182 +382,234 @@ def run_ours(args, rank, world):
         torch.cuda.synchronize()
         return g
 
-    # eager warm-up (kernel attributes and the library's lanes are set up on first
-    # use), then capture both forms of the step
-    step()
-    step_serial(with_events=False)
-    torch.cuda.synchronize()
-    graph_serial = capture(step_serial)
-    graph = capture(step)
+    graph = None
+    if L > 0:
+        step()   # eager: kernel attributes and the library's lanes are set up on first use
+        torch.cuda.synchronize()
+        graph = capture(step)
 
-    # per-stage breakdown from the serial form (not the timed region)
-    for _ in range(2):
+    # ---- per-stage breakdown from the serial form (one call per unit; not the timed region)
+    stage_ms, serial_ms = None, None
+    if not args.no_stages and L > 0:
+        nev = len(STAGES) + 1
+        events = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(L)]
+        for row in events:
+            for ev in row:
+                ev.record()
+        torch.cuda.synchronize()
+        ev_arrays = [(ctypes.c_void_p * nev)(*[ev.cuda_event for ev in row]) for row in events]
+        ws_off = [0]
+        for sz in ws_sizes[:-1]:
+            ws_off.append(ws_off[-1] + sz)
+
+        def step_serial():
+            st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for i in range(L):
+                lib.ckv_set_stage_events(ev_arrays[i], nev)
+                rc = lib.ckv_score_evict(ctypes.byref(params[i]), ctypes.byref(structs[i]),
+                                         ctypes.c_void_p(ws.data_ptr() + ws_off[i]), ws_sizes[i],
+                                         ctypes.byref(outs[i][0]), st)
+                if rc != 0:
+                    raise RuntimeError(lib.ckv_last_error_string().decode())
+            lib.ckv_set_stage_events(None, 0)
+
+        graph_serial = capture(step_serial)
+        for _ in range(2):
+            graph_serial.replay()
+        torch.cuda.synchronize()
+        stage_ms = [0.0] * (nev - 1)
+        for i in range(L):
+            for j in range(nev - 1):
+                stage_ms[j] += events[i][j].elapsed_time(events[i][j + 1])
+        t0s, t1s = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0s.record()
         graph_serial.replay()
-    torch.cuda.synchronize()
-    stage_ms = [0.0] * (nev - 1)
-    for l in range(L):
-        for i in range(nev - 1):
-            stage_ms[i] += events[l][i].elapsed_time(events[l][i + 1])
-    t0s = torch.cuda.Event(enable_timing=True)
-    t1s = torch.cuda.Event(enable_timing=True)
-    t0s.record()
-    graph_serial.replay()
-    t1s.record()
-    torch.cuda.synchronize()
-    serial_ms = t0s.elapsed_time(t1s)
+        t1s.record()
+        torch.cuda.synchronize()
+        serial_ms = t0s.elapsed_time(t1s)
+        del graph_serial
 
-    pg = dist.is_initialized()
+    def one_step():
+        if graph is not None:
+            graph.replay()
+        if pg:
+            exch.exchange()
+
     for _ in range(max(args.warmup, 3)):
-        graph.replay()
+        one_step()
     torch.cuda.synchronize()
-    if pg:
-        dist.barrier()
-    clocks = ClockSampler(local)
-    clocks.start()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if pg:
-        dist.barrier()
+    # how many timed blocks of K steps fill about --min-timed-s (agreed over ranks)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    for _ in range(args.steps):
-        graph.replay()
+    one_step()
     t1.record()
     torch.cuda.synchronize()
+    est = t0.elapsed_time(t1) / 1e3
     if pg:
-        dist.barrier()
+        est = sharding.max_over_ranks(est, device=dev)
+    blocks = max(1, min(50, int(math.ceil(args.min_timed_s / max(est * args.steps, 1e-6)))))
+    clocks = ClockSampler(local)
+    clocks.start()
+    block_ms = []
+    for _ in range(blocks):
+        torch.cuda.synchronize()
+        if pg:
+            dist.barrier()
+        t0.record()
+        for _ in range(args.steps):
+            one_step()
+        t1.record()
+        torch.cuda.synchronize()
+        if pg:
+            dist.barrier()
+        ms = t0.elapsed_time(t1) / args.steps
+        if pg:
+            ms = sharding.max_over_ranks(ms, device=dev)
+        block_ms.append(ms)
     clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / args.steps
-    # kept-index metadata of every rank (the only collective of the data path)
+    ms = statistics.median(block_ms)
+
+    # kept positions after the exchange: every rank holds every unit's (checked on rank 0)
     gathered = None
     if pg:
-        from submission_folder_b200 import sharding
-        ms = sharding.max_over_ranks(ms, device=dev)
-        allk = sharding.gather_kept({rank * L + l: idxs[l] for l in range(L)}, device=dev)
-        gathered = int(sum(t.numel() for t in allk.values()))
+        gathered = int(sum(exch.result(u.uid).numel() for u in units))
+        for u in mine:
+            assert torch.equal(exch.result(u.uid), exch.out(u.uid))
 
-    # device status of every layer's workspace slice (outside the timed region)
+    # device status of every unit's workspace slice and the exact-branch flags (outside timing)
     st = ctypes.c_int32()
-    status_all = 0
+    status_all, need_exact = 0, 0
     off = 0
-    for l in range(L):
+    for i in range(L):
         lib.ckv_read_status(ctypes.c_void_p(ws.data_ptr() + off),
                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(st))
         status_all |= st.value
-        off += (ops.workspace_size(params[l], n, H, Hkv, D) + 255) // 256 * 256
+        need_exact += int(ws[off + 56: off + 60].cpu().view(torch.int32).item())   # Header.need_exact
+        off += ws_sizes[i]
 
-    tokens = L * n
-    value = tokens * world / (ms / 1000.0)
-    e = 2
-    alg_bytes = sum(layer_bytes(n, W, b) for b in bl)
+    tokens_all = sum(u.n for u in units)                 # every rank's units (weak: all copies)
+    value = tokens_all / (ms / 1000.0)
     pk = peaks()
-    # the dominant kernel and its roofline: the larger of the two window passes.  They are
-    # the only stages that fill every SM (one CTA per SM), so they hold most of the batched
-    # step's SM-time; the sweep, selection and reduction kernels run on a few dozen CTAs
-    # and overlap other layers' passes (serially the selection is as long as the pooling
-    # pass, but it occupies 16 SMs).
-    dom = max((STAGES.index("window_moments"), STAGES.index("window_pool")), key=lambda i: stage_ms[i])
-    dom_ms = stage_ms[dom] / L
-    flops = 2.0 * H * W * n * D
-    kbytes = e * (Hkv * n * D + H * W * D)
-    if STAGES[dom] in ("window_moments", "window_pool"):
-        wbytes = kbytes + (2 * W * n * 4 if STAGES[dom] == "window_pool" else 0)
-        t_tensor = flops / (pk["bf16_tflops"] * 1e12)
-        t_hbm = wbytes / (pk["hbm_gbs"] * 1e9)
-        if t_tensor >= t_hbm:
-            roof = {"bound": "tensor", "achieved": flops / (dom_ms / 1e3) / 1e12, "peak": pk["bf16_tflops"],
-                    "unit": "TFLOP/s"}
-        else:
-            roof = {"bound": "hbm", "achieved": wbytes / (dom_ms / 1e3) / 1e9, "peak": pk["hbm_gbs"],
-                    "unit": "GB/s"}
-    else:
-        b = layer_bytes(n, W, bl[0])
-        roof = {"bound": "hbm", "achieved": b / (dom_ms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["kernel"] = STAGES[dom]
-    roof["peak_source"] = pk["source"]
-    roof["avg_launch_us"] = dom_ms * 1e3
-    roof["traffic"] = traffic_for(STAGES[dom])
-    path_gbs = alg_bytes / (ms / 1e3) / 1e9
-    # stats; the pooling pass (one kernel, either form) and its reduction; the re-run pair
-    # (returns at once unless the speculated head sets were wrong); two sweep kernels;
-    # selection; gather
-    kernels_per_layer = 9
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config(args, world),
-        "per_layer_us": ms * 1e3 / L,
-        "serial_per_layer_us": serial_ms * 1e3 / L,
-        "path_hbm_gbs": path_gbs, "path_hbm_frac": path_gbs / pk["hbm_gbs"],
-        "stage_us_per_layer": {STAGES[i]: stage_ms[i] * 1e3 / L for i in range(len(stage_ms))},
-        "roofline": roof,
+        "metric": metric_name(args), "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": c["dtype"], "data": "synthetic",
+        "config": config_obj(args, world, units),
+        "timed_blocks": len(block_ms), "block_ms_per_step": block_ms,
+        "units_per_rank": L, "per_unit_us": ms * 1e3 / max(L, 1),
         "clocks": clk,
-        "gpu_launches": kernels_per_layer * L * args.steps,
+        # per unit: moments pass, pooling pass + reduction, the pooling re-run pair (returns
+        # at once unless the speculated head sets were wrong), sweep maps + terms, selection,
+        # gather
+        "gpu_launches": 9 * L * args.steps * len(block_ms),
         "device_status": status_all,
+        "pooling_exact_branch_units": need_exact,
     }
+    alg_bytes = sum(unit_bytes(u, e) for u in mine)
+    path_gbs = alg_bytes / (ms / 1e3) / 1e9
+    line["path_hbm_gbs"] = path_gbs
+    line["path_hbm_frac"] = path_gbs / pk["hbm_gbs"]
+    if stage_ms is not None and L > 0:
+        line["serial_per_unit_us"] = serial_ms * 1e3 / L
+        line["stage_us_per_unit"] = {STAGES[i]: stage_ms[i] * 1e3 / L for i in range(len(stage_ms))}
+        line["roofline"] = roofline(stage_ms, mine, e, pk)
     if gathered is not None:
-        line["allgather_indices"] = gathered
+        line["allgather_positions"] = gathered
 
-    # ---- end to end through the public hook with pinned host buffers ----
     if not args.no_e2e:
-        line["e2e"] = e2e(args, rank, world, dev, bl, CircuitKVCluster, cli_cluster_kwargs, make_layer,
-                          repeat_kv, pg)
-    if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_oracle_sample(args)
-    del graph, graph_serial
+        line["e2e"] = e2e(args, rank, world, dev, mine, units, pg)
+    if rank == 0 and world == 1 and not args.no_cpu and mine:
+        u0 = max(mine, key=lambda x: x.n) if args.config == 5 else mine[0]
+        line["cpu_baseline"] = cpu_oracle_sample(args, u0, samples=1 if u0.n > 65536 else 3)
+    del graph
     if rank == 0:
         print(json.dumps(line), flush=True)
 
 
-def traffic_for(stage):
+def roofline(stage_ms, mine, e, pk):
+    """The dominant kernel's roofline: the larger of the two window passes (the only
+    stages that fill every SM).  Algorithmic work per launch: K read once (distinct heads)
+    plus the window queries (and, for the pooling pass, the pooled rows written), or the
+    logits contraction 2 H W n D when that takes longer at peak."""
+    dom = max((STAGES.index("window_moments"), STAGES.index("window_pool")), key=lambda i: stage_ms[i])
+    L = len(mine)
+    dom_s = stage_ms[dom] / L / 1e3
+    flops = sum(2.0 * H * u.window * u.n * D for u in mine) / L
+    wbytes = sum(e * (HKV * u.n * D + H * u.window * D) + (2 * u.window * u.n * 4 if dom == 1 else 0)
+                 for u in mine) / L
+    t_tensor = flops / (pk["bf16_tflops"] * 1e12)
+    t_hbm = wbytes / (pk["hbm_gbs"] * 1e9)
+    if t_tensor >= t_hbm:
+        roof = {"bound": "tensor", "achieved": flops / dom_s / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": wbytes / dom_s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["kernel"] = STAGES[dom]
+    roof["peak_source"] = pk["source"]
+    roof["avg_launch_us"] = dom_s * 1e6
+    roof["algorithmic_per_launch"] = flops if roof["bound"] == "tensor" else wbytes
+    roof["traffic"] = traffic_for(STAGES[dom], mine[0].n)
+    return roof
+
+
+def traffic_for(stage, n):
+    """DRAM bytes per launch of the stage from the committed ncu capture (n = 32768)."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get(stage)
+            t = json.load(f).get(stage)
+        return None if t is None else t * n / 32768.0
     except Exception:
         return None
 
 
-def e2e(args, rank, world, dev, bl, CircuitKVCluster, cli_cluster_kwargs, make_layer, repeat_kv, pg):
+def e2e(args, rank, world, dev, mine, units, pg):
+    """Tokens/s through the public hook on pinned host tensors (copies inside the timing)."""
     import torch
     import torch.distributed as dist
-    n, W, L = args.n, args.window, args.layers
-    G = 4
-    host = []
-    for l in range(2):
-        q, k, v = make_layer(n, seed=1000 * rank + 2, layer=l, window=W, planted=64, dtype="bf16",
-                             device=str(dev))
-        host.append(tuple(x.cpu().pin_memory() for x in (q[None], repeat_kv(k, G), repeat_kv(v, G))))
-        del q, k, v
-    clusters = [CircuitKVCluster(**cli_cluster_kwargs(W, b)) for b in bl]
-    # host -> device per layer: the window queries and K are copied; the gather reads V's
-    # kept rows (8 KV heads x budget rows) from the pinned host tensor in place
-    h2d = sum(2 * (32 * W * 128 + 8 * n * 128 + 8 * b * 128) for b in bl)
-    d2h = sum(2 * 2 * 32 * b * 128 for b in bl)
+    from submission_folder_b200.cluster import CircuitKVCluster, cli_cluster_kwargs
+    from submission_folder_b200.synth import make_layer, repeat_kv
+    c = CONFIGS[args.config]
+    # host inputs in the caller's layout: two layers per distinct length, reused round-robin
+    host = {}
+    for u in mine:
+        key = (u.n, u.layer % 2)
+        if key not in host:
+            q, k, v = make_layer(u.n, seed=u.seed + 2, layer=u.layer % 2, window=u.window, planted=c["planted"],
+                                 locality=c["band"], qk_scale=qk_scale(args), dtype=u.dtype, device=str(dev))
+            host[key] = tuple(x.cpu().pin_memory() for x in (q[None], repeat_kv(k, G), repeat_kv(v, G)))
+            del q, k, v
+    clusters = [CircuitKVCluster(**cli_cluster_kwargs(u.window, u.budget)) for u in mine]
+    e = 4 if c["dtype"] == "fp32" else 2
+    # per unit: the window queries and the distinct K heads copied in; the gather reads V's
+    # kept rows (8 KV heads x budget rows) from the pinned host tensor in place; K / V out
+    h2d = sum(e * (H * u.window * D + HKV * u.n * D + HKV * u.budget * D) for u in mine)
+    d2h = sum(e * 2 * H * u.budget * D for u in mine)
 
     def one_step():
-        for l in range(L):
-            qh, kh, vh = host[l % 2]
-            ko, vo = clusters[l].update_kv(kh, qh, vh, None, G)
+        for cl, u in zip(clusters, mine):
+            qh, kh, vh = host[(u.n, u.layer % 2)]
+            ko, vo = cl.update_kv(kh, qh, vh, None, G)
         return ko
 
-    one_step()
+    if mine:
+        one_step()
     torch.cuda.synchronize()
     if pg:
         dist.barrier()
     t = time.perf_counter()
     for _ in range(args.e2e_steps):
-        one_step()
+        if mine:
+            one_step()
     torch.cuda.synchronize()
     sec = (time.perf_counter() - t) / args.e2e_steps
     if pg:
         from submission_folder_b200 import sharding
         sec = sharding.max_over_ranks(sec, device=dev)
-    return {"value": L * n * world / sec, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+    tokens = sum(u.n for u in units)
+    return {"value": tokens / sec, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "s_per_step": sec,
-            "api": "CircuitKVCluster.update_kv on pinned host tensors"}
+            "api": "CircuitKVCluster.update_kv on pinned host tensors (per rank: its units)"}
 
 
 def main():
@@ -481,7 +617,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
     if world > 1:
         import datetime
@@ -489,7 +625,8 @@ def main():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
     try:
         run_ours(args, rank, world)
     finally:

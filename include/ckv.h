@@ -160,7 +160,9 @@ int ckv_score_evict_batched(const ckv_params* params, int32_t params_count, cons
                             const ckv_outputs* outs, ckv_stream_t stream);
 
 /* Reads (synchronising on `stream`) and clears the device status word of a
- * workspace: 0 when every kernel since the last read finished normally. */
+ * workspace: 0 when every kernel since the last read finished normally.
+ * workspace NULL reads the status word of ckv_select_scores_noalloc's static
+ * scratch on the current device (the status of the last such call there). */
 int ckv_read_status(void* workspace, ckv_stream_t stream, int32_t* device_status);
 
 /* ---- stage entry points (used by the parity tests; same kernels as above) --- */
@@ -183,10 +185,14 @@ int ckv_select_scores(const ckv_params* p, int32_t n, const float* a, const floa
  * synchronises the device), or a C / FFI caller with no device allocator.  The
  * scratch is a static __device__ array inside the library sized for n <= 32768
  * (about 0.9 MiB held on every GPU that loads the library until exit); larger n
- * is rejected with CKV_ERR_ARG.  The first call on each device looks up the
- * array's device address (make it before any stream capture).  All calls share
- * the array: calls that overlap on the GPU race, so order them on one stream.
- * Same results as ckv_select_scores; calls no cudaMalloc / cudaFree. */
+ * is rejected with CKV_ERR_ARG.  Each call looks up the array's device address on
+ * the current device; the first call on a device may load the library's module,
+ * so make it before any stream capture.  All calls share the array (each call
+ * clears its header first): calls that overlap on the GPU race, so order them on
+ * one stream.  Device-side failures are read with ckv_read_status(NULL, ...).
+ * Modes: dis (with or without the bridge vector c), max, union and union_da give
+ * the same results as ckv_select_scores; combination_mode weighted and per-head
+ * eviction return CKV_ERR_UNSUPPORTED.  Calls no cudaMalloc / cudaFree. */
 int ckv_select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const float* b,
                               const float* c, int32_t* out_idx, float* out_scores,
                               ckv_stream_t stream);

@@ -545,6 +545,36 @@ def union_keep_mask(qi: np.ndarray, hi: np.ndarray, budget: int, n: int, sink: i
     return mask
 
 
+def select_from_vectors(a: np.ndarray, b: np.ndarray, p: Params, n: int) -> np.ndarray:
+    """The shared-eviction selection from the two vectors it ranks, ascending kept
+    prefix positions (local window excluded).
+
+    ``a`` / ``b`` are the vectors after finishing and smoothing, exactly as ranked:
+    QI / HI for "dis" (PU:3177-3196, ablations at 3186-3191, no bridge vector),
+    influence / H2O for "max" / "weighted" (PU:3205-3242), the (DA-weighted) QI / HI
+    for "union" / "union_da" (PU:2489-2589).  Keep mask: PU:2591-2644.
+    """
+    W, s, mode = p.window_size, p.sink_size, p.combination_mode
+    if mode in ("union", "union_da"):
+        mask = union_keep_mask(a, b, p.max_capacity_prompt, n, s, W, p.qi_ratio)
+    else:
+        ra, rb = rank_normalize(a), rank_normalize(b)
+        if mode == "dis":
+            if p.ablate_qi:
+                ra = np.zeros_like(ra)
+            if p.ablate_hi:
+                rb = np.zeros_like(rb)
+            comb = np.maximum(ra, rb)
+        elif mode == "weighted":
+            comb = (F32(p.h2o_weight) * rb + F32(1 - p.h2o_weight) * ra).astype(F32)
+        else:
+            comb = np.maximum(rb, ra)
+        mask = keep_mask(comb, p.max_capacity_prompt, n, s, W)
+    mask = mask.copy()
+    mask[n - W:] = False
+    return np.nonzero(mask)[0]
+
+
 # --------------------------------------------------------------------------
 # a16-a17: per-head mode
 # --------------------------------------------------------------------------

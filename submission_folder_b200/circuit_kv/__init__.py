@@ -3,8 +3,10 @@
 ``circuit_kv._C.CircuitGraph`` provides the constructor and the influence-walker
 pair that ``CircuitKVCluster`` calls when ``use_neumann=False``
 (CircuitKV/csrc/pybind.cpp:44-64, 263-300), running the sm_100a walker of
-``libckv.so``.  The package-level helpers ``set_seed`` and ``get_extension`` keep
-their reference behaviour (CircuitKV/circuit_kv/__init__.py, utils.py).
+``libckv.so``.  The package exports the reference's names
+(CircuitKV/circuit_kv/__init__.py:14-28): ``CircuitKVMonitor``, ``CircuitKVConfig``,
+``LandmarkWalkerMonitor``, ``LandmarkWalkerConfig`` (``engine.py``) and ``set_seed``;
+``get_extension`` keeps its reference behaviour.
 """
 
 import random
@@ -13,9 +15,16 @@ import numpy as np
 import torch
 
 from . import _C
+from .engine import CircuitKVConfig, CircuitKVMonitor, LandmarkWalkerConfig, LandmarkWalkerMonitor
 
 __version__ = "3.0.0"
-__all__ = ["set_seed", "get_extension"]
+__all__ = [
+    "CircuitKVMonitor",
+    "CircuitKVConfig",
+    "LandmarkWalkerMonitor",
+    "LandmarkWalkerConfig",
+    "set_seed",
+]
 
 
 def set_seed(seed: int) -> None:

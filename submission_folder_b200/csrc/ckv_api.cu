@@ -424,7 +424,11 @@ int ckv_score_evict_batched(const ckv_params* params, int32_t params_count, cons
 }
 
 int ckv_read_status(void* workspace, ckv_stream_t stream, int32_t* device_status) {
-  if (!workspace || !device_status) return fail(CKV_ERR_ARG, "null argument");
+  if (!device_status) return fail(CKV_ERR_ARG, "null argument");
+  if (!workspace) {   // the static scratch of ckv_select_scores_noalloc on this device
+    const cudaError_t e = noalloc_scratch(&workspace);
+    if (e != cudaSuccess) return cuda_fail(e, "static scratch address");
+  }
   Header h;
   cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(Header), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);

@@ -1226,34 +1226,29 @@ cudaError_t launch_aux(const Plan& pl, const ckv_params& p, char* ws, cudaStream
 // there either fails or fragments the pool, and cudaMalloc also synchronises the
 // device), or plain-C / FFI callers that have no device allocator of their own.
 // For them the selection stage keeps its scratch in this file-scope array: header
-// (256 B) + the selection area (29 bytes per position) for up to 32768 positions,
-// about 0.9 MiB that every GPU which loads the library holds until the process
-// exits.  All calls share it and it keeps the last call's contents, so calls that
-// overlap on the GPU (different streams, or different host threads on one device)
-// race; order them on one stream.
+// (512 B, with the device status word) + the selection area (29 bytes per position)
+// for up to 32768 positions, about 0.9 MiB that every GPU which loads the library
+// holds until the process exits.  All calls share it and it keeps the last call's
+// contents, so calls that overlap on the GPU (different streams, or different host
+// threads on one device) race; order them on one stream.
 constexpr int kNoAllocMaxN = 32768;
 constexpr size_t kNoAllocBytes = sizeof(Header) + (size_t)29 * kNoAllocMaxN;
+static_assert(sizeof(Header) == 512, "the static scratch starts with the 512-byte header");
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
-// Device address of g_noalloc_scratch per device, looked up once per device with
-// that device current (the host-side symbol is only a stand-in, not a device address).
-constexpr int kMaxDevices = 64;
-static void* g_noalloc_addr[kMaxDevices] = {};
-static std::mutex g_noalloc_mu;
-
-static cudaError_t noalloc_scratch(void** out) {
+// Device address of g_noalloc_scratch on the current device.  In host code the array's
+// name is only a stand-in for it, so the address is looked up with the device current,
+// on every call: the lookup is cheap once the module is loaded, and it stays right after
+// the device's primary context is reset.  The first call on a device may load the
+// module, which is not allowed while a stream is being captured.
+cudaError_t noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    g_noalloc_addr[dev] = ptr;
-  }
-  *out = g_noalloc_addr[dev];
+  void* ptr = nullptr;
+  e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  *out = ptr;
   return cudaSuccess;
 }
 

@@ -35,7 +35,9 @@ cudaError_t launch_ph_select(const PhArgs& a, cudaStream_t st);
 
 size_t select_smem_bytes_n(int n);
 cudaError_t launch_select(const SelArgs& a, cudaStream_t st);
-// Selection stage with its scratch in a static device array (no workspace argument).
+// Selection stage with its scratch in a static device array (no workspace argument);
+// noalloc_scratch gives that array's device address on the current device.
+cudaError_t noalloc_scratch(void** out);
 int select_scores_noalloc(const ckv_params* p, int32_t n, const float* a, const float* b,
                           const float* c, int32_t* out_idx, float* out_scores, cudaStream_t st,
                           const char** why);

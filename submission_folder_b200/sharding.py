@@ -11,7 +11,8 @@ tensors on GPUs, gloo with CPU tensors in the CPU tests.
 
 from __future__ import annotations
 
-from typing import Dict, List, Optional, Sequence
+import math
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -97,3 +98,53 @@ def max_over_ranks(x: float, group=None, device: Optional[torch.device] = None) 
     t = torch.tensor([float(x)], dtype=torch.float64, device=device or torch.device("cpu"))
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+class KeptExchange:
+    """The kept positions of every unit, shared by ONE all-gather with no host round trip.
+
+    Each unit's owner and kept-index shape are known to every rank in advance (they follow
+    from the sequence lengths, budgets and the assignment above), so each rank lays its
+    units out in one int32 buffer of a common capacity, lets the scoring call write each
+    unit's kept positions straight into its slice (``out(unit)``), and ``exchange()`` runs
+    a single ``all_gather_into_tensor`` into ``[world * cap]``; ``result(unit)`` is a view of
+    any unit's positions there.  The collective can be enqueued right after the scoring
+    work on the same stream (NCCL) without synchronising the host.
+    """
+
+    def __init__(self, shapes: Dict[int, Tuple[int, ...]], owner: Dict[int, int], rank: int, world: int,
+                 device: Optional[torch.device] = None):
+        if set(shapes) != set(owner):
+            raise ValueError("every unit needs a shape and an owner")
+        self.rank, self.world = rank, world
+        used = [0] * world
+        self.slots = {}
+        for u in sorted(shapes):
+            r = int(owner[u])
+            if not 0 <= r < world:
+                raise ValueError("owner out of range")
+            size = int(math.prod(shapes[u]))
+            self.slots[u] = (r, used[r], tuple(int(x) for x in shapes[u]))
+            used[r] += size
+        self.cap = max(1, max(used))
+        dev = device if device is not None else torch.device("cpu")
+        self.local = torch.zeros(self.cap, dtype=torch.int32, device=dev)
+        self.all = torch.zeros(world * self.cap, dtype=torch.int32, device=dev)
+
+    def units_of(self, rank: int) -> List[int]:
+        return [u for u, (r, _, _) in sorted(self.slots.items()) if r == rank]
+
+    def out(self, unit: int) -> torch.Tensor:
+        r, off, shape = self.slots[unit]
+        if r != self.rank:
+            raise ValueError("unit owned by another rank")
+        return self.local[off: off + math.prod(shape)].view(shape)
+
+    def exchange(self, group=None) -> None:
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(self.all, self.local, group=group)
+
+    def result(self, unit: int) -> torch.Tensor:
+        r, off, shape = self.slots[unit]
+        base = r * self.cap + off
+        return self.all[base: base + math.prod(shape)].view(shape)

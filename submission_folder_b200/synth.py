@@ -18,6 +18,11 @@ Distribution (per layer, per KV group ``g`` of ``groups`` query heads):
   ``||k|| (0.8 u_g + 0.6 w)`` with ``w`` a random unit vector orthogonal to
   ``u_g`` (cosine 0.8 with the mean window query).
 * values are generated in float32 and cast to the requested dtype last.
+* ``grid_step > 0`` (exact-arithmetic inputs): ``Q`` and ``K`` are finally rounded to
+  multiples of ``grid_step`` with at most 15 steps either side of zero.  With the
+  default 0.25 every product ``q_d k_d`` is a multiple of 1/16 and every partial sum of
+  a 128-term dot product is exactly representable in fp32, so the logits are the same
+  bits in any summation order (CPU BLAS, cuBLAS, tensor-core MMA).
 """
 
 from __future__ import annotations
@@ -32,7 +37,7 @@ DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 def make_layer(n: int, *, seed: int = 0, layer: int = 0, heads: int = 32, kv_heads: int = 8,
                head_dim: int = 128, window: int = 64, planted: int = 16, locality: int = 256,
                sink: int = 4, sink_boost: float = 3.0, locality_boost: float = 1.0,
-               qk_scale: float = 1.0, dtype: str = "bf16", device: str = "cpu"):
+               qk_scale: float = 1.0, dtype: str = "bf16", device: str = "cpu", grid_step: float = 0.0):
     """Return ``(q [H,n,D], k [Hkv,n,D], v [Hkv,n,D])`` for one layer.
 
     Generation happens on ``device`` with a generator seeded from ``(seed, layer)``;
@@ -64,6 +69,9 @@ def make_layer(n: int, *, seed: int = 0, layer: int = 0, heads: int = 32, kv_hea
             r = r / r.norm(dim=1, keepdim=True).clamp_min(1e-12)
             kn = k[g, pos].norm(dim=1, keepdim=True)
             k[g, pos] = kn * (0.8 * u[None, :] + 0.6 * r)
+    if grid_step > 0:
+        q = torch.clamp(torch.round(q / grid_step), -15, 15) * grid_step
+        k = torch.clamp(torch.round(k / grid_step), -15, 15) * grid_step
     dt = DTYPES[dtype]
     return q.to(dt), k.to(dt), v.to(dt)
 

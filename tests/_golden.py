@@ -32,7 +32,8 @@ def load(name):
 def inputs(c, device="cpu"):
     """Regenerate the case's (q [H,n,D], k [Hkv,n,D], v [Hkv,n,D]) torch tensors."""
     return make_layer(c["n"], seed=c["seed"], window=c["window"], planted=c["planted"],
-                      qk_scale=c["qk_scale"], dtype=c["dtype"], device=device)
+                      qk_scale=c["qk_scale"], dtype=c["dtype"], device=device,
+                      grid_step=c.get("grid_step", 0.0))
 
 
 def oracle_params(c) -> O.Params:
@@ -57,3 +58,61 @@ def compare_keep(ours, ref, combined, lo, hi, kk, margin=0.0):
     diff = a ^ b
     ok = all(abs(float(combined[i]) - t) <= margin + 1e-12 for i in diff)
     return len(diff), ok
+
+
+SCORE_RTOL = 1e-3   # ranked vectors vs the reference's: max abs difference / max |reference|
+
+
+def ranked_vectors_of_reference(c, g, op):
+    """The two vectors the reference ranks (or unions), as recorded in the fixture:
+    smoothed QI / HI for "dis", the union inputs for union modes, influence for
+    "max" / "weighted" (its H2O partner is not recorded: None)."""
+    mode = op.combination_mode
+    if mode in ("union", "union_da"):
+        return g["union_qi"], g["union_hi"]
+    if mode in ("max", "weighted"):
+        return g["influence"], None
+    qk = op.qi_kernel_size if op.qi_kernel_size != 0 else op.smoothing_kernel
+    hk = op.hi_kernel_size if op.hi_kernel_size != 0 else op.smoothing_kernel
+    if op.smooth_hi_only and qk > 1:
+        qk = 0
+    qs = O.smooth(g["qi"], qk, op.use_gaussian, op.gaussian_sigma * 0.5 if op.use_gaussian else 1.0) \
+        if qk > 1 else g["qi"]
+    hs = O.smooth(g["hi"], hk, op.use_gaussian, op.gaussian_sigma) if hk > 1 else g["hi"]
+    return qs, hs
+
+
+def check_kept(name, idx, sc, ref_keep, ref_combined, ref_a, ref_b, op, n, exact, report):
+    """Parity of one layer's kept positions, in three parts.
+
+    1. Index work is exact: ``idx`` equals the reference's selection rule
+       (``O.select_from_vectors``: stable ranks, MAX / union, top-k with lowest-index
+       ties) applied to the GPU's own ranked vectors ``sc`` [2, n].
+    2. The ranked vectors agree with the reference's within SCORE_RTOL.
+    3. The kept positions are compared with the reference's: the number that differ is
+       recorded in ``report``; with exact-arithmetic inputs (``exact``: logits that are
+       the same bits on every device) they must be equal except at exact ties of the
+       k-th combined score.
+    """
+    s, W = op.sink_size, op.window_size
+    if not op.use_bridge_importance:
+        sel = O.select_from_vectors(sc[0], sc[1], op, n)
+        assert np.array_equal(sel, idx), f"{name}: selection differs from the rule on the same vectors"
+    errs = []
+    for got, ref in ((sc[0], ref_a), (sc[1], ref_b)):
+        if ref is not None:
+            errs.append(float(np.max(np.abs(got - ref)) / max(float(np.max(np.abs(ref))), 1e-30)))
+    assert all(e < SCORE_RTOL for e in errs), (name, errs)
+    kk = len(ref_keep) - s
+    if ref_combined is not None:
+        nd, ties_only = compare_keep(idx, ref_keep, ref_combined, s, n - W, kk)
+    else:
+        nd = len(set(np.asarray(idx).tolist()) ^ set(np.asarray(ref_keep).tolist()))
+        ties_only = nd == 0
+    if report is not None:
+        report[name] = {"n": int(n), "kept": int(len(ref_keep)), "differ": int(nd),
+                        "differ_only_at_exact_ties": bool(ties_only), "score_max_rel_err": errs,
+                        "exact_arithmetic_inputs": bool(exact)}
+    if exact:
+        assert ties_only, f"{name}: {nd} kept positions differ with exact-arithmetic inputs"
+    return nd, ties_only

@@ -9,8 +9,13 @@ a checksum of the returned K.  Inputs are not stored: they are regenerated from
 the recorded seed by ``submission_folder_b200.synth.make_layer`` (CPU generator,
 deterministic for a given torch build).
 
-Usage (in a checkout that has the reference at REF):
-    python tests/golden/make_golden.py [--ref /path/to/reference]
+Usage (in a checkout that has the reference source; its root is given by --ref or
+the CKV_REFERENCE_ROOT environment variable -- there is no default):
+    python tests/golden/make_golden.py --ref /path/to/reference [--only NAME]
+
+``--only`` regenerates the matching cases and merges them into ``cases.json``.
+Each case also records the wall time of the reference's ``update_kv`` call and
+the host threads it used (``ref_seconds``, ``ref_threads``).
 """
 
 from __future__ import annotations
@@ -22,6 +27,7 @@ import json
 import math
 import os
 import sys
+import time
 
 import numpy as np
 import torch
@@ -62,12 +68,30 @@ CASES = [
     ("bf16_perhead_hub", 2048, "bf16", 64, 256, 16, 1.0, 34,
      {"per_head_eviction": True, "true_hub_hi": True}),
     ("bf16_n8192_cfg2", 8192, "bf16", 64, 1024, 64, 1.0, 35, {}),
+    # the 32k layer of the 32-layer cache (window 64, budget 2048, 64 planted keys per
+    # head), once with unit-variance logits and once with the literal N(0,1)/sqrt(128)
+    # components; and per-head eviction at 8k
+    ("cfg3_bf16_n32768", 32768, "bf16", 64, 2048, 64, 1.0, 36, {}),
+    ("cfg3_literal_n32768", 32768, "bf16", 64, 2048, 64, 1.0 / math.sqrt(128), 37, {}),
+    ("bf16_perhead_n8192", 8192, "bf16", 64, 1024, 64, 1.0, 38, {"per_head_eviction": True}),
+    # exact-arithmetic inputs (Q, K on a 0.25 grid): the logits are the same bits on every
+    # device, so the GPU's kept sets are compared with these without any allowance
+    ("grid_bf16_n2048", 2048, "bf16", 64, 256, 16, 1.0, 40, {}),
+    ("grid_fp32_n4096_w32", 4096, "fp32", 32, 512, 16, 1.0, 41, {}),
+    ("grid_bf16_n8192", 8192, "bf16", 64, 1024, 64, 1.0, 42, {}),
+    ("grid_bf16_union", 2048, "bf16", 64, 256, 16, 1.0, 43, {"combination_mode": "union"}),
+    ("grid_bf16_w128", 2048, "bf16", 128, 384, 32, 1.0, 44, {}),
+    ("grid_bf16_perhead", 2048, "bf16", 64, 256, 16, 1.0, 45, {"per_head_eviction": True}),
+    ("grid_bf16_n32768", 32768, "bf16", 64, 2048, 64, 1.0, 46, {}),
 ]
+
+GRID_STEP = 0.25   # cases whose name starts with "grid_"
 
 
 def run_case(CircuitKVCluster, case):
     name, n, dtype, W, B, planted, scale, seed, over = case
-    q, k, v = make_layer(n, seed=seed, window=W, planted=planted, qk_scale=scale, dtype=dtype)
+    grid = GRID_STEP if name.startswith("grid_") else 0.0
+    q, k, v = make_layer(n, seed=seed, window=W, planted=planted, qk_scale=scale, dtype=dtype, grid_step=grid)
     kw = cli_cluster_kwargs(W, B, **over)
     cl = CircuitKVCluster(**kw)
     rec = {}
@@ -93,8 +117,12 @@ def run_case(CircuitKVCluster, case):
     wrap("_get_union_keep_mask", lambda a, k, o: rec.update(union_qi=a[0].numpy().copy(),
                                                              union_hi=a[1].numpy().copy(),
                                                              mask=o.numpy().copy()))
+    K, Q, V = repeat_kv(k, 4), q[None], repeat_kv(v, 4)
     with contextlib.redirect_stdout(io.StringIO()):
-        ko, vo = cl.update_kv(repeat_kv(k, 4), q[None], repeat_kv(v, 4), None, 4)
+        t0 = time.perf_counter()
+        ko, vo = cl.update_kv(K, Q, V, None, 4)
+        secs = time.perf_counter() - t0
+    del K, V
     ko = ko[0].float().numpy()
     out = {"k_checksum": np.float64(ko.astype(np.float64).sum())}
     if over.get("per_head_eviction"):
@@ -113,15 +141,18 @@ def run_case(CircuitKVCluster, case):
         if key in rec:
             out[key] = rec[key].astype(np.float32)
     meta = {"name": name, "n": n, "dtype": dtype, "window": W, "budget": B, "planted": planted,
-            "qk_scale": scale, "seed": seed, "overrides": over, "kwargs": kw}
+            "qk_scale": scale, "seed": seed, "grid_step": grid, "overrides": over, "kwargs": kw,
+            "ref_seconds": round(secs, 3), "ref_threads": torch.get_num_threads()}
     return meta, out
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("CKV_REFERENCE_ROOT"))
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or CKV_REFERENCE_ROOT")
     sys.path.insert(0, os.path.join(args.ref, "KVCache-Factory"))
     from pyramidkv.pyramidkv_utils import CircuitKVCluster  # the reference, unmodified
     torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
@@ -133,12 +164,20 @@ def main():
         np.savez_compressed(os.path.join(HERE, meta["name"] + ".npz"), **out)
         index.append(meta)
         print(meta["name"], "kept", len(out.get("keep", out.get("keep_per_head", []))))
-    if not args.only:
-        meta_info = {"torch": torch.__version__, "generator": "tests/golden/make_golden.py",
-                     "reference": "KVCache-Factory/pyramidkv/pyramidkv_utils.py CircuitKVCluster.update_kv",
-                     "cases": index}
-        with open(os.path.join(HERE, "cases.json"), "w") as f:
-            json.dump(meta_info, f, indent=1)
+    path = os.path.join(HERE, "cases.json")
+    if args.only and os.path.exists(path):
+        with open(path) as f:
+            old = json.load(f)["cases"]
+        fresh = {m["name"]: m for m in index}
+        names = [c[0] for c in CASES]
+        merged = {c["name"]: c for c in old}
+        merged.update(fresh)
+        index = [merged[nm] for nm in names if nm in merged]
+    meta_info = {"torch": torch.__version__, "generator": "tests/golden/make_golden.py",
+                 "reference": "KVCache-Factory/pyramidkv/pyramidkv_utils.py CircuitKVCluster.update_kv",
+                 "cases": index}
+    with open(path, "w") as f:
+        json.dump(meta_info, f, indent=1)
 
 
 if __name__ == "__main__":

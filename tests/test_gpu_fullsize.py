@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import ckv_oracle as O
-from _golden import compare_keep
+from _golden import check_kept
 from submission_folder_b200 import ops
 from submission_folder_b200.cluster import CircuitKVCluster, cli_cluster_kwargs
 from submission_folder_b200.synth import make_layer
@@ -21,10 +21,14 @@ def _cuda():
     return torch.device("cuda", 0)
 
 
-@pytest.mark.parametrize("n,W,B,planted", [(32768, 64, 2048, 64), (131072, 128, 4096, 256)])
-def test_full_size_layer(n, W, B, planted):
+@pytest.mark.parametrize("n,W,B,planted,band", [(32768, 64, 2048, 64, 256), (131072, 128, 4096, 256, 1024)])
+def test_full_size_layer(n, W, B, planted, band, parity_report):
+    """The 32k layer of the 32-layer cache and the 131k Mistral-shaped layer (window
+    128, 256 planted keys, locality band 1024): determinism, gathered rows, and the kept
+    set against the structured oracle (the reference itself cannot hold the n x n
+    matrices at 131k)."""
     dev = _cuda()
-    q, k, v = make_layer(n, seed=7, window=W, planted=planted, dtype="bf16", device="cpu")
+    q, k, v = make_layer(n, seed=7, window=W, planted=planted, locality=band, dtype="bf16", device="cpu")
     cl = CircuitKVCluster(**cli_cluster_kwargs(W, B))
     p = cl.params(n)
     qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
@@ -44,22 +48,17 @@ def test_full_size_layer(n, W, B, planted):
             assert torch.equal(ko[g * 4 + r, : B - W], rows[g])
             assert torch.equal(ko[g * 4 + r, B - W:], kd[g, n - W:])
     assert torch.equal(vo[5, : B - W], vd[1, idx.long()])
-    # planted keys (aligned with the window queries) should mostly survive
-    # and the structured oracle agrees on the kept set up to near-ties
+    # the structured oracle: exact selection on our vectors, vectors within 1e-3
     op = O.Params(window_size=W, max_capacity_prompt=B)
-    if n <= 32768:
-        r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4, op, dtype="bf16")
-        nd, ok = compare_keep(ii, r.keep_idx, r.combined, 4, n - W, B - W - 4, margin=16.0 / (n - 1))
-        assert ok, nd
-        got = sc.cpu().numpy()
-        assert np.max(np.abs(got[0] - r.qi)) / np.abs(r.qi).max() < 1e-3
-        assert np.max(np.abs(got[1] - r.hi)) / np.abs(r.hi).max() < 1e-3
+    r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4, op, dtype="bf16")
+    check_kept(f"fullsize_n{n}_w{W}", ii, sc.cpu().numpy(), r.keep_idx, r.combined, r.qi, r.hi, op, n, False,
+               parity_report)
 
 
-def test_ragged_batch_of_sequences():
+def test_ragged_batch_of_sequences(parity_report):
     """A ragged batch of 16 sequences, n_i ~ U[2048, 32768] (seeded), window 32, budget
     int(0.1 n_i), bf16, as independent units in one batched call: bit-identical to one
-    call per sequence, valid kept sets, and the two shortest against the structured oracle."""
+    call per sequence, valid kept sets, and every sequence against the structured oracle."""
     from submission_folder_b200 import sharding
     dev = _cuda()
     rng = np.random.default_rng(2024)
@@ -90,10 +89,9 @@ def test_ragged_batch_of_sequences():
         assert len(ii) == B - W and np.all(np.diff(ii) > 0) and np.all(ii[:4] == np.arange(4)) and ii[-1] < n - W
         kd = layers[i][1]
         assert torch.equal(ko[0, : B - W], kd[0, idx.long()]) and torch.equal(ko[31, B - W:], kd[7, n - W:])
-    for i in sorted(range(16), key=lambda i: lengths[i])[:2]:
+    for i in range(16):
         n, (q, k, v) = lengths[i], cpu[i]
-        r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4,
-                        O.Params(window_size=W, max_capacity_prompt=int(0.1 * n)), dtype="bf16")
-        ii = batched[i][2].cpu().numpy()
-        nd, ok = compare_keep(ii, r.keep_idx, r.combined, 4, n - W, int(0.1 * n) - W - 4, margin=16.0 / (n - 1))
-        assert ok, (i, n, nd)
+        op = O.Params(window_size=W, max_capacity_prompt=int(0.1 * n))
+        r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4, op, dtype="bf16")
+        check_kept(f"ragged_seq{i}_n{n}", batched[i][2].cpu().numpy(), batched[i][3].cpu().numpy(), r.keep_idx,
+                   r.combined, r.qi, r.hi, op, n, False, parity_report)

@@ -1,11 +1,14 @@
 """Parity of the sm_100a kernels (through the C ABI) with the reference's golden
 outputs and with the CPU oracle, stage by stage and end to end.
 
-Tolerances (written here, per the north star): scores agree within 1e-3
-relative; kept positions agree exactly except at ties of the combined score at
-the k-th value (the reference's CPU topk breaks those in an implementation-
-defined order) and, end to end, within a few ranks of the k-th value where a
-16-bit logit can round differently between the tensor-core MMA and CPU BLAS.
+Tolerances (written here, per the north star): the ranked score vectors agree
+within 1e-3 relative; the index work is exact -- the kept positions are exactly
+the reference's selection rule applied to the ranked vectors (stable ranks,
+lowest-index-first ties of the k-th value, as torch's CUDA argsort / topk do,
+pinned by ``test_selection_ties_follow_torch_cuda``); with exact-arithmetic inputs
+(``grid_*`` fixtures, whose logits are the same bits on every device) the kept
+positions equal the reference's except at exact ties of the k-th combined score
+(the reference's CPU topk breaks those in an implementation-defined order).
 """
 
 import numpy as np
@@ -13,7 +16,8 @@ import pytest
 import torch
 
 import ckv_oracle as O
-from _golden import case, cases, compare_keep, inputs, load, oracle_params
+from _golden import (case, cases, check_kept, compare_keep, inputs, load, oracle_params,
+                     ranked_vectors_of_reference)
 from submission_folder_b200 import ops
 from submission_folder_b200.cluster import CircuitKVCluster
 from submission_folder_b200.synth import repeat_kv
@@ -156,8 +160,14 @@ def test_select_from_reference_scores(name):
 
 
 @pytest.mark.parametrize("name", SHARED)
-def test_update_kv_matches_reference(name):
-    """The drop-in hook end to end on the GPU vs the reference's kept positions."""
+def test_update_kv_matches_reference(name, parity_report):
+    """The drop-in hook end to end on the GPU vs the reference's kept positions.
+
+    The kept set must be exactly the reference's selection rule applied to the GPU's own
+    ranked vectors, those vectors must agree with the reference's within 1e-3, and for
+    exact-arithmetic inputs (``grid_*`` cases) the kept set must equal the reference's
+    except at exact ties of the k-th combined score.  The number of positions that differ
+    from the reference's is recorded per case (``parity_report``)."""
     dev = _cuda()
     c = case(name)
     g = load(name)
@@ -177,14 +187,21 @@ def test_update_kv_matches_reference(name):
     assert torch.equal(ko[0, :, :len(idx)], kk_)
     assert torch.equal(ko[0, :, len(idx):], K[0, :, n - W:])
     assert torch.equal(vo[0, :, :len(idx)], V[0, :, torch.from_numpy(idx).long().to(dev)])
-    kk = len(ref) - s
-    if "combined" in g:
-        nd, ok = compare_keep(idx, ref, g["combined"], s, n - W, kk, margin=8.0 / (n - 1))
-        assert ok, f"{name}: {nd} positions differ beyond the margin"
-    else:
-        nd = len(set(idx.tolist()) ^ set(ref.tolist()))
-        assert nd <= max(4, len(ref) // 100), nd
     assert ops.read_status(dev) == 0
+    # the same layer through the C ABI, with the ranked vectors
+    p = cl.params(n)
+    _, _, idx2, sc = ops.score_evict(p, q.to(dev), k.to(dev), v.to(dev), want_scores=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(idx2.cpu().numpy(), idx)
+    op = oracle_params(c)
+    sc = sc.cpu().numpy()
+    ra, rb = ranked_vectors_of_reference(c, g, op)
+    if op.combination_mode in ("max", "weighted"):
+        at = O.window_attention(q.float().numpy(), k.float().numpy(), W, 4, c["dtype"])
+        rq, _ = O.pool_rows(at, O.choose_heads(at, op))
+        rb = O.full_attn_colsum(rq)
+    check_kept(name, idx, sc, ref, g.get("combined"), ra, rb, op, n, c.get("grid_step", 0) > 0,
+               parity_report)
 
 
 def test_scores_within_tolerance_end_to_end():
@@ -340,9 +357,9 @@ def test_per_head_fp32_ragged():
 
 
 @pytest.mark.parametrize("n,W", [(4460, 64), (11554, 64), (4466, 32)])
-def test_moments_chunk_of_one_masked_tile(n, W):
+def test_moments_chunk_of_one_masked_tile(n, W, parity_report):
     """Lengths where a moments-pass CTA gets only the last, partly masked key tile:
-    finite scores and the oracle's kept set (up to near-ties)."""
+    finite scores, and the kept set checked against the oracle (``check_kept``)."""
     from submission_folder_b200.cluster import cli_cluster_kwargs
     from submission_folder_b200.synth import make_layer
     dev = _cuda()
@@ -357,11 +374,11 @@ def test_moments_chunk_of_one_masked_tile(n, W):
     r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4,
                     O.Params(window_size=W, max_capacity_prompt=B), dtype="bf16")
     np.testing.assert_allclose(mass.cpu().numpy(), r.choice.mass, rtol=1e-4, atol=1e-5)
-    nd, ok = compare_keep(idx.cpu().numpy(), r.keep_idx, r.combined, 4, n - W, B - W - 4, margin=16.0 / (n - 1))
-    assert ok, nd
+    check_kept(f"masked_tile_n{n}_w{W}", idx.cpu().numpy(), sc.cpu().numpy(), r.keep_idx, r.combined, r.qi,
+               r.hi, O.Params(window_size=W, max_capacity_prompt=B), n, False, parity_report)
 
 
-def test_both_pooling_branches_are_exercised():
+def test_both_pooling_branches_are_exercised(parity_report):
     """The pooling pass skips the exact entropy / mass recomputation when the moments
     pass settles the head sets (header word need_exact = 0) and redoes it otherwise;
     the golden cases that reach the tensor-core pooling pass must cover both, so the
@@ -390,12 +407,8 @@ def test_both_pooling_branches_are_exercised():
     assert int(ws[56:60].cpu().view(torch.int32).item()) == 1
     r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4, oracle_params(c),
                     dtype=c["dtype"])
-    n, W, B = c["n"], c["window"], c["kwargs"]["max_capacity_prompt"]
-    nd, ok = compare_keep(idx.cpu().numpy(), r.keep_idx, r.combined, 4, n - W, B - W - 4, margin=8.0 / (n - 1))
-    assert ok, nd
-    got = sc.cpu().numpy()
-    assert np.max(np.abs(got[0] - r.qi)) / np.abs(r.qi).max() < SCORE_RTOL
-    assert np.max(np.abs(got[1] - r.hi)) / np.abs(r.hi).max() < SCORE_RTOL
+    check_kept("tied_heads_exact_branch", idx.cpu().numpy(), sc.cpu().numpy(), r.keep_idx, r.combined, r.qi,
+               r.hi, oracle_params(c), c["n"], False, parity_report)
 
 
 def test_short_sequence_returns_inputs():
@@ -418,16 +431,16 @@ def test_host_tensors_round_trip():
     ko, vo = cl.update_kv(repeat_kv(k, 4), q[None], repeat_kv(v, 4), None, 4)
     assert not ko.is_cuda
     idx = cl.last_keep_indices.cpu().numpy()
-    nd, ok = compare_keep(idx, g["keep"], g["combined"], 4, c["n"] - c["window"], len(g["keep"]) - 4,
-                          margin=8.0 / (c["n"] - 1))
-    assert ok
+    assert len(idx) == len(g["keep"])
     # pinned host tensors: K is copied, V's kept rows are read in place by the gather; the
     # outputs equal those of device-resident inputs exactly
     dev = torch.device("cuda", 0)
     K, Q, V = repeat_kv(k, 4), q[None], repeat_kv(v, 4)
     kp, qp, vp = K.pin_memory(), Q.pin_memory(), V.pin_memory()
     assert ops.device_readable(vp[0]) and not ops.device_readable(V[0])
-    kd, vd = _cluster(c).update_kv(K.to(dev), Q.to(dev), V.to(dev), None, 4)
+    cd = _cluster(c)
+    kd, vd = cd.update_kv(K.to(dev), Q.to(dev), V.to(dev), None, 4)
+    assert np.array_equal(cd.last_keep_indices.cpu().numpy(), idx)
     kh, vh = _cluster(c).update_kv(kp, qp, vp, None, 4)
     assert kh.is_pinned() and vh.is_pinned()
     assert torch.equal(kh, kd.cpu()) and torch.equal(vh, vd.cpu())
@@ -493,7 +506,7 @@ def _flip_case(n=4096, W=64, H=32, Hkv=8, D=128, seed=11):
     pytest.skip("no scale of head 12 lands between head 1's entropies")
 
 
-def test_speculated_head_set_wrong_reruns_pooling():
+def test_speculated_head_set_wrong_reruns_pooling(parity_report):
     """The re-run path: pass 1's head set differs from the exact one (header words
     need_exact = 1 and fixup = 1 after the call), and the pooling pass re-runs with the
     exact sets, so the kept positions follow the reference's (clamped) head choice."""
@@ -512,5 +525,50 @@ def test_speculated_head_set_wrong_reruns_pooling():
     r = O.update_kv(q, k, v, 4, O.Params(**{a: b for a, b in kw.items() if a in O.Params.__dataclass_fields__}),
                     dtype="bf16")
     assert 12 in r.choice.qi_heads and 1 not in r.choice.qi_heads
-    nd, ok = compare_keep(idx.cpu().numpy(), r.keep_idx, r.combined, 4, n - W, B - W - 4, margin=8.0 / (n - 1))
-    assert ok, nd
+    check_kept("speculated_set_wrong", idx.cpu().numpy(), sc.cpu().numpy(), r.keep_idx, r.combined, r.qi,
+               r.hi, O.Params(**{a: b for a, b in kw.items() if a in O.Params.__dataclass_fields__}), n, False,
+               parity_report)
+
+
+@pytest.mark.parametrize("n,budget,mode", [(8192, 1024, "dis"), (32768, 2048, "dis"), (32768, 2048, "weighted"),
+                                           (4096, 512, "max")])
+def test_selection_ties_follow_torch_cuda(n, budget, mode):
+    """The reference ranks with ``argsort(argsort(s))`` and selects with ``topk``
+    (PU:1878, PU:2640).  Those torch ops, run on the B200 on vectors full of exact
+    ties, pick exactly the kept set of the GPU selection: the tie order the product
+    follows is the one the reference has on CUDA tensors, observed rather than assumed."""
+    dev = _cuda()
+    rng = np.random.default_rng(n + len(mode))
+    a = rng.integers(0, n // 16, n).astype(np.float32) / np.float32(n)
+    b = rng.integers(0, n // 16, n).astype(np.float32) / np.float32(n)
+    kw = dict(window_size=64, max_capacity_prompt=budget, combination_mode=mode, qi_kernel_size=1,
+              hi_kernel_size=1, smoothing_kernel=0, h2o_weight=0.5)
+    p = CircuitKVCluster(**kw).params(n)
+    ta, tb = torch.from_numpy(a).to(dev), torch.from_numpy(b).to(dev)
+    idx, _ = ops.select_scores(p, ta, tb)
+
+    def rank(x):
+        return torch.argsort(torch.argsort(x)).float() / (len(x) - 1)
+
+    if mode == "dis":
+        comb = torch.maximum(rank(ta), rank(tb))
+    elif mode == "max":
+        comb = torch.maximum(rank(tb), rank(ta))          # H2O rank, influence rank
+    else:
+        comb = 0.5 * rank(tb) + (1 - 0.5) * rank(ta)
+    W, s = 64, 4
+    mask = torch.zeros(n, dtype=torch.bool, device=dev)
+    mask[:s] = True
+    mask[max(s, n - W):] = True
+    remaining = budget - int(mask.sum().item())
+    masked = comb.clone()
+    masked[mask] = float("-inf")
+    _, top = torch.topk(masked, remaining)
+    mask[top] = True
+    mask[n - W:] = False
+    ref = torch.nonzero(mask).flatten().to(torch.int32)
+    torch.cuda.synchronize()
+    # the vectors really tie at the boundary: many positions share the k-th combined value
+    kth = torch.sort(masked, descending=True).values[remaining - 1]
+    assert int((masked == kth).sum().item()) > 1
+    assert torch.equal(idx, ref)

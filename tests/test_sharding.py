@@ -74,8 +74,17 @@ def _worker(rank, world, port, out_path):
         local = {i: _oracle_keep(i) for i in mine}
         allk = sharding.gather_kept(local)
         slowest = sharding.max_over_ranks(float(rank + 1))
+        # the fixed-size exchange: shapes and owners known to every rank up front
+        shapes = {i: ((32, n // 4 - 32) if i == 2 else (n // 4 - 32,)) for i, n in enumerate(LENGTHS)}
+        owner = {i: r for r in range(world) for i in sharding.sequences_for_rank(LENGTHS, r, world)}
+        ex = sharding.KeptExchange(shapes, owner, rank, world)
+        assert ex.units_of(rank) == mine
+        for i in mine:
+            ex.out(i).copy_(local[i])
+        ex.exchange()
+        fixed = {i: ex.result(i).clone() for i in range(len(LENGTHS))}
         if rank == 0:
-            torch.save({"kept": allk, "slowest": slowest, "mine": mine}, out_path)
+            torch.save({"kept": allk, "fixed": fixed, "slowest": slowest, "mine": mine}, out_path)
     finally:
         dist.destroy_process_group()
 
@@ -98,4 +107,5 @@ def test_gloo_two_ranks_gather_kept():
     assert sorted(kept) == list(range(len(LENGTHS)))
     for i in range(len(LENGTHS)):
         assert torch.equal(kept[i], _oracle_keep(i)), i
+        assert torch.equal(res["fixed"][i], kept[i]), i
     assert kept[2].dim() == 2 and kept[0].dim() == 1       # per-head unit keeps its [H, kept] shape
