@@ -112,6 +112,9 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   // tensor-core pooling: 4 query heads per KV group, W = 64, and at least two KV groups
   // (its per-tile handshake relies on a tile spanning two or more steps)
   pl.tc_pool = (pl.tc && pl.G == 4 && pl.W == 64 && pl.Hkv >= 2) ? 1 : 0;
+  // W = 32 / 128: the keys-on-lanes form alone (its exact branch is the SIMT pass)
+  pl.lanes_pool = (pl.tc && pl.G == 4 && (pl.W == 32 || pl.W == 128) && pl.Hkv >= 2) ? 1 : 0;
+  pl.pool_blocks = pl.W > 64 ? pl.W / 16 : 4;
   pl.hi_rows = (pl.nchains == 2 && p.entropy_aware) ? 1 : 0;
   pl.ncol_tiles = (n + kColTile - 1) / kColTile;
   pl.n_pad = pl.ncol_tiles * kColTile;
@@ -126,7 +129,7 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   if (pl.nscan < 1) pl.nscan = 1;
   pl.tc_nclusters = pl.ncol_tiles < 148 ? pl.ncol_tiles : 148;   // CTAs of the tensor-core pooling pass
   pl.e_parts = pl.tc_pool ? pl.tc_nclusters : pl.ncol_tiles;   // TC: one partial per CTA
-  pl.rs_parts = pl.tc_pool ? 2 * pl.ncol_tiles : pl.ncol_tiles;
+  pl.rs_parts = (pl.tc_pool || pl.lanes_pool) ? 2 * pl.ncol_tiles : pl.ncol_tiles;
   pl.g_slice = kColTile;
   if (window_smem_bytes(pl, true) > 227 * 1024 || window_smem_bytes(pl, false) > 227 * 1024) {
     *why = "window tile does not fit in shared memory"; return CKV_ERR_UNSUPPORTED;
@@ -147,7 +150,7 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.off_colsum = take((size_t)2 * pl.n_pad * 4);
   pl.off_gtile = take((size_t)2 * pl.ncol_tiles * 8 * 4);
   pl.off_rspart = take((size_t)2 * pl.ncol_tiles * 8 * pl.W * 4);
-  pl.off_colpart = take(pl.tc_pool ? (size_t)2 * 4 * pl.n_pad * 4 : 0);
+  pl.off_colpart = take((pl.tc_pool || pl.lanes_pool) ? (size_t)2 * pl.pool_blocks * pl.n_pad * 4 : 0);
   pl.off_wk = take((size_t)2 * pl.K * pl.W * 4);
   pl.off_yk = take((size_t)2 * (pl.K + 1) * pl.W * 4);
   pl.off_ymax = take((size_t)2 * (pl.K + 1) * 4);
@@ -490,6 +493,7 @@ int ckv_neumann_rows(const ckv_params* p, int32_t n, const float* rows_qi, const
   if (rc) return rc;
   // rows given by the caller: 64-column partial layout of the prep kernel
   pl.tc_pool = 0;
+  pl.lanes_pool = 0;
   pl.rs_parts = pl.ncol_tiles;
   pl.g_slice = kColTile;
   pl.e_parts = pl.ncol_tiles;

@@ -143,6 +143,23 @@ CKV_DEV float warp_sum16(float (&v)[16]) {
   }
   return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
+// The same transpose reduction for 8 values: lanes 4r .. 4r + 3 end with row r's total,
+// for row r = (lane >> 2) & 7.
+CKV_DEV float warp_sum8(float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16, m = 4; o >= 4; o >>= 1, m >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int k = 0; k < m; ++k) {
+      const float keep = up ? v[m + k] : v[k];
+      const float send = up ? v[k] : v[m + k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  const float t = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 2);
+  return t + __shfl_xor_sync(0xffffffffu, t, 1);
+}
 CKV_DEV float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -45,6 +45,9 @@ struct Plan {
   int nchains;        // 2 (QI, HI) or 1 (single-chain influence)
   int tc;             // 1: window moments on tcgen05 tensor cores (16-bit inputs, G*W a multiple of 128)
   int tc_pool;        // 1: pooling pass on tcgen05 with one cluster CTA per KV group
+  int lanes_pool;     // 1: W = 32 / 128: keys-on-lanes tcgen05 pooling when the head sets are
+                      //    settled; the exact recomputation runs on the SIMT / mma.sync pass
+  int pool_blocks;    // row blocks of the keys-on-lanes column-sum partials (W / 16, at least 4)
   int tc_nclusters;   // clusters of the tensor-core pooling pass
   int e_parts;        // exact entropy / mass partials per row
   int rs_parts;       // row-sum partials per chain (tensor-core pooling: one per 32 keys)
@@ -66,7 +69,7 @@ struct Plan {
   size_t off_stats, off_lse, off_lastlogit, off_spec, off_epart, off_mpart;
   size_t off_minx;    // [nstat_chunks][H][W] row minimum of the rounded logits (tensor-core moments)
   size_t off_rows_qi, off_rows_hi, off_colsum, off_gtile, off_rspart;
-  size_t off_colpart;  // [2][4][n_pad] column-sum partials of the keys-on-lanes pooling pass (4 row blocks)
+  size_t off_colpart;  // [2][pool_blocks][n_pad] column-sum partials of the keys-on-lanes pooling pass
   size_t off_wk, off_yk, off_ymax, off_bk, off_cg, off_agg, off_sin, off_cum, off_cmax;
   size_t off_sel, off_ph;
   // per-head eviction (PU:2208-2382, 3296-3464): only allocated in that mode

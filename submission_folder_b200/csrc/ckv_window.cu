@@ -599,7 +599,7 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh, int g
     hdr->n_hi = nhi;
     hdr->fixup = 0;
     hdr->cnt_stats = 0;
-    hdr->need_exact = (a.force_exact || !pl.tc_pool ||
+    hdr->need_exact = (a.force_exact || !(pl.tc_pool || pl.lanes_pool) ||
                        !selection_certain(a.p, pl.H, sSpec, sSpec + pl.H, sSpec + 2 * pl.H, qs)) ? 1 : 0;
   }
 }
@@ -617,6 +617,9 @@ __global__ void __launch_bounds__(256) k_window_pool(WinArgs a) {
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
   if (a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->fixup) == 0) return;
+  // with a keys-on-lanes pass beside it, this pass runs only when the head sets need the
+  // exact recomputation (or for the re-run)
+  if (pl.lanes_pool && !a.fixup_pass && *reinterpret_cast<volatile int32_t*>(&hdr->need_exact) == 0) return;
 
   const int tile = blockIdx.x;
   const int j0 = tile * kColTile;
@@ -2119,6 +2122,13 @@ static cudaError_t launch_tc_pool(const WinArgs& a0, cudaStream_t st) {
 // heads is in-thread, and its rows' pooled values accumulate over the KV groups in
 // registers until the tile's rows, column sums, row-sum partials and g totals are written
 // (the head-pair form's layout, per 64-key half).
+//
+// Other windows (template WIN): a step covers RS = min(W, 64) window rows of one KV group
+// (N = 4 RS).  W = 32: N = 128, a thread's quarter is 8 rows.  W = 128: the window is
+// walked in two halves of 64 rows; the steps of a tile run half by half (all KV groups
+// of rows 0..63, then of rows 64..127), each half accumulating and writing its own rows,
+// so a thread holds 16 rows' accumulators as for W = 64 (the K tile is loaded once per
+// half; the second load comes from L2).
 constexpr int kPTTN = 128;                 // keys per tile
 constexpr int kPTStages = 2;               // (queries, K tile) stages
 constexpr int kPTEpiWarps = 16;
@@ -2130,7 +2140,7 @@ struct PTSmem {
 
 static __host__ __device__ PTSmem pt_layout(const Plan& pl) {
   PTSmem L;
-  const size_t R = (size_t)pl.G * pl.W;
+  const size_t R = (size_t)pl.G * (pl.W < 64 ? pl.W : 64);   // query rows per step
   L.stage_bytes = R * 256 + (size_t)kPTTN * 256;
   size_t off = kPTStages * L.stage_bytes;
   L.off_lse = off; off += (size_t)pl.H * pl.W * 4;       // [group][row][head of the group]
@@ -2138,18 +2148,26 @@ static __host__ __device__ PTSmem pt_layout(const Plan& pl) {
   return L;
 }
 
-template <int DT>
+template <int DT, int WIN>
 __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUtensorMap& tmk, const WinArgs& a) {
+  static_assert(WIN == 32 || WIN == 64 || WIN == 128, "windows of 32, 64 or 128 rows");
+  constexpr int RS = WIN < 64 ? WIN : 64;           // window rows per step
+  constexpr int HALVES = WIN / RS;                  // 2 for W = 128
+  constexpr int RPQ = RS / 4;                       // rows of a thread's column quarter
+  constexpr int NCH = RPQ / 4;                      // 16-column TMEM loads per quarter
+  constexpr int NCOL = 4 * RS;                      // UMMA N: RS rows x 4 heads
   extern __shared__ char smem_raw[];
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
-  if (*reinterpret_cast<volatile int32_t*>(&hdr->need_exact) != 0) return;   // the head-pair form runs
+  if (*reinterpret_cast<volatile int32_t*>(&hdr->need_exact) != 0) return;   // the exact form runs
   int32_t* status = &hdr->status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int W = pl.W, G = pl.G, R = G * W;          // 64, 4, 256
+  constexpr int W = WIN;
+  const int G = pl.G, R = G * RS;                   // 4, 4 RS
   const int TN = kPTTN, S = kPTStages;
   const int ntn = (pl.n + TN - 1) / TN;
   const int ngroups = pl.Hkv;
+  const int nvg = HALVES * ngroups;                 // steps per tile (half-major)
   const PTSmem Ly = pt_layout(pl);
   char* base = align1024(smem_raw);
   char* stg = base;
@@ -2160,7 +2178,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
   __shared__ volatile int epi_abort;      // written by epilogue warps only, read after a barrier
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
-  const uint32_t ncols = 512;             // two accumulator buffers of N = 256
+  constexpr uint32_t ncols = 2 * NCOL;    // two accumulator buffers of N = NCOL
   if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { tc::mbar_init(&bar_ld[i], 1); tc::mbar_init(&bar_sfree[i], 1); }
@@ -2198,15 +2216,16 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
   if (warp == kPTEpiWarps) {
     // ---------------- producer: tiles, TMA loads and UMMA issue (one thread) ----------------
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, 256);
+      const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, NCOL);
       uint32_t* ctr = &hdr->tile_ctr[0];
       int load_tile = -1;
       int next_tile = (int)atomicAdd(ctr, 1u);   // fetched one tile ahead: the atomic's latency hides
-      int ld_g = 0;                              // KV group of the next step to load (steps load in order)
+      int ld_vg = 0;                             // (half, group) of the next step to load (in order)
       auto load_step = [&](int s) {
-        const int st = s % S, g = ld_g;
-        ld_g = ld_g + 1 == ngroups ? 0 : ld_g + 1;
-        if (g == 0) {
+        const int st = s % S, vg = ld_vg;
+        ld_vg = ld_vg + 1 == nvg ? 0 : ld_vg + 1;
+        const int hf = HALVES > 1 ? vg / ngroups : 0, g = HALVES > 1 ? vg - hf * ngroups : vg;
+        if (vg == 0) {
           load_tile = next_tile;
           if (load_tile < ntn) next_tile = (int)atomicAdd(ctr, 1u);
         }
@@ -2214,8 +2233,8 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         stage_tile[st] = load_tile;
         char* sb = stg + st * Ly.stage_bytes;
         tc::mbar_expect_tx(&bar_ld[st], (uint32_t)(R * 256 + TN * 256));
-        for (int p = 0; p < 2; ++p)   // rows (window row, head) of group g: heads 4g .. 4g + 3, tokens n - W ..
-          tc::tma_load_3d(sb + p * R * 128, &tmq, &bar_ld[st], p * 64, g * G, pl.n - W);
+        for (int p = 0; p < 2; ++p)   // rows (window row, head) of group g: heads 4g .. 4g + 3, tokens n - W + RS hf ..
+          tc::tma_load_3d(sb + p * R * 128, &tmq, &bar_ld[st], p * 64, g * G, pl.n - W + RS * hf);
         for (int p = 0; p < 2; ++p)   // the K tile: 128 keys of KV head g
           tc::tma_load_3d(sb + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, load_tile * TN, g);
       };
@@ -2223,7 +2242,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
       static_assert(kPTStages == 2, "one descriptor base per stage below");
       const uint64_t base0 = tc::sw128_kmajor_desc(tc::smem_addr(stg));
       const uint64_t base1 = tc::sw128_kmajor_desc(tc::smem_addr(stg + Ly.stage_bytes));
-      for (int s = 0, g = 0, k = 0;; ++s) {   // g: KV group of step s, k: this CTA's tile count
+      for (int s = 0, g = 0, k = 0;; ++s) {   // g: step of the tile (half-major), k: this CTA's tile count
         const int st = s % S, b = s & 1;
         if (abort_sh) break;
         if (s >= 2 && !tc::mbar_wait(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
@@ -2232,7 +2251,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
           tile_slot[k & 1] = tile;
           tc::mbar_arrive(&bar_tile);
         }
-        if (++g == ngroups) { g = 0; ++k; }
+        if (++g == nvg) { g = 0; ++k; }
         if (tile < 0) break;      // no tile left: the epilogue stops at this tile boundary
         if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
         tc::fence_after_sync();
@@ -2242,7 +2261,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
           const int p = ks >> 2, koff = (ks & 3) * 32;
           const uint64_t ad = sbase + (uint64_t)((R * 256 + p * TN * 128 + koff) >> 4);   // keys (M)
           const uint64_t bd = sbase + (uint64_t)((p * R * 128 + koff) >> 4);              // query rows (N)
-          tc::umma_f16(tmem + (uint32_t)(b * 256), ad, bd, idesc, ks > 0 ? 1u : 0u);
+          tc::umma_f16(tmem + (uint32_t)(b * NCOL), ad, bd, idesc, ks > 0 ? 1u : 0u);
         }
         tc::umma_commit(&bar_full[b]);
         tc::umma_commit(&bar_sfree[st]);
@@ -2258,11 +2277,22 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
     const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
     // (values used once per tile are re-read there, not held in registers across the steps)
     const float rs = 1.0f / sqrtf((float)pl.D);
-    float qacc[16], hacc[16];                           // rows 16 q + i of this thread's key
+    float qacc[RPQ], hacc[RPQ];                         // rows RS hf + RPQ q + i of this thread's key
     int tile = -1;
-    // s: step, g: its KV group, k: tiles this warp has started (no integer division per step)
-    for (int s = 0, g = 0, k = 0; s < ntn * ngroups; ++s, g = g + 1 == ngroups ? 0 : g + 1) {
-      if (g == 0) {
+    // s: step, vg: its (half, KV group), k: tiles this warp has started (no integer division
+    // per step); g: the KV group, hf: the half
+    int vg = 0, hf = 0;
+    // the next step: the group, then the half, then the tile
+    auto advance = [&](int& g) {
+      if constexpr (HALVES == 1) {
+        g = g + 1 == ngroups ? 0 : g + 1;
+      } else {
+        vg = vg + 1 == nvg ? 0 : vg + 1;
+        if (++g == ngroups) { g = 0; hf = hf + 1 == HALVES ? 0 : hf + 1; }
+      }
+    };
+    for (int s = 0, g = 0, k = 0; s < ntn * nvg; ++s, advance(g)) {
+      if (HALVES == 1 ? g == 0 : vg == 0) {   // a new tile
         // no barrier among the epilogue warps: the producer's wait for all of them to free
         // a TMEM buffer keeps them within a step of one another, so the tile slot and the
         // tile barrier's phase of the current tile are still the ones each warp reads
@@ -2275,8 +2305,16 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         tile = tile_slot[k & 1];
         ++k;
         if (tile < 0) break;
+        if constexpr (HALVES == 1) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) { qacc[i] = 0.f; hacc[i] = 0.f; }
+          for (int i = 0; i < RPQ; ++i) { qacc[i] = 0.f; hacc[i] = 0.f; }
+        }
+      }
+      if constexpr (HALVES > 1) {
+        if (g == 0) {   // the first group of a half: fresh accumulators
+#pragma unroll
+          for (int i = 0; i < RPQ; ++i) { qacc[i] = 0.f; hacc[i] = 0.f; }
+        }
       }
       const int j = tile * TN + key;
       bool ok = !epi_abort;
@@ -2291,7 +2329,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         const F2 qm01 = f2(q4.x, q4.y), qm23 = f2(q4.z, q4.w);
         const F2 hm01 = f2(h4.x, h4.y), hm23 = f2(h4.z, h4.w);
         const F2 l2e = f2(kLog2e, kLog2e);
-        const uint32_t col0 = (uint32_t)((s & 1) * 256 + 64 * q);
+        const uint32_t col0 = (uint32_t)((s & 1) * NCOL + 4 * RPQ * q);
         // the causal mask only touches the tile that reaches the window (warp-uniform)
         const bool edge = tile * TN + TN - 1 > pl.n - W;
         // QANY: some head of the group is in the QI set (else its max-pooling is skipped)
@@ -2300,19 +2338,19 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
           constexpr bool EDGE = decltype(etag)::value;
           constexpr bool QANY = decltype(qtag)::value;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {   // 16 columns: window rows 16 q + 4 c + i, heads 0..3
+          for (int c = 0; c < NCH; ++c) {   // 16 columns: window rows RS hf + RPQ q + 4 c + i, heads 0..3
             uint32_t r16[16];
             __syncwarp();
             tc::tmem_ld16_nowait(lane_base + col0 + 16 * c, r16);
             tc::tmem_wait_ld();
-            if (c == 3) {   // the last load of the step: the accumulator buffer is free
+            if (c == NCH - 1) {   // the last load of the step: the accumulator buffer is free
               tc::fence_before_sync();
               __syncwarp();
               if (lane == 0) tc::mbar_arrive(&bar_tfree[s & 1]);
             }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const int r = 16 * q + 4 * c + i;
+              const int r = RS * hf + RPQ * q + 4 * c + i;
               const float4 nL = snlse4[g * W + r];   // -log2-sum-exp of (row, head 0..3)
               const F2 x01 = round_f2<DT>(__uint_as_float(r16[4 * i]), __uint_as_float(r16[4 * i + 1]), rs);
               const F2 x23 = round_f2<DT>(__uint_as_float(r16[4 * i + 2]), __uint_as_float(r16[4 * i + 3]), rs);
@@ -2348,12 +2386,12 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         }
       }
       if (g == ngroups - 1) {
-        // ---- the tile is complete: rows, then partial sums that the reduction kernel
-        // completes (no barrier: each warp writes its own partials)
+        // ---- the tile (or its half) is complete: rows, then partial sums that the
+        // reduction kernel completes (no barrier: each warp writes its own partials)
         float* rows_qi = reinterpret_cast<float*>(a.ws + pl.off_rows_qi);
         float* rows_hi = reinterpret_cast<float*>(a.ws + pl.off_rows_hi);
         float* rspart = reinterpret_cast<float*>(a.ws + pl.off_rspart);     // [2][rs_parts][W]
-        float* colpart = reinterpret_cast<float*>(a.ws + pl.off_colpart);   // [2][4][n_pad]
+        float* colpart = reinterpret_cast<float*>(a.ws + pl.off_colpart);   // [2][pool_blocks][n_pad]
         const int t32 = tile * 4 + lg;                  // 32-key row-sum partial of this lane group
         const bool hi_rows = pl.hi_rows != 0, hmax = s_hi_kind == kHiMax;
         const int nch = hi_rows ? 2 : 1;
@@ -2365,10 +2403,10 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         // registers take each set's row-sum terms (both sets start again at zero next tile)
 #pragma unroll 1
         for (int c2 = 0; c2 < nch; ++c2) {
-          float* rp = (c2 == 0 ? rows_qi : rows_hi) + (size_t)(16 * q) * pl.n_pad + j;
+          float* rp = (c2 == 0 ? rows_qi : rows_hi) + (size_t)(RS * hf + RPQ * q) * pl.n_pad + j;
           float cs = 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < RPQ; ++i) {
             float v = c2 == 0 ? qacc[i] : hacc[i];
             if (c2 == 1 && !hmax) v = v * inv_nhi;
             if (j >= pl.n) v = 0.f;
@@ -2376,12 +2414,19 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
             cs += v;
             qacc[i] = tempered ? pow_pos(v, invT) : v;
           }
-          // row sums over this lane group's 32 keys: row 16 q + ((lane >> 1) & 15) in lane pairs
-          const float t = warp_sum16(qacc);
-          if ((lane & 1) == 0 && t32 < pl.rs_parts)
-            rspart[((size_t)c2 * pl.rs_parts + t32) * W + 16 * q + ((lane >> 1) & 15)] = t;
-          // column sum of this key over the row block's 16 rows
-          if (j < pl.n_pad) colpart[((size_t)c2 * 4 + q) * pl.n_pad + j] = cs;
+          // row sums over this lane group's 32 keys: with 16 rows, row 16 q + ((lane >> 1) & 15)
+          // in lane pairs; with 8, row 8 q + ((lane >> 2) & 7) in lane quads
+          if constexpr (RPQ == 16) {
+            const float t = warp_sum16(qacc);
+            if ((lane & 1) == 0 && t32 < pl.rs_parts)
+              rspart[((size_t)c2 * pl.rs_parts + t32) * W + RS * hf + 16 * q + ((lane >> 1) & 15)] = t;
+          } else {
+            const float t = warp_sum8(qacc);
+            if ((lane & 3) == 0 && t32 < pl.rs_parts)
+              rspart[((size_t)c2 * pl.rs_parts + t32) * W + 8 * q + ((lane >> 2) & 7)] = t;
+          }
+          // column sum of this key over the row block's RPQ rows
+          if (j < pl.n_pad) colpart[((size_t)c2 * (4 * HALVES) + 4 * hf + q) * pl.n_pad + j] = cs;
         }
       }
     }
@@ -2405,7 +2450,7 @@ __global__ void __launch_bounds__(kPTThreads, 1)
                   const __grid_constant__ CUtensorMap tmq4, const __grid_constant__ CUtensorMap tmk4,
                   const __grid_constant__ WinArgs a) {
   const Header* hdr = reinterpret_cast<const Header*>(a.ws);
-  if (*reinterpret_cast<const volatile int32_t*>(&hdr->need_exact) == 0) tc_pool_t_body<DT>(tmq4, tmk4, a);
+  if (*reinterpret_cast<const volatile int32_t*>(&hdr->need_exact) == 0) tc_pool_t_body<DT, 64>(tmq4, tmk4, a);
   else tc_pool_body<DT>(tmq2, tmk2, a);
 }
 
@@ -2425,6 +2470,38 @@ static cudaError_t launch_tc_pool_any(const WinArgs& a0, cudaStream_t st) {
   // grid: one CTA per exact-branch partial (tc_nclusters >= the keys-on-lanes tile count
   // up to 148; surplus CTAs of that branch find no tile and return)
   k_tc_pool_any<DT><<<pl.tc_nclusters, kPTThreads, smem, st>>>(tq2, tk2, tq4, tk4, a);
+  return cudaGetLastError();
+}
+
+// W = 32 / 128: the keys-on-lanes form as its own launch (returns at once when the head
+// sets need the exact recomputation, which the SIMT pass launched after it does).
+template <int DT, int WIN>
+__global__ void __launch_bounds__(kPTThreads, 1)
+    k_tc_pool_lanes(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                    const __grid_constant__ WinArgs a) {
+  tc_pool_t_body<DT, WIN>(tmq, tmk, a);
+}
+
+template <int DT>
+static cudaError_t launch_tc_pool_lanes(const WinArgs& a, cudaStream_t st) {
+  const Plan& pl = a.pl;
+  const int rs = pl.W < 64 ? pl.W : 64;
+  CUtensorMap tq, tk;
+  if (!make_tmap_pairs(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, rs, pl.G) ||
+      !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kPTTN))
+    return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
+  const size_t smem = pt_layout(pl).total;
+  const int ntn = (pl.n + kPTTN - 1) / kPTTN;
+  const int grid = ntn < 148 ? ntn : 148;   // persistent CTAs take 128-key tiles from a counter
+  if (pl.W == 32) {
+    const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool_lanes<DT, 32>, smem);
+    if (e != cudaSuccess) return e;
+    k_tc_pool_lanes<DT, 32><<<grid, kPTThreads, smem, st>>>(tq, tk, a);
+  } else {
+    const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_pool_lanes<DT, 128>, smem);
+    if (e != cudaSuccess) return e;
+    k_tc_pool_lanes<DT, 128><<<grid, kPTThreads, smem, st>>>(tq, tk, a);
+  }
   return cudaGetLastError();
 }
 
@@ -2478,7 +2555,10 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
     } else if (row < nrows) {
       const int ch = (row - 2 * HW) / pl.W, rr = (row - 2 * HW) % pl.W;
       const int src = (ch == 1 && pl.hi_rows) ? 1 : 0;
-      e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, pl.rs_parts, (size_t)pl.W, q, kReduceStreams);
+      // the SIMT pass (the exact branch beside a keys-on-lanes pass) writes one partial
+      // per 64-key tile, the keys-on-lanes forms one per 32 keys
+      const int nrs = (pl.lanes_pool && exact) ? pl.ncol_tiles : pl.rs_parts;
+      e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, nrs, (size_t)pl.W, q, kReduceStreams);
     }
     sp[q][lane] = e;
     __syncthreads();
@@ -2489,10 +2569,10 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
     }
     __syncthreads();   // sp is reused by the next block
   }
-  if (pl.tc_pool && !exact) {
-    // column sums and g totals behind the keys-on-lanes pooling pass: four row-block
-    // partials per key, one 64-key slice per warp (added in the order that pass used)
-    const float* colpart = reinterpret_cast<const float*>(a.ws + pl.off_colpart);   // [2][4][n_pad]
+  if ((pl.tc_pool || pl.lanes_pool) && !exact) {
+    // column sums and g totals behind the keys-on-lanes pooling pass: pool_blocks row-block
+    // partials per key (4, or 8 for W = 128), one 64-key slice per warp, added in a fixed order
+    const float* colpart = reinterpret_cast<const float*>(a.ws + pl.off_colpart);   // [2][pool_blocks][n_pad]
     float* colsum = reinterpret_cast<float*>(a.ws + pl.off_colsum);
     float* gtile = reinterpret_cast<float*>(a.ws + pl.off_gtile);
     const bool tempered = a.p.neumann_temperature != 1.0f && a.p.neumann_temperature > 0.f;
@@ -2505,8 +2585,12 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int jj = t * 64 + 32 * h + lane;   // < n_pad
-        const float* cp = colpart + (size_t)c2 * 4 * pl.n_pad + jj;
-        const float c = (__ldcg(cp) + __ldcg(cp + pl.n_pad)) + (__ldcg(cp + 2 * (size_t)pl.n_pad) + __ldcg(cp + 3 * (size_t)pl.n_pad));
+        const float* cp = colpart + (size_t)c2 * pl.pool_blocks * pl.n_pad + jj;
+        float c = (__ldcg(cp) + __ldcg(cp + pl.n_pad)) + (__ldcg(cp + 2 * (size_t)pl.n_pad) + __ldcg(cp + 3 * (size_t)pl.n_pad));
+        if (pl.pool_blocks == 8) {
+          const float* cq = cp + 4 * (size_t)pl.n_pad;
+          c += (__ldcg(cq) + __ldcg(cq + pl.n_pad)) + (__ldcg(cq + 2 * (size_t)pl.n_pad) + __ldcg(cq + 3 * (size_t)pl.n_pad));
+        }
         colsum[(size_t)c2 * pl.n_pad + jj] = c;
         float gg = 0.f;
         if (jj < pl.n_p) {
@@ -2578,6 +2662,11 @@ static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st)
         const cudaError_t e = stage == 1 ? launch_tc_pool_any<DT>(b, st) : launch_tc_pool<DT>(b, st);
         if (e != cudaSuccess) return e;
         launched = true;
+      } else if (pl.lanes_pool && stage == 1) {
+        // keys-on-lanes pooling (settled head sets); the SIMT pass below returns at once
+        // then, and runs the exact branch otherwise
+        const cudaError_t e = launch_tc_pool_lanes<DT>(b, st);
+        if (e != cudaSuccess) return e;
       }
     }
     if (!launched) k_window_pool<DT><<<pl.ncol_tiles, 256, pool_smem<DT>(pl), st>>>(b);

@@ -89,10 +89,11 @@ def check_kept(name, idx, sc, ref_keep, ref_combined, ref_a, ref_b, op, n, exact
        (``O.select_from_vectors``: stable ranks, MAX / union, top-k with lowest-index
        ties) applied to the GPU's own ranked vectors ``sc`` [2, n].
     2. The ranked vectors agree with the reference's within SCORE_RTOL.
-    3. The kept positions are compared with the reference's: the number that differ is
-       recorded in ``report``; with exact-arithmetic inputs (``exact``: logits that are
-       the same bits on every device) they must be equal except at exact ties of the
-       k-th combined score.
+    3. The kept positions equal the reference's except at exact ties of the k-th combined
+       score (the reference's CPU topk orders those in an implementation-defined way; for
+       union modes, which record no combined score, they must be equal).  ``exact`` marks
+       inputs whose logits are the same bits on every device (``grid_*`` fixtures); the
+       figures go to ``report`` either way.
     """
     s, W = op.sink_size, op.window_size
     if not op.use_bridge_importance:
@@ -113,6 +114,5 @@ def check_kept(name, idx, sc, ref_keep, ref_combined, ref_a, ref_b, op, n, exact
         report[name] = {"n": int(n), "kept": int(len(ref_keep)), "differ": int(nd),
                         "differ_only_at_exact_ties": bool(ties_only), "score_max_rel_err": errs,
                         "exact_arithmetic_inputs": bool(exact)}
-    if exact:
-        assert ties_only, f"{name}: {nd} kept positions differ with exact-arithmetic inputs"
+    assert ties_only, f"{name}: {nd} kept positions differ beyond exact ties of the k-th combined score"
     return nd, ties_only

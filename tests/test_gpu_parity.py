@@ -5,10 +5,10 @@ Tolerances (written here, per the north star): the ranked score vectors agree
 within 1e-3 relative; the index work is exact -- the kept positions are exactly
 the reference's selection rule applied to the ranked vectors (stable ranks,
 lowest-index-first ties of the k-th value, as torch's CUDA argsort / topk do,
-pinned by ``test_selection_ties_follow_torch_cuda``); with exact-arithmetic inputs
-(``grid_*`` fixtures, whose logits are the same bits on every device) the kept
-positions equal the reference's except at exact ties of the k-th combined score
-(the reference's CPU topk breaks those in an implementation-defined order).
+pinned by ``test_selection_ties_follow_torch_cuda``); and the kept positions equal
+the reference's except at exact ties of the k-th combined score (the reference's
+CPU topk breaks those in an implementation-defined order).  The ``grid_*`` fixtures
+use exact-arithmetic inputs, whose logits are the same bits on every device.
 """
 
 import numpy as np
@@ -164,10 +164,10 @@ def test_update_kv_matches_reference(name, parity_report):
     """The drop-in hook end to end on the GPU vs the reference's kept positions.
 
     The kept set must be exactly the reference's selection rule applied to the GPU's own
-    ranked vectors, those vectors must agree with the reference's within 1e-3, and for
-    exact-arithmetic inputs (``grid_*`` cases) the kept set must equal the reference's
-    except at exact ties of the k-th combined score.  The number of positions that differ
-    from the reference's is recorded per case (``parity_report``)."""
+    ranked vectors, those vectors must agree with the reference's within 1e-3, and the kept
+    set must equal the reference's except at exact ties of the k-th combined score.  The
+    number of positions that differ (all at such ties) is recorded per case
+    (``parity_report``)."""
     dev = _cuda()
     c = case(name)
     g = load(name)
@@ -572,3 +572,25 @@ def test_selection_ties_follow_torch_cuda(n, budget, mode):
     kth = torch.sort(masked, descending=True).values[remaining - 1]
     assert int((masked == kth).sum().item()) > 1
     assert torch.equal(idx, ref)
+
+
+@pytest.mark.parametrize("n,W,B,dtype", [(8192, 32, 819, "bf16"), (6000, 128, 1024, "bf16"), (4096, 32, 512, "fp16"),
+                                         (20000, 128, 2048, "fp16")])
+def test_keys_on_lanes_pooling_other_windows(n, W, B, dtype, parity_report):
+    """Windows of 32 and 128 rows: when the moments pass settles the head sets (header
+    word need_exact = 0) the pooling pass runs the tcgen05 keys-on-lanes form (W = 128 in
+    two 64-row halves); the kept set is checked against the oracle (``check_kept``)."""
+    from submission_folder_b200.cluster import cli_cluster_kwargs
+    from submission_folder_b200.synth import make_layer
+    dev = _cuda()
+    q, k, v = make_layer(n, seed=n + W, window=W, planted=32, dtype=dtype, device="cpu")
+    p = CircuitKVCluster(**cli_cluster_kwargs(W, B)).params(n)
+    ko, vo, idx, sc = ops.score_evict(p, q.to(dev), k.to(dev), v.to(dev), want_scores=True)
+    torch.cuda.synchronize()
+    ws = ops._workspaces[(dev.type, dev.index)]
+    assert int(ws[56:60].cpu().view(torch.int32).item()) == 0   # Header.need_exact: the lanes form ran
+    assert ops.read_status(dev) == 0
+    op = O.Params(window_size=W, max_capacity_prompt=B)
+    r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4, op, dtype=dtype)
+    check_kept(f"lanes_w{W}_n{n}_{dtype}", idx.cpu().numpy(), sc.cpu().numpy(), r.keep_idx, r.combined, r.qi, r.hi,
+               op, n, False, parity_report)
