@@ -160,6 +160,11 @@ CKV_DEV float warp_sum8(float (&v)[8]) {
   const float t = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 2);
   return t + __shfl_xor_sync(0xffffffffu, t, 1);
 }
+CKV_DEV float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
 CKV_DEV float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -116,6 +116,12 @@ CKV_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// Register budget of the calling warpgroup (all four of its warps execute it): the
+// producer warpgroup of a warp-specialised kernel gives registers back to the pool that
+// the block was launched with, the epilogue warpgroups take them.
+template <uint32_t N> CKV_DEV void reg_dealloc() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N)); }
+template <uint32_t N> CKV_DEV void reg_alloc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N)); }
+
 CKV_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // 8 consecutive fp32 columns of this thread's TMEM lane into r[0..7] (no wait).
 CKV_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t* r) {

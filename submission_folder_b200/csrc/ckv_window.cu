@@ -311,6 +311,108 @@ __device__ bool selection_certain(const ckv_params& p, int H, const float* ent, 
   return true;
 }
 
+// The same head sets (and their certainty) computed by ONE warp for H <= 32: lane h holds
+// head h's entropy, mass and clamp bound in registers, ranks come from 32 shuffles, sets from
+// ballots and the certainty margins from warp max / min reductions.  It runs once per layer
+// at the end of a pass, as cold code on one SM, so it keeps to one short loop and no
+// shared-memory round trips (the block-wide form above spent ~10 us there).  Same
+// decisions as select_heads / selection_certain; the CDF mode keeps their sequential
+// fp32 running sum (lane 0, in mass order).
+struct HeadSets {
+  uint64_t qs, hs;
+  int hm, nhi, certain;
+};
+
+__device__ HeadSets select_heads_warp(const ckv_params& p, int H, float ent, float mass, float bnd) {
+  const int lane = threadIdx.x & 31;
+  const bool valid = lane < H;
+  const uint32_t all32 = H >= 32 ? 0xffffffffu : ((1u << H) - 1u);
+  HeadSets r;
+  r.certain = 1;
+  if (!p.entropy_aware) {
+    r.qs = all32; r.hs = all32; r.hm = 2; r.nhi = H;
+    return r;
+  }
+  const int k = min(p.top_k_heads, H);
+  const bool by_mass = p.head_selection_mode == 1;
+  int rank_q = 0, rank_m = 0;
+  for (int o = 0; o < H; ++o) {
+    const float eo = __shfl_sync(0xffffffffu, ent, o), mo = __shfl_sync(0xffffffffu, mass, o);
+    rank_q += (by_mass ? (mo > mass || (mo == mass && o < lane)) : (eo < ent || (eo == ent && o < lane))) ? 1 : 0;
+    rank_m += (mo > mass || (mo == mass && o < lane)) ? 1 : 0;   // descending mass
+  }
+  const uint32_t qs = __ballot_sync(0xffffffffu, valid && rank_q < k);
+  uint32_t hs = all32;
+  int mode = 0;
+  __shared__ float s_sorted[32];
+  if (p.hi_pooling_mode == 1) {
+    mode = 1;
+  } else if (p.hi_mass_cdf > 0.f || p.hi_top_k_heads > 0) {
+    if (valid) s_sorted[rank_m] = mass;
+    __syncwarp();
+    if (p.hi_mass_cdf > 0.f) {
+      int need = H;
+      // the running sum in mass order, sequential as the block-wide form (lane 0)
+      float total = 0.f;
+      for (int o = 0; o < H; ++o) total += __shfl_sync(0xffffffffu, mass, o);
+      int below = 0;
+      if (total > 0.f) {
+        if (lane == 0) {
+          float cum = 0.f;
+          for (int i = 0; i < H; ++i) { cum += s_sorted[i]; if (cum / total < p.hi_mass_cdf) ++below; }
+        }
+        below = __shfl_sync(0xffffffffu, below, 0);
+        need = min(below + 1, H);
+        hs = __ballot_sync(0xffffffffu, valid && rank_m < need);
+      }
+    } else {
+      hs = __ballot_sync(0xffffffffu, valid && rank_m < min(p.hi_top_k_heads, H));
+    }
+  } else if (p.hi_mass_threshold > 0.f) {
+    hs = __ballot_sync(0xffffffffu, valid && mass >= p.hi_mass_threshold);
+    if (hs == 0) hs = all32;
+  }
+  r.qs = qs; r.hs = hs; r.hm = mode; r.nhi = __popc(hs);
+  // certainty of the decisions (selection_certain)
+  bool ok = true;
+  const bool in_q = (qs >> lane) & 1u;
+  if (k < H) {
+    if (by_mass) {
+      const float lo_in = warp_min(valid && in_q ? mass : INFINITY);
+      const float hi_out = warp_max(valid && !in_q ? mass : -INFINITY);
+      ok = lo_in - hi_out > certainty_slack(lo_in, hi_out);
+    } else {
+      const float hi_in = warp_max(valid && in_q ? ent + bnd : -INFINITY);
+      const float lo_out = warp_min(valid && !in_q ? ent : INFINITY);
+      ok = lo_out - hi_in > certainty_slack(hi_in, lo_out);
+    }
+  }
+  if (ok && p.hi_pooling_mode != 1) {
+    if (p.hi_mass_cdf > 0.f || p.hi_top_k_heads > 0) {
+      // masses in descending order with clear gaps, and clear CDF crossings
+      float total = 0.f;
+      for (int o = 0; o < H; ++o) total += __shfl_sync(0xffffffffu, mass, o);
+      int bad = 0;
+      if (lane == 0) {
+        float prev = INFINITY, cum = 0.f;
+        for (int i = 0; i < H && !bad; ++i) {
+          const float m = s_sorted[i];
+          if (i > 0 && !(prev - m > certainty_slack(prev, m))) bad = 1;
+          prev = m;
+          cum += m;
+          if (p.hi_mass_cdf > 0.f && total > 0.f && !(fabsf(cum / total - p.hi_mass_cdf) > 1e-5f)) bad = 1;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, bad, 0) == 0;
+    } else if (p.hi_mass_threshold > 0.f) {
+      ok = __ballot_sync(0xffffffffu, valid && !(fabsf(mass - p.hi_mass_threshold) >
+                                                 certainty_slack(mass, p.hi_mass_threshold))) == 0;
+    }
+  }
+  r.certain = ok ? 1 : 0;
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // common per-CTA setup of the window kernels
 // ---------------------------------------------------------------------------
@@ -585,6 +687,26 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh, int g
   __syncthreads();
   if (!last) return;
   __threadfence();
+  if (pl.H <= 32) {   // one warp, registers and shuffles
+    if (threadIdx.x < 32) {
+      const int h = threadIdx.x;
+      const bool v = h < pl.H;
+      const float e = v ? __ldcg(spec + h) : INFINITY;
+      const float m = v ? __ldcg(spec + pl.H + h) : -INFINITY;
+      const float b = v ? __ldcg(spec + 4 * pl.H + h) : 0.f;
+      const HeadSets r = select_heads_warp(a.p, pl.H, e, m, b);
+      if (h == 0) {
+        hdr->qi_heads = r.qs;
+        hdr->hi_heads = r.hs;
+        hdr->hi_mode = r.hm;
+        hdr->n_hi = r.nhi;
+        hdr->fixup = 0;
+        hdr->cnt_stats = 0;
+        hdr->need_exact = (a.force_exact || !(pl.tc_pool || pl.lanes_pool) || !r.certain) ? 1 : 0;
+      }
+    }
+    return;
+  }
   float* sSpec = rowE;                                           // [2H] + [H] bounds
   for (int h = threadIdx.x; h < 2 * pl.H; h += blockDim.x) sSpec[h] = __ldcg(spec + h);
   for (int h = threadIdx.x; h < pl.H; h += blockDim.x) sSpec[2 * pl.H + h] = __ldcg(spec + 4 * pl.H + h);
@@ -1181,9 +1303,18 @@ __device__ __forceinline__ void window_pool_finish(const WinArgs& a, char* smem_
   }
   __syncthreads();
   __shared__ int redo;
-  uint64_t qs, hs;
-  int hm, nh;
-  select_heads(a.p, pl.H, sHead, sHead + pl.H, &qs, &hs, &hm, &nh);
+  uint64_t qs = 0, hs = 0;
+  int hm = 0, nh = 0;
+  if (pl.H <= 32) {   // one warp, registers and shuffles
+    if (threadIdx.x < 32) {
+      const int h = threadIdx.x;
+      const bool v = h < pl.H;
+      const HeadSets r = select_heads_warp(a.p, pl.H, v ? sHead[h] : INFINITY, v ? sHead[pl.H + h] : -INFINITY, 0.f);
+      qs = r.qs; hs = r.hs; hm = r.hm; nh = r.nhi;
+    }
+  } else {
+    select_heads(a.p, pl.H, sHead, sHead + pl.H, &qs, &hs, &hm, &nh);
+  }
   if (threadIdx.x == 0) {
     redo = (qs != hdr->qi_heads || hs != hdr->hi_heads || hm != hdr->hi_mode) ? 1 : 0;
     if (redo && !a.fixup_pass) {
@@ -1667,7 +1798,15 @@ constexpr int kHiNone = 3;      // no HI rows of its own (the HI chain reuses th
 constexpr int kP2TN = 64;                 // keys per tile
 constexpr int kP2Stages = 2;              // (queries, K tile) stages
 constexpr int kP2EpiWarps = 16;           // epilogue warps
-constexpr int kP2Threads = 32 * (kP2EpiWarps + 1);
+// Five warpgroups: four of epilogue warps and one whose first warp is the producer (the
+// other three only give their registers back).  Launched at 96 registers a thread (the
+// most 640 threads can have), the producer warpgroup keeps 64 and the epilogue warps get
+// 104: 4 x 128 x 104 + 128 x 64 = 640 x 96 (at 96 the epilogue spilled; the producer
+// spills below 64).
+constexpr int kP2Threads = 32 * (kP2EpiWarps + 4);
+constexpr uint32_t kPoolEpiRegs = 104, kPoolProdRegs = 64, kPoolLaunchRegs = 96;
+static_assert(4 * 128 * kPoolEpiRegs + 128 * kPoolProdRegs <= kP2Threads * kPoolLaunchRegs,
+              "register split above the launch budget");
 constexpr int kP2Pitch = kP2TN + 1;       // staging row pitch (conflict-free column writes)
 
 struct P2Smem {
@@ -1745,9 +1884,14 @@ __device__ __forceinline__ void tc_pool_body(const CUtensorMap& tmq, const CUten
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
 
-  if (warp == kP2EpiWarps) {
+  if (warp >= kP2EpiWarps) {
+    tc::reg_dealloc<kPoolProdRegs>();
+  } else {
+    tc::reg_alloc<kPoolEpiRegs>();
+  }
+  if (warp >= kP2EpiWarps) {
     // ---------------- producer: tiles, TMA loads and UMMA issue (one thread) ----------------
-    if (lane == 0) {
+    if (warp == kP2EpiWarps && lane == 0) {
       const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, TN);
       uint32_t* ctr = &hdr->tile_ctr[a.fixup_pass ? 1 : 0];
       int load_tile = -1;
@@ -2132,7 +2276,7 @@ static cudaError_t launch_tc_pool(const WinArgs& a0, cudaStream_t st) {
 constexpr int kPTTN = 128;                 // keys per tile
 constexpr int kPTStages = 2;               // (queries, K tile) stages
 constexpr int kPTEpiWarps = 16;
-constexpr int kPTThreads = 32 * (kPTEpiWarps + 1);
+constexpr int kPTThreads = 32 * (kPTEpiWarps + 4);   // as the head-pair form: five warpgroups
 
 struct PTSmem {
   size_t stage_bytes, off_lse, total;
@@ -2213,9 +2357,14 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base_sh;
 
-  if (warp == kPTEpiWarps) {
+  if (warp >= kPTEpiWarps) {
+    tc::reg_dealloc<kPoolProdRegs>();
+  } else {
+    tc::reg_alloc<kPoolEpiRegs>();
+  }
+  if (warp >= kPTEpiWarps) {
     // ---------------- producer: tiles, TMA loads and UMMA issue (one thread) ----------------
-    if (lane == 0) {
+    if (warp == kPTEpiWarps && lane == 0) {
       const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, NCOL);
       uint32_t* ctr = &hdr->tile_ctr[0];
       int load_tile = -1;
