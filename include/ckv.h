@@ -213,6 +213,36 @@ int ckv_window_pool(const ckv_params* p, const ckv_layer* layer, void* workspace
                     uint64_t* out_qi_heads, uint64_t* out_hi_heads, float* rows_qi, float* rows_hi,
                     ckv_stream_t stream);
 
+/* ---- head-sharded (tensor-parallel) scoring -------------------------------------
+ * No counterpart in the reference, which scores all heads of a layer in one process
+ * (the entropy ranking and the QI / HI pooling run across heads, PU:2905-2999).  With the
+ * KV heads split over ranks, each rank:
+ *   1. computes its heads' exact entropy / transient mass (ckv_window_pool);
+ *   2. all-gathers them and derives the layer's head sets with ckv_choose_heads (the same
+ *      sets on every rank);
+ *   3. pools its heads with those sets (ckv_pool_rows_given): QI rows = max over its QI
+ *      heads, HI rows = SUM over its HI heads;
+ *   4. all-reduces the rows (max for QI, sum for HI) and scales HI by 1 / (HI head count);
+ *   5. scores and selects from the combined rows (ckv_neumann_rows, ckv_select_scores;
+ *      combination modes dis / union) and gathers its heads' K / V (ckv_gather).
+ * The host side is submission_folder_b200.tp.  Layers with at most 32 query heads. */
+
+/* Head sets of a layer from its per-head exact entropy / mass (device arrays [num_heads]):
+ * out_sets[0] = QI heads, out_sets[1] = HI heads (bit h), out_mode[0] = HI mode (0 mean,
+ * 1 max, 2 the HI chain reuses the QI rows), out_mode[1] = number of HI heads (device
+ * memory; PU:2905-2999 with the tie rules of the single-process path). */
+int ckv_choose_heads(const ckv_params* p, int32_t num_heads, const float* entropy, const float* mass,
+                     uint64_t* out_sets, int32_t* out_mode, ckv_stream_t stream);
+
+/* This rank's pooled window rows [W, n] fp32 for given head sets (device arrays from
+ * ckv_choose_heads): layer holds the rank's heads, which are heads head_offset ..
+ * head_offset + num_heads - 1 of the layer.  rows_qi = max over the rank's QI heads (0
+ * where it has none), rows_hi = sum over its HI heads (untouched when the HI chain reuses
+ * the QI rows).  Workspace as ckv_workspace_size for the local layer. */
+int ckv_pool_rows_given(const ckv_params* p, const ckv_layer* layer, int32_t head_offset, const uint64_t* sets,
+                        const int32_t* mode, void* workspace, size_t workspace_bytes, float* rows_qi,
+                        float* rows_hi, ckv_stream_t stream);
+
 /* ---- influence walker (legacy use_neumann=False path) ------------------------
  * Replaces CircuitGraph.update_and_step_influence_walker + get_influence_scores /
  * get_influence_raw_visits (CircuitKV/csrc/pybind.cpp:263-300; circuit_manager.cpp:

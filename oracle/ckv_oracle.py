@@ -207,9 +207,14 @@ class HeadChoice:
 
 def choose_heads(attn: np.ndarray, p: Params) -> HeadChoice:
     """Head sets of PU:2905-2999 (entropy-aware) or all heads (PU:2996-2999)."""
-    H = attn.shape[0]
-    ent = head_entropy(attn)
-    mass = head_transient_mass(attn, p.sink_size)
+    return choose_heads_from(head_entropy(attn), head_transient_mass(attn, p.sink_size), p)
+
+
+def choose_heads_from(ent: np.ndarray, mass: np.ndarray, p: Params) -> HeadChoice:
+    """The same head sets from per-head entropy / transient mass ``[H]``."""
+    H = len(ent)
+    ent = np.asarray(ent, dtype=F32)
+    mass = np.asarray(mass, dtype=F32)
     if not p.entropy_aware:
         return HeadChoice(np.arange(H), None, "max", ent, mass)
     k = min(p.top_k_heads, H)

@@ -605,6 +605,51 @@ static WalkArgs walk_args(int32_t n, int32_t current_idx, int32_t num_walkers, i
   return a;
 }
 
+int ckv_choose_heads(const ckv_params* p, int32_t num_heads, const float* entropy, const float* mass,
+                     uint64_t* out_sets, int32_t* out_mode, ckv_stream_t stream) {
+  if (!p || !entropy || !mass || !out_sets || !out_mode) return fail(CKV_ERR_ARG, "null argument");
+  if (num_heads < 1 || num_heads > 32) return fail(CKV_ERR_UNSUPPORTED, "ckv_choose_heads: 1 to 32 heads");
+  const cudaError_t e = launch_choose_heads(*p, num_heads, entropy, mass, out_sets, out_mode, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "choose heads");
+}
+
+int ckv_pool_rows_given(const ckv_params* p, const ckv_layer* layer, int32_t head_offset, const uint64_t* sets,
+                        const int32_t* mode, void* workspace, size_t workspace_bytes, float* rows_qi,
+                        float* rows_hi, ckv_stream_t stream) {
+  if (!p || !sets || !mode || !rows_qi) return fail(CKV_ERR_ARG, "null argument");
+  int rc = check_layer(layer);
+  if (rc) return rc;
+  if (head_offset < 0 || head_offset + layer->num_heads > 64)
+    return fail(CKV_ERR_ARG, "head_offset + num_heads must be at most 64");
+  if (p->per_head_eviction) return fail(CKV_ERR_UNSUPPORTED, "head-sharded pooling is for shared eviction");
+  ckv_params q = *p;
+  if (q.max_capacity_prompt > layer->n) q.max_capacity_prompt = layer->n;
+  Plan pl;
+  const char* why = "";
+  rc = make_plan(q, layer->n, layer->num_heads, layer->num_kv_heads, layer->head_dim, layer->dtype, &pl, &why);
+  if (rc) return fail(rc, why);
+  rc = check_ws(pl, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(Header), st);
+  WinArgs wa;
+  wa.q = layer->q; wa.qhs = layer->q_head_stride; wa.qts = layer->q_tok_stride;
+  wa.k = layer->k; wa.khs = layer->k_head_stride; wa.kts = layer->k_tok_stride;
+  wa.ws = ws; wa.fixup_pass = 0; wa.p = q; wa.pl = pl;
+  wa.tc_min = 0; wa.force_exact = 0;
+  if (e == cudaSuccess) e = launch_window_stage(wa, 0, st);   // row moments (log-sum-exp) of the local heads
+  if (e == cudaSuccess) e = launch_set_heads(ws, head_offset, pl.H, sets, mode, st);
+  if (e == cudaSuccess) e = launch_window_stage(wa, 1, st);   // pooling with the given sets
+  if (e != cudaSuccess) return cuda_fail(e, "head-sharded pooling");
+  e = cudaMemcpy2DAsync(rows_qi, (size_t)pl.n * 4, ws + pl.off_rows_qi, (size_t)pl.n_pad * 4, (size_t)pl.n * 4,
+                        pl.W, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && rows_hi && pl.hi_rows)
+    e = cudaMemcpy2DAsync(rows_hi, (size_t)pl.n * 4, ws + pl.off_rows_hi, (size_t)pl.n_pad * 4,
+                          (size_t)pl.n * 4, pl.W, cudaMemcpyDeviceToDevice, st);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "head-sharded pooling output");
+}
+
 int ckv_influence_walk_dense(const float* attn, int32_t n, int32_t current_idx, int32_t num_walkers,
                              int32_t max_steps, int32_t sink_size, float temperature, float explore_temp,
                              float explore_ratio, int32_t rng_mode, uint64_t seed, uint64_t* rng_state,

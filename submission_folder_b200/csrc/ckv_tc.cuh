@@ -122,6 +122,15 @@ CKV_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
 template <uint32_t N> CKV_DEV void reg_dealloc() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N)); }
 template <uint32_t N> CKV_DEV void reg_alloc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N)); }
 
+// Wait for this thread's TMEM loads with the 16 destination registers of the one being
+// waited for tied to the wait (their uses cannot move above it).
+CKV_DEV void tmem_wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
 CKV_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // 8 consecutive fp32 columns of this thread's TMEM lane into r[0..7] (no wait).
 CKV_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t* r) {

@@ -2486,12 +2486,19 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
           constexpr int HM = decltype(htag)::value;
           constexpr bool EDGE = decltype(etag)::value;
           constexpr bool QANY = decltype(qtag)::value;
+          // TMEM loads one 16-column chunk ahead: chunk c + 1 is in flight while chunk c is
+          // turned into probabilities
+          uint32_t rbuf[2][16];
+          __syncwarp();
+          tc::tmem_ld16_nowait(lane_base + col0, rbuf[0]);
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {   // 16 columns: window rows RS hf + RPQ q + 4 c + i, heads 0..3
-            uint32_t r16[16];
-            __syncwarp();
-            tc::tmem_ld16_nowait(lane_base + col0 + 16 * c, r16);
-            tc::tmem_wait_ld();
+            uint32_t (&r16)[16] = rbuf[c & 1];
+            tc::tmem_wait_ld16(r16);
+            if (c + 1 < NCH) {
+              __syncwarp();
+              tc::tmem_ld16_nowait(lane_base + col0 + 16 * (c + 1), rbuf[(c + 1) & 1]);
+            }
             if (c == NCH - 1) {   // the last load of the step: the accumulator buffer is free
               tc::fence_before_sync();
               __syncwarp();
@@ -2835,6 +2842,46 @@ cudaError_t launch_window_stage(const WinArgs& a, int stage, cudaStream_t st) {
     case CKV_FP16: return launch_window_t<CKV_FP16>(a, stage, st);
     default: return launch_window_t<CKV_FP32>(a, stage, st);
   }
+}
+
+// ---------------------------------------------------------------------------
+// head-sharded scoring: head sets from all ranks' statistics, pooling with given sets
+// ---------------------------------------------------------------------------
+// One warp: the head sets of the whole layer from its per-head entropy / mass (every
+// rank computes the same sets from the same all-gathered values).
+__global__ void __launch_bounds__(32) k_choose_heads(ckv_params p, int H, const float* ent, const float* mass,
+                                                     uint64_t* sets, int32_t* mode) {
+  const int h = threadIdx.x;
+  const bool v = h < H;
+  const HeadSets r = select_heads_warp(p, H, v ? ent[h] : INFINITY, v ? mass[h] : -INFINITY, 0.f);
+  if (h == 0) { sets[0] = r.qs; sets[1] = r.hs; mode[0] = r.hm; mode[1] = r.nhi; }
+}
+
+cudaError_t launch_choose_heads(const ckv_params& p, int H, const float* ent, const float* mass, uint64_t* sets,
+                                int32_t* mode, cudaStream_t st) {
+  k_choose_heads<<<1, 32, 0, st>>>(p, H, ent, mass, sets, mode);
+  return cudaGetLastError();
+}
+
+// After the moments pass: this rank's share of the given sets (heads head_off ..
+// head_off + H_local - 1 of the layer) replaces the workspace's own, the pooling pass
+// takes the settled branch, and HI pools as a SUM (n_hi = 1): the ranks' partial rows
+// are combined by a max (QI) and a sum (HI) before the mean.
+__global__ void k_set_heads(char* ws, int head_off, int h_local, const uint64_t* sets, const int32_t* mode) {
+  Header* hdr = reinterpret_cast<Header*>(ws);
+  const uint64_t mask = h_local >= 64 ? ~0ull : ((1ull << h_local) - 1ull);
+  hdr->qi_heads = (sets[0] >> head_off) & mask;
+  hdr->hi_heads = (sets[1] >> head_off) & mask;
+  hdr->hi_mode = mode[0];
+  hdr->n_hi = 1;
+  hdr->need_exact = 0;
+  hdr->fixup = 0;
+}
+
+cudaError_t launch_set_heads(char* ws, int head_off, int h_local, const uint64_t* sets, const int32_t* mode,
+                             cudaStream_t st) {
+  k_set_heads<<<1, 1, 0, st>>>(ws, head_off, h_local, sets, mode);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_window(const WinArgs& a, cudaStream_t st) {

@@ -31,6 +31,13 @@ cudaError_t launch_window_stage(const WinArgs& a, int stage, cudaStream_t st);
 void stage_mark(cudaStream_t st);
 // Per-head eviction pass: query rows, two-hop terms, column sums, query-row entropy.
 cudaError_t launch_ph_pass(const WinArgs& a, cudaStream_t st);
+// Head-sharded scoring: head sets of the whole layer from all heads' entropy / mass
+// (sets[0] QI, sets[1] HI; mode[0] HI mode, mode[1] HI head count), and the given sets
+// written into a workspace header after its moments pass (HI pooled as a sum).
+cudaError_t launch_choose_heads(const ckv_params& p, int H, const float* ent, const float* mass, uint64_t* sets,
+                                int32_t* mode, cudaStream_t st);
+cudaError_t launch_set_heads(char* ws, int head_off, int h_local, const uint64_t* sets, const int32_t* mode,
+                             cudaStream_t st);
 // Column sums / row sums / window chain of pooled rows already in the workspace.
 cudaError_t launch_rows_prep(const Plan& pl, const ckv_params& prm, char* ws, cudaStream_t st);
 

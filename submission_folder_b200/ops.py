@@ -244,6 +244,36 @@ def window_pool(p: Params, q: torch.Tensor, k: torch.Tensor):
     return ent, mass, sets, rq, rh
 
 
+def choose_heads(p: Params, entropy: torch.Tensor, mass: torch.Tensor):
+    """Head sets of a layer from all its heads' entropy / mass: (sets int64 [2] = QI, HI
+    bit masks; mode int32 [2] = HI mode, HI head count), on the device."""
+    _require_cuda(entropy, mass)
+    dev = entropy.device
+    e, m = entropy.float().contiguous(), mass.float().contiguous()
+    sets = torch.zeros(2, dtype=torch.int64, device=dev)
+    mode = torch.zeros(2, dtype=torch.int32, device=dev)
+    check(_lib.load().ckv_choose_heads(ctypes.byref(p), e.numel(), e.data_ptr(), m.data_ptr(), sets.data_ptr(),
+                                       mode.data_ptr(), _stream(dev)), "ckv_choose_heads")
+    return sets, mode
+
+
+def pool_rows_given(p: Params, q: torch.Tensor, k: torch.Tensor, head_offset: int, sets: torch.Tensor,
+                    mode: torch.Tensor):
+    """This rank's pooled rows for given head sets: (rows_qi [W, n] = max over its QI heads,
+    rows_hi [W, n] = sum over its HI heads).  ``q`` / ``k``: the rank's heads."""
+    _require_cuda(q, k, sets, mode)
+    H, n, D = q.shape
+    dev = q.device
+    L = make_layer(q, k, k)
+    rq = torch.empty(p.window_size, n, dtype=torch.float32, device=dev)
+    rh = torch.zeros(p.window_size, n, dtype=torch.float32, device=dev)
+    ws = workspace(workspace_size(p, max(n, p.max_capacity_prompt), H, k.shape[0], D), dev)
+    check(_lib.load().ckv_pool_rows_given(ctypes.byref(p), ctypes.byref(L), int(head_offset), sets.data_ptr(),
+                                          mode.data_ptr(), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+                                          rq.data_ptr(), rh.data_ptr(), _stream(dev)), "ckv_pool_rows_given")
+    return rq, rh
+
+
 # ---------------------------------------------------------------------------
 # influence walker (legacy use_neumann=False path) and stand-alone gather
 # ---------------------------------------------------------------------------
