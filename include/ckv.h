@@ -122,12 +122,18 @@ typedef struct ckv_layer {
  * dtype.  out_idx: the kept prefix positions in ascending order (sinks
  * included, local window excluded) -- [out_len - W] for shared eviction,
  * [H, out_len - W] for per-head eviction.  out_scores (optional, may be NULL):
- * fp32 [n] combined score of every position (shared eviction only). */
+ * fp32 [n] combined score of every position (shared eviction only).
+ * distinct_kv_heads: 0 (zero-initialised callers) writes the reference's layout, every
+ * query head its KV head's rows (repeat_kv, llama_model.py:2918-2928); 1 writes each
+ * DISTINCT KV head once, out_k / out_v [num_kv_heads, out_len, D] -- a quarter of the
+ * writes and of the decode cache for 4 query heads per KV head, for a GQA-aware decode
+ * attention (no reference counterpart; shared eviction only). */
 typedef struct ckv_outputs {
   void* out_k;
   void* out_v;
   int32_t* out_idx;
   float* out_scores;
+  int32_t distinct_kv_heads;
 } ckv_outputs;
 
 /* Fill *p with the CLI defaults of the reference (see above). */

@@ -84,6 +84,7 @@ class Outputs(ctypes.Structure):
     _fields_ = [
         ("out_k", ctypes.c_void_p), ("out_v", ctypes.c_void_p),
         ("out_idx", ctypes.c_void_p), ("out_scores", ctypes.c_void_p),
+        ("distinct_kv_heads", ctypes.c_int32),
     ]
 
 

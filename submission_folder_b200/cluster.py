@@ -92,6 +92,7 @@ class CircuitKVCluster:
         hi_log_head_stats: bool = False,
         use_bridge_importance: bool = False,
         bi_kernel_size: int = 5,
+        distinct_kv_heads: bool = False,
     ):
         self.window_size = window_size
         self.max_capacity_prompt = max_capacity_prompt
@@ -153,6 +154,9 @@ class CircuitKVCluster:
         self.hi_log_head_stats = hi_log_head_stats
         self.use_bridge_importance = use_bridge_importance
         self.bi_kernel_size = bi_kernel_size
+        # not a reference kwarg: return each KV head once ([1, Hkv, B, D], no repeat_kv
+        # copies) for a decode cache that keeps the distinct heads (cache.DistinctKVCache)
+        self.distinct_kv_heads = distinct_kv_heads
         # state of the last call (for callers that want the kept positions)
         self.last_keep_indices: Optional[torch.Tensor] = None
         self._graph = None
@@ -251,7 +255,7 @@ class CircuitKVCluster:
         if not self.use_neumann and self.combination_mode not in ("dis", "union", "union_da"):
             k_out, v_out, idx = self._walker_path(p, q, k, v, q_len)
         else:
-            k_out, v_out, idx, _ = ops.score_evict(p, q, k, v)
+            k_out, v_out, idx, _ = ops.score_evict(p, q, k, v, distinct_kv_heads=self.distinct_kv_heads)
         self.last_keep_indices = idx
         k_out, v_out = k_out.unsqueeze(0), v_out.unsqueeze(0)
         if host:
@@ -266,6 +270,8 @@ class CircuitKVCluster:
         return k_out, v_out
 
     def _walker_path(self, p, q, k, v, q_len):
+        if self.distinct_kv_heads:
+            raise NotImplementedError("distinct_kv_heads with use_neumann=False")
         """use_neumann=False (PU:3244-3263): pooled window rows, the influence walker on
         the structured full_attn (its PCG states kept across calls like the reference's
         CircuitGraph, seeded once with 42 + 3000), H2O = full_attn column sums, rank MAX,

@@ -211,6 +211,7 @@ static int launch_gather_layer(const Plan& pl, const ckv_layer* L, const ckv_out
   g.out_k = out->out_k; g.out_v = out->out_v; g.idx = idx;
   g.n = pl.n; g.W = identity ? 0 : pl.W; g.H = pl.H; g.Hkv = pl.Hkv; g.G = pl.G; g.D = pl.D;
   g.out_len = pl.out_len; g.per_head = pl.per_head; g.identity = identity;
+  g.distinct = out->distinct_kv_heads ? 1 : 0;
   const cudaError_t e = launch_gather(g, pl.dtype, st);
   return e == cudaSuccess ? CKV_OK : cuda_fail(e, "gather launch");
 }
@@ -218,6 +219,8 @@ static int launch_gather_layer(const Plan& pl, const ckv_layer* L, const ckv_out
 static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* workspace,
                            size_t ws_bytes, const ckv_outputs* out, cudaStream_t st, bool marks = true) {
   if (!p || !out || !out->out_k || !out->out_v) return fail(CKV_ERR_ARG, "null params or outputs");
+  if (out->distinct_kv_heads && p->per_head_eviction)
+    return fail(CKV_ERR_UNSUPPORTED, "distinct_kv_heads outputs are for shared eviction");
   int rc = check_layer(L);
   if (rc) return rc;
   Plan pl;
@@ -396,6 +399,8 @@ int ckv_score_evict_batched(const ckv_params* params, int32_t params_count, cons
     if (rc) return rc;
     if (!outs[i].out_k || !outs[i].out_v || (layers[i].n >= par(i)->max_capacity_prompt && !outs[i].out_idx))
       return fail(CKV_ERR_ARG, "null output pointer");
+    if (outs[i].distinct_kv_heads && par(i)->per_head_eviction)
+      return fail(CKV_ERR_UNSUPPORTED, "distinct_kv_heads outputs are for shared eviction");
     offs[i + 1] = offs[i] + align256(need);
     if (offs[i + 1] > workspace_bytes) return fail(CKV_ERR_WORKSPACE, "batched workspace too small");
   }
@@ -720,7 +725,7 @@ int ckv_gather(const ckv_layer* layer, int32_t window, const int32_t* idx, int32
   GatherArgs g;
   g.k = layer->k; g.khs = layer->k_head_stride; g.kts = layer->k_tok_stride;
   g.v = layer->v; g.vhs = layer->v_head_stride; g.vts = layer->v_tok_stride;
-  g.out_k = out_k; g.out_v = out_v; g.idx = idx;
+  g.out_k = out_k; g.out_v = out_v; g.distinct = 0; g.idx = idx;
   g.n = layer->n; g.W = window; g.H = layer->num_heads; g.Hkv = layer->num_kv_heads;
   g.G = layer->num_heads / layer->num_kv_heads; g.D = layer->head_dim;
   g.out_len = kept + window; g.per_head = per_head ? 1 : 0; g.identity = 0;

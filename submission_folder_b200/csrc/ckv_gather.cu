@@ -36,8 +36,12 @@ __global__ void __launch_bounds__(256) k_gather(const GatherArgs a) {
     int tok = a.identity ? t : ((t < nk) ? __ldg(a.idx + t) : (a.n - a.W + (t - nk)));
     if (tok < 0 || tok >= a.n) tok = 0;            // never expected: keeps the read in bounds
     const uint4 x = __ldg(reinterpret_cast<const uint4*>(src + g * hs + (int64_t)tok * ts) + v);
-    for (int r = 0; r < a.G; ++r)
-      reinterpret_cast<uint4*>(dst + ((size_t)(g * a.G + r) * a.out_len + t) * a.D)[v] = x;
+    if (a.distinct) {   // each KV head once
+      reinterpret_cast<uint4*>(dst + ((size_t)g * a.out_len + t) * a.D)[v] = x;
+    } else {
+      for (int r = 0; r < a.G; ++r)
+        reinterpret_cast<uint4*>(dst + ((size_t)(g * a.G + r) * a.out_len + t) * a.D)[v] = x;
+    }
   }
 }
 

@@ -17,6 +17,7 @@ struct GatherArgs {
   int n, W, H, Hkv, G, D, out_len;
   int per_head;
   int identity;         // 1: keep every token (n < budget)
+  int distinct;         // 1: write each KV head once ([Hkv, out_len, D]) instead of per query head
 };
 
 cudaError_t launch_gather(const GatherArgs& a, int dtype, cudaStream_t st);

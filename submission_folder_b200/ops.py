@@ -105,13 +105,15 @@ def _index_tensor(p: Params, heads: int, out_len: int, dev: torch.device) -> tor
 
 
 def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                want_scores: bool = False) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor,
-                                                     Optional[torch.Tensor]]:
+                want_scores: bool = False, distinct_kv_heads: bool = False) -> Tuple[torch.Tensor, torch.Tensor,
+                                                                                    torch.Tensor,
+                                                                                    Optional[torch.Tensor]]:
     """One layer: returns ``(k_out [H,B,D], v_out [H,B,D], keep_idx, scores)``; ``keep_idx``
     is ``[B-W]`` int32 (shared eviction) or ``[H, B-W]`` (per-head eviction).
 
     ``scores`` (when requested) is ``[2, n]`` fp32: the two vectors ranked by the
     selection (QI / HI after smoothing for "dis"; influence / H2O for "max").
+    ``distinct_kv_heads``: K / V outputs hold each KV head once, ``[Hkv, B, D]``.
     """
     _require_cuda(q, k)
     _require_readable(v)
@@ -119,13 +121,15 @@ def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     L = make_layer(q, k, v)
     out_len = output_len(p, n)
     dev = q.device
-    k_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
-    v_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
+    ho = k.shape[0] if distinct_kv_heads else H
+    k_out = torch.empty(ho, out_len, D, dtype=q.dtype, device=dev)
+    v_out = torch.empty(ho, out_len, D, dtype=q.dtype, device=dev)
     idx = _index_tensor(p, H, out_len, dev)
     scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
     ws = workspace(workspace_size(p, n, H, k.shape[0], D), dev)
     O = Outputs()
     O.out_k, O.out_v, O.out_idx, O.out_scores = k_out.data_ptr(), v_out.data_ptr(), idx.data_ptr(), _ptr(scores)
+    O.distinct_kv_heads = 1 if distinct_kv_heads else 0
     check(_lib.load().ckv_score_evict(ctypes.byref(p), ctypes.byref(L), ctypes.c_void_p(ws.data_ptr()),
                                       ws.numel(), ctypes.byref(O), _stream(dev)), "ckv_score_evict")
     if n < p.max_capacity_prompt:
