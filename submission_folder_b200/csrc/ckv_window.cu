@@ -2486,19 +2486,12 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
           constexpr int HM = decltype(htag)::value;
           constexpr bool EDGE = decltype(etag)::value;
           constexpr bool QANY = decltype(qtag)::value;
-          // TMEM loads one 16-column chunk ahead: chunk c + 1 is in flight while chunk c is
-          // turned into probabilities
-          uint32_t rbuf[2][16];
-          __syncwarp();
-          tc::tmem_ld16_nowait(lane_base + col0, rbuf[0]);
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {   // 16 columns: window rows RS hf + RPQ q + 4 c + i, heads 0..3
-            uint32_t (&r16)[16] = rbuf[c & 1];
-            tc::tmem_wait_ld16(r16);
-            if (c + 1 < NCH) {
-              __syncwarp();
-              tc::tmem_ld16_nowait(lane_base + col0 + 16 * (c + 1), rbuf[(c + 1) & 1]);
-            }
+            uint32_t r16[16];
+            __syncwarp();
+            tc::tmem_ld16_nowait(lane_base + col0 + 16 * c, r16);
+            tc::tmem_wait_ld();
             if (c == NCH - 1) {   // the last load of the step: the accumulator buffer is free
               tc::fence_before_sync();
               __syncwarp();

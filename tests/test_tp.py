@@ -148,3 +148,25 @@ def test_head_sharded_kernels_match_single_call(world, parity_report):
     d = set(idx.cpu().numpy().tolist()) ^ set(idx1.cpu().numpy().tolist())
     parity_report[f"head_sharded_{world}_ranks"] = {"n": n, "kept": int(idx.numel()), "differ_from_single_call": len(d)}
     assert not d, sorted(d)[:10]
+
+
+@pytest.mark.gpu
+def test_head_sharded_over_nccl_on_two_gpus(tmp_path):
+    """With two or more GPUs: two ranks (one per GPU, NCCL) score a layer's heads in halves;
+    both hold the kept positions of the single-process path, and rank 0's heads' K / V are
+    the single-process rows."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    out = tmp_path / "tp.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(here, "_tp_nccl_worker.py"), str(out)]
+    subprocess.run(["timeout", "-k", "30", "300"] + cmd, check=True, env=env)
+    import json
+    res = json.loads(out.read_text())
+    assert res["same_on_all_ranks"] and res["differ_from_single_call"] == 0, res
+    assert res["score_max_rel_err"] < 1e-5 and res["kv_match"], res
