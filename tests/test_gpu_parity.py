@@ -305,9 +305,10 @@ def _per_head_run(c, kwargs, dev):
     return q, k, idx
 
 
-@pytest.mark.parametrize("name", ["bf16_perhead", "bf16_perhead_hub"])
-def test_per_head_matches_reference(name):
-    """Per-head eviction (PU:2208-2382, 3296-3464) end to end vs the reference's kept sets."""
+@pytest.mark.parametrize("name", ["bf16_perhead", "bf16_perhead_hub", "grid_bf16_perhead", "bf16_perhead_n8192"])
+def test_per_head_matches_reference(name, parity_report):
+    """Per-head eviction (PU:2208-2382, 3296-3464) end to end vs the reference's kept sets
+    (per-head differences recorded in ``parity_report``)."""
     dev = _cuda()
     c = case(name)
     g = load(name)
@@ -315,6 +316,7 @@ def test_per_head_matches_reference(name):
     ref = g["keep_per_head"]
     assert idx.shape == ref.shape
     d = [len(set(idx[h].tolist()) ^ set(ref[h].tolist())) for h in range(ref.shape[0])]
+    parity_report["per_head_" + name] = {"n": c["n"], "kept_per_head": int(ref.shape[1]), "differ_per_head": d}
     assert max(d) <= 4 and np.mean(d) <= 1.0, d
     assert ops.read_status(dev) == 0
 
