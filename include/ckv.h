@@ -282,6 +282,43 @@ int ckv_influence_walk(const float* rows, int32_t W, int32_t ld, int32_t n, int3
                        uint64_t* rng_state, int32_t init_state, void* workspace, size_t workspace_bytes,
                        float* visits, float* scores, float* h2o, ckv_stream_t stream);
 
+/* ---- decode-time graph scoring (circuit walker, spectral, combined) -------------
+ * Replace the CircuitGraph methods behind CircuitKVMonitor (CircuitKV/csrc/pybind.cpp:
+ * 65-130, circuit_manager.cpp:433-766; kernels graph_update.cu, circuit_walker.cu,
+ * spectral_power.cu).  The caller owns the sparse graph (adj_list int32 and adj_weights
+ * fp32, [max_seq_len, top_k], empty rows -1 / 0), the per-walker PCG states
+ * ([num_walkers][2] uint64) and the visit counts (int32). */
+
+/* Row current_idx of the graph: the top_k keys (of keys [n, head_dim], dtype fp16, bf16 or
+ * fp32, like query [head_dim]) by dot product with the query, in descending order (ties:
+ * lower key index first), the dot products as weights; -1 / 0 past n keys
+ * (graph_update.cu:174-325).  scratch: [n] floats.  top_k in (0, 64]. */
+int ckv_graph_update(const void* query, const void* keys, int32_t dtype, int32_t n, int32_t head_dim,
+                     int32_t current_idx, int32_t top_k, float* scratch, int32_t* adj_list, float* adj_weights,
+                     ckv_stream_t stream);
+
+/* Absorbing walkers (circuit_walker.cu:69-147): num_walkers walkers start at source, add 1 to
+ * visits at every position they reach, step to a neighbour with probability proportional to
+ * its weight, and stop at the sink tokens [0, 4), a dead end or 1500 steps.  clear_visits = 1
+ * zeroes visits [n] first.  rng_state is advanced in place. */
+int ckv_circuit_walk(const int32_t* adj_list, const float* adj_weights, int32_t n, int32_t top_k, int32_t source,
+                     int32_t num_walkers, uint64_t* rng_state, int32_t* visits, int32_t clear_visits,
+                     ckv_stream_t stream);
+
+/* PCG states of num_walkers walkers seeded (seed, walker) (circuit_walker.cu:157-171). */
+int ckv_pcg_seed(uint64_t seed, int32_t num_walkers, uint64_t* rng_state, ckv_stream_t stream);
+
+/* Spectral scores (spectral_power.cu:379-404): iters power iterations v <- A v / ||A v||_2 from
+ * v = 1 / sqrt(n) over the graph's first n rows.  v, scratch: [n]. */
+int ckv_spectral_scores(const int32_t* adj_list, const float* adj_weights, int32_t n, int32_t top_k, int32_t iters,
+                        float* v, float* scratch, ckv_stream_t stream);
+
+/* Combined scores (circuit_manager.cpp:700-730): walker_scores = visits as floats; spectral and
+ * walker_scores each divided by their maximum (in place, when it is above 1e-8); combined =
+ * their element-wise maximum.  All [n]. */
+int ckv_combine_scores(const int32_t* visits, float* spectral, float* walker_scores, float* combined, int32_t n,
+                       ckv_stream_t stream);
+
 /* Raw generator output (no reference counterpart; tests and callers that reproduce a
  * walk): CKV_RNG_PHILOX: out[i] = Philox4x64-10(key (seed, 0), counter (i / 4, stream_id,
  * 0, 0))[i % 4]; CKV_RNG_PCG: out[i] = the i-th pcg32 output of the state seeded

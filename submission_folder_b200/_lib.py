@@ -21,7 +21,8 @@ EXPORTED = (
     "ckv_default_params", "ckv_output_len", "ckv_workspace_size", "ckv_score_evict",
     "ckv_score_evict_batched", "ckv_read_status", "ckv_select_scores", "ckv_select_scores_noalloc",
     "ckv_neumann_rows",
-    "ckv_window_pool", "ckv_choose_heads", "ckv_pool_rows_given", "ckv_influence_walk", "ckv_influence_walk_dense", "ckv_walk_workspace_size",
+    "ckv_window_pool", "ckv_choose_heads", "ckv_pool_rows_given", "ckv_graph_update", "ckv_circuit_walk",
+    "ckv_pcg_seed", "ckv_spectral_scores", "ckv_combine_scores", "ckv_influence_walk", "ckv_influence_walk_dense", "ckv_walk_workspace_size",
     "ckv_rng_fill", "ckv_gather", "ckv_device_accessible", "ckv_set_stage_events", "ckv_last_error_string",
     "ckv_version",
 )
@@ -119,6 +120,11 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "ckv_neumann_rows": (i32, [P, i32, vp, vp, i32, vp, sz, vp, vp, vp, vp]),
         "ckv_window_pool": (i32, [P, L, vp, sz, vp, vp, vp, vp, vp, vp, vp]),
         "ckv_choose_heads": (i32, [P, i32, vp, vp, vp, vp, vp]),
+        "ckv_graph_update": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp]),
+        "ckv_circuit_walk": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, i32, vp]),
+        "ckv_pcg_seed": (i32, [u64, i32, vp, vp]),
+        "ckv_spectral_scores": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
+        "ckv_combine_scores": (i32, [vp, vp, vp, vp, i32, vp]),
         "ckv_pool_rows_given": (i32, [P, L, i32, vp, vp, vp, sz, vp, vp, vp]),
         "ckv_influence_walk": (i32, [vp, i32, i32, i32, i32, i32, i32, i32, f32, f32, f32, i32, u64,
                                      vp, i32, vp, sz, vp, vp, vp, vp]),

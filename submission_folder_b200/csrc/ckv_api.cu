@@ -13,6 +13,7 @@
 
 #include "ckv_common.cuh"
 #include "ckv_gather.h"
+#include "ckv_monitor.h"
 #include "ckv_neumann.h"
 #include "ckv_plan.h"
 #include "ckv_select.h"
@@ -653,6 +654,52 @@ int ckv_pool_rows_given(const ckv_params* p, const ckv_layer* layer, int32_t hea
     e = cudaMemcpy2DAsync(rows_hi, (size_t)pl.n * 4, ws + pl.off_rows_hi, (size_t)pl.n_pad * 4,
                           (size_t)pl.n * 4, pl.W, cudaMemcpyDeviceToDevice, st);
   return e == cudaSuccess ? CKV_OK : cuda_fail(e, "head-sharded pooling output");
+}
+
+int ckv_graph_update(const void* query, const void* keys, int32_t dtype, int32_t n, int32_t head_dim,
+                     int32_t current_idx, int32_t top_k, float* scratch, int32_t* adj_list, float* adj_weights,
+                     ckv_stream_t stream) {
+  if (!query || !keys || !scratch || !adj_list || !adj_weights) return fail(CKV_ERR_ARG, "null argument");
+  if (dtype != CKV_BF16 && dtype != CKV_FP16 && dtype != CKV_FP32) return fail(CKV_ERR_DTYPE, "dtype must be bf16, fp16 or fp32");
+  if (top_k <= 0 || top_k > 64) return fail(CKV_ERR_ARG, "top_k must be in (0, 64]");
+  if (n <= 0 || head_dim <= 0 || head_dim > 1024 || current_idx < 0) return fail(CKV_ERR_ARG, "bad n, head_dim or current_idx");
+  const cudaError_t e = launch_graph_update(query, keys, dtype, n, head_dim, current_idx, top_k, scratch, adj_list,
+                                            adj_weights, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "graph update");
+}
+
+int ckv_circuit_walk(const int32_t* adj_list, const float* adj_weights, int32_t n, int32_t top_k, int32_t source,
+                     int32_t num_walkers, uint64_t* rng_state, int32_t* visits, int32_t clear_visits,
+                     ckv_stream_t stream) {
+  if (!adj_list || !adj_weights || !rng_state || !visits) return fail(CKV_ERR_ARG, "null argument");
+  if (top_k <= 0 || top_k > 64 || n <= 0 || num_walkers <= 0) return fail(CKV_ERR_ARG, "bad n, top_k or num_walkers");
+  if (source < 0 || source >= n) source = n - 1;   // as the reference's launcher
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = clear_visits ? cudaMemsetAsync(visits, 0, (size_t)n * sizeof(int32_t), st) : cudaSuccess;
+  if (e == cudaSuccess) e = launch_circuit_walk(adj_list, adj_weights, visits, rng_state, source, n, top_k, num_walkers, st);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "circuit walk");
+}
+
+int ckv_pcg_seed(uint64_t seed, int32_t num_walkers, uint64_t* rng_state, ckv_stream_t stream) {
+  if (!rng_state || num_walkers <= 0) return fail(CKV_ERR_ARG, "bad arguments");
+  const cudaError_t e = launch_pcg_init(rng_state, seed, num_walkers, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "pcg seed");
+}
+
+int ckv_spectral_scores(const int32_t* adj_list, const float* adj_weights, int32_t n, int32_t top_k, int32_t iters,
+                        float* v, float* scratch, ckv_stream_t stream) {
+  if (!adj_list || !adj_weights || !v || !scratch) return fail(CKV_ERR_ARG, "null argument");
+  if (n <= 0 || top_k <= 0 || top_k > 64 || iters < 0) return fail(CKV_ERR_ARG, "bad n, top_k or iters");
+  if (iters == 0) return CKV_OK;   // the reference leaves the vector as it was
+  const cudaError_t e = launch_spectral(adj_list, adj_weights, n, top_k, iters, v, scratch, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "spectral scores");
+}
+
+int ckv_combine_scores(const int32_t* visits, float* spectral, float* walker_scores, float* combined, int32_t n,
+                       ckv_stream_t stream) {
+  if (!visits || !spectral || !walker_scores || !combined || n <= 0) return fail(CKV_ERR_ARG, "bad arguments");
+  const cudaError_t e = launch_combine(visits, spectral, walker_scores, combined, n, (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "combine scores");
 }
 
 int ckv_influence_walk_dense(const float* attn, int32_t n, int32_t current_idx, int32_t num_walkers,
