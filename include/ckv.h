@@ -319,6 +319,34 @@ int ckv_spectral_scores(const int32_t* adj_list, const float* adj_weights, int32
 int ckv_combine_scores(const int32_t* visits, float* spectral, float* walker_scores, float* combined, int32_t n,
                        ckv_stream_t stream);
 
+/* Landmark walkers (CircuitGraph.update_and_step_landmark_walker and
+ * update_and_step_landmark_absorbing_walker, CircuitKV/csrc/circuit_manager.cpp:768-1164;
+ * kernels landmark_walker.cu, landmark_absorbing_walker.cu) over a dense fp32 attention
+ * matrix attn [n, n] (row-major):
+ *   1. H2O scores: column sums of attn over the rows at or below the diagonal;
+ *   2. landmarks: [24, n - 64) cut into num_landmarks equal segments (fewer when a segment
+ *      would be shorter than min_spacing > 0), the highest H2O score of each; written to
+ *      positions [32] and their number to count [1] (0 when n < 89);
+ *   3. walkers_per_source walkers from each landmark and from the query (the last token,
+ *      whose attention row is attn[current_idx]); visits [n] (int32) is cleared first, then
+ *      gets 1 per landmark-walker visit and (int)query_boost per query-walker visit; walkers
+ *      stop at [0, 4) or after 1500 steps (CKV_LANDMARK_ABSORBING with absorb_at_landmarks:
+ *      also with probability 0.1 at another source's landmark);
+ *   4. scores [n]: CKV_LANDMARK_POSITIONAL visits / (1 / (p - 3)^position_alpha + 1e-8),
+ *      CKV_LANDMARK_REACHABILITY visits / (walkers able to reach p), CKV_LANDMARK_ABSORBING
+ *      the same with 0.9 pass-through per landmark; 0 on [0, 4).
+ * rng_state: [(num_landmarks + 1) * walkers_per_source][2] PCG states (ckv_pcg_seed), walker
+ * w = source * walkers_per_source + k, advanced in place.  num_landmarks in [1, 32].
+ * workspace: ckv_landmark_workspace_size(n) bytes, 16-byte aligned.  No host
+ * synchronisation: the landmark count stays on the device. */
+enum { CKV_LANDMARK_POSITIONAL = 0, CKV_LANDMARK_REACHABILITY = 1, CKV_LANDMARK_ABSORBING = 2 };
+int ckv_landmark_workspace_size(int32_t n, size_t* bytes);
+int ckv_landmark_walk(const float* attn, int32_t n, int32_t current_idx, int32_t mode, int32_t num_landmarks,
+                      int32_t walkers_per_source, float query_boost, int32_t min_spacing, float position_alpha,
+                      int32_t absorb_at_landmarks, uint64_t* rng_state, int32_t* visits, float* scores,
+                      int32_t* positions, int32_t* count, void* workspace, size_t workspace_bytes,
+                      ckv_stream_t stream);
+
 /* Raw generator output (no reference counterpart; tests and callers that reproduce a
  * walk): CKV_RNG_PHILOX: out[i] = Philox4x64-10(key (seed, 0), counter (i / 4, stream_id,
  * 0, 0))[i % 4]; CKV_RNG_PCG: out[i] = the i-th pcg32 output of the state seeded

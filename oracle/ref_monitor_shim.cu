@@ -1,9 +1,10 @@
 // Test infrastructure only: C entry points onto the reference's own decode-time graph
 // kernels (CircuitKV/csrc/kernels/graph_update.cu, circuit_walker.cu, spectral_power.cu,
-// compiled from their sources in place by oracle/Makefile with the reference's flags), so
-// that GPU tests can compare the sm_100a kernels with them on the same inputs and PCG
-// states.  The sequences follow CircuitGraph::update_and_step_circuit_combined
-// (circuit_manager.cpp:592-740).
+// landmark_walker.cu, landmark_absorbing_walker.cu, compiled from their sources in place by
+// oracle/Makefile with the reference's flags), so that GPU tests can compare the sm_100a
+// kernels with them on the same inputs and PCG states.  The sequences follow
+// CircuitGraph::update_and_step_circuit_combined (circuit_manager.cpp:592-740) and the two
+// landmark methods (circuit_manager.cpp:768-1164).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -25,6 +26,34 @@ void launch_normalize_to_unit_max(float* v, float* partial_max, float* max_out, 
                                   cudaStream_t stream);
 void launch_max_combine_kernel(const float* spectral_scores, const float* walker_scores, float* combined_scores,
                                int seq_len, cudaStream_t stream);
+void launch_reset_counts_kernel(int32_t* visit_counts, int max_seq_len, cudaStream_t stream);
+void launch_compute_h2o_scores_kernel(const float* attention_matrix, float* h2o_scores, int seq_len,
+                                      cudaStream_t stream);
+void launch_select_landmarks_kernel(const float* attention_row_sums, int32_t* landmark_positions,
+                                    int* num_landmarks_out, int seq_len, int max_landmarks, int min_spacing,
+                                    int sink_buffer, int window_size, cudaStream_t stream);
+void launch_cache_landmark_attention_kernel(const float* full_attention, float* landmark_attention,
+                                            const int32_t* landmark_positions, int num_landmarks, int seq_len,
+                                            cudaStream_t stream);
+void launch_landmark_walker_kernel(const float* landmark_attention, const float* query_attention,
+                                   const float* h2o_scores, int32_t* visit_counts, uint64_t* rng_states,
+                                   const int32_t* landmark_positions, int num_landmarks, int walkers_per_source,
+                                   float query_boost, int seq_len, cudaStream_t stream);
+void launch_positional_normalize_kernel(const int32_t* visit_counts, float* normalized_scores, float* partial_max,
+                                        int seq_len, int sink_size, float alpha, cudaStream_t stream);
+void launch_reachability_normalize_kernel(const int32_t* visit_counts, float* normalized_scores,
+                                          const int32_t* landmark_positions, int num_landmarks,
+                                          int walkers_per_source, float query_boost, int seq_len, int sink_size,
+                                          cudaStream_t stream);
+void launch_landmark_absorbing_walker_kernel(const float* landmark_attention, const float* query_attention,
+                                             const float* h2o_scores, int32_t* visit_counts, uint64_t* rng_states,
+                                             const int32_t* landmark_positions, int num_landmarks,
+                                             int walkers_per_source, float query_boost, int seq_len,
+                                             bool absorb_at_landmarks, cudaStream_t stream);
+void launch_landmark_reachability_normalize_kernel(const int32_t* visit_counts, float* normalized_scores,
+                                                   const int32_t* landmark_positions, int num_landmarks,
+                                                   int walkers_per_source, float query_boost, int seq_len,
+                                                   int sink_size, cudaStream_t stream);
 }  // namespace circuit_kv
 
 // dtype 1: fp16, 2: fp32 (the reference's two graph kernels)
@@ -65,4 +94,48 @@ extern "C" int ref_spectral_combined(const int32_t* adj, const float* w, const i
   circuit_kv::launch_normalize_to_unit_max(walker, scratch, scratch + 256, n, nb, st);
   circuit_kv::launch_max_combine_kernel(v, walker, combined, n, st);
   return (int)cudaGetLastError();
+}
+
+// The landmark methods' sequence (circuit_manager.cpp:768-1164) on caller buffers: mode 0
+// positional, 1 reachability (update_and_step_landmark_walker), 2 the absorbing walker.
+// positions [32] and count [1] as the reference's landmark_positions_ / num_landmarks_selected_
+// (count zeroed first, as at the reference's allocation); h2o [n] out.  Synchronises.
+extern "C" int ref_landmark_walk(const float* attn, int n, int current_idx, int mode, int num_landmarks,
+                                 int walkers_per_source, float query_boost, int min_spacing, float alpha,
+                                 int absorb_at_landmarks, uint64_t* states, int32_t* visits, float* scores,
+                                 int32_t* positions, int32_t* count, float* h2o, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float *lm_attn = nullptr, *q_attn = nullptr, *pmax = nullptr;
+  cudaMalloc(&lm_attn, (size_t)32 * n * sizeof(float));
+  cudaMalloc(&q_attn, (size_t)n * sizeof(float));
+  cudaMalloc(&pmax, (size_t)((n + 255) / 256 + 1) * sizeof(float));
+  circuit_kv::launch_compute_h2o_scores_kernel(attn, h2o, n, st);
+  circuit_kv::launch_select_landmarks_kernel(h2o, positions, count, n, num_landmarks, min_spacing, 20, 64, st);
+  cudaStreamSynchronize(st);
+  int actual = 0;
+  cudaMemcpy(&actual, count, sizeof(int), cudaMemcpyDeviceToHost);
+  if (actual > 0) circuit_kv::launch_cache_landmark_attention_kernel(attn, lm_attn, positions, actual, n, st);
+  cudaMemcpyAsync(q_attn, attn + (size_t)current_idx * n, (size_t)n * sizeof(float), cudaMemcpyDeviceToDevice, st);
+  circuit_kv::launch_reset_counts_kernel(visits, n, st);
+  if (mode == 2) {
+    circuit_kv::launch_landmark_absorbing_walker_kernel(lm_attn, q_attn, h2o, visits, states, positions, actual,
+                                                        walkers_per_source, query_boost, n, absorb_at_landmarks != 0,
+                                                        st);
+    circuit_kv::launch_landmark_reachability_normalize_kernel(visits, scores, positions, actual, walkers_per_source,
+                                                              query_boost, n, 4, st);
+  } else {
+    circuit_kv::launch_landmark_walker_kernel(lm_attn, q_attn, h2o, visits, states, positions, actual,
+                                              walkers_per_source, query_boost, n, st);
+    if (mode == 1)
+      circuit_kv::launch_reachability_normalize_kernel(visits, scores, positions, actual, walkers_per_source,
+                                                       query_boost, n, 4, st);
+    else
+      circuit_kv::launch_positional_normalize_kernel(visits, scores, pmax, n, 4, alpha, st);
+  }
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  cudaFree(lm_attn);
+  cudaFree(q_attn);
+  cudaFree(pmax);
+  return (int)e;
 }

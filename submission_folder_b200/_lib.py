@@ -22,11 +22,13 @@ EXPORTED = (
     "ckv_score_evict_batched", "ckv_read_status", "ckv_select_scores", "ckv_select_scores_noalloc",
     "ckv_neumann_rows",
     "ckv_window_pool", "ckv_choose_heads", "ckv_pool_rows_given", "ckv_graph_update", "ckv_circuit_walk",
-    "ckv_pcg_seed", "ckv_spectral_scores", "ckv_combine_scores", "ckv_influence_walk", "ckv_influence_walk_dense", "ckv_walk_workspace_size",
+    "ckv_pcg_seed", "ckv_spectral_scores", "ckv_combine_scores", "ckv_landmark_workspace_size",
+    "ckv_landmark_walk", "ckv_influence_walk", "ckv_influence_walk_dense", "ckv_walk_workspace_size",
     "ckv_rng_fill", "ckv_gather", "ckv_device_accessible", "ckv_set_stage_events", "ckv_last_error_string",
     "ckv_version",
 )
 RNG_PHILOX, RNG_PCG = 0, 1
+LANDMARK_POSITIONAL, LANDMARK_REACHABILITY, LANDMARK_ABSORBING = 0, 1, 2
 
 
 class Params(ctypes.Structure):
@@ -125,6 +127,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "ckv_pcg_seed": (i32, [u64, i32, vp, vp]),
         "ckv_spectral_scores": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
         "ckv_combine_scores": (i32, [vp, vp, vp, vp, i32, vp]),
+        "ckv_landmark_workspace_size": (i32, [i32, ctypes.POINTER(sz)]),
+        "ckv_landmark_walk": (i32, [vp, i32, i32, i32, i32, i32, f32, i32, f32, i32, vp, vp, vp, vp, vp, vp, sz,
+                                    vp]),
         "ckv_pool_rows_given": (i32, [P, L, i32, vp, vp, vp, sz, vp, vp, vp]),
         "ckv_influence_walk": (i32, [vp, i32, i32, i32, i32, i32, i32, i32, f32, f32, f32, i32, u64,
                                      vp, i32, vp, sz, vp, vp, vp, vp]),

@@ -1,18 +1,20 @@
 """``circuit_kv._C``: ``CircuitGraph`` with the reference's constructor, its
 influence-walker methods (the prefill path's legacy branch) and the decode-time graph
 methods behind ``CircuitKVMonitor`` (CircuitKV/csrc/pybind.cpp:44-300;
-circuit_manager.cpp:26-84, 433-766, 1190-1330), on the sm_100a kernels of ``libckv.so``.
+circuit_manager.cpp:26-84, 433-1330), on the sm_100a kernels of ``libckv.so``.
 
 Like the reference, the object owns its buffers: the sparse attention graph
 (``[max_seq_len, top_k]`` neighbours, -1 where empty, and weights), PCG states for
-``num_walkers`` circuit walkers seeded once with ``seed`` and for up to 10000 influence
-walkers seeded once with ``seed + 3000`` (walker w: ``pcg_init(seed, w)``), all carried
-across calls, visit counts, spectral / walker / combined scores.  The landmark walkers
-(``update_and_step_landmark_walker`` and the absorbing variant) raise
-``NotImplementedError``.
+``num_walkers`` circuit walkers seeded once with ``seed``, for up to 10000 influence
+walkers seeded once with ``seed + 3000`` and for (32 + 1) x 500 landmark walkers seeded once
+with ``seed + 1000`` or ``seed + 2000`` (whichever landmark method runs first; walker w:
+``pcg_init(seed, w)``), all carried across calls, visit counts (shared by the circuit and
+landmark walkers, as the reference's), spectral / walker / combined / landmark scores.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -21,6 +23,8 @@ from .. import _lib, ops
 __version__ = "4.3.0"
 
 _INFLUENCE_MAX_WALKERS = 10000
+_LANDMARK_MAX = 32
+_LANDMARK_MAX_WALKERS = (_LANDMARK_MAX + 1) * 500
 _GRAPH_DTYPES = {torch.float16: 1, torch.float32: 2, torch.bfloat16: 0}
 
 
@@ -57,6 +61,13 @@ class CircuitGraph:
         self._combined = torch.zeros(self.max_seq_len, dtype=torch.float32, device=dev)
         self._graph_scratch = torch.zeros(self.max_seq_len, dtype=torch.float32, device=dev)
         self._num_power_iterations = 10
+        # landmark walkers: PCG states for (32 + 1) x 500 walkers, landmark positions and count
+        self._lm_rng = torch.zeros(2 * _LANDMARK_MAX_WALKERS, dtype=torch.int64, device=dev)
+        self._lm_rng_initialized = False
+        self._lm_positions = torch.zeros(_LANDMARK_MAX, dtype=torch.int32, device=dev)
+        self._lm_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._lm_scores = torch.zeros(self.max_seq_len, dtype=torch.float32, device=dev)
+        self._lm_ws = None
         lib = _lib.load()
         _lib.check(lib.ckv_pcg_seed(int(self.seed), self.num_walkers, self._circuit_rng.data_ptr(),
                                     ops._stream(dev)), "ckv_pcg_seed")
@@ -168,10 +179,88 @@ class CircuitGraph:
     def synchronize(self) -> None:
         torch.cuda.current_stream(self._dev).synchronize()
 
-    # -- landmark walkers: not built ------------------------------------------------
-    def _not_here(self, *args, **kwargs):
-        raise NotImplementedError("the landmark walkers of CircuitGraph are not built in this library")
+    # -- landmark walkers ----------------------------------------------------------------
+    def _landmark_step(self, attention_matrix: torch.Tensor, current_idx: int, num_landmarks: int,
+                       walkers_per_source: int, query_boost: float, min_spacing: int, mode: int,
+                       position_alpha: float, absorb_at_landmarks: bool, seed_offset: int) -> None:
+        a = attention_matrix
+        if not a.is_cuda:
+            raise RuntimeError("attention_matrix must be a CUDA tensor")
+        if not a.is_contiguous():
+            raise RuntimeError("attention_matrix must be contiguous")
+        if a.dtype != torch.float32:
+            raise RuntimeError("attention_matrix must be float32")
+        if a.dim() != 2:
+            raise RuntimeError("attention_matrix must be 2D [seq_len, seq_len]")
+        n = a.shape[0]
+        if a.shape[1] != n:
+            raise RuntimeError("attention_matrix must be square")
+        if not (0 <= current_idx < n):
+            raise RuntimeError("current_idx out of bounds")
+        if n > self.max_seq_len:
+            raise RuntimeError("seq_len exceeds max_seq_len")
+        if num_landmarks > _LANDMARK_MAX:
+            raise RuntimeError("num_landmarks exceeds MAX_LANDMARKS")
+        if (num_landmarks + 1) * walkers_per_source > _LANDMARK_MAX_WALKERS:
+            raise RuntimeError("total_walkers exceeds max_landmark_walkers")
+        if num_landmarks < 1:
+            raise RuntimeError("num_landmarks must be at least 1")
+        if walkers_per_source < 0:
+            raise RuntimeError("walkers_per_source must be non-negative")
+        lib, st = _lib.load(), ops._stream(self._dev)
+        if self._lm_ws is None:
+            sz = ctypes.c_size_t()
+            _lib.check(lib.ckv_landmark_workspace_size(self.max_seq_len, ctypes.byref(sz)),
+                       "ckv_landmark_workspace_size")
+            self._lm_ws = torch.empty(sz.value, dtype=torch.uint8, device=self._dev)
+        if not self._lm_rng_initialized:
+            _lib.check(lib.ckv_pcg_seed(int(self.seed + seed_offset), _LANDMARK_MAX_WALKERS,
+                                        self._lm_rng.data_ptr(), st), "ckv_pcg_seed")
+            self._lm_rng_initialized = True
+        self._seq_len = n
+        _lib.check(lib.ckv_landmark_walk(a.data_ptr(), n, int(current_idx), mode, int(num_landmarks),
+                                         int(walkers_per_source), float(query_boost), int(min_spacing),
+                                         float(position_alpha), 1 if absorb_at_landmarks else 0,
+                                         self._lm_rng.data_ptr(), self._counts.data_ptr(),
+                                         self._lm_scores.data_ptr(), self._lm_positions.data_ptr(),
+                                         self._lm_count.data_ptr(), self._lm_ws.data_ptr(), self._lm_ws.numel(), st),
+                   "ckv_landmark_walk")
 
-    update_and_step_landmark_walker = get_landmark_scores = _not_here
-    update_and_step_landmark_absorbing_walker = get_landmark_absorbing_scores = _not_here
-    get_landmark_absorbing_raw_visits = get_landmark_positions = _not_here
+    def update_and_step_landmark_walker(self, attention_matrix: torch.Tensor, current_idx: int,
+                                        num_landmarks: int = 32, walkers_per_source: int = 100,
+                                        query_boost: float = 2.0, min_spacing: int = 50,
+                                        position_alpha: float = 0.6, use_reachability: bool = False) -> None:
+        """Walkers from stratified landmarks and the query; scores normalised by position
+        (visits / (1 / d^alpha + 1e-8)) or, with use_reachability, by the walkers able to reach
+        each position.  Landmark PCG states seeded once with seed + 1000 (shared with the
+        absorbing form, whichever runs first)."""
+        mode = _lib.LANDMARK_REACHABILITY if use_reachability else _lib.LANDMARK_POSITIONAL
+        self._landmark_step(attention_matrix, current_idx, num_landmarks, walkers_per_source, query_boost,
+                            min_spacing, mode, position_alpha, False, 1000)
+
+    def get_landmark_scores(self) -> torch.Tensor:
+        self.synchronize()
+        return self._lm_scores[:self._seq_len].clone()
+
+    def update_and_step_landmark_absorbing_walker(self, attention_matrix: torch.Tensor, current_idx: int,
+                                                  num_landmarks: int = 8, walkers_per_source: int = 100,
+                                                  query_boost: float = 2.0, min_spacing: int = 50,
+                                                  absorb_at_landmarks: bool = True) -> None:
+        """Landmarks as sources and (with probability 0.1) sinks; reachability with 0.9
+        pass-through per landmark.  Landmark PCG states seeded once with seed + 2000 (shared
+        with the plain landmark walker, whichever runs first)."""
+        self._landmark_step(attention_matrix, current_idx, num_landmarks, walkers_per_source, query_boost,
+                            min_spacing, _lib.LANDMARK_ABSORBING, 0.0, absorb_at_landmarks, 2000)
+
+    def get_landmark_absorbing_scores(self) -> torch.Tensor:
+        self.synchronize()
+        return self._lm_scores[:self._seq_len].clone()
+
+    def get_landmark_absorbing_raw_visits(self) -> torch.Tensor:
+        self.synchronize()
+        return self._counts[:self._seq_len].clone()
+
+    def get_landmark_positions(self) -> torch.Tensor:
+        self.synchronize()
+        k = int(self._lm_count.item())
+        return self._lm_positions[:max(k, 0)].clone()

@@ -173,7 +173,16 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
     pl.off_ph_qrow = take(Hs * nn * 4);
     pl.off_ph_two = take(Hs * nn * 4);
     pl.off_ph_col = take(Hs * nn * 4);
-    pl.off_ph_ent = take((size_t)(pl.ncol_tiles + 1) * Hs * 4);   // + the per-head totals
+    // tcgen05 per-head pass: the pooling pass's keys-on-lanes shapes, and its shared memory
+    // (two stages, log-sum-exp and q2w re-laid) within the 227 KB a CTA may have
+    const int rs = pl.W < 64 ? pl.W : 64;
+    const size_t ph_smem = 2 * ((size_t)pl.G * rs * 256 + 128 * 256) + 2 * Hs * pl.W * 4 + 1024;
+    pl.ph_tc = (pl.tc && pl.G == 4 && (pl.W == 32 || pl.W == 64 || pl.W == 128) && pl.Hkv >= 2 &&
+                ph_smem + 1024 <= 227 * 1024) ? 1 : 0;
+    pl.ph_slots = pl.ph_tc ? 4 * (pl.W / rs) : 0;
+    pl.ph_ent_parts = pl.ph_tc ? 4 * ((n + 127) / 128) : pl.ncol_tiles;
+    pl.off_ph_ent = take((size_t)(pl.ph_ent_parts + 1) * Hs * 4);   // + the per-head totals
+    pl.off_ph_part = take((size_t)2 * pl.ph_slots * Hs * nn * 4);
     pl.off_ph_vec = take(Hs * 2 * nw * 4);
     pl.off_ph_ghi = take(nw * 4);
     pl.off_ph_gbuf = take(nw * 2 * 8 + nw * 4);
@@ -700,6 +709,33 @@ int ckv_combine_scores(const int32_t* visits, float* spectral, float* walker_sco
   if (!visits || !spectral || !walker_scores || !combined || n <= 0) return fail(CKV_ERR_ARG, "bad arguments");
   const cudaError_t e = launch_combine(visits, spectral, walker_scores, combined, n, (cudaStream_t)stream);
   return e == cudaSuccess ? CKV_OK : cuda_fail(e, "combine scores");
+}
+
+int ckv_landmark_workspace_size(int32_t n, size_t* bytes) {
+  if (!bytes || n <= 0) return fail(CKV_ERR_ARG, "bad n or null pointer");
+  *bytes = landmark_workspace_floats(n) * sizeof(float);
+  return CKV_OK;
+}
+
+int ckv_landmark_walk(const float* attn, int32_t n, int32_t current_idx, int32_t mode, int32_t num_landmarks,
+                      int32_t walkers_per_source, float query_boost, int32_t min_spacing, float position_alpha,
+                      int32_t absorb_at_landmarks, uint64_t* rng_state, int32_t* visits, float* scores,
+                      int32_t* positions, int32_t* count, void* workspace, size_t workspace_bytes,
+                      ckv_stream_t stream) {
+  if (!attn || !rng_state || !visits || !scores || !positions || !count || !workspace)
+    return fail(CKV_ERR_ARG, "null argument");
+  if (n <= 0 || current_idx < 0 || current_idx >= n) return fail(CKV_ERR_ARG, "bad n or current_idx");
+  if (mode < CKV_LANDMARK_POSITIONAL || mode > CKV_LANDMARK_ABSORBING) return fail(CKV_ERR_ARG, "bad mode");
+  if (num_landmarks < 1 || num_landmarks > 32) return fail(CKV_ERR_ARG, "num_landmarks must be in [1, 32]");
+  if (walkers_per_source < 0 || (long long)(num_landmarks + 1) * walkers_per_source > INT32_MAX)
+    return fail(CKV_ERR_ARG, "bad walkers_per_source");
+  if (workspace_bytes < landmark_workspace_floats(n) * sizeof(float) || ((uintptr_t)workspace & 15u))
+    return fail(CKV_ERR_WORKSPACE, "landmark workspace too small or misaligned");
+  const cudaError_t e = launch_landmark_walk(attn, n, current_idx, mode, num_landmarks, walkers_per_source, query_boost,
+                                             min_spacing, position_alpha, absorb_at_landmarks, rng_state, visits,
+                                             scores, positions, count, static_cast<float*>(workspace),
+                                             (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "landmark walk");
 }
 
 int ckv_influence_walk_dense(const float* attn, int32_t n, int32_t current_idx, int32_t num_walkers,

@@ -245,6 +245,293 @@ __global__ void __launch_bounds__(kMonThreads) k_combine(const int32_t* __restri
   for (int i = threadIdx.x; i < n; i += blockDim.x) combined[i] = fmaxf(spectral[i], walker[i]);
 }
 
+// ---- landmark walkers ------------------------------------------------------------------
+// CircuitGraph::update_and_step_landmark_walker / _absorbing_walker (circuit_manager.cpp:
+// 768-1164; landmark_walker.cu, landmark_absorbing_walker.cu) over a dense fp32 attention
+// matrix.  Every sum the reference forms by a sequential scan over a row (a source's start
+// distribution over [4, source), a transition's total over [0, pos), the running cumsum of
+// its sampling scan) is an fp32 prefix sum of that row taken in the same order.  So each
+// row's prefix array is built once, sequentially, and a walker step reads its total from it
+// and finds the first position whose running sum reaches the target by binary search: the
+// same additions and comparisons as the reference's O(n) scans, in O(log n) per step.
+// Where a row holds a negative or NaN value (the running sums are then not monotone) the
+// walker scans that row's prefix array linearly instead.
+
+constexpr int kLmMaxLandmarks = 32;   // landmarks per call
+constexpr int kLmSinkBuffer = 20;     // landmark range starts at sink + 20 ...
+constexpr int kLmWindow = 64;         // ... and ends 64 tokens before the end
+constexpr int kLmRows = 3 + 2 * kLmMaxLandmarks;   // prefix rows: H2O, query x2, landmarks x2
+
+// Column sums over the causal rows (H2O scores, landmark_walker.cu:476-505) in the
+// reference's order: the partial of residue t (t < 256) sums rows i = t, t + 256, ... with
+// i >= column, in increasing i; the 256 partials reduce as a halving tree.  A CTA owns 32
+// adjacent columns: lanes are columns (coalesced 128-byte row reads), warp w keeps the
+// partials of residues w, w + 8, ..., w + 248 in registers.
+__global__ void __launch_bounds__(256) k_lm_h2o(const float* __restrict__ a, int n, float* __restrict__ h2o) {
+  __shared__ float part[256][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 32, c = c0 + lane;
+  float acc[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+  if (c < n) {
+    for (int b = (c0 / 256) * 256; b < n; b += 256) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const int i = b + warp + 8 * k;
+        if (i < n && i >= c) acc[k] += a[(size_t)i * n + c];
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 32; ++k) part[warp + 8 * k][lane] = acc[k];
+  __syncthreads();
+  for (int stride = 128; stride > 0; stride >>= 1) {
+    for (int e = threadIdx.x; e < stride * 32; e += 256) part[e >> 5][e & 31] += part[(e >> 5) + stride][e & 31];
+    __syncthreads();
+  }
+  if (warp == 0 && c < n) h2o[c] = part[0][lane];
+}
+
+// Stratified landmarks (landmark_walker.cu:404-464): [24, n - 64) in num_landmarks equal
+// segments (fewer, of at least min_spacing, when a segment would be shorter), the highest
+// H2O score of each (first index among equals; NaN and values <= -1e30 never chosen), in
+// segment order.  One warp per segment.
+__global__ void __launch_bounds__(1024) k_lm_select(const float* __restrict__ h2o, int n, int max_landmarks,
+                                                    int min_spacing, int32_t* __restrict__ positions,
+                                                    int32_t* __restrict__ count) {
+  __shared__ int best[kLmMaxLandmarks];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int valid_start = kMonSink + kLmSinkBuffer, valid_end = n - kLmWindow;
+  const int range = valid_end - valid_start;
+  if (range <= 0) {
+    if (threadIdx.x == 0) *count = 0;
+    return;
+  }
+  int segs = max_landmarks, seg = range / segs;
+  if (seg < min_spacing && min_spacing > 0) {
+    segs = max(range / min_spacing, 1);
+    seg = range / segs;
+  }
+  if (warp < segs) {
+    const int s0 = valid_start + warp * seg, s1 = warp == segs - 1 ? valid_end : s0 + seg;
+    float bv = -1e30f;
+    int bi = -1;
+    for (int i = s0 + lane; i < s1; i += 32) {
+      const float x = h2o[i];
+      if (x > bv) { bv = x; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) best[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int cnt = 0;
+    for (int w = 0; w < segs; ++w)
+      if (best[w] >= 0) positions[cnt++] = best[w];
+    *count = cnt;
+  }
+}
+
+// Prefix rows, each of `stride` floats: P[m] = src[start] + ... + src[m - 1] summed left
+// to right (0 for m <= start), for m <= len.  Row 0: H2O from 0; rows 1 / 2: the query's
+// attention row from 0 / from the sink end; rows 3 + 2 l / 4 + 2 l: landmark l's row from 0 /
+// from the sink end, up to its position.  mono[r] = 1 when every summed value is >= 0.
+// One CTA per row: chunks staged in shared memory, summed in order by one thread.
+__global__ void __launch_bounds__(1024) k_lm_prefix(const float* __restrict__ a, int n, int current_idx,
+                                                    const float* __restrict__ h2o,
+                                                    const int32_t* __restrict__ positions,
+                                                    const int32_t* __restrict__ count, float* __restrict__ pref,
+                                                    int stride, int32_t* __restrict__ mono) {
+  __shared__ float buf[1024];
+  __shared__ float carry;
+  const int r = blockIdx.x;
+  const float* src;
+  int start = 0, len = n;
+  if (r == 0) {
+    src = h2o;
+  } else if (r <= 2) {
+    src = a + (size_t)current_idx * n;
+    start = r == 2 ? kMonSink : 0;
+  } else {
+    const int l = (r - 3) >> 1;
+    if (l >= *count) return;
+    const int pos = positions[l];
+    src = a + (size_t)pos * n;
+    start = ((r - 3) & 1) ? kMonSink : 0;
+    len = pos;
+  }
+  float* P = pref + (size_t)r * stride;
+  for (int m = threadIdx.x; m <= min(start, len); m += blockDim.x) P[m] = 0.f;
+  if (threadIdx.x == 0) carry = 0.f;
+  bool ok = true;
+  for (int j0 = start; j0 < len; j0 += 1024) {
+    const int j = j0 + threadIdx.x;
+    const int cnt = min(1024, len - j0);
+    __syncthreads();
+    if (j < len) {
+      const float x = src[j];
+      ok = ok && (x >= 0.f);
+      buf[threadIdx.x] = x;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float run = carry;
+      for (int t = 0; t < cnt; ++t) {
+        run += buf[t];
+        buf[t] = run;
+      }
+      carry = run;
+    }
+    __syncthreads();
+    if (j < len) P[j + 1] = buf[threadIdx.x];
+  }
+  ok = __syncthreads_and(ok);
+  if (threadIdx.x == 0) mono[r] = ok ? 1 : 0;
+}
+
+// The first j in [lo, hi) whose running sum P[j + 1] reaches target, else dflt.
+CKV_DEV int lm_first_reach(const float* __restrict__ P, int lo, int hi, float target, bool mono, int dflt) {
+  if (mono) {
+    int x = lo, y = hi;
+    while (x < y) {
+      const int m = (x + y) >> 1;
+      if (P[m + 1] >= target) y = m;
+      else x = m + 1;
+    }
+    return x < hi ? x : dflt;
+  }
+  for (int j = lo; j < hi; ++j)
+    if (P[j + 1] >= target) return j;
+  return dflt;
+}
+
+// One thread per walker (landmark_walker.cu:59-236, landmark_absorbing_walker.cu:66-238):
+// walkers_per_source walkers from every landmark and from the query (the last token, its
+// row the attention row of current_idx), a start drawn from the source's row over
+// [4, source); then at each position a visit of weight 1 (landmark walkers) or
+// (int)query_boost (query walkers), absorption at [0, 4) (and, absorbing form, with
+// probability 0.1 at another source's landmark), and a step to an earlier position drawn
+// from the query's row (last 64 tokens), the landmark's row (at a landmark) or the H2O
+// scores (elsewhere); a row with no mass jumps a random 2-10 % of the way to the sink.
+__global__ void __launch_bounds__(256) k_lm_walk(const float* __restrict__ pref, int stride,
+                                                 const int32_t* __restrict__ mono,
+                                                 const int32_t* __restrict__ positions,
+                                                 const int32_t* __restrict__ count, int n, int walkers_per_source,
+                                                 float query_boost, int absorbing, int absorb_at_landmarks,
+                                                 uint64_t* __restrict__ states, int32_t* __restrict__ visits) {
+  __shared__ int32_t lm[kLmMaxLandmarks];
+  const int L = *count;
+  if (threadIdx.x < L) lm[threadIdx.x] = positions[threadIdx.x];
+  __syncthreads();
+  const int wk = blockIdx.x * blockDim.x + threadIdx.x;
+  if (wk >= (L + 1) * walkers_per_source) return;
+  const int src = wk / walkers_per_source;
+  const bool is_q = src == L;
+  const int src_lm = is_q ? -1 : src;
+  const int source_pos = is_q ? n - 1 : lm[src];
+  const int32_t weight = (int32_t)(is_q ? query_boost : 1.0f);
+  const int srow = is_q ? 2 : 4 + 2 * src;
+  const float* S = pref + (size_t)srow * stride;
+  MonPcg r{states[2 * wk], states[2 * wk + 1]};
+  float total = source_pos > kMonSink ? S[source_pos] : 0.f;
+  if (total <= 1e-8f) {
+    states[2 * wk] = r.state;
+    states[2 * wk + 1] = r.inc;
+    return;
+  }
+  float target = mon_uniform(r) * total;
+  int pos = lm_first_reach(S, kMonSink, source_pos, target, mono[srow] != 0, kMonSink);
+  const int window_start = max(0, n - kLmWindow);
+  for (int step = 0; step < kMonMaxSteps; ++step) {
+    atomicAdd(&visits[pos], weight);
+    if (pos < kMonSink) break;
+    if (absorbing && absorb_at_landmarks && L > 0) {
+      bool absorbed = false;
+      for (int l = 0; l < L; ++l)
+        if (lm[l] == pos && l != src_lm) {
+          absorbed = mon_uniform(r) < 0.1f;
+          break;
+        }
+      if (absorbed) break;
+    }
+    int row = 0;   // H2O
+    if (pos >= window_start) {
+      row = 1;
+    } else {
+      for (int l = 0; l < L; ++l)
+        if (lm[l] == pos) { row = 3 + 2 * l; break; }
+    }
+    const float* P = pref + (size_t)row * stride;
+    total = P[pos];
+    if (total <= 1e-8f) {
+      const int distance = pos - kMonSink;
+      const int jump = max(1, (int)((float)distance * fmaf(mon_uniform(r), 0.08f, 0.02f)));
+      pos = max(kMonSink, pos - jump);
+      continue;
+    }
+    target = mon_uniform(r) * total;
+    pos = lm_first_reach(P, 0, pos, target, mono[row] != 0, 0);
+  }
+  states[2 * wk] = r.state;
+  states[2 * wk + 1] = r.inc;
+}
+
+// Scores from the visits: mode 0 positional (visits / (1 / d^alpha + 1e-8), d = p - 3;
+// landmark_walker.cu:305-341), 1 reachability (visits / the walkers able to reach p;
+// :255-296), 2 reachability with 0.9 pass-through per landmark (absorbing form;
+// landmark_absorbing_walker.cu:254-309).  [0, 4) scores 0.
+__global__ void __launch_bounds__(256) k_lm_normalize(const int32_t* __restrict__ visits,
+                                                      const int32_t* __restrict__ positions,
+                                                      const int32_t* __restrict__ count, int n, int mode,
+                                                      int walkers_per_source, float query_boost, float alpha,
+                                                      float* __restrict__ scores) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n) return;
+  if (idx < kMonSink) {
+    scores[idx] = 0.f;
+    return;
+  }
+  const int L = *count;
+  const float v = (float)visits[idx];
+  const float wps = (float)walkers_per_source;
+  if (mode == 0) {
+    const float distance = (float)(idx - kMonSink + 1);
+    const float expected = 1.0f / powf(distance, alpha);
+    scores[idx] = v / (expected + 1e-8f);
+    return;
+  }
+  float reach = 0.f;
+  if (mode == 1) {
+    for (int l = 0; l < L; ++l)
+      if (positions[l] > idx) reach += wps;
+    if (n - 1 > idx) reach = fmaf(wps, query_boost, reach);
+    scores[idx] = reach > 1e-8f ? v / reach : 0.f;
+    return;
+  }
+  int after = 0;
+  for (int l = 0; l < L; ++l)
+    if (positions[l] > idx) ++after;
+  if (after > 0) reach = wps * (float)after * 0.9f;
+  if (n - 1 > idx) {
+    float p;
+    if (after == 0) p = 1.0f;
+    else if (after <= 8) {
+      const float decay[9] = {1.0f, 0.9f, 0.81f, 0.729f, 0.656f, 0.590f, 0.531f, 0.478f, 0.430f};
+      p = decay[after];
+    } else {
+      p = fmaxf(0.1f, powf(0.9f, (float)after));
+    }
+    reach = fmaf(wps * query_boost, p, reach);
+  }
+  scores[idx] = reach > 1e-8f ? v / reach : v / ((float)(L + 1) * wps);
+}
+
 // ---- launchers -------------------------------------------------------------------------
 cudaError_t launch_graph_update(const void* q, const void* keys, int dtype, int n, int D, int row, int top_k,
                                 float* scores, int32_t* adj, float* weights, cudaStream_t st) {
@@ -283,6 +570,36 @@ cudaError_t launch_spectral(const int32_t* adj, const float* w, int n, int top_k
 cudaError_t launch_combine(const int32_t* visits, float* spectral, float* walker, float* combined, int n,
                            cudaStream_t st) {
   k_combine<<<1, kMonThreads, 0, st>>>(visits, spectral, walker, combined, n);
+  return cudaGetLastError();
+}
+
+
+size_t landmark_workspace_floats(int n) {
+  const size_t stride = ((size_t)n + 1 + 3) & ~(size_t)3;
+  return ((size_t)n + 3) / 4 * 4 + kLmRows * stride + 128;
+}
+
+cudaError_t launch_landmark_walk(const float* attn, int n, int current_idx, int mode, int num_landmarks,
+                                 int walkers_per_source, float query_boost, int min_spacing, float alpha,
+                                 int absorb_at_landmarks, uint64_t* states, int32_t* visits, float* scores,
+                                 int32_t* positions, int32_t* count, float* ws, cudaStream_t st) {
+  const int stride = (int)(((size_t)n + 1 + 3) & ~(size_t)3);
+  float* h2o = ws;
+  float* pref = ws + ((size_t)n + 3) / 4 * 4;
+  int32_t* mono = reinterpret_cast<int32_t*>(pref + (size_t)kLmRows * stride);
+  cudaError_t e = cudaMemsetAsync(visits, 0, (size_t)n * sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  k_lm_h2o<<<(n + 31) / 32, 256, 0, st>>>(attn, n, h2o);
+  k_lm_select<<<1, 1024, 0, st>>>(h2o, n, num_landmarks, min_spacing, positions, count);
+  k_lm_prefix<<<3 + 2 * num_landmarks, 1024, 0, st>>>(attn, n, current_idx, h2o, positions, count, pref, stride,
+                                                      mono);
+  const long long walkers = (long long)(num_landmarks + 1) * walkers_per_source;
+  if (walkers > 0)
+    k_lm_walk<<<(unsigned)((walkers + 255) / 256), 256, 0, st>>>(pref, stride, mono, positions, count, n,
+                                                                walkers_per_source, query_boost, mode == 2 ? 1 : 0,
+                                                                absorb_at_landmarks, states, visits);
+  k_lm_normalize<<<(n + 255) / 256, 256, 0, st>>>(visits, positions, count, n, mode, walkers_per_source, query_boost,
+                                                  alpha, scores);
   return cudaGetLastError();
 }
 

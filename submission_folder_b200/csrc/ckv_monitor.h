@@ -23,4 +23,13 @@ cudaError_t launch_spectral(const int32_t* adj, const float* w, int n, int top_k
 cudaError_t launch_combine(const int32_t* visits, float* spectral, float* walker, float* combined, int n,
                            cudaStream_t st);
 
+// Landmark walkers: H2O scores, stratified landmarks, walkers from every landmark and the
+// query, normalised scores (mode 0 positional, 1 reachability, 2 absorbing form).  visits
+// [n] cleared first; positions [32], count [1]; ws: landmark_workspace_floats(n) floats.
+size_t landmark_workspace_floats(int n);
+cudaError_t launch_landmark_walk(const float* attn, int n, int current_idx, int mode, int num_landmarks,
+                                 int walkers_per_source, float query_boost, int min_spacing, float alpha,
+                                 int absorb_at_landmarks, uint64_t* states, int32_t* visits, float* scores,
+                                 int32_t* positions, int32_t* count, float* ws, cudaStream_t st);
+
 }  // namespace ckv

@@ -77,7 +77,8 @@ struct Plan {
   size_t off_ph_qrow;  // [H][n] query row
   size_t off_ph_two;   // [H][n] two-hop attention through the window rows
   size_t off_ph_col;   // [H][n] column sums over the window rows
-  size_t off_ph_ent;   // [ncol_tiles][H] query-row entropy partials, then [H] totals
+  size_t off_ph_ent;   // [ph_ent_parts][H] query-row entropy partials, then [H] totals
+  size_t off_ph_part;  // tcgen05 per-head pass: [2][ph_slots][H][n] two-hop / column-sum partials
   size_t off_ph_vec;   // [H][2][nw] finished, truncated, smoothed QI / HI (or H2O)
   size_t off_ph_ghi;   // [nw] rank-normalised mean over heads of HI
   size_t off_ph_gbuf;  // [2][nw] u64 + [nw] int: ranking scratch of the mean HI
@@ -85,6 +86,9 @@ struct Plan {
   size_t off_ph_ranks; // [H][2][nw] int
   size_t off_ph_bits;  // [H][ceil(nw / 32)] keep bits
   int ph_nw;           // n - W
+  int ph_tc;           // 1: per-head pass on tcgen05 (keys-on-lanes form)
+  int ph_slots;        // its partial slots per (head, key): 4 row blocks per 64-row half
+  int ph_ent_parts;    // entropy partials per head: one per 32 keys (tcgen05) or per 64-key tile
   size_t sel_bytes;
   size_t total;
 };

@@ -898,10 +898,10 @@ __global__ void __launch_bounds__(kSelThreads) k_ph_finish(PhArgs a) {
   if (v == 0) {   // the head's query-row entropy: -sum_j p ln(p + 1e-10)
     const float* entp = reinterpret_cast<const float*>(a.ws + pl.off_ph_ent);
     float t = 0.f;
-    for (int i = threadIdx.x; i < pl.ncol_tiles; i += blockDim.x) t += __ldcg(entp + (size_t)i * pl.H + h);
+    for (int i = threadIdx.x; i < pl.ph_ent_parts; i += blockDim.x) t += __ldcg(entp + (size_t)i * pl.H + h);
     t = block_reduce<false>(t, red);
     if (threadIdx.x == 0)
-      reinterpret_cast<float*>(a.ws + pl.off_ph_ent)[(size_t)pl.ncol_tiles * pl.H + h] = -t;
+      reinterpret_cast<float*>(a.ws + pl.off_ph_ent)[(size_t)pl.ph_ent_parts * pl.H + h] = -t;
   }
   if (v == 1 && prm.ablate_qi && prm.ablate_hi) {   // H2O per head: raw column sums
     for (int j = threadIdx.x; j < nw; j += blockDim.x) vec[j] = __ldcg(col + j);
@@ -1035,7 +1035,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_ph_select(PhArgs a) {
   const bool aq = prm.ablate_qi, ah = prm.ablate_hi;
   float wq = 0.5f;
   if (!aq && !ah && prm.entropy_adaptive) {
-    const float* ent = reinterpret_cast<const float*>(a.ws + pl.off_ph_ent) + (size_t)pl.ncol_tiles * pl.H;
+    const float* ent = reinterpret_cast<const float*>(a.ws + pl.off_ph_ent) + (size_t)pl.ph_ent_parts * pl.H;
     float lo = INFINITY, hi = -INFINITY;
     for (int q = 0; q < pl.H; ++q) { const float e = __ldcg(ent + q); lo = fminf(lo, e); hi = fmaxf(hi, e); }
     if (hi > lo) wq = __fsub_rn(1.0f, __fdiv_rn(__fsub_rn(__ldcg(ent + h), lo), __fsub_rn(hi, lo)));

@@ -1018,7 +1018,7 @@ static cudaError_t launch_ph_pass_t(const WinArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_ph_pass(const WinArgs& a, cudaStream_t st) {
+static cudaError_t launch_ph_pass_mma(const WinArgs& a, cudaStream_t st) {
   switch (a.pl.dtype) {
     case CKV_BF16: return launch_ph_pass_t<CKV_BF16>(a, st);
     case CKV_FP16: return launch_ph_pass_t<CKV_FP16>(a, st);
@@ -2280,6 +2280,7 @@ constexpr int kPTThreads = 32 * (kPTEpiWarps + 4);   // as the head-pair form: f
 
 struct PTSmem {
   size_t stage_bytes, off_lse, total;
+  size_t off_q2w = 0;   // per-head pass: q2w re-laid like the log-sum-exp
 };
 
 static __host__ __device__ PTSmem pt_layout(const Plan& pl) {
@@ -2652,6 +2653,330 @@ static cudaError_t launch_tc_pool_lanes(const WinArgs& a, cudaStream_t st) {
     k_tc_pool_lanes<DT, 128><<<grid, kPTThreads, smem, st>>>(tq, tk, a);
   }
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// per-head pass on tcgen05 (PU:2208-2382): the keys-on-lanes form of the pooling pass
+// ---------------------------------------------------------------------------
+// Per step one KV group's 4 heads x RS window rows against a 128-key tile (UMMA M = 128
+// keys on TMEM lanes, N = 4 RS).  A thread owns one key and a quarter of the step's rows;
+// per head it keeps the two-hop sum (q2w-weighted) and the column sum over those rows and
+// writes them, per row block, to partial slots that k_ph_combine adds up in a fixed order.
+// The thread holding the last window row (last quarter of the last half) writes the query
+// row and the query row's entropy partial per 32 keys.  The prelude launch (PRE) runs only
+// the tiles holding the window columns and writes q2w from the same UMMA tiles, so both
+// launches see bit-identical probabilities.
+static __host__ __device__ PTSmem ph_layout(const Plan& pl) {
+  PTSmem L = pt_layout(pl);
+  L.off_q2w = L.total - 1024;
+  L.total += (size_t)pl.H * pl.W * 4;
+  return L;
+}
+
+template <int DT, int WIN, bool PRE>
+__device__ __forceinline__ void tc_ph_body(const CUtensorMap& tmq, const CUtensorMap& tmk, const WinArgs& a) {
+  static_assert(WIN == 32 || WIN == 64 || WIN == 128, "windows of 32, 64 or 128 rows");
+  constexpr int RS = WIN < 64 ? WIN : 64;           // window rows per step
+  constexpr int HALVES = WIN / RS;
+  constexpr int RPQ = RS / 4;                       // rows of a thread's column quarter
+  constexpr int NCH = RPQ / 4;                      // 16-column TMEM loads per quarter
+  constexpr int NCOL = 4 * RS;                      // UMMA N: RS rows x 4 heads
+  constexpr int W = WIN;
+  extern __shared__ char smem_raw[];
+  const Plan& pl = a.pl;
+  Header* hdr = reinterpret_cast<Header*>(a.ws);
+  int32_t* status = &hdr->status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = pl.G, R = G * RS;
+  const int TN = kPTTN, S = kPTStages;
+  const int t_first = PRE ? (pl.n - W) / TN : 0;
+  const int t_end = PRE ? (pl.n - 1) / TN + 1 : (pl.n + TN - 1) / TN;
+  const int ntiles = t_end - t_first;
+  const int ngroups = pl.Hkv;
+  const int nvg = HALVES * ngroups;
+  const PTSmem Ly = ph_layout(pl);
+  char* base = align1024(smem_raw);
+  char* stg = base;
+  const float4* snlse4 = reinterpret_cast<const float4*>(base + Ly.off_lse);
+  const float4* sq2w4 = reinterpret_cast<const float4*>(base + Ly.off_q2w);
+  __shared__ __align__(8) uint64_t bar_ld[kPTStages], bar_sfree[kPTStages], bar_full[2], bar_tfree[2], bar_tile;
+  __shared__ int stage_tile[kPTStages];
+  __shared__ int tile_slot[2];
+  __shared__ volatile int epi_abort;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+  constexpr uint32_t ncols = 2 * NCOL;
+  if (warp == 0) tc::tmem_alloc(&tmem_base_sh, ncols);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) { tc::mbar_init(&bar_ld[i], 1); tc::mbar_init(&bar_sfree[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bar_full[i], 1);
+      tc::mbar_init(&bar_tfree[i], kPTEpiWarps);
+    }
+    tc::mbar_init(&bar_tile, 1);
+    epi_abort = 0;
+    tc::fence_barrier_init();
+    abort_sh = 0;
+  }
+  {   // negated log-sum-exp and (main pass) q2w as [group][window row][head of the group]
+    const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);   // [H][W]
+    const float* q2w = reinterpret_cast<const float*>(a.ws + pl.off_ph_q2w);
+    float* sl = reinterpret_cast<float*>(base + Ly.off_lse);
+    float* sw = reinterpret_cast<float*>(base + Ly.off_q2w);
+    for (int i = threadIdx.x; i < pl.H * W; i += blockDim.x) {
+      const int h = i / W, r = i % W, o = ((h / G) * W + r) * G + (h % G);
+      sl[o] = -__ldcg(lse + i);
+      sw[o] = PRE ? 0.f : __ldcg(q2w + i);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp >= kPTEpiWarps) {
+    tc::reg_dealloc<kPoolProdRegs>();
+  } else {
+    tc::reg_alloc<kPoolEpiRegs>();
+  }
+  if (warp >= kPTEpiWarps) {
+    // ---------------- producer: tiles, TMA loads and UMMA issue (one thread) ----------------
+    if (warp == kPTEpiWarps && lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, NCOL);
+      uint32_t* ctr = &hdr->tile_ctr[PRE ? 1 : 0];
+      int load_tile = -1;
+      int next_tile = t_first + (int)atomicAdd(ctr, 1u);
+      int ld_vg = 0;
+      auto load_step = [&](int s) {
+        const int st = s % S, vg = ld_vg;
+        ld_vg = ld_vg + 1 == nvg ? 0 : ld_vg + 1;
+        const int hf = HALVES > 1 ? vg / ngroups : 0, g = HALVES > 1 ? vg - hf * ngroups : vg;
+        if (vg == 0) {
+          load_tile = next_tile;
+          if (load_tile < t_end) next_tile = t_first + (int)atomicAdd(ctr, 1u);
+        }
+        if (load_tile >= t_end) { stage_tile[st] = -1; return; }
+        stage_tile[st] = load_tile;
+        char* sb = stg + st * Ly.stage_bytes;
+        tc::mbar_expect_tx(&bar_ld[st], (uint32_t)(R * 256 + TN * 256));
+        for (int p = 0; p < 2; ++p)
+          tc::tma_load_3d(sb + p * R * 128, &tmq, &bar_ld[st], p * 64, g * G, pl.n - W + RS * hf);
+        for (int p = 0; p < 2; ++p)
+          tc::tma_load_3d(sb + R * 256 + p * TN * 128, &tmk, &bar_ld[st], p * 64, load_tile * TN, g);
+      };
+      for (int s = 0; s < S; ++s) load_step(s);
+      static_assert(kPTStages == 2, "one descriptor base per stage below");
+      const uint64_t base0 = tc::sw128_kmajor_desc(tc::smem_addr(stg));
+      const uint64_t base1 = tc::sw128_kmajor_desc(tc::smem_addr(stg + Ly.stage_bytes));
+      for (int s = 0, g = 0, k = 0;; ++s) {
+        const int st = s % S, b = s & 1;
+        if (abort_sh) break;
+        if (s >= 2 && !tc::mbar_wait(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
+        const int tile = stage_tile[st];
+        if (g == 0) {
+          tile_slot[k & 1] = tile;
+          tc::mbar_arrive(&bar_tile);
+        }
+        if (++g == nvg) { g = 0; ++k; }
+        if (tile < 0) break;
+        if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        tc::fence_after_sync();
+        const uint64_t sbase = st == 0 ? base0 : base1;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int p = ks >> 2, koff = (ks & 3) * 32;
+          const uint64_t ad = sbase + (uint64_t)((R * 256 + p * TN * 128 + koff) >> 4);   // keys (M)
+          const uint64_t bd = sbase + (uint64_t)((p * R * 128 + koff) >> 4);              // query rows (N)
+          tc::umma_f16(tmem + (uint32_t)(b * NCOL), ad, bd, idesc, ks > 0 ? 1u : 0u);
+        }
+        tc::umma_commit(&bar_full[b]);
+        tc::umma_commit(&bar_sfree[st]);
+        if (!tc::mbar_wait(&bar_sfree[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        load_step(s + S);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: 16 warps ----------------
+    const int lg = warp & 3, q = warp >> 2;             // TMEM lane group (32 keys), column quarter
+    const int key = 32 * lg + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
+    const float rs = 1.0f / sqrtf((float)pl.D);
+    const bool last_row = q == 3;                       // this quarter ends with window row W - 1 ...
+    float* part = reinterpret_cast<float*>(a.ws + pl.off_ph_part);   // [2][slots][H][n]
+    float* qrow = reinterpret_cast<float*>(a.ws + pl.off_ph_qrow);
+    float* q2w = reinterpret_cast<float*>(a.ws + pl.off_ph_q2w);
+    float* entp = reinterpret_cast<float*>(a.ws + pl.off_ph_ent);   // [ph_ent_parts][H]
+    const size_t slot_stride = (size_t)pl.H * pl.n;
+    const int nslots = 4 * HALVES;
+    int tile = -1, vg = 0, hf = 0;
+    auto advance = [&](int& g) {
+      if constexpr (HALVES == 1) {
+        g = g + 1 == ngroups ? 0 : g + 1;
+      } else {
+        vg = vg + 1 == nvg ? 0 : vg + 1;
+        if (++g == ngroups) { g = 0; hf = hf + 1 == HALVES ? 0 : hf + 1; }
+      }
+    };
+    for (int s = 0, g = 0, k = 0; s < ntiles * nvg; ++s, advance(g)) {
+      if (HALVES == 1 ? g == 0 : vg == 0) {   // a new tile
+        bool got = __shfl_sync(0xffffffffu, epi_abort == 0, 0);
+        if (got) got = __all_sync(0xffffffffu, tc::mbar_wait(&bar_tile, k & 1, status));
+        if (!got) {
+          if (lane == 0) { epi_abort = 1; abort_sh = 1; }
+          break;
+        }
+        tile = tile_slot[k & 1];
+        ++k;
+        if (tile < 0) break;
+      }
+      const int j = tile * TN + key;
+      bool ok = !epi_abort;
+      if (ok && !tc::mbar_wait(&bar_full[s & 1], (s >> 1) & 1, status)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) epi_abort = 1;
+      if (!ok) continue;
+      tc::fence_after_sync();
+      const F2 l2e = f2(kLog2e, kLog2e);
+      const uint32_t col0 = (uint32_t)((s & 1) * NCOL + 4 * RPQ * q);
+      const bool edge = tile * TN + TN - 1 > pl.n - W;
+      F2 tw01 = f2(0.f, 0.f), tw23 = tw01, cl01 = tw01, cl23 = tw01, qa01 = tw01, qa23 = tw01;
+      auto chunks = [&](auto etag) {
+        constexpr bool EDGE = decltype(etag)::value;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {   // 16 columns: window rows RS hf + RPQ q + 4 c + i, heads 0..3
+          uint32_t r16[16];
+          __syncwarp();
+          tc::tmem_ld16_nowait(lane_base + col0 + 16 * c, r16);
+          tc::tmem_wait_ld();
+          if (c == NCH - 1) {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bar_tfree[s & 1]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = RS * hf + RPQ * q + 4 * c + i;
+            const float4 nL = snlse4[g * W + r];
+            const F2 x01 = round_f2<DT>(__uint_as_float(r16[4 * i]), __uint_as_float(r16[4 * i + 1]), rs);
+            const F2 x23 = round_f2<DT>(__uint_as_float(r16[4 * i + 2]), __uint_as_float(r16[4 * i + 3]), rs);
+            F2 p01 = ex2_2(fma2(x01, l2e, f2(nL.x, nL.y)));
+            F2 p23 = ex2_2(fma2(x23, l2e, f2(nL.z, nL.w)));
+            if constexpr (EDGE) {
+              if (j > pl.n - W + r) { p01 = f2(0.f, 0.f); p23 = p01; }   // causal mask (and keys past n)
+            }
+            if constexpr (!PRE) {
+              const float4 w4 = sq2w4[g * W + r];
+              tw01 = fma2(p01, f2(w4.x, w4.y), tw01);
+              tw23 = fma2(p23, f2(w4.z, w4.w), tw23);
+              cl01 = add2(cl01, p01);
+              cl23 = add2(cl23, p23);
+            }
+            if (c == NCH - 1 && i == 3) { qa01 = p01; qa23 = p23; }
+          }
+        }
+      };
+      if (edge) chunks(BoolTag<true>{});
+      else chunks(BoolTag<false>{});
+      const int h0 = g * G;
+      const float qa[4] = {f2lo(qa01), f2hi(qa01), f2lo(qa23), f2hi(qa23)};
+      if constexpr (PRE) {
+        if (last_row && hf == HALVES - 1 && j >= pl.n - W && j < pl.n)
+#pragma unroll
+          for (int hd = 0; hd < 4; ++hd) q2w[(size_t)(h0 + hd) * W + (j - (pl.n - W))] = qa[hd];
+      } else {
+        if (j < pl.n) {
+          const int slot = 4 * hf + q;
+          float* pt = part + (size_t)slot * pl.H * pl.n + (size_t)h0 * pl.n + j;
+          float* pc = pt + (size_t)nslots * slot_stride;
+          const float tw[4] = {f2lo(tw01), f2hi(tw01), f2lo(tw23), f2hi(tw23)};
+          const float cl[4] = {f2lo(cl01), f2hi(cl01), f2lo(cl23), f2hi(cl23)};
+#pragma unroll
+          for (int hd = 0; hd < 4; ++hd) {
+            pt[(size_t)hd * pl.n] = tw[hd];
+            pc[(size_t)hd * pl.n] = cl[hd];
+          }
+        }
+        if (last_row && hf == HALVES - 1) {   // warp-uniform
+          const int t32 = tile * 4 + lg;
+#pragma unroll
+          for (int hd = 0; hd < 4; ++hd) {
+            if (j < pl.n) qrow[(size_t)(h0 + hd) * pl.n + j] = qa[hd];
+            const float t = warp_sum(j < pl.n ? qa[hd] * logf(qa[hd] + 1e-10f) : 0.f);
+            if (lane == 0) entp[(size_t)t32 * pl.H + h0 + hd] = t;
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 0) tc::tmem_dealloc(tmem, ncols);
+}
+
+template <int DT, int WIN, bool PRE>
+__global__ void __launch_bounds__(kPTThreads, 1)
+    k_tc_ph(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+            const __grid_constant__ WinArgs a) {
+  tc_ph_body<DT, WIN, PRE>(tmq, tmk, a);
+}
+
+// two / col [H][n] = the sum of the per-head pass's partial slots, in slot order
+__global__ void __launch_bounds__(256) k_ph_combine(WinArgs a) {
+  const Plan& pl = a.pl;
+  const float* part = reinterpret_cast<const float*>(a.ws + pl.off_ph_part);
+  float* two = reinterpret_cast<float*>(a.ws + pl.off_ph_two);
+  float* col = reinterpret_cast<float*>(a.ws + pl.off_ph_col);
+  const size_t total = (size_t)pl.H * pl.n, nsl = (size_t)pl.ph_slots;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    float t = 0.f, c = 0.f;
+    for (size_t k = 0; k < nsl; ++k) {
+      t += __ldcg(part + k * total + i);
+      c += __ldcg(part + (nsl + k) * total + i);
+    }
+    two[i] = t;
+    col[i] = c;
+  }
+}
+
+template <int DT, int WIN>
+static cudaError_t launch_tc_ph_w(const WinArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, cudaStream_t st) {
+  const Plan& pl = a.pl;
+  const size_t smem = ph_layout(pl).total;
+  cudaError_t e = ensure_dynamic_smem((const void*)k_tc_ph<DT, WIN, true>, smem);
+  if (e == cudaSuccess) e = ensure_dynamic_smem((const void*)k_tc_ph<DT, WIN, false>, smem);
+  if (e != cudaSuccess) return e;
+  const int pre = (pl.n - 1) / kPTTN - (pl.n - WIN) / kPTTN + 1;
+  const int ntn = (pl.n + kPTTN - 1) / kPTTN;
+  k_tc_ph<DT, WIN, true><<<pre, kPTThreads, smem, st>>>(tq, tk, a);
+  k_tc_ph<DT, WIN, false><<<ntn < 148 ? ntn : 148, kPTThreads, smem, st>>>(tq, tk, a);
+  return cudaGetLastError();
+}
+
+template <int DT>
+static cudaError_t launch_tc_ph(const WinArgs& a, cudaStream_t st) {
+  const Plan& pl = a.pl;
+  const int rs = pl.W < 64 ? pl.W : 64;
+  CUtensorMap tq, tk;
+  if (!make_tmap_pairs(&tq, a.q, DT, pl.n, pl.H, a.qhs, a.qts, rs, pl.G) ||
+      !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, kPTTN))
+    return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
+  cudaError_t e;
+  if (pl.W == 32) e = launch_tc_ph_w<DT, 32>(a, tq, tk, st);
+  else if (pl.W == 64) e = launch_tc_ph_w<DT, 64>(a, tq, tk, st);
+  else e = launch_tc_ph_w<DT, 128>(a, tq, tk, st);
+  if (e != cudaSuccess) return e;
+  const size_t total = (size_t)pl.H * pl.n;
+  const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+  k_ph_combine<<<blocks, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// per-head pass: tcgen05 keys-on-lanes form where the plan allows it, else mma.sync / SIMT
+cudaError_t launch_ph_pass(const WinArgs& a, cudaStream_t st) {
+  if (a.pl.ph_tc) return a.pl.dtype == CKV_BF16 ? launch_tc_ph<CKV_BF16>(a, st) : launch_tc_ph<CKV_FP16>(a, st);
+  return launch_ph_pass_mma(a, st);
 }
 
 // ---------------------------------------------------------------------------

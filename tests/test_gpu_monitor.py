@@ -36,6 +36,8 @@ def _ref():
     lib.ref_init_rng.argtypes = [vp, u64, i32, vp]
     lib.ref_circuit_walk.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, vp]
     lib.ref_spectral_combined.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp, vp, vp, vp, vp]
+    f32 = ctypes.c_float
+    lib.ref_landmark_walk.argtypes = [vp, i32, i32, i32, i32, i32, f32, i32, f32, i32, vp, vp, vp, vp, vp, vp, vp]
     return lib
 
 
@@ -134,8 +136,6 @@ def test_circuit_graph_and_monitor_api():
     assert float(g.get_scores().sum().item()) == 0.0
     with pytest.raises(RuntimeError):
         g.update_and_step_circuit(torch.rand(128, device=dev), keys[:10].float().cpu(), 9)
-    with pytest.raises(NotImplementedError):
-        g.update_and_step_landmark_walker(torch.rand(8, 8, device=dev), 7, 4, 10, 2.0, 2, 0.6, False)
     # the monitor on top: prefill charge, then the EMA of the circuit current
     mon = CircuitKVMonitor(CircuitKVConfig(max_seq_len=512, top_k=16, num_walkers=512))
     attn = torch.rand(n, n, device=dev)
@@ -148,3 +148,102 @@ def test_circuit_graph_and_monitor_api():
     torch.testing.assert_close(after, expect)
     m = mon.get_keep_mask(0.5, n)
     assert int(m.sum().item()) == n // 2 and bool(m[:4].all()) and bool(m[n - 64:].all())
+
+
+def _causal_attention(dev, n, seed, zero_cols=0, negative=False):
+    """Softmax rows of random logits under a causal mask (row i over keys [0, i]); optionally
+    the first zero_cols columns zeroed (rows without mass there, so walkers jump) or a few
+    negative entries (running sums not monotone)."""
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(n, n, generator=g) * 2.0
+    logits = logits.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
+    a = torch.softmax(logits, dim=-1)
+    if zero_cols:
+        a[:, :zero_cols] = 0.0
+    if negative:
+        idx = torch.randint(0, n, (n // 4, 2), generator=g)
+        a[idx[:, 0], idx[:, 1]] = -1e-3
+    return a.contiguous().to(dev)
+
+
+LANDMARK_CASES = [
+    # n, mode (0 positional, 1 reachability, 2 absorbing), landmarks, walkers/source, boost, spacing, alpha, absorb, kind
+    (700, 0, 32, 100, 2.0, 50, 0.6, 0, "plain"),
+    (900, 1, 16, 37, 1.3, 20, 0.6, 0, "plain"),
+    (1024, 2, 8, 100, 2.0, 50, 0.0, 1, "plain"),
+    (800, 2, 12, 50, 3.7, 10, 0.0, 0, "plain"),
+    (600, 1, 8, 64, 2.0, 50, 0.6, 0, "zero_cols"),
+    (640, 0, 8, 64, 2.5, 30, 0.8, 0, "negative"),
+    (80, 1, 8, 64, 2.0, 50, 0.6, 0, "plain"),          # shorter than 89: no landmarks
+]
+
+
+@pytest.mark.parametrize("case", LANDMARK_CASES, ids=[f"n{c[0]}_m{c[1]}_{c[8]}" for c in LANDMARK_CASES])
+def test_landmark_walk_matches_reference(case):
+    n, mode, L, wps, boost, spacing, alpha, absorb, kind = case
+    dev = _cuda()
+    lib, ref = _lib.load(), _ref()
+    a = _causal_attention(dev, n, seed=n + mode, zero_cols=40 if kind == "zero_cols" else 0,
+                          negative=kind == "negative")
+    walkers = (L + 1) * wps
+    st = torch.zeros(2 * walkers, dtype=torch.int64, device=dev)
+    assert lib.ckv_pcg_seed(42 + 1000, walkers, st.data_ptr(), _st(dev)) == 0
+    rst = st.clone()
+    sz = ctypes.c_size_t()
+    assert lib.ckv_landmark_workspace_size(n, ctypes.byref(sz)) == 0
+    ws = torch.zeros(sz.value, dtype=torch.uint8, device=dev)
+    mine = dict(v=torch.zeros(n, dtype=torch.int32, device=dev), s=torch.zeros(n, device=dev),
+                p=torch.zeros(32, dtype=torch.int32, device=dev), c=torch.zeros(1, dtype=torch.int32, device=dev))
+    theirs = {k: torch.zeros_like(t) for k, t in mine.items()}
+    rh2o = torch.zeros(n, device=dev)
+    for call in range(2):   # PCG states carried over
+        assert lib.ckv_landmark_walk(a.data_ptr(), n, n - 1, mode, L, wps, boost, spacing, alpha, absorb,
+                                     st.data_ptr(), mine["v"].data_ptr(), mine["s"].data_ptr(), mine["p"].data_ptr(),
+                                     mine["c"].data_ptr(), ws.data_ptr(), ws.numel(), _st(dev)) == 0
+        assert ref.ref_landmark_walk(a.data_ptr(), n, n - 1, mode, L, wps, boost, spacing, alpha, absorb,
+                                     rst.data_ptr(), theirs["v"].data_ptr(), theirs["s"].data_ptr(),
+                                     theirs["p"].data_ptr(), theirs["c"].data_ptr(), rh2o.data_ptr(), _st(dev)) == 0
+        torch.cuda.synchronize()
+        k = int(theirs["c"].item())
+        assert int(mine["c"].item()) == k, call
+        assert torch.equal(mine["p"][:k], theirs["p"][:k]), call
+        assert torch.equal(ws[: 4 * n].view(torch.float32), rh2o), call      # H2O scores
+        assert torch.equal(mine["v"], theirs["v"]), (call, int((mine["v"] != theirs["v"]).sum()))
+        assert torch.equal(st, rst), call
+        assert torch.equal(mine["s"], theirs["s"]), call
+    if n >= 89:
+        assert k >= 1
+    else:
+        assert k == 0
+    assert int(mine["v"].sum().item()) > 0
+
+
+def test_landmark_methods_of_circuit_graph():
+    dev = _cuda()
+    n = 512
+    a = _causal_attention(dev, n, seed=5)
+    g = _C.CircuitGraph(1024, 16, 0.85, 1024, 100)
+    assert g.get_landmark_positions().numel() == 0
+    g.update_and_step_landmark_walker(a, n - 1)
+    sc = g.get_landmark_scores()
+    pos = g.get_landmark_positions()
+    assert sc.shape == (n,) and float(sc[:4].abs().sum().item()) == 0.0 and float(sc.max().item()) > 0
+    assert pos.numel() >= 1 and bool((pos[1:] > pos[:-1]).all()) and int(pos.min()) >= 24 and int(pos.max()) < n - 64
+    g.update_and_step_landmark_absorbing_walker(a, n - 1, num_landmarks=8)
+    raw = g.get_landmark_absorbing_raw_visits()
+    assert raw.dtype == torch.int32 and raw.shape == (n,) and int(raw.sum().item()) > 0
+    assert g.get_landmark_absorbing_scores().shape == (n,)
+    with pytest.raises(RuntimeError):
+        g.update_and_step_landmark_walker(a, n - 1, num_landmarks=33)
+    with pytest.raises(RuntimeError):
+        g.update_and_step_landmark_walker(a, n - 1, num_landmarks=32, walkers_per_source=600)
+    with pytest.raises(RuntimeError):
+        g.update_and_step_landmark_walker(a.half(), n - 1)
+    # the monitor on top
+    from submission_folder_b200.circuit_kv import LandmarkWalkerConfig, LandmarkWalkerMonitor
+    mon = LandmarkWalkerMonitor(LandmarkWalkerConfig(max_seq_len=1024))
+    mon.update(a, n - 1)
+    s = mon.get_scores()
+    assert s.shape == (n,) and float(s.max().item()) > 0
+    m = mon.get_keep_mask(0.5, n)
+    assert int(m.sum().item()) == n // 2

@@ -358,6 +358,28 @@ def test_per_head_fp32_ragged():
     assert ops.read_status(dev) == 0
 
 
+@pytest.mark.parametrize("n,W,dtype", [(3001, 32, "bf16"), (5000, 128, "bf16"), (4222, 64, "fp16")])
+def test_per_head_tensor_core_windows(n, W, dtype):
+    """The tcgen05 per-head pass for windows of 32, 64 and 128 rows (ragged n, the last key
+    tile partly past n): kept sets per head exactly the oracle's."""
+    dev = _cuda()
+    from submission_folder_b200.synth import make_layer
+    q, k, v = make_layer(n, seed=n, window=W, dtype=dtype)
+    kwargs = dict(window_size=W, max_capacity_prompt=512, per_head_eviction=True, qi_kernel_size=3,
+                  hi_kernel_size=5, use_gaussian=True)
+    cl = CircuitKVCluster(**kwargs)
+    K, V = repeat_kv(k, 4).to(dev), repeat_kv(v, 4).to(dev)
+    cl.update_kv(K, q[None].to(dev), V, None, 4)
+    torch.cuda.synchronize()
+    idx = cl.last_keep_indices.cpu().numpy()
+    op = O.Params(**kwargs)
+    attn = O.window_attention(q.float().numpy(), k.float().numpy(), W, 4, dtype)
+    oidx = O.per_head_select(attn, op, n)
+    d = [len(set(idx[h].tolist()) ^ set(oidx[h].tolist())) for h in range(32)]
+    assert max(d) == 0, d
+    assert ops.read_status(dev) == 0
+
+
 @pytest.mark.parametrize("n,W", [(4460, 64), (11554, 64), (4466, 32)])
 def test_moments_chunk_of_one_masked_tile(n, W, parity_report):
     """Lengths where a moments-pass CTA gets only the last, partly masked key tile:
