@@ -121,8 +121,11 @@ typedef struct ckv_layer {
 /* Outputs of one layer.  out_k / out_v: contiguous [H, out_len, D] in the input
  * dtype.  out_idx: the kept prefix positions in ascending order (sinks
  * included, local window excluded) -- [out_len - W] for shared eviction,
- * [H, out_len - W] for per-head eviction.  out_scores (optional, may be NULL):
- * fp32 [n] combined score of every position (shared eviction only).
+ * [H, out_len - W] for per-head eviction.  out_scores (optional, may be NULL): the
+ * vectors the selection ranks, fp32.  Shared eviction: [2, n], the two smoothed vectors
+ * (QI / HI for dis / union, influence / H2O for max / weighted).  Per-head eviction:
+ * [H, 2, n - W] per head the finished, smoothed QI and HI vectors (HI: the raw window-row
+ * column sums, H2O, when both are ablated), then [H] the query rows' entropies.
  * distinct_kv_heads: 0 (zero-initialised callers) writes the reference's layout, every
  * query head its KV head's rows (repeat_kv, llama_model.py:2918-2928); 1 writes each
  * DISTINCT KV head once, out_k / out_v [num_kv_heads, out_len, D] -- a quarter of the

@@ -612,10 +612,11 @@ def per_head_importance(attn: np.ndarray, p: Params):
     return out[0], out[1]
 
 
-def per_head_select(attn: np.ndarray, p: Params, n: int):
-    """PU:3296-3446: per-head index sets (sorted ascending), excluding the local window."""
+def per_head_vectors(attn: np.ndarray, p: Params, n: int):
+    """PU:3296-3400: the per-head vectors the selection ranks, ``[H, 2, n - W]`` (QI and HI
+    truncated to n - W and smoothed; with both ablations the second is the raw column sum
+    over the window rows, H2O), and the query rows' entropies ``[H]``."""
     H, W, _ = attn.shape
-    s = p.sink_size
     qi, hi = per_head_importance(attn, p)
     nw = n - W
     qi, hi = qi[:, :nw], hi[:, :nw]
@@ -623,28 +624,44 @@ def per_head_select(attn: np.ndarray, p: Params, n: int):
     if ksz > 1:
         qi = np.stack([smooth(qi[h], ksz, True, p.gaussian_sigma) for h in range(H)])
         hi = np.stack([smooth(hi[h], ksz, True, p.gaussian_sigma) for h in range(H)])
+    if p.ablate_hi and p.ablate_qi:
+        hi = attn[:, :, :nw].sum(axis=1, dtype=F32)
+    qa = attn[:, -1, :]
+    ent = -(qa * np.log(qa + F32(1e-10))).sum(axis=-1, dtype=F32)
+    return np.stack([qi, hi], axis=1).astype(F32), ent.astype(F32)
+
+
+def per_head_scores_from(vec: np.ndarray, ent: np.ndarray, p: Params) -> np.ndarray:
+    """PU:3400-3446: the per-head combined scores ``[H, nw]`` from the ranked vectors
+    ``vec [H, 2, nw]`` and the query-row entropies ``ent [H]``."""
+    H = vec.shape[0]
+    qi, hi = vec[:, 0], vec[:, 1]
     qr = np.stack([rank_normalize(qi[h]) for h in range(H)])
     hr = np.stack([rank_normalize(hi[h]) for h in range(H)])
     if p.ablate_hi and not p.ablate_qi:
-        sc = qr
-    elif p.ablate_qi and not p.ablate_hi:
+        return qr
+    if p.ablate_qi and not p.ablate_hi:
         ghi = rank_normalize(hi.mean(axis=0, dtype=F32).astype(F32))
-        sc = np.broadcast_to(ghi, qr.shape)
-    elif p.ablate_hi and p.ablate_qi:
-        h2o = attn[:, :, :nw].sum(axis=1, dtype=F32)
-        sc = np.stack([rank_normalize(h2o[h]) for h in range(H)])
-    elif p.entropy_adaptive:
-        qa = attn[:, -1, :]
-        ent = -(qa * np.log(qa + F32(1e-10))).sum(axis=-1, dtype=F32)
+        return np.broadcast_to(ghi, qr.shape)
+    if p.ablate_hi and p.ablate_qi:
+        return hr
+    if p.entropy_adaptive:
         lo, hi_e = ent.min(), ent.max()
         if hi_e > lo:
             w = (F32(1.0) - (ent - lo) / (hi_e - lo)).astype(F32)
         else:
             w = np.full(H, F32(0.5), dtype=F32)
-        sc = (w[:, None] * qr + (F32(1.0) - w[:, None]) * hr).astype(F32)
-    else:
-        ghi = rank_normalize(hi.mean(axis=0, dtype=F32).astype(F32))
-        sc = np.maximum(qr, ghi[None, :])
+        return (w[:, None] * qr + (F32(1.0) - w[:, None]) * hr).astype(F32)
+    ghi = rank_normalize(hi.mean(axis=0, dtype=F32).astype(F32))
+    return np.maximum(qr, ghi[None, :])
+
+
+def per_head_select_from(vec: np.ndarray, ent: np.ndarray, p: Params, n: int):
+    """PU:3400-3446: per-head index sets (sorted ascending) from the ranked vectors."""
+    H, _, nw = vec.shape
+    s = p.sink_size
+    W = n - nw
+    sc = per_head_scores_from(vec, ent, p)
     budget = p.max_capacity_prompt - W - s
     middle = nw - s
     sinks = np.arange(s)
@@ -654,6 +671,12 @@ def per_head_select(attn: np.ndarray, p: Params, n: int):
                for h in range(H)]
         return np.stack(idx)
     return np.stack([sinks for _ in range(H)])
+
+
+def per_head_select(attn: np.ndarray, p: Params, n: int):
+    """PU:3296-3446: per-head index sets (sorted ascending), excluding the local window."""
+    vec, ent = per_head_vectors(attn, p, n)
+    return per_head_select_from(vec, ent, p, n)
 
 
 # --------------------------------------------------------------------------

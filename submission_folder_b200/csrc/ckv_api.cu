@@ -262,6 +262,14 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
     ph.eh = (float)pow((double)p->hi_gamma, pl.K / 2.0);
     e = launch_ph_select(ph, st);
     if (e != cudaSuccess) return cuda_fail(e, "per-head selection");
+    if (out->out_scores) {   // [H][2][n - W] ranked vectors, then [H] entropies
+      const size_t nv = (size_t)pl.H * 2 * pl.ph_nw;
+      e = cudaMemcpyAsync(out->out_scores, ws + pl.off_ph_vec, nv * 4, cudaMemcpyDeviceToDevice, st);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(out->out_scores + nv, ws + pl.off_ph_ent + (size_t)pl.ph_ent_parts * pl.H * 4,
+                            (size_t)pl.H * 4, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_fail(e, "per-head score copy");
+    }
     return launch_gather_layer(pl, L, out, out->out_idx, 0, st);
   }
   for (int s = 0; s < 3; ++s) {

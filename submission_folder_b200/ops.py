@@ -112,7 +112,8 @@ def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     is ``[B-W]`` int32 (shared eviction) or ``[H, B-W]`` (per-head eviction).
 
     ``scores`` (when requested) is ``[2, n]`` fp32: the two vectors ranked by the
-    selection (QI / HI after smoothing for "dis"; influence / H2O for "max").
+    selection (QI / HI after smoothing for "dis"; influence / H2O for "max"); with per-head
+    eviction ``(vectors [H, 2, n - W], entropies [H])``.
     ``distinct_kv_heads``: K / V outputs hold each KV head once, ``[Hkv, B, D]``.
     """
     _require_cuda(q, k)
@@ -125,7 +126,9 @@ def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     k_out = torch.empty(ho, out_len, D, dtype=q.dtype, device=dev)
     v_out = torch.empty(ho, out_len, D, dtype=q.dtype, device=dev)
     idx = _index_tensor(p, H, out_len, dev)
-    scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
+    per_head = bool(p.per_head_eviction) and n >= p.max_capacity_prompt
+    nsc = H * 2 * (n - p.window_size) + H if per_head else 2 * n
+    scores = torch.empty(nsc, dtype=torch.float32, device=dev) if want_scores else None
     ws = workspace(workspace_size(p, n, H, k.shape[0], D), dev)
     O = Outputs()
     O.out_k, O.out_v, O.out_idx, O.out_scores = k_out.data_ptr(), v_out.data_ptr(), idx.data_ptr(), _ptr(scores)
@@ -134,7 +137,17 @@ def score_evict(p: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                                       ws.numel(), ctypes.byref(O), _stream(dev)), "ckv_score_evict")
     if n < p.max_capacity_prompt:
         idx = torch.arange(max(n - p.window_size, 0), dtype=torch.int32, device=dev)
-    return k_out, v_out, idx, scores
+    return k_out, v_out, idx, _shape_scores(scores, p, H, n)
+
+
+def _shape_scores(scores: Optional[torch.Tensor], p: Params, H: int, n: int):
+    """The flat out_scores buffer as ``[2, n]``, or per head ``([H, 2, n - W], [H])``."""
+    if scores is None:
+        return None
+    if bool(p.per_head_eviction) and n >= p.max_capacity_prompt:
+        nw = n - p.window_size
+        return scores[:H * 2 * nw].view(H, 2, nw), scores[H * 2 * nw:]
+    return scores.view(2, n)
 
 
 def score_evict_batched(params, layers, want_scores: bool = False):
@@ -164,7 +177,9 @@ def score_evict_batched(params, layers, want_scores: bool = False):
         k_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
         v_out = torch.empty(H, out_len, D, dtype=q.dtype, device=dev)
         idx = _index_tensor(p, H, out_len, dev)
-        scores = torch.empty(2, n, dtype=torch.float32, device=dev) if want_scores else None
+        per_head = bool(p.per_head_eviction) and n >= p.max_capacity_prompt
+        nsc = H * 2 * (n - p.window_size) + H if per_head else 2 * n
+        scores = torch.empty(nsc, dtype=torch.float32, device=dev) if want_scores else None
         Os[i].out_k, Os[i].out_v, Os[i].out_idx, Os[i].out_scores = (k_out.data_ptr(), v_out.data_ptr(),
                                                                      idx.data_ptr(), _ptr(scores))
         results.append([k_out, v_out, idx, scores, n, p])
@@ -177,7 +192,7 @@ def score_evict_batched(params, layers, want_scores: bool = False):
     for k_out, v_out, idx, scores, n, p in results:
         if n < p.max_capacity_prompt:
             idx = torch.arange(max(n - p.window_size, 0), dtype=torch.int32, device=dev)
-        out.append((k_out, v_out, idx, scores))
+        out.append((k_out, v_out, idx, _shape_scores(scores, p, k_out.shape[0], n)))
     return out
 
 

@@ -116,3 +116,63 @@ def check_kept(name, idx, sc, ref_keep, ref_combined, ref_a, ref_b, op, n, exact
                         "exact_arithmetic_inputs": bool(exact)}
     assert ties_only, f"{name}: {nd} kept positions differ beyond exact ties of the k-th combined score"
     return nd, ties_only
+
+
+PH_VEC_RTOL = SCORE_RTOL   # per-head vectors vs the oracle's: max abs difference / max |oracle| per head
+
+
+def check_per_head(idx, vec, ent, attn, op, n, report=None, key=None):
+    """Decomposed parity of per-head eviction (PU:3296-3446) against the oracle:
+
+    1. the selection is exact: the oracle's selection rule applied to the device's own ranked
+       vectors and entropies gives exactly the device's kept set, head by head;
+    2. the device's vectors and entropies equal the oracle's within ``PH_VEC_RTOL``;
+    3. the kept sets equal the oracle's, except in a head whose oracle vectors hold a near tie
+       at the kept boundary: two values closer than twice the head's measured vector
+       difference (so that the device's rounding -- a 16-bit logit rounded after a different
+       fp32 accumulation order, a different summation order -- can order them the other
+       way), one of them at a position whose oracle score lies within two rank steps of the
+       head's k-th score; every differing position must lie within those two rank steps.
+    Returns the number of differing positions per head."""
+    idx = np.asarray(idx)
+    vec = np.asarray(vec, dtype=np.float32)
+    ent = np.asarray(ent, dtype=np.float32)
+    own = O.per_head_select_from(vec, ent, op, n)
+    for h in range(idx.shape[0]):
+        assert set(own[h].tolist()) == set(idx[h].tolist()), ("selection not exact", h)
+    ovec, oent = O.per_head_vectors(attn, op, n)
+    abs_err = np.zeros((ovec.shape[0], 2))
+    for h in range(ovec.shape[0]):
+        for v in range(2):
+            scale = max(float(np.abs(ovec[h, v]).max()), 1e-30)
+            abs_err[h, v] = float(np.abs(vec[h, v].astype(np.float64) - ovec[h, v]).max())
+            assert abs_err[h, v] / scale <= PH_VEC_RTOL, ("vector", h, v, abs_err[h, v] / scale)
+    np.testing.assert_allclose(ent, oent, rtol=PH_VEC_RTOL, atol=1e-6)
+    oidx = O.per_head_select_from(ovec, oent, op, n)
+    osc = O.per_head_scores_from(ovec, oent, op)
+    nw = ovec.shape[2]
+    s = op.sink_size
+    step = 1.0 / max(nw - 1, 1)
+    diffs = []
+    for h in range(idx.shape[0]):
+        d = set(idx[h].tolist()) ^ set(oidx[h].tolist())
+        diffs.append(len(d))
+        if not d:
+            continue
+        kept = [j for j in oidx[h].tolist() if j >= s]
+        T = float(osc[h, kept].min())
+        near = [j for j in d if abs(float(osc[h, j]) - T) <= 2 * step + 1e-7]
+        assert len(near) == len(d), ("difference away from the kept boundary", h, sorted(d), T)
+        boundary = np.where(np.abs(osc[h].astype(np.float64) - T) <= 2 * step + 1e-7)[0]
+        tie = False
+        for v in range(2):
+            x = ovec[h, v].astype(np.float64)
+            order = np.argsort(x, kind="stable")
+            gaps = np.diff(x[order]) <= 2 * abs_err[h, v] + 1e-12
+            pairs = set(order[:-1][gaps].tolist()) | set(order[1:][gaps].tolist())
+            if pairs & set(boundary.tolist()):
+                tie = True
+        assert tie, ("difference without a near tie at the kept boundary", h, sorted(d))
+    if report is not None and key is not None:
+        report[key] = {"n": int(n), "kept_per_head": int(idx.shape[1]), "differ_per_head": diffs}
+    return diffs

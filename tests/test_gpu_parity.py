@@ -16,7 +16,7 @@ import pytest
 import torch
 
 import ckv_oracle as O
-from _golden import (case, cases, check_kept, compare_keep, inputs, load, oracle_params,
+from _golden import (case, cases, check_kept, check_per_head, compare_keep, inputs, load, oracle_params,
                      ranked_vectors_of_reference)
 from submission_folder_b200 import ops
 from submission_folder_b200.cluster import CircuitKVCluster
@@ -302,7 +302,10 @@ def _per_head_run(c, kwargs, dev):
         assert torch.equal(ko[0, h, :nk], K[0, h, hk[h]])
         assert torch.equal(vo[0, h, :nk], V[0, h, hk[h]])
         assert torch.equal(ko[0, h, nk:], K[0, h, c["n"] - c["window"]:])
-    return q, k, idx
+    # the same call through ops, with the ranked vectors: deterministic kept sets
+    _, _, idx2, (vec, ent) = ops.score_evict(cl.params(c["n"]), q.to(dev), k.to(dev), v.to(dev), want_scores=True)
+    assert np.array_equal(idx2.cpu().numpy(), idx)
+    return q, k, idx, vec.cpu().numpy(), ent.cpu().numpy()
 
 
 @pytest.mark.parametrize("name", ["bf16_perhead", "bf16_perhead_hub", "grid_bf16_perhead", "bf16_perhead_n8192"])
@@ -312,7 +315,7 @@ def test_per_head_matches_reference(name, parity_report):
     dev = _cuda()
     c = case(name)
     g = load(name)
-    _, _, idx = _per_head_run(c, c["kwargs"], dev)
+    _, _, idx, _, _ = _per_head_run(c, c["kwargs"], dev)
     ref = g["keep_per_head"]
     assert idx.shape == ref.shape
     d = [len(set(idx[h].tolist()) ^ set(ref[h].tolist())) for h in range(ref.shape[0])]
@@ -324,19 +327,18 @@ def test_per_head_matches_reference(name, parity_report):
 @pytest.mark.parametrize("extra", [dict(ablate_qi=True), dict(ablate_hi=True),
                                    dict(ablate_qi=True, ablate_hi=True), dict(entropy_adaptive=False),
                                    dict(smoothing_kernel=3), dict(true_hub_hi=True, entropy_adaptive=False)])
-def test_per_head_variants_match_oracle(extra):
+def test_per_head_variants_match_oracle(extra, parity_report):
+    """Ablations and variants: decomposed parity against the oracle (``check_per_head``)."""
     dev = _cuda()
     c = case("bf16_perhead")
     kwargs = dict(c["kwargs"], **extra)
-    q, k, idx = _per_head_run(c, kwargs, dev)
+    q, k, idx, vec, ent = _per_head_run(c, kwargs, dev)
     op = oracle_params(dict(c, kwargs=kwargs))
     attn = O.window_attention(q.float().numpy(), k.float().numpy(), c["window"], 4, c["dtype"])
-    oidx = O.per_head_select(attn, op, c["n"])
-    d = [len(set(idx[h].tolist()) ^ set(oidx[h].tolist())) for h in range(oidx.shape[0])]
-    assert max(d) == 0, (extra, d)
+    check_per_head(idx, vec, ent, attn, op, c["n"], parity_report, "per_head_variant_" + "_".join(sorted(extra)))
 
 
-def test_per_head_fp32_ragged():
+def test_per_head_fp32_ragged(parity_report):
     """fp32 inputs, W = 32, n not a multiple of the column tile."""
     dev = _cuda()
     torch.manual_seed(3)
@@ -350,18 +352,17 @@ def test_per_head_fp32_ragged():
     ko, vo = cl.update_kv(K, q[None].to(dev), V, None, 4)
     torch.cuda.synchronize()
     idx = cl.last_keep_indices.cpu().numpy()
+    _, _, _, (vec, ent) = ops.score_evict(cl.params(n), q.to(dev), k.to(dev), v.to(dev), want_scores=True)
     op = O.Params(**kwargs)
     attn = O.window_attention(q.numpy(), k.numpy(), W, 4, "fp32")
-    oidx = O.per_head_select(attn, op, n)
-    d = [len(set(idx[h].tolist()) ^ set(oidx[h].tolist())) for h in range(32)]
-    assert max(d) == 0, d
+    check_per_head(idx, vec.cpu().numpy(), ent.cpu().numpy(), attn, op, n, parity_report, "per_head_fp32_ragged")
     assert ops.read_status(dev) == 0
 
 
 @pytest.mark.parametrize("n,W,dtype", [(3001, 32, "bf16"), (5000, 128, "bf16"), (4222, 64, "fp16")])
-def test_per_head_tensor_core_windows(n, W, dtype):
+def test_per_head_tensor_core_windows(n, W, dtype, parity_report):
     """The tcgen05 per-head pass for windows of 32, 64 and 128 rows (ragged n, the last key
-    tile partly past n): kept sets per head exactly the oracle's."""
+    tile partly past n): decomposed parity against the oracle (``check_per_head``)."""
     dev = _cuda()
     from submission_folder_b200.synth import make_layer
     q, k, v = make_layer(n, seed=n, window=W, dtype=dtype)
@@ -372,11 +373,11 @@ def test_per_head_tensor_core_windows(n, W, dtype):
     cl.update_kv(K, q[None].to(dev), V, None, 4)
     torch.cuda.synchronize()
     idx = cl.last_keep_indices.cpu().numpy()
+    _, _, _, (vec, ent) = ops.score_evict(cl.params(n), q.to(dev), k.to(dev), v.to(dev), want_scores=True)
     op = O.Params(**kwargs)
     attn = O.window_attention(q.float().numpy(), k.float().numpy(), W, 4, dtype)
-    oidx = O.per_head_select(attn, op, n)
-    d = [len(set(idx[h].tolist()) ^ set(oidx[h].tolist())) for h in range(32)]
-    assert max(d) == 0, d
+    check_per_head(idx, vec.cpu().numpy(), ent.cpu().numpy(), attn, op, n, parity_report,
+                   f"per_head_tc_{dtype}_w{W}_n{n}")
     assert ops.read_status(dev) == 0
 
 
