@@ -87,8 +87,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override the workload's layer count")
     ap.add_argument("--pyramid", action="store_true", help="config 3: budget 4096 -> 512 over the layers")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong")
-    ap.add_argument("--qk", choices=["unit", "literal"], default="unit",
-                    help="Q/K component scale: unit (logits ~ N(0,1)) or literal N(0,1)/sqrt(128)")
+    ap.add_argument("--qk", choices=["unit", "literal"], default="literal",
+                    help="Q/K component scale: literal N(0,1)/sqrt(128) (the workloads' generator) or "
+                         "unit (logits ~ N(0,1))")
     ap.add_argument("--min-timed-s", type=float, default=1.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
