@@ -62,6 +62,28 @@ def philox4x64_10(ctr, key):
     return c
 
 
+class PhiloxWalker:
+    """A walker's counter-based uniforms (the library's Philox mode): draw d of walker w
+    in call c is word d % 4 of Philox4x64-10(counter (d // 4, w, c, 0), key (seed, 0)),
+    its top 24 bits times 2^-24."""
+
+    def __init__(self, seed: int, walker: int, call: int = 0):
+        self.key = (seed & MASK64, 0)
+        self.walker, self.call, self.draw = walker, call, 0
+        self.blk = None
+
+    def uniform(self) -> np.float32:
+        if self.draw % 4 == 0:
+            self.blk = philox4x64_10((self.draw // 4, self.walker, self.call, 0), self.key)
+        bits = self.blk[self.draw % 4] >> 40
+        self.draw += 1
+        return np.float32(bits) * np.float32(1.0 / 16777216.0)
+
+
+def philox_walkers(seed: int, num_walkers: int, call: int = 0):
+    return [PhiloxWalker(seed, w, call) for w in range(num_walkers)]
+
+
 def philox_stream(seed: int, stream_id: int, count: int):
     """The library's ckv_rng_fill(PHILOX) layout: block b = counter (b, stream, 0, 0)."""
     out = []

@@ -141,6 +141,56 @@ __global__ void __launch_bounds__(256) k_walk_dense(const WalkArgs a) {
   walker_store(a, w, g);
 }
 
+// ---- dense walker, one warp per walker (Philox mode) ----------------------------
+// The same walk with the row work spread over the warp: lanes read 32 consecutive weights
+// at a time (coalesced), the row total is a warp sum, and the sampled position is found by
+// a warp prefix scan per 32-position block with a ballot on the first crossing.  The
+// random draws are the thread-per-walker kernel's (lane 0 holds the counter-based
+// generator, so the draw sequence of each walker is the same); only the order of the fp32
+// additions differs, so a step can land one position over where a running sum crosses the
+// target within its rounding.  PCG mode keeps k_walk_dense: there the visit counts must be
+// the reference's bit for bit, which needs its sequential sums.
+constexpr int kWalkWarps = 8;
+__global__ void __launch_bounds__(32 * kWalkWarps) k_walk_dense_warp(const WalkArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int w = blockIdx.x * kWalkWarps + (threadIdx.x >> 5);
+  if (w >= a.num_walkers) return;   // warp-uniform
+  WalkRng g = walker_rng(a, w);
+  float it = 0.f;
+  int pos = 0;
+  if (lane == 0) pos = walker_start(a, w, g, &it);
+  pos = __shfl_sync(0xffffffffu, pos, 0);
+  it = __shfl_sync(0xffffffffu, it, 0);
+  for (int step = 0; step < a.max_steps; ++step) {
+    if (pos < a.sink) break;
+    const float* row = a.attn + (size_t)pos * a.n;
+    float part = 0.f;
+    for (int j = a.sink + lane; j <= pos; j += 32) part += __powf(fmaxf(__ldg(row + j), 1e-10f), it);
+    const float sum = warp_sum(part);
+    if (sum < 1e-10f) break;
+    float r = 0.f;
+    if (lane == 0) r = g.uniform() * sum;
+    r = __shfl_sync(0xffffffffu, r, 0);
+    float base = 0.f;
+    int next = pos;   // no crossing within rounding: the last position, as the scan ends there
+    for (int j0 = a.sink; j0 <= pos; j0 += 32) {
+      const int j = j0 + lane;
+      float v = j <= pos ? __powf(fmaxf(__ldg(row + j), 1e-10f), it) : 0.f;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {   // inclusive prefix sum over the block
+        const float t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, j <= pos && r < base + v);
+      if (hit) { next = j0 + __ffs(hit) - 1; break; }
+      base += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) atomicAdd(&a.visits[next], 1.0f);
+    pos = next;
+  }
+  if (lane == 0) walker_store(a, w, g);
+}
+
 // ---- structured walker --------------------------------------------------------
 // Prefix row pos < n_p: A[pos, j] = h[j] * cinv[pos] for j < pos, 0 at j = pos, so the
 // weights are h[j]^(1/T) * cinv^(1/T) (the 1e-10 floor never binds: h >= 1e-6 and the
@@ -295,7 +345,10 @@ __global__ void __launch_bounds__(1024) k_walk_normalize(const WalkArgs a) {
 cudaError_t launch_walk_dense(const WalkArgs& a, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(a.visits, 0, (size_t)a.n * sizeof(float), st);
   if (e != cudaSuccess) return e;
-  k_walk_dense<<<(a.num_walkers + 255) / 256, 256, 0, st>>>(a);
+  if (a.rng_mode == 0)
+    k_walk_dense_warp<<<(a.num_walkers + kWalkWarps - 1) / kWalkWarps, 32 * kWalkWarps, 0, st>>>(a);
+  else
+    k_walk_dense<<<(a.num_walkers + 255) / 256, 256, 0, st>>>(a);
   k_walk_normalize<<<1, 1024, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -27,7 +27,8 @@ struct WalkArgs {
   float* h2o;              // [n] column sums of full_attn (structured form)
 };
 
-// Dense walker: the reference's sampling, step for step.
+// Dense walker: the reference's sampling, step for step (PCG: one thread per walker, the
+// reference's sequential sums; Philox: one warp per walker, coalesced row reads).
 cudaError_t launch_walk_dense(const WalkArgs& a, cudaStream_t st);
 // Structured walker over pooled window rows: prefix rows sampled by binary search on
 // prefix sums, window rows scanned; needs rows, hclamp, cinv and pre (see launch_walk_prep).

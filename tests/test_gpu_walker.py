@@ -190,6 +190,23 @@ def test_philox_walker_statistics_and_counter():
     assert _l1(v2.cpu().numpy(), exp) < 0.05
 
 
+@pytest.mark.parametrize("n,steps", [(96, 10), (700, 20)])
+def test_philox_warp_walker_matches_oracle_draws(n, steps):
+    """The dense walker in Philox mode (one warp per walker, coalesced row reads, warp
+    scans) against the oracle walker fed the same counter-based draws: the walks are the
+    same except where a running sum crosses the target within fp32 rounding."""
+    dev = _cuda()
+    walkers, sink = 4000, 4
+    A = _row_stochastic(n, 17)
+    _, v_or, _ = WO.influence_walk_dense(A, n - 1, walkers, steps, sink, gens=WO.philox_walkers(7, walkers))
+    _, v_g = ops.influence_walk_dense(torch.from_numpy(A).to(dev), n - 1, walkers, steps, sink,
+                                      rng_mode=_lib.RNG_PHILOX, seed=7, rng_state=None)
+    torch.cuda.synchronize()
+    v_g = v_g.cpu().numpy()
+    assert v_g.sum() == v_or.sum()
+    assert _l1(v_g, v_or) < 2e-3
+
+
 # ---- structured walker ----------------------------------------------------------------
 @pytest.mark.parametrize("n,W,cur_off,mode", [(300, 64, 1, _lib.RNG_PCG), (300, 64, 1, _lib.RNG_PHILOX),
                                               (200, 32, 60, _lib.RNG_PCG), (130, 64, 1, _lib.RNG_PCG)])

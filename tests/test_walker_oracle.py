@@ -87,3 +87,13 @@ def test_circuit_graph_argument_checks():
                  (100, 8, 0.85, 0, 10)]:
         with pytest.raises(RuntimeError):
             _C.CircuitGraph(*args)
+
+
+def test_philox_walker_draws_follow_the_stream_layout():
+    """A walker's counter-based draws are the top 24 bits of its Philox stream (call 0:
+    the same counters as ckv_rng_fill's stream = walker)."""
+    for w in (0, 5, 1234):
+        g = W.PhiloxWalker(7, w)
+        raw = W.philox_stream(7, w, 9)
+        for d in range(9):
+            assert g.uniform() == np.float32(raw[d] >> 40) * np.float32(1.0 / 16777216.0)
