@@ -86,6 +86,8 @@ def parse():
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=3)
     ap.add_argument("--layers", type=int, default=None, help="override the workload's layer count")
     ap.add_argument("--pyramid", action="store_true", help="config 3: budget 4096 -> 512 over the layers")
+    ap.add_argument("--per-head", action="store_true",
+                    help="per-head eviction (per_head_eviction=True; configs 1, 2, 3 and 5: n - window <= 65536)")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong")
     ap.add_argument("--qk", choices=["unit", "literal"], default="literal",
                     help="Q/K component scale: literal N(0,1)/sqrt(128) (the workloads' generator) or "
@@ -171,7 +173,8 @@ def unit_bytes(u, e):
 def config_obj(args, world, units):
     c = CONFIGS[args.config]
     L = args.layers or c["layers"]
-    cfg = {"workload": c["name"] + (" (pyramid budget 4096 -> 512)" if args.pyramid else ""),
+    cfg = {"workload": c["name"] + (" (pyramid budget 4096 -> 512)" if args.pyramid else "")
+                       + (", per-head eviction" if args.per_head else ""),
            "config": args.config, "layers": L, "units": len(units) // (world if args.scaling == "weak" else 1),
            "window": c["window"], "dtype": c["dtype"],
            "qk_scale": "N(0,1)/sqrt(128) (literal)" if args.qk == "literal" else "N(0,1) (unit-variance logits)",
@@ -260,7 +263,7 @@ def cpu_oracle_sample(args, u, samples=3, seconds_cap=30.0):
     q, k, v = make_layer(u.n, seed=u.seed, window=u.window, planted=c["planted"], locality=c["band"],
                          qk_scale=qk_scale(args), dtype=u.dtype)
     qn, kn, vn = (x.float().numpy() for x in (q, k, v))
-    p = O.Params(window_size=u.window, max_capacity_prompt=u.budget)
+    p = O.Params(window_size=u.window, max_capacity_prompt=u.budget, per_head_eviction=args.per_head)
     times = []
     t_all = time.perf_counter()
     try:   # every host core for numpy's BLAS too (torchrun sets OMP_NUM_THREADS=1)
@@ -288,7 +291,8 @@ def qk_scale(args):
 
 def metric_name(args):
     c = CONFIGS[args.config]
-    return f"tokens scored/s (per-layer CircuitKV scoring+eviction; {c['name']})"
+    return (f"tokens scored/s (per-layer CircuitKV scoring+eviction; {c['name']}"
+            + (", per-head eviction)" if args.per_head else ")"))
 
 
 def run_reference(args, rank, world):
@@ -348,10 +352,11 @@ def run_ours(args, rank, world):
         del q, k, v
     torch.cuda.synchronize()
 
-    exch = sharding.KeptExchange({u.uid: (u.budget - u.window,) for u in units}, owner, rank, world, device=dev)
+    kept_shape = (lambda u: (H, u.budget - u.window)) if args.per_head else (lambda u: (u.budget - u.window,))
+    exch = sharding.KeptExchange({u.uid: kept_shape(u) for u in units}, owner, rank, world, device=dev)
     params, structs, outs, ws_sizes = [], [], [], []
     for u in mine:
-        p = CircuitKVCluster(**cli_cluster_kwargs(u.window, u.budget)).params(u.n)
+        p = CircuitKVCluster(**cli_cluster_kwargs(u.window, u.budget, per_head_eviction=args.per_head)).params(u.n)
         params.append(p)
         ws_sizes.append((ops.workspace_size(p, u.n, H, HKV, D) + 255) // 256 * 256)
     ws = torch.empty(max(1, sum(ws_sizes)), dtype=torch.uint8, device=dev)
@@ -587,7 +592,8 @@ def e2e(args, rank, world, dev, mine, units, pg):
                                  locality=c["band"], qk_scale=qk_scale(args), dtype=u.dtype, device=str(dev))
             host[key] = tuple(x.cpu().pin_memory() for x in (q[None], repeat_kv(k, G), repeat_kv(v, G)))
             del q, k, v
-    clusters = [CircuitKVCluster(**cli_cluster_kwargs(u.window, u.budget)) for u in mine]
+    clusters = [CircuitKVCluster(**cli_cluster_kwargs(u.window, u.budget, per_head_eviction=args.per_head))
+                for u in mine]
     e = 4 if c["dtype"] == "fp32" else 2
     # per unit: the window queries and the distinct K heads copied in; the gather reads V's
     # kept rows (8 KV heads x budget rows) from the pinned host tensor in place; K / V out
@@ -622,6 +628,8 @@ def e2e(args, rank, world, dev, mine, units, pg):
 
 def main():
     args = parse()
+    if args.per_head and args.config == 4:
+        raise SystemExit("--per-head: the per-head pass supports n - window <= 65536 (config 4 is 131072 tokens)")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
