@@ -525,7 +525,7 @@ def run_ours(args, rank, world):
     if stage_ms is not None and L > 0:
         line["serial_per_unit_us"] = serial_ms * 1e3 / L
         line["stage_us_per_unit"] = {STAGES[i]: stage_ms[i] * 1e3 / L for i in range(len(stage_ms))}
-        line["roofline"] = roofline(stage_ms, mine, e, pk)
+        line["roofline"] = roofline(stage_ms, mine, e, pk, per_head=args.per_head)
     if gathered is not None:
         line["allgather_positions"] = gathered
 
@@ -539,7 +539,7 @@ def run_ours(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
-def roofline(stage_ms, mine, e, pk):
+def roofline(stage_ms, mine, e, pk, per_head=False):
     """The dominant kernel's roofline: the larger of the two window passes (the only
     stages that fill every SM).  Algorithmic work per launch: K read once (distinct heads)
     plus the window queries (and, for the pooling pass, the pooled rows written), or the
@@ -548,7 +548,10 @@ def roofline(stage_ms, mine, e, pk):
     L = len(mine)
     dom_s = stage_ms[dom] / L / 1e3
     flops = sum(2.0 * H * u.window * u.n * D for u in mine) / L
-    wbytes = sum(e * (HKV * u.n * D + H * u.window * D) + (2 * u.window * u.n * 4 if dom == 1 else 0)
+    # the pooling pass also writes the pooled rows (2 x W x n fp32); the per-head pass in its
+    # place writes per-head partials, counted as traffic, not as algorithmic bytes
+    pooled = 0 if per_head else 1
+    wbytes = sum(e * (HKV * u.n * D + H * u.window * D) + (2 * u.window * u.n * 4 * pooled if dom == 1 else 0)
                  for u in mine) / L
     t_tensor = flops / (pk["bf16_tflops"] * 1e12)
     t_hbm = wbytes / (pk["hbm_gbs"] * 1e9)
@@ -557,11 +560,11 @@ def roofline(stage_ms, mine, e, pk):
     else:
         roof = {"bound": "hbm", "achieved": wbytes / dom_s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["kernel"] = STAGES[dom]
+    roof["kernel"] = "per_head_pass" if (per_head and dom == 1) else STAGES[dom]
     roof["peak_source"] = pk["source"]
     roof["avg_launch_us"] = dom_s * 1e6
     roof["algorithmic_per_launch"] = flops if roof["bound"] == "tensor" else wbytes
-    roof["traffic"] = traffic_for(STAGES[dom], mine[0].n)
+    roof["traffic"] = traffic_for(roof["kernel"], mine[0].n)
     return roof
 
 

@@ -254,14 +254,19 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
   if (pl.per_head) {   // PU:3296-3464: per-head importance and selection, per-head gather
     e = launch_window_stage(wa, 0, st);
     if (e != cudaSuccess) return cuda_fail(e, "window moments");
+    stage_mark(st);
     e = launch_ph_pass(wa, st);
     if (e != cudaSuccess) return cuda_fail(e, "per-head pass");
+    // stage marks as the shared path's: the per-head pass stands where the pooling pass
+    // does; reduction, re-run, sweep and aux take no time here
+    for (int i = 0; i < 6; ++i) stage_mark(st);
     PhArgs ph;
     ph.pl = pl; ph.p = *p; ph.ws = ws; ph.out_idx = out->out_idx;
     ph.eq = (float)pow((double)p->qi_gamma, pl.K / 2.0);
     ph.eh = (float)pow((double)p->hi_gamma, pl.K / 2.0);
     e = launch_ph_select(ph, st);
     if (e != cudaSuccess) return cuda_fail(e, "per-head selection");
+    stage_mark(st);
     if (out->out_scores) {   // [H][2][n - W] ranked vectors, then [H] entropies
       const size_t nv = (size_t)pl.H * 2 * pl.ph_nw;
       e = cudaMemcpyAsync(out->out_scores, ws + pl.off_ph_vec, nv * 4, cudaMemcpyDeviceToDevice, st);
@@ -270,7 +275,9 @@ static int score_evict_one(const ckv_params* p, const ckv_layer* L, void* worksp
                             (size_t)pl.H * 4, cudaMemcpyDeviceToDevice, st);
       if (e != cudaSuccess) return cuda_fail(e, "per-head score copy");
     }
-    return launch_gather_layer(pl, L, out, out->out_idx, 0, st);
+    const int rc_g = launch_gather_layer(pl, L, out, out->out_idx, 0, st);
+    stage_mark(st);
+    return rc_g;
   }
   for (int s = 0; s < 3; ++s) {
     e = launch_window_stage(wa, s, st);

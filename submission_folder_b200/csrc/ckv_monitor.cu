@@ -264,33 +264,64 @@ constexpr int kLmRows = 3 + 2 * kLmMaxLandmarks;   // prefix rows: H2O, query x2
 
 // Column sums over the causal rows (H2O scores, landmark_walker.cu:476-505) in the
 // reference's order: the partial of residue t (t < 256) sums rows i = t, t + 256, ... with
-// i >= column, in increasing i; the 256 partials reduce as a halving tree.  A CTA owns 32
-// adjacent columns: lanes are columns (coalesced 128-byte row reads), warp w keeps the
-// partials of residues w, w + 8, ..., w + 248 in registers.
-__global__ void __launch_bounds__(256) k_lm_h2o(const float* __restrict__ a, int n, float* __restrict__ h2o) {
-  __shared__ float part[256][33];
+// i >= column, in increasing i; the 256 partials reduce as a halving tree.  A CTA owns 128
+// adjacent columns: a lane reads 4 of them as one float4, so a warp reads 512 contiguous
+// bytes of a row; warp w keeps the partials of residues w, w + 16, ..., w + 240 for its 4
+// columns in registers (4 row loads in flight per warp at a time).  The partials
+// meet in shared memory for the tree.  VEC = 0 (n not a multiple of 4): scalar loads.
+constexpr int kH2oCols = 128;
+constexpr int kH2oWarps = 16;
+template <bool VEC>
+__global__ void __launch_bounds__(32 * kH2oWarps) k_lm_h2o(const float* __restrict__ a, int n,
+                                                            float* __restrict__ h2o) {
+  extern __shared__ float part[];   // [256][kH2oCols]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int c0 = blockIdx.x * 32, c = c0 + lane;
-  float acc[32];
+  const int c0 = blockIdx.x * kH2oCols, cl = c0 + 4 * lane;   // this lane's first column
+  float acc[16][4];
 #pragma unroll
-  for (int k = 0; k < 32; ++k) acc[k] = 0.f;
-  if (c < n) {
-    for (int b = (c0 / 256) * 256; b < n; b += 256) {
+  for (int m = 0; m < 16; ++m)
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const int i = b + warp + 8 * k;
-        if (i < n && i >= c) acc[k] += a[(size_t)i * n + c];
+    for (int e = 0; e < 4; ++e) acc[m][e] = 0.f;
+  for (int b = (c0 / 256) * 256; b < n; b += 256) {
+#pragma unroll
+    for (int h = 0; h < 16; h += 4) {   // groups of 4 rows in flight
+      float4 x[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int i = b + warp + 16 * (h + m);
+        const float* row = a + (size_t)i * n;
+        if (VEC) {
+          x[m] = (i < n && cl < n) ? __ldg(reinterpret_cast<const float4*>(row + cl)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+          x[m].x = (i < n && cl < n) ? __ldg(row + cl) : 0.f;
+          x[m].y = (i < n && cl + 1 < n) ? __ldg(row + cl + 1) : 0.f;
+          x[m].z = (i < n && cl + 2 < n) ? __ldg(row + cl + 2) : 0.f;
+          x[m].w = (i < n && cl + 3 < n) ? __ldg(row + cl + 3) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int i = b + warp + 16 * (h + m);
+        if (i < n) {   // rows at or below the diagonal of each column (i >= c)
+          if (i >= cl) acc[h + m][0] += x[m].x;
+          if (i >= cl + 1) acc[h + m][1] += x[m].y;
+          if (i >= cl + 2) acc[h + m][2] += x[m].z;
+          if (i >= cl + 3) acc[h + m][3] += x[m].w;
+        }
       }
     }
   }
 #pragma unroll
-  for (int k = 0; k < 32; ++k) part[warp + 8 * k][lane] = acc[k];
+  for (int m = 0; m < 16; ++m)
+    *reinterpret_cast<float4*>(part + (warp + 16 * m) * kH2oCols + 4 * lane) =
+        make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
   __syncthreads();
   for (int stride = 128; stride > 0; stride >>= 1) {
-    for (int e = threadIdx.x; e < stride * 32; e += 256) part[e >> 5][e & 31] += part[(e >> 5) + stride][e & 31];
+    for (int e = threadIdx.x; e < stride * kH2oCols; e += blockDim.x)
+      part[e] += part[e + stride * kH2oCols];   // residue e / 128 += residue e / 128 + stride
     __syncthreads();
   }
-  if (warp == 0 && c < n) h2o[c] = part[0][lane];
+  if (threadIdx.x < kH2oCols && c0 + threadIdx.x < n) h2o[c0 + threadIdx.x] = part[threadIdx.x];
 }
 
 // Stratified landmarks (landmark_walker.cu:404-464): [24, n - 64) in num_landmarks equal
@@ -589,7 +620,19 @@ cudaError_t launch_landmark_walk(const float* attn, int n, int current_idx, int 
   int32_t* mono = reinterpret_cast<int32_t*>(pref + (size_t)kLmRows * stride);
   cudaError_t e = cudaMemsetAsync(visits, 0, (size_t)n * sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
-  k_lm_h2o<<<(n + 31) / 32, 256, 0, st>>>(attn, n, h2o);
+  {
+    const size_t sm = (size_t)256 * kH2oCols * sizeof(float);
+    const unsigned blocks = (unsigned)((n + kH2oCols - 1) / kH2oCols);
+    if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(attn) & 15u) == 0) {   // 16-byte row segments
+      e = cudaFuncSetAttribute(k_lm_h2o<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      if (e != cudaSuccess) return e;
+      k_lm_h2o<true><<<blocks, 32 * kH2oWarps, sm, st>>>(attn, n, h2o);
+    } else {
+      e = cudaFuncSetAttribute(k_lm_h2o<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      if (e != cudaSuccess) return e;
+      k_lm_h2o<false><<<blocks, 32 * kH2oWarps, sm, st>>>(attn, n, h2o);
+    }
+  }
   k_lm_select<<<1, 1024, 0, st>>>(h2o, n, num_landmarks, min_spacing, positions, count);
   k_lm_prefix<<<3 + 2 * num_landmarks, 1024, 0, st>>>(attn, n, current_idx, h2o, positions, count, pref, stride,
                                                       mono);

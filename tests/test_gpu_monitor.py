@@ -175,6 +175,8 @@ LANDMARK_CASES = [
     (600, 1, 8, 64, 2.0, 50, 0.6, 0, "zero_cols"),
     (640, 0, 8, 64, 2.5, 30, 0.8, 0, "negative"),
     (80, 1, 8, 64, 2.0, 50, 0.6, 0, "plain"),          # shorter than 89: no landmarks
+    (701, 1, 8, 37, 1.3, 20, 0.6, 0, "plain"),         # n not a multiple of 4: scalar row reads
+    (2309, 2, 16, 64, 2.0, 50, 0.0, 1, "plain"),       # several 128-column blocks, ragged edge
 ]
 
 
