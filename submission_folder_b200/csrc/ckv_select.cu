@@ -320,38 +320,60 @@ __device__ void top_sorted(cg::cluster_group& cl, const float* x, int b0, int b1
 // ---------------------------------------------------------------------------
 // argsort(argsort(x)) with a stable sort, over the P CTAs that hold the vector's
 // slices: a 4-pass LSD radix sort of the 32-bit keys (float_key) carried with their
-// indices through two global buffers (L2-resident).  Each pass: per-CTA digit
-// histograms exchanged through distributed shared memory give every (digit, CTA)
-// its output base; inside a CTA, rounds of blockDim consecutive elements are ranked
-// stably with warp match_any and per-warp digit counts.  Stable passes over a
-// sequence that starts in index order leave equal keys in index order, so
-// rank[i] = the final position of element i.  All CTAs of the cluster call it.
+// indices through two global buffers (L2-resident).  Each pass: inside a CTA every warp
+// owns a contiguous range of the slice and sweeps it in 32-element steps with match_any,
+// counting its digits (one counting sweep); the per-warp counts give each (digit, warp)
+// its offset within the CTA, the per-CTA totals exchanged through distributed shared
+// memory give each (digit, CTA) its output base, and a second sweep places the elements
+// (within a warp: step order, then lane order).  Stable passes over a sequence that
+// starts in index order leave equal keys in index order, so rank[i] = the final
+// position of element i.  All CTAs of the cluster call it.
 __device__ void full_ranks(cg::cluster_group& cl, const float* x, int b0, int b1, int vbase, int P, int part,
                            unsigned long long* bufA, unsigned long long* bufB, int* rank, SelSmem& sh) {
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, bd = blockDim.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, bd = blockDim.x, nwarps = bd >> 5;
   int* tot = sh.rk;              // [256] digit totals over the vector
   int* below = sh.rk + 256;      // [256] digit counts of lower-ranked CTAs
   int* base = sh.rk + 512;       // [256] output base of each digit for this CTA
-  int* run = sh.rk + 768;        // [256] elements of each digit placed so far
-  int* rtot = sh.rk + 1024;      // [256] per-round digit totals
-  int* wcnt = sh.hist;           // [32 warps][256] per-round warp digit counts
+  int* rtot = sh.rk + 1024;      // [256] scan scratch
+  int* wcnt = sh.hist;           // [warps][256] per-warp digit counts, then running offsets
   for (int j = b0 + tid; j < b1; j += bd)
     bufA[j] = ((unsigned long long)float_key(x[j - b0]) << 32) | (uint32_t)j;
   __syncthreads();
   unsigned long long* in = bufA;
   unsigned long long* out = bufB;
-  const int nrounds = (b1 - b0 + bd - 1) / bd;
+  // warp w owns [b0 + w E, b0 + (w + 1) E): E a multiple of 32
+  const int E = ((b1 - b0 + 32 * nwarps - 1) / (32 * nwarps)) * 32;
+  const int w0 = b0 + wid * E, w1 = min(b1, w0 + E);
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 32 + 8 * pass;
     int* hx = sh.hx + (pass & 1) * 256;
-    for (int i = tid; i < 256; i += bd) hx[i] = 0;
+    for (int i = tid; i < nwarps * 256; i += bd) wcnt[i] = 0;
     __syncthreads();
-    for (int r = 0; r < nrounds; ++r) {
-      const int pos = b0 + r * bd + tid;
-      const bool act = pos < b1;
-      const int d = act ? (int)((__ldcg(in + pos) >> shift) & 255u) : 256;
-      const unsigned peers = __match_any_sync(0xffffffffu, d);
-      if (act && lane == __ffs(peers) - 1) atomicAdd(&hx[d], __popc(peers));
+    int* wc = wcnt + wid * 256;
+    for (int q0 = w0; q0 < w1; q0 += 4 * 32) {   // counting sweep, 4 steps' loads in flight
+      int dg[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int pos = q0 + 32 * u + lane;
+        dg[u] = pos < w1 ? (int)((__ldcg(in + pos) >> shift) & 255u) : 256;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int d = dg[u];
+        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        if (d < 256 && lane == __ffs(peers) - 1) wc[d] += __popc(peers);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    if (tid < 256) {   // per digit: exclusive offsets of the warps, and this CTA's total
+      int acc = 0;
+      for (int q = 0; q < nwarps; ++q) {
+        const int c = wcnt[q * 256 + tid];
+        wcnt[q * 256 + tid] = acc;
+        acc += c;
+      }
+      hx[tid] = acc;
     }
     cl.sync();
     if (tid < 256) {
@@ -363,7 +385,6 @@ __device__ void full_ranks(cg::cluster_group& cl, const float* x, int b0, int b1
       }
       tot[tid] = t;
       below[tid] = bl;
-      run[tid] = 0;
     }
     __syncthreads();
     if (wid < 8) {   // exclusive scan of the 256 digit totals
@@ -383,31 +404,23 @@ __device__ void full_ranks(cg::cluster_group& cl, const float* x, int b0, int b1
       base[tid] = off + rtot[tid] - tot[tid] + below[tid];
     }
     __syncthreads();
-    for (int r = 0; r < nrounds; ++r) {
-      for (int i = tid; i < 32 * 256; i += bd) wcnt[i] = 0;
-      __syncthreads();
-      const int pos = b0 + r * bd + tid;
-      const bool act = pos < b1;
-      const unsigned long long e = act ? __ldcg(in + pos) : 0ull;
-      const int d = act ? (int)((e >> shift) & 255u) : 256;
-      const unsigned peers = __match_any_sync(0xffffffffu, d);
-      const int rk = __popc(peers & lanemask_lt());
-      if (act && rk == 0) wcnt[wid * 256 + d] = __popc(peers);
-      __syncthreads();
-      if (tid < 256) {   // exclusive prefix over warps, per digit
-        int s = 0;
-        for (int q = 0; q < (bd >> 5); ++q) {
-          const int c = wcnt[q * 256 + tid];
-          wcnt[q * 256 + tid] = s;
-          s += c;
-        }
-        rtot[tid] = s;
+    for (int q0 = w0; q0 < w1; q0 += 4 * 32) {   // placing sweep, 4 steps' loads in flight
+      unsigned long long ev[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int pos = q0 + 32 * u + lane;
+        ev[u] = pos < w1 ? __ldcg(in + pos) : ~0ull;
       }
-      __syncthreads();
-      if (act) out[base[d] + run[d] + wcnt[wid * 256 + d] + rk] = e;
-      __syncthreads();
-      if (tid < 256) run[tid] += rtot[tid];
-      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const bool act = q0 + 32 * u + lane < w1;
+        const int d = act ? (int)((ev[u] >> shift) & 255u) : 256;
+        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        if (act) out[base[d] + wc[d] + __popc(peers & lanemask_lt())] = ev[u];
+        __syncwarp();
+        if (act && lane == __ffs(peers) - 1) wc[d] += __popc(peers);
+        __syncwarp();
+      }
     }
     cl.sync();   // every element of the pass is placed
     unsigned long long* t = in;

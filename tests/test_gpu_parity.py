@@ -359,7 +359,8 @@ def test_per_head_fp32_ragged(parity_report):
     assert ops.read_status(dev) == 0
 
 
-@pytest.mark.parametrize("n,W,dtype", [(3001, 32, "bf16"), (5000, 128, "bf16"), (4222, 64, "fp16")])
+@pytest.mark.parametrize("n,W,dtype", [(3001, 32, "bf16"), (5000, 128, "bf16"), (4222, 64, "fp16"),
+                                       (1100, 128, "bf16"), (640, 64, "bf16"), (1153, 32, "fp16")])
 def test_per_head_tensor_core_windows(n, W, dtype, parity_report):
     """The tcgen05 per-head pass for windows of 32, 64 and 128 rows (ragged n, the last key
     tile partly past n): decomposed parity against the oracle (``check_per_head``)."""
