@@ -2337,9 +2337,11 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
     abort_sh = 0;
   }
   __shared__ float4 smask[2 * kMaxHeads / 4];   // per KV group: QI, HI membership factors of its 4 heads
-  __shared__ int s_hi_kind;                      // kHiMean / kHiMax / kHiNone
+  __shared__ int s_hi_kind;                      // kHiMeanAll / kHiMean / kHiMax / kHiNone
   if (threadIdx.x == 0)
-    s_hi_kind = pl.hi_rows == 0 ? kHiNone : (hdr->hi_mode == 1 ? kHiMax : kHiMean);
+    s_hi_kind = pl.hi_rows == 0 ? kHiNone
+              : (hdr->hi_mode == 1 ? kHiMax
+                 : (hdr->hi_heads == (pl.H >= 64 ? ~0ull : (1ull << pl.H) - 1ull) ? kHiMeanAll : kHiMean));
   if (threadIdx.x < 2 * ngroups) {
     const int g = threadIdx.x >> 1;
     const uint32_t m = (uint32_t)(((threadIdx.x & 1) ? hdr->hi_heads : hdr->qi_heads) >> (g * G)) & 0xFu;
@@ -2514,7 +2516,10 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
                 const F2 a = mul2(p01, qm01), b = mul2(p23, qm23);
                 qacc[u] = max3f(max3f(qacc[u], f2lo(a), f2hi(a)), f2lo(b), f2hi(b));
               }
-              if constexpr (HM == kHiMean) {
+              if constexpr (HM == kHiMeanAll) {   // every head in the set: factors of 1 dropped
+                const F2 t = add2(p01, p23);                 // (the same sums: p * 1 is exact)
+                hacc[u] += f2lo(t) + f2hi(t);
+              } else if constexpr (HM == kHiMean) {
                 const F2 t = fma2(p23, hm23, mul2(p01, hm01));
                 hacc[u] += f2lo(t) + f2hi(t);
               } else if constexpr (HM == kHiMax) {
@@ -2530,6 +2535,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
           else chunks(htag, BoolTag<false>{}, BoolTag<false>{});
         };
         switch (s_hi_kind) {
+          case kHiMeanAll: run(IntTag<kHiMeanAll>{}); break;
           case kHiMean: run(IntTag<kHiMean>{}); break;
           case kHiMax: run(IntTag<kHiMax>{}); break;
           default: run(IntTag<kHiNone>{}); break;
