@@ -364,6 +364,13 @@ int ckv_rng_fill(int32_t mode, uint64_t seed, uint64_t stream_id, int32_t count,
  * *accessible to 0 for pageable host memory and unknown pointers. */
 int ckv_device_accessible(const void* ptr, int32_t* accessible);
 
+/* `rows` rows of row_bytes each, from src (rows src_pitch bytes apart) to dst (dst_pitch bytes
+ * apart), either direction, as one asynchronous DMA on the stream (no reference counterpart:
+ * the hook moves the window queries of all heads, 32 strided row blocks of a host tensor, in
+ * one copy instead of one per head). */
+int ckv_copy_rows(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t row_bytes, int32_t rows,
+                  ckv_stream_t stream);
+
 /* K / V compaction alone (PU:3496-3517 shared, PU:3448-3462 per head): the `kept`
  * positions idx ([kept] or [H, kept] with per_head) then the last `window` rows, into
  * [H, kept + window, D] outputs.  For callers that chose the positions themselves (the

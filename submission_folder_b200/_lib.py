@@ -24,7 +24,7 @@ EXPORTED = (
     "ckv_window_pool", "ckv_choose_heads", "ckv_pool_rows_given", "ckv_graph_update", "ckv_circuit_walk",
     "ckv_pcg_seed", "ckv_spectral_scores", "ckv_combine_scores", "ckv_landmark_workspace_size",
     "ckv_landmark_walk", "ckv_influence_walk", "ckv_influence_walk_dense", "ckv_walk_workspace_size",
-    "ckv_rng_fill", "ckv_gather", "ckv_device_accessible", "ckv_set_stage_events", "ckv_last_error_string",
+    "ckv_rng_fill", "ckv_gather", "ckv_device_accessible", "ckv_copy_rows", "ckv_set_stage_events", "ckv_last_error_string",
     "ckv_version",
 )
 RNG_PHILOX, RNG_PCG = 0, 1
@@ -139,6 +139,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "ckv_rng_fill": (i32, [i32, u64, u64, i32, vp, vp]),
         "ckv_gather": (i32, [L, i32, vp, i32, i32, vp, vp, vp]),
         "ckv_device_accessible": (i32, [vp, ctypes.POINTER(i32)]),
+        "ckv_copy_rows": (i32, [vp, sz, vp, sz, sz, i32, vp]),
         "ckv_set_stage_events": (i32, [ctypes.POINTER(vp), i32]),
         "ckv_last_error_string": (ctypes.c_char_p, []),
         "ckv_version": (ctypes.c_char_p, []),

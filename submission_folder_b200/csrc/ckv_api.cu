@@ -831,6 +831,16 @@ int ckv_gather(const ckv_layer* layer, int32_t window, const int32_t* idx, int32
   return e == cudaSuccess ? CKV_OK : cuda_fail(e, "gather");
 }
 
+int ckv_copy_rows(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t row_bytes, int32_t rows,
+                  ckv_stream_t stream) {
+  if (!dst || !src || rows < 0 || row_bytes > dst_pitch || row_bytes > src_pitch)
+    return fail(CKV_ERR_ARG, "bad copy geometry");
+  if (rows == 0 || row_bytes == 0) return CKV_OK;
+  const cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, row_bytes, (size_t)rows, cudaMemcpyDefault,
+                                          (cudaStream_t)stream);
+  return e == cudaSuccess ? CKV_OK : cuda_fail(e, "strided row copy");
+}
+
 int ckv_device_accessible(const void* ptr, int32_t* accessible) {
   if (!accessible) return fail(CKV_ERR_ARG, "null argument");
   *accessible = 0;

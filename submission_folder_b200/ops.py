@@ -63,6 +63,25 @@ def device_readable(t: torch.Tensor) -> bool:
     return ok.value == 1
 
 
+def copy_rows_async(dst: torch.Tensor, src: torch.Tensor) -> bool:
+    """``dst.copy_(src)`` for ``[R, ...]`` tensors whose every ``[r]`` slice is contiguous
+    (e.g. one head's rows of a host tensor with heads far apart) as ONE strided DMA on the
+    current stream; returns False (nothing copied) when the layout does not allow it."""
+    if dst.shape != src.shape or dst.dtype != src.dtype or dst.dim() < 2 or dst.shape[0] == 0:
+        return False
+    if not (dst[0].is_contiguous() and src[0].is_contiguous()):
+        return False
+    e = dst.element_size()
+    row = dst[0].numel() * e
+    if dst.shape[0] > 1 and (dst.stride(0) * e < row or src.stride(0) * e < row):
+        return False
+    dev = dst.device if dst.is_cuda else src.device
+    check(_lib.load().ckv_copy_rows(ctypes.c_void_p(dst.data_ptr()), dst.stride(0) * e,
+                                     ctypes.c_void_p(src.data_ptr()), src.stride(0) * e, row, dst.shape[0],
+                                     _stream(dev)), "ckv_copy_rows")
+    return True
+
+
 def _require_readable(v: torch.Tensor) -> None:
     """V is read only by the final gather: device memory, or page-locked host memory the
     device reads in place."""

@@ -473,6 +473,25 @@ def test_host_tensors_round_trip():
     assert torch.equal(ko, kd.cpu()) and torch.equal(vo, vd.cpu())
 
 
+def test_copy_rows_strided_heads():
+    """ckv_copy_rows: strided row blocks (the window rows of every head; every 4th head) in
+    one DMA, host to device and back, pinned and pageable; layouts it cannot take decline."""
+    dev = _cuda()
+    x = torch.randn(32, 300, 128).to(torch.bfloat16)
+    for src in (x, x.pin_memory()):
+        d = torch.zeros(32, 300, 128, dtype=torch.bfloat16, device=dev)
+        assert ops.copy_rows_async(d[:, 236:], src[:, 236:])
+        torch.cuda.synchronize()
+        assert torch.equal(d[:, 236:].cpu(), x[:, 236:]) and int(d[:, :236].abs().sum().item()) == 0
+        e = torch.empty(8, 300, 128, dtype=torch.bfloat16, device=dev)
+        assert ops.copy_rows_async(e, src[::4])
+        back = torch.empty(8, 300, 128, dtype=torch.bfloat16).pin_memory()
+        assert ops.copy_rows_async(back, e)
+        torch.cuda.synchronize()
+        assert torch.equal(back, x[::4])
+    assert not ops.copy_rows_async(torch.empty(4, 8, device=dev), torch.randn(8, 4).t())
+
+
 def _flip_case(n=4096, W=64, H=32, Hkv=8, D=128, seed=11):
     """Window queries whose speculated QI head set is wrong.
 
