@@ -1012,7 +1012,6 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_ph_select(PhArgs a) {
   cg::cluster_group cl = cg::this_cluster();
   const int C = (int)cl.num_blocks(), rank = (int)cl.block_rank();
   const int P = C / 2, v = rank / P, part = rank % P, vbase = v * P;
-  const bool leader = part == 0;
   const int h = (int)blockIdx.x / C;
   const Plan& pl = a.pl;
   const ckv_params& prm = a.p;
@@ -1044,7 +1043,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_ph_select(PhArgs a) {
   __syncthreads();
   full_ranks(cl, x, b0, b1, vbase, P, part, bufs + (size_t)v * 2 * nw, bufs + (size_t)v * 2 * nw + nw,
              ranks + (size_t)v * nw, sh);
-  // per-head combined score of this slice (both vectors' CTAs compute it)
+  // per-head combined score weights
   const bool aq = prm.ablate_qi, ah = prm.ablate_hi;
   float wq = 0.5f;
   if (!aq && !ah && prm.entropy_adaptive) {
@@ -1053,8 +1052,12 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_ph_select(PhArgs a) {
     for (int q = 0; q < pl.H; ++q) { const float e = __ldcg(ent + q); lo = fminf(lo, e); hi = fmaxf(hi, e); }
     if (hi > lo) wq = __fsub_rn(1.0f, __fdiv_rn(__fsub_rn(__ldcg(ent + h), lo), __fsub_rn(hi, lo)));
   }
+  // the combined score and its top list over all C CTAs of the cluster (both vectors' CTAs
+  // share the work): this CTA's 1/C slice of the positions, ranks read back from global memory
   const float den = (float)(nw - 1), iden = nw > 1 ? 1.0f / den : 0.f;
-  for (int j = b0 + threadIdx.x; j < b1; j += blockDim.x) {
+  const SelLayout LC = sel_layout(nw, C);
+  const int c0 = min(nw, rank * LC.S), c1 = min(nw, c0 + LC.S);
+  for (int j = c0 + threadIdx.x; j < c1; j += blockDim.x) {
     const float qr = nw > 1 ? div_rcp((float)__ldcg(ranks + j), den, iden) : 1.f;
     const float hr = nw > 1 ? div_rcp((float)__ldcg(ranks + nw + j), den, iden) : 1.f;
     float sc;
@@ -1063,10 +1066,10 @@ __global__ void __launch_bounds__(kSelThreads, 1) k_ph_select(PhArgs a) {
     else if (aq && ah) sc = hr;
     else if (prm.entropy_adaptive) sc = __fadd_rn(__fmul_rn(wq, qr), __fmul_rn(__fsub_rn(1.0f, wq), hr));
     else sc = fmaxf(qr, __ldcg(ghi + j));
-    x[j - b0] = sc;
+    x[j - c0] = sc;
   }
   __syncthreads();
-  top_sorted(cl, x, b0, b1, s, nw, max(m, 1), false, vbase, P, leader, sh);
+  top_sorted(cl, x, c0, c1, s, nw, max(m, 1), false, 0, C, rank == 0, sh);
   cl.sync();
   if (rank == 0 && m > 0)
     for (int q = threadIdx.x; q < m; q += blockDim.x) {
