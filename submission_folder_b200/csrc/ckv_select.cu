@@ -318,11 +318,24 @@ __device__ void top_sorted(cg::cluster_group& cl, const float* x, int b0, int b1
 // ---------------------------------------------------------------------------
 // full stable ranks of one vector (weighted combination, PU:1865-1882)
 // ---------------------------------------------------------------------------
+// The lanes of the warp whose 9-bit values d (0..256) equal this lane's: one ballot per bit
+// (cheaper here than match.any, whose cost dominated the radix passes).
+CKV_DEV unsigned warp_peers9(int d) {
+  unsigned peers = 0xffffffffu;
+#pragma unroll
+  for (int b = 0; b < 9; ++b) {
+    const bool bit = (d >> b) & 1;
+    const unsigned m = __ballot_sync(0xffffffffu, bit);
+    peers &= bit ? m : ~m;
+  }
+  return peers;
+}
+
 // argsort(argsort(x)) with a stable sort, over the P CTAs that hold the vector's
 // slices: a 4-pass LSD radix sort of the 32-bit keys (float_key) carried with their
 // indices through two global buffers (L2-resident).  Each pass: inside a CTA every warp
-// owns a contiguous range of the slice and sweeps it in 32-element steps with match_any,
-// counting its digits (one counting sweep); the per-warp counts give each (digit, warp)
+// owns a contiguous range of the slice and sweeps it in 32-element steps (digit peers from
+// ballots), counting its digits (one counting sweep); the per-warp counts give each (digit, warp)
 // its offset within the CTA, the per-CTA totals exchanged through distributed shared
 // memory give each (digit, CTA) its output base, and a second sweep places the elements
 // (within a warp: step order, then lane order).  Stable passes over a sequence that
@@ -360,7 +373,7 @@ __device__ void full_ranks(cg::cluster_group& cl, const float* x, int b0, int b1
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int d = dg[u];
-        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        const unsigned peers = warp_peers9(d);
         if (d < 256 && lane == __ffs(peers) - 1) wc[d] += __popc(peers);
         __syncwarp();
       }
@@ -415,7 +428,7 @@ __device__ void full_ranks(cg::cluster_group& cl, const float* x, int b0, int b1
       for (int u = 0; u < 4; ++u) {
         const bool act = q0 + 32 * u + lane < w1;
         const int d = act ? (int)((ev[u] >> shift) & 255u) : 256;
-        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        const unsigned peers = warp_peers9(d);
         if (act) out[base[d] + wc[d] + __popc(peers & lanemask_lt())] = ev[u];
         __syncwarp();
         if (act && lane == __ffs(peers) - 1) wc[d] += __popc(peers);
