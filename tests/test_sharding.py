@@ -95,14 +95,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_gloo_two_ranks_gather_kept():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_gather_kept(world):
     with tempfile.TemporaryDirectory() as d:
         out = os.path.join(d, "r0.pt")
         mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, join=True,
                            start_method="spawn")
         res = torch.load(out)
-    assert res["slowest"] == 2.0
+    assert res["slowest"] == float(world)
     kept = res["kept"]
     assert sorted(kept) == list(range(len(LENGTHS)))
     for i in range(len(LENGTHS)):
