@@ -404,6 +404,30 @@ def test_moments_chunk_of_one_masked_tile(n, W, parity_report):
                r.hi, O.Params(window_size=W, max_capacity_prompt=B), n, False, parity_report)
 
 
+@pytest.mark.parametrize("H,Hkv,W,n", [(28, 4, 64, 3000), (32, 4, 64, 2600), (32, 2, 32, 2500)])
+def test_other_head_groupings(H, Hkv, W, n, parity_report):
+    """Query heads per KV head other than 4 (Qwen2-style 28 / 4, 8 and 16 per KV head): the
+    kept set checked against the oracle (``check_kept``) and the gathered rows against the
+    inputs."""
+    from submission_folder_b200.cluster import cli_cluster_kwargs
+    from submission_folder_b200.synth import make_layer
+    dev = _cuda()
+    B = n // 8
+    q, k, v = make_layer(n, seed=n + H, heads=H, kv_heads=Hkv, window=W, planted=16, dtype="bf16")
+    p = CircuitKVCluster(**cli_cluster_kwargs(W, B)).params(n)
+    ko, vo, idx, sc = ops.score_evict(p, q.to(dev), k.to(dev), v.to(dev), want_scores=True)
+    torch.cuda.synchronize()
+    assert ops.read_status(dev) == 0 and torch.isfinite(sc).all()
+    r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), H // Hkv,
+                    O.Params(window_size=W, max_capacity_prompt=B), dtype="bf16")
+    check_kept(f"groups_{H}_{Hkv}_w{W}", idx.cpu().numpy(), sc.cpu().numpy(), r.keep_idx, r.combined, r.qi,
+               r.hi, O.Params(window_size=W, max_capacity_prompt=B), n, False, parity_report)
+    kk = torch.from_numpy(np.asarray(idx.cpu().numpy(), dtype=np.int64))
+    rows = torch.cat([kk, torch.arange(n - W, n)])
+    for h in (0, H // Hkv, H - 1):
+        assert torch.equal(ko[h].cpu(), k[h // (H // Hkv), rows]) and torch.equal(vo[h].cpu(), v[h // (H // Hkv), rows])
+
+
 def test_both_pooling_branches_are_exercised(parity_report):
     """The pooling pass skips the exact entropy / mass recomputation when the moments
     pass settles the head sets (header word need_exact = 0) and redoes it otherwise;
