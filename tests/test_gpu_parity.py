@@ -1,7 +1,7 @@
 """Parity of the sm_100a kernels (through the C ABI) with the reference's golden
 outputs and with the CPU oracle, stage by stage and end to end.
 
-Tolerances (written here, per the north star): the ranked score vectors agree
+Tolerances: the ranked score vectors agree
 within 1e-3 relative; the index work is exact -- the kept positions are exactly
 the reference's selection rule applied to the ranked vectors (stable ranks,
 lowest-index-first ties of the k-th value, as torch's CUDA argsort / topk do,
