@@ -629,21 +629,26 @@ def e2e(args, rank, world, dev, mine, units, pg):
             "api": "CircuitKVCluster.update_kv on pinned host tensors (per rank: its units)"}
     # the same units through the pipelined host-cache call (uploads, scoring and downloads of
     # consecutive layers overlapped; the same copies per step)
+    from submission_folder_b200.ops import output_len as ops_output_len
     from submission_folder_b200.pipeline import score_evict_pipelined
     params = [cl.params(u.n) for cl, u in zip(clusters, mine)]
     layers = []
     for u in mine:
         qh, kh, vh = host[(u.n, u.layer % 2)]
         layers.append((qh[0], kh[0, ::G], vh[0, ::G]))
-    if mine:
-        score_evict_pipelined(params, layers, dev)
+    # the host output buffers are allocated once (page-locked allocation is slow the first time)
+    outs = [tuple(torch.empty(H, ops_output_len(p_, u.n), D, dtype=kh_.dtype, pin_memory=True) for _ in range(2))
+            for p_, u, (_, kh_, _) in zip(params, mine, layers)]
+    for _ in range(2):
+        if mine:
+            score_evict_pipelined(params, layers, dev, out=outs)
     torch.cuda.synchronize()
     if pg:
         dist.barrier()
     t = time.perf_counter()
     for _ in range(args.e2e_steps):
         if mine:
-            score_evict_pipelined(params, layers, dev)
+            score_evict_pipelined(params, layers, dev, out=outs)
     torch.cuda.synchronize()
     sec_p = (time.perf_counter() - t) / args.e2e_steps
     if pg:

@@ -23,17 +23,22 @@ from ._lib import Outputs, Params, check
 
 
 def score_evict_pipelined(params, layers: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
-                          device: Optional[torch.device] = None
+                          device: Optional[torch.device] = None,
+                          out: Optional[Sequence[Tuple[torch.Tensor, torch.Tensor]]] = None
                           ) -> List[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
     """``layers``: per layer ``(q [H, n, D], k [Hkv, n, D], v [Hkv, n, D])`` host tensors
     (views with contiguous rows per head, e.g. every ``groups``-th head of a repeat_kv'd
     tensor; page-locked for full link speed, V page-locked to be read in place);
     ``params``: one ``Params`` or one per layer.  Returns per layer ``(k_out, v_out, keep_idx)``:
     ``[H, out_len, D]`` page-locked host tensors and the kept positions (device tensors),
-    all complete on return."""
+    all complete on return.  ``out``: per layer ``(k_out, v_out)`` host tensors to fill instead
+    (contiguous, page-locked: a caller that scores caches repeatedly keeps them, which spares
+    the page-locked allocations; the first allocation of page-locked memory is slow)."""
     plist = list(params) if isinstance(params, (list, tuple)) else [params] * len(layers)
     if len(plist) != len(layers):
         raise ValueError("params: one struct or one per layer")
+    if out is not None and len(out) != len(layers):
+        raise ValueError("out: one (k_out, v_out) pair per layer")
     if not layers:
         return []
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -103,8 +108,13 @@ def score_evict_pipelined(params, layers: Sequence[Tuple[torch.Tensor, torch.Ten
         # download of the compacted K / V into page-locked host tensors
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_cmp[i])
-            kh = torch.empty(H, olen, D, dtype=dt, pin_memory=True)
-            vh = torch.empty(H, olen, D, dtype=dt, pin_memory=True)
+            if out is not None:
+                kh, vh = out[i]
+                if kh.shape != (H, olen, D) or vh.shape != (H, olen, D) or not (kh.is_contiguous() and vh.is_contiguous()):
+                    raise ValueError(f"out[{i}]: contiguous [{H}, {olen}, {D}] host tensors expected")
+            else:
+                kh = torch.empty(H, olen, D, dtype=dt, pin_memory=True)
+                vh = torch.empty(H, olen, D, dtype=dt, pin_memory=True)
             kh.copy_(ko, non_blocking=True)
             vh.copy_(vo, non_blocking=True)
             ev_out[i].record(s_out)

@@ -46,4 +46,10 @@ def test_pipelined_equals_per_layer_calls():
             continue
         assert torch.equal(ko, kref[0]) and torch.equal(vo, vref[0]), i
         assert np.array_equal(idx.cpu().numpy(), cl.last_keep_indices.cpu().numpy()), i
+    # again into caller-provided page-locked buffers: the same results
+    bufs = [(torch.zeros_like(ko).pin_memory(), torch.zeros_like(vo).pin_memory()) for ko, vo, _ in out]
+    again = score_evict_pipelined(params, layers, out=bufs)
+    for (ko, vo, idx), (k2, v2, i2), (bk, bv) in zip(out, again, bufs):
+        assert k2 is bk and v2 is bv
+        assert torch.equal(ko, k2) and torch.equal(vo, v2) and torch.equal(idx, i2)
     assert ops.read_status(dev) == 0
