@@ -1449,6 +1449,18 @@ template <> CKV_DEV uint32_t round_pack<CKV_BF16>(float a, float b, float rs, fl
   y = __uint_as_float(p & 0xffff0000u);
   return p;
 }
+// A packed pair of rounded logits (low half first) as a packed fp32 pair (exact).
+template <int DT> CKV_DEV F2 unpack_f2(uint32_t p) {
+  if constexpr (DT == CKV_BF16) {
+    F2 r;
+    asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xffff0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(r.v) : "r"(p));
+    return r;
+  } else {
+    return f2(__half2float(__ushort_as_half((unsigned short)(p & 0xffffu))),
+              __half2float(__ushort_as_half((unsigned short)(p >> 16))));
+  }
+}
 template <int DT> CKV_DEV uint32_t pmax2(uint32_t a, uint32_t b) {
   uint32_t r;
   if constexpr (DT == CKV_BF16) asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -1595,7 +1607,112 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
   } else {
     // ---------------- epilogue: running moments of this thread's row ----------------
     const float rs = 1.0f / sqrtf((float)pl.D);
-    for (int i = 0; i < ntile; ++i) {
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
+    // Tiles whose every column each row of the m-tile sees (no causal mask, no keys past
+    // n): all but the sequence's last one or two.  Their chunks run software-pipelined:
+    // chunk k + 1 is loaded from TMEM, rounded and max-reduced in the same straight-line
+    // block as chunk k's exponentials and sums, so one chunk's MUFU work overlaps the
+    // next chunk's ALU work within a warp.  Every sum, rescale and their order are those
+    // of the per-chunk loop further down, which takes the remaining (masked) tiles.
+    const int nclean = cw == 64 ? max(0, min(ntile, (pl.n - pl.W + 1) / TN - t0)) : 0;
+    bool alive = true;
+    // a chunk's 32 rounded logits as 16 packed pairs, with their packed max / min
+    auto load_round = [&](uint32_t taddr, uint32_t(&pk)[16], uint32_t& px, uint32_t& pn) {
+      float v[32];
+      __syncwarp();
+      tc::tmem_ld32(taddr, v);
+      float xd, yd;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) pk[u] = round_pack<DT>(v[2 * u], v[2 * u + 1], rs, xd, yd);
+      uint32_t mx[8], mn[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { mx[i] = pmax2<DT>(pk[i], pk[i + 8]); mn[i] = pmin2<DT>(pk[i], pk[i + 8]); }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { mx[i] = pmax2<DT>(mx[i], mx[i + 4]); mn[i] = pmin2<DT>(mn[i], mn[i + 4]); }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) { mx[i] = pmax2<DT>(mx[i], mx[i + 2]); mn[i] = pmin2<DT>(mn[i], mn[i + 2]); }
+      px = pmax2<DT>(mx[0], mx[1]);
+      pn = pmin2<DT>(mn[0], mn[1]);
+    };
+    // fold a chunk's max into the running moments (rescaling them when it rises)
+    auto fold_max = [&](uint32_t px, uint32_t pn) {
+      xmin = fminf(xmin, phalf_min<DT>(pn));
+      const float cm2 = phalf_max<DT>(px) * kLog2e;
+      if (cm2 > M.m) {
+        if (M.m != -INFINITY) {
+          const float d = cm2 - M.m;
+          const float sc = ex2(-d);
+          M.t = sc * (M.t - d * M.z);
+          M.z *= sc;
+          M.s *= sc;
+        }
+        M.m = cm2;
+      }
+    };
+    // a clean chunk's exponentials against the running max: sums, entropy moment, sinks
+    auto chunk_exps = [&](const uint32_t(&pk)[16], int jb) {
+      const float nm = -M.m;
+      const F2 l2e = f2(kLog2e, kLog2e), nm2 = f2(nm, nm);
+      F2 z2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)}, t2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const F2 d2 = fma2(unpack_f2<DT>(pk[u]), l2e, nm2);
+        const F2 e2 = f2(ex2(f2lo(d2)), ex2(f2hi(d2)));
+        const int q = u & 1;
+        z2[q] = add2(z2[q], e2);
+        t2[q] = fma2(e2, d2, t2[q]);
+      }
+      const F2 zs = add2(z2[0], z2[1]), ts = add2(t2[0], t2[1]);
+      M.z += f2lo(zs) + f2hi(zs);
+      M.t += f2lo(ts) + f2hi(ts);
+      if (jb < pl.s) {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const F2 x2 = unpack_f2<DT>(pk[u]);
+          if (jb + 2 * u < pl.s) M.s += ex2(fmaf(f2lo(x2), kLog2e, nm));
+          if (jb + 2 * u + 1 < pl.s) M.s += ex2(fmaf(f2hi(x2), kLog2e, nm));
+        }
+      }
+    };
+    if (nclean > 0) {
+      alive = __all_sync(0xffffffffu, tc::mbar_wait(&bar_full[0], 0, status));
+      if (alive) {
+        tc::fence_after_sync();
+        uint32_t pc[16], pnx[16], px, pn;   // the chunk whose exponentials are next; the one after it
+        load_round(lane_base + (uint32_t)(sp * cw), pc, px, pn);   // chunk (0, 0)
+        fold_max(px, pn);
+        for (int i = 0; i < nclean; ++i) {
+          const int b = i & 1;
+          const int jb0 = (t0 + i) * TN + sp * cw;
+          // chunk (i, 1) in, chunk (i, 0) out; then the warp's loads of tile i are done
+          load_round(lane_base + (uint32_t)(b * TN + sp * cw + 32), pnx, px, pn);
+          chunk_exps(pc, jb0);
+          fold_max(px, pn);
+#pragma unroll
+          for (int u = 0; u < 16; ++u) pc[u] = pnx[u];
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bar_tfree[b]);
+          // chunk (i + 1, 0) in, chunk (i, 1) out
+          if (i + 1 < nclean) {
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&bar_full[b ^ 1], ((i + 1) >> 1) & 1, status))) {
+              alive = false;
+              break;
+            }
+            tc::fence_after_sync();
+            load_round(lane_base + (uint32_t)((b ^ 1) * TN + sp * cw), pnx, px, pn);
+            chunk_exps(pc, jb0 + 32);
+            fold_max(px, pn);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) pc[u] = pnx[u];
+          } else {
+            chunk_exps(pc, jb0 + 32);
+          }
+        }
+      }
+    }
+    // the remaining tiles, one chunk at a time (causal mask and keys past n)
+    for (int i = nclean; alive && i < ntile; ++i) {
       const int b = i & 1;
       if (!__all_sync(0xffffffffu, tc::mbar_wait(&bar_full[b], (i >> 1) & 1, status))) break;
       tc::fence_after_sync();
