@@ -55,6 +55,36 @@ CKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
   return false;
 }
 
+// The same wait for a warp-specialised producer thread: after a failed try_wait it sleeps
+// briefly before polling again, so a producer that waits most of the time (on the epilogue
+// warps freeing an accumulator buffer) does not take issue slots from the epilogue warps of
+// its scheduler.  Bounded: kSleepLimit rounds of at most ~0.1 us each.
+constexpr uint32_t kSleepLimit = 1u << 23;
+CKV_DEV bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, int32_t* status) {
+  const uint32_t a = smem_addr(bar);
+  for (uint32_t i = 0; i < kSleepLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    __nanosleep(64);
+  }
+  set_status(status, kStatusTimeout);
+  return false;
+}
+
+// 16 bytes from shared memory at a shared-window address (an explicit shared load: a
+// pointer derived from the dynamic shared memory base through integer arithmetic would
+// otherwise be loaded through the generic path).
+CKV_DEV float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
 // 3-D TMA tile load (no multicast) completing on `bar`.
 CKV_DEV void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(

@@ -1572,11 +1572,11 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
           tc::tma_load_3d(sA + p * 128 * 128 + hl * pl.W * 128, &tmq, &bar_q, p * 64, pl.n - pl.W, hfirst + hl);
       int issued = min(S, ntile), consumed = 0, mmas = 0;
       for (int i = 0; i < issued; ++i) load_tile(i);
-      bool ok = tc::mbar_wait(&bar_q, 0, status);
+      bool ok = tc::mbar_wait_backoff(&bar_q, 0, status);
       for (int i = 0; ok && i < ntile; ++i) {
         const int st = i % S, b = i & 1;
-        if (i >= 2 && !tc::mbar_wait(&bar_tfree[b], ((i - 2) >> 1) & 1, status)) { ok = false; break; }
-        if (!tc::mbar_wait(&bar_k[st], (i / S) & 1, status)) { ok = false; break; }
+        if (i >= 2 && !tc::mbar_wait_backoff(&bar_tfree[b], ((i - 2) >> 1) & 1, status)) { ok = false; break; }
+        if (!tc::mbar_wait_backoff(&bar_k[st], (i / S) & 1, status)) { ok = false; break; }
         consumed = i + 1;
         tc::fence_after_sync();
         const uint32_t dcol = (uint32_t)(b * TN);
@@ -1591,7 +1591,7 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
         tc::umma_commit(&bar_kfree[st]);
         mmas = i + 1;
         if (i + S < ntile) {
-          if (!tc::mbar_wait(&bar_kfree[st], (i / S) & 1, status)) { ok = false; break; }
+          if (!tc::mbar_wait_backoff(&bar_kfree[st], (i / S) & 1, status)) { ok = false; break; }
           load_tile(i + S);
           issued = i + S + 1;
         }
@@ -2433,7 +2433,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
   const PTSmem Ly = pt_layout(pl);
   char* base = align1024(smem_raw);
   char* stg = base;
-  const float4* snlse4 = reinterpret_cast<const float4*>(base + Ly.off_lse);
+  const uint32_t snl_base = tc::smem_addr(base + Ly.off_lse);   // -lse table, [group][row][head]
   __shared__ __align__(8) uint64_t bar_ld[kPTStages], bar_sfree[kPTStages], bar_full[2], bar_tfree[2], bar_tile;
   __shared__ int stage_tile[kPTStages];   // producer only: tile loaded into each stage (-1: none)
   __shared__ int tile_slot[2];            // tile k of this CTA in slot k & 1 (-1: no tile left)
@@ -2514,7 +2514,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
       for (int s = 0, g = 0, k = 0;; ++s) {   // g: step of the tile (half-major), k: this CTA's tile count
         const int st = s % S, b = s & 1;
         if (abort_sh) break;
-        if (s >= 2 && !tc::mbar_wait(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
+        if (s >= 2 && !tc::mbar_wait_backoff(&bar_tfree[b], ((s - 2) >> 1) & 1, status)) { abort_sh = 1; break; }
         const int tile = stage_tile[st];
         if (g == 0) {   // a new tile (or none): publish it to the epilogue
           tile_slot[k & 1] = tile;
@@ -2522,7 +2522,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         }
         if (++g == nvg) { g = 0; ++k; }
         if (tile < 0) break;      // no tile left: the epilogue stops at this tile boundary
-        if (!tc::mbar_wait(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        if (!tc::mbar_wait_backoff(&bar_ld[st], (s / S) & 1, status)) { abort_sh = 1; break; }
         tc::fence_after_sync();
         const uint64_t sbase = st == 0 ? base0 : base1;   // descriptors: base + (offset >> 4)
 #pragma unroll
@@ -2534,7 +2534,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         }
         tc::umma_commit(&bar_full[b]);
         tc::umma_commit(&bar_sfree[st]);
-        if (!tc::mbar_wait(&bar_sfree[st], (s / S) & 1, status)) { abort_sh = 1; break; }
+        if (!tc::mbar_wait_backoff(&bar_sfree[st], (s / S) & 1, status)) { abort_sh = 1; break; }
         load_step(s + S);
       }
     }
@@ -2620,7 +2620,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int r = RS * hf + RPQ * q + 4 * c + i;
-              const float4 nL = snlse4[g * W + r];   // -log2-sum-exp of (row, head 0..3)
+              const float4 nL = tc::lds128(snl_base + (uint32_t)((g * W + r) * 16));   // -log2-sum-exp of (row, head 0..3)
               const F2 x01 = round_f2<DT>(__uint_as_float(r16[4 * i]), __uint_as_float(r16[4 * i + 1]), rs);
               const F2 x23 = round_f2<DT>(__uint_as_float(r16[4 * i + 2]), __uint_as_float(r16[4 * i + 3]), rs);
               F2 p01 = ex2_2(fma2(x01, l2e, f2(nL.x, nL.y)));
