@@ -2594,18 +2594,18 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
         tc::fence_after_sync();
         // head membership factors (1 in the set, 0 outside) as pairs (heads 0 1, 2 3)
         const float4 q4 = smask[2 * g], h4 = smask[2 * g + 1];
-        const bool qany = (q4.x + q4.y) + (q4.z + q4.w) > 0.f;
         const F2 qm01 = f2(q4.x, q4.y), qm23 = f2(q4.z, q4.w);
         const F2 hm01 = f2(h4.x, h4.y), hm23 = f2(h4.z, h4.w);
         const F2 l2e = f2(kLog2e, kLog2e);
         const uint32_t col0 = (uint32_t)((s & 1) * NCOL + 4 * RPQ * q);
         // the causal mask only touches the tile that reaches the window (warp-uniform)
         const bool edge = tile * TN + TN - 1 > pl.n - W;
-        // QANY: some head of the group is in the QI set (else its max-pooling is skipped)
-        auto chunks = [&](auto htag, auto etag, auto qtag) {
+        // One copy of the step loop for every group: a group with no QI head has factors of 0
+        // and its max stays at 0, as if skipped (a second, QI-free copy of the loop measured
+        // slower: the hot code no longer fit the instruction cache as well).
+        auto chunks = [&](auto htag, auto etag) {
           constexpr int HM = decltype(htag)::value;
           constexpr bool EDGE = decltype(etag)::value;
-          constexpr bool QANY = decltype(qtag)::value;
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {   // 16 columns: window rows RS hf + RPQ q + 4 c + i, heads 0..3
             uint32_t r16[16];
@@ -2629,7 +2629,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
                 if (j > pl.n - W + r) { p01 = f2(0.f, 0.f); p23 = p01; }   // causal mask (and keys past n)
               }
               const int u = 4 * c + i;
-              if constexpr (QANY) {
+              {
                 const F2 a = mul2(p01, qm01), b = mul2(p23, qm23);
                 qacc[u] = max3f(max3f(qacc[u], f2lo(a), f2hi(a)), f2lo(b), f2hi(b));
               }
@@ -2647,9 +2647,8 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
           }
         };
         auto run = [&](auto htag) {
-          if (edge) chunks(htag, BoolTag<true>{}, BoolTag<true>{});
-          else if (qany) chunks(htag, BoolTag<false>{}, BoolTag<true>{});
-          else chunks(htag, BoolTag<false>{}, BoolTag<false>{});
+          if (edge) chunks(htag, BoolTag<true>{});
+          else chunks(htag, BoolTag<false>{});
         };
         switch (s_hi_kind) {
           case kHiMeanAll: run(IntTag<kHiMeanAll>{}); break;
