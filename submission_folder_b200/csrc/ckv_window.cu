@@ -49,8 +49,12 @@ CKV_DEV void cp_async16(void* smem, const void* gmem, int src_bytes) {
 CKV_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N> CKV_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
-// Bytes of one staged row of D=128 elements.
-template <int DT> __host__ __device__ constexpr int row_bytes() { return DT == CKV_FP32 ? 512 : 256; }
+// Bytes of one row of D=128 elements, and the stride of a staged row in shared memory.
+// fp32 rows are padded by 16 bytes (132 words): the SIMT tile reads float4s of 8 query rows
+// (or 4 key rows 2 apart) at one offset, which then fall in distinct banks (an unpadded
+// 512-byte stride put them all in the same four banks).
+template <int DT> __host__ __device__ constexpr int row_data_bytes() { return DT == CKV_FP32 ? 512 : 256; }
+template <int DT> __host__ __device__ constexpr int row_bytes() { return DT == CKV_FP32 ? 528 : 256; }
 
 // 16-byte chunk position inside a staged row (XOR swizzle for the 16-bit ldmatrix path).
 template <int DT> CKV_DEV int chunk_off(int row, int chunk) {
@@ -61,7 +65,7 @@ template <int DT> CKV_DEV int chunk_off(int row, int chunk) {
 // Stage `rows` rows of 128 elements; row i comes from base + row_src(i) (nullptr -> zeros).
 template <int DT>
 CKV_DEV void stage_rows(char* smem, const char* const* srcs, int rows) {
-  constexpr int kChunks = row_bytes<DT>() / 16;
+  constexpr int kChunks = row_data_bytes<DT>() / 16;
   for (int i = threadIdx.x; i < rows * kChunks; i += blockDim.x) {
     const int row = i / kChunks, ch = i % kChunks;
     const char* src = srcs[row];
@@ -113,8 +117,9 @@ template <int DT> struct WarpTile {
         for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
     if constexpr (DT == CKV_FP32) {
       const int g = lane >> 2, t = lane & 3;
-      const float* qa = reinterpret_cast<const float*>(sQ + (row0 + g) * 512);
-      const float* qb = reinterpret_cast<const float*>(sQ + (row0 + g + 8) * 512);
+      constexpr int RB = row_bytes<CKV_FP32>();
+      const float* qa = reinterpret_cast<const float*>(sQ + (row0 + g) * RB);
+      const float* qb = reinterpret_cast<const float*>(sQ + (row0 + g + 8) * RB);
       for (int k = 0; k < kHeadDim; k += 4) {
         const float4 a = *reinterpret_cast<const float4*>(qa + k);
         const float4 b = *reinterpret_cast<const float4*>(qb + k);
@@ -123,7 +128,7 @@ template <int DT> struct WarpTile {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const float4 kv =
-                *reinterpret_cast<const float4*>(sK + (nt * 8 + 2 * t + e) * 512 + k * 4);
+                *reinterpret_cast<const float4*>(sK + (nt * 8 + 2 * t + e) * RB + k * 4);
             float s0 = acc[0][nt][e], s1 = acc[0][nt][2 + e];
             s0 = fmaf(a.x, kv.x, s0); s0 = fmaf(a.y, kv.y, s0);
             s0 = fmaf(a.z, kv.z, s0); s0 = fmaf(a.w, kv.w, s0);
