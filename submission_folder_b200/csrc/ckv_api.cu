@@ -121,7 +121,10 @@ int make_plan(const ckv_params& p, int n, int H, int Hkv, int D, int dtype, Plan
   pl.n_pad = pl.ncol_tiles * kColTile;
   // moments pass: one wave of CTAs (tensor-core path: one CTA per SM per KV group)
   // tensor-core moments: one CTA per (column chunk, KV group, 128-row m-tile), one wave
-  int chunks = pl.tc ? 148 / (Hkv * ((pl.G * pl.W) / 128)) : (296 + pl.nbatch - 1) / pl.nbatch;
+  // (SIMT: two CTAs per SM for 16-bit rows; one for fp32, whose staged rows fill most of
+  // the shared memory, so one wave of 148 CTAs with longer column chunks)
+  int chunks = pl.tc ? 148 / (Hkv * ((pl.G * pl.W) / 128))
+                     : ((dtype == CKV_FP32 ? 148 : 296) + pl.nbatch - 1) / pl.nbatch;
   if (chunks > pl.ncol_tiles) chunks = pl.ncol_tiles;
   if (chunks < 1) chunks = 1;
   pl.tiles_per_chunk = (pl.ncol_tiles + chunks - 1) / chunks;
