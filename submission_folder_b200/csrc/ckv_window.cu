@@ -1516,12 +1516,19 @@ __device__ __noinline__ float pow_pos(float v, float e) { return v > 0.f ? powf(
 constexpr int kStatsEpiWarps = 16;                       // epilogue warps of the moments pass
 constexpr int kStatsThreads = 32 * (kStatsEpiWarps + 1);  // + one producer warp
 
-template <int DT>
+// EXACT: the exact branch of the W = 32 / 128 pooling pass instead (returns at once when the
+// moments pass settled the head sets): the same tiles, with each row's log-sum-exp known,
+// give the clamped entropy and the transient mass of PU:1452-1508 as one partial per
+// 64-key tile (the layout the reduction kernel sums), no moments.
+template <int DT, bool EXACT>
 __global__ void __launch_bounds__(kStatsThreads, 1)
     k_tc_stats(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, WinArgs a) {
   extern __shared__ char smem_raw[];
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
+  if constexpr (EXACT) {
+    if (*reinterpret_cast<volatile int32_t*>(&hdr->need_exact) == 0) return;
+  }
   int32_t* status = &hdr->status;
   const int m_tiles = (pl.G * pl.W) / 128;            // 128-row m-tiles of a KV group
   const int chunk = blockIdx.x, g = blockIdx.y / m_tiles, mtc = blockIdx.y % m_tiles;
@@ -1609,6 +1616,54 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
       }
     }
     __syncwarp();
+  } else if constexpr (EXACT) {
+    // ---------------- epilogue: clamped entropy and transient mass of this thread's row ----
+    // warp (lg, sp) holds keys [64 sp, 64 sp + 64) of each 256-key tile: one 64-key tile
+    const float rs = 1.0f / sqrtf((float)pl.D);
+    const int h = hfirst + row / pl.W;
+    const float L = __ldcg(reinterpret_cast<const float*>(a.ws + pl.off_lse) + h * pl.W + r);   // log2 units
+    float* epart = reinterpret_cast<float*>(a.ws + pl.off_epart);
+    float* mpart = reinterpret_cast<float*>(a.ws + pl.off_mpart);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
+    for (int i = 0; i < ntile; ++i) {
+      const int b = i & 1;
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&bar_full[b], (i >> 1) & 1, status))) break;
+      tc::fence_after_sync();
+      float ent = 0.f, mass = 0.f;
+      for (int c = sp * cw; c < (sp + 1) * cw; c += 32) {
+        float v[32];
+        __syncwarp();
+        tc::tmem_ld32(lane_base + (uint32_t)(b * TN + c), v);
+        if (c + 32 >= (sp + 1) * cw) {   // this warp's last load of the tile: release the buffer
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bar_tfree[b]);
+        }
+        const int jb = (t0 + i) * TN + c;
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          float x[2];
+          round_pair<DT>(v[k], v[k + 1], rs, x[0], x[1]);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = jb + k + e;
+            if (j <= lim) {
+              const float d = fmaf(x[e], kLog2e, -L);
+              const float p = ex2(d);
+              ent += (p >= 1e-8f) ? -p * d * kLn2 : kGeps;   // -c ln c, c = max(p, 1e-8)
+              if (j >= pl.s) mass += p;
+            } else if (j < pl.n) {
+              ent += kGeps;   // masked entry: probability 0, clamped to 1e-8
+            }
+          }
+        }
+      }
+      const int t64 = (t0 + i) * (TN / 64) + sp;   // cw == 64
+      if (t64 < pl.ncol_tiles) {
+        epart[((size_t)t64 * pl.H + h) * pl.W + r] = ent;
+        mpart[((size_t)t64 * pl.H + h) * pl.W + r] = mass;
+      }
+    }
   } else {
     // ---------------- epilogue: running moments of this thread's row ----------------
     const float rs = 1.0f / sqrtf((float)pl.D);
@@ -1803,6 +1858,13 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
     }
   }
 
+  if constexpr (EXACT) {
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tmem, ncols);
+    return;
+  }
   // merge the column splits of each row, then write this chunk's partial moments
   float4* part = reinterpret_cast<float4*>(a.ws + pl.off_stats);
   tc::fence_before_sync();
@@ -1866,7 +1928,7 @@ size_t tc_stats_smem(const Plan& pl, int TN, int S) {
   return 1024 + (size_t)2 * 128 * 128 + (size_t)S * 2 * TN * 128;
 }
 
-template <int DT>
+template <int DT, bool EXACT = false>
 static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
   WinArgs a = a0;
   const Plan& pl = a.pl;
@@ -1881,8 +1943,8 @@ static cudaError_t launch_tc_stats(const WinArgs& a0, cudaStream_t st) {
       !make_tmap(&tk, a.k, DT, pl.n, pl.Hkv, a.khs, a.kts, a.tc_tn))
     return cudaErrorInvalidResourceHandle;   // TMA descriptor encoding refused the layout
   const size_t smem = tc_stats_smem(pl, a.tc_tn, a.tc_stages);
-  { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_stats<DT>, smem); if (e != cudaSuccess) return e; }
-  k_tc_stats<DT><<<dim3(pl.nstat_chunks, pl.Hkv * m_tiles), kStatsThreads, smem, st>>>(tq, tk, a);
+  { const cudaError_t e = ensure_dynamic_smem((const void*)k_tc_stats<DT, EXACT>, smem); if (e != cudaSuccess) return e; }
+  k_tc_stats<DT, EXACT><<<dim3(pl.nstat_chunks, pl.Hkv * m_tiles), kStatsThreads, smem, st>>>(tq, tk, a);
   return cudaGetLastError();
 }
 
@@ -2426,7 +2488,6 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
   extern __shared__ char smem_raw[];
   const Plan& pl = a.pl;
   Header* hdr = reinterpret_cast<Header*>(a.ws);
-  if (*reinterpret_cast<volatile int32_t*>(&hdr->need_exact) != 0) return;   // the exact form runs
   int32_t* status = &hdr->status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int W = WIN;
@@ -2491,7 +2552,7 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
     // ---------------- producer: tiles, TMA loads and UMMA issue (one thread) ----------------
     if (warp == kPTEpiWarps && lane == 0) {
       const uint32_t idesc = tc::idesc_f16(DT == CKV_BF16, 128, NCOL);
-      uint32_t* ctr = &hdr->tile_ctr[0];
+      uint32_t* ctr = &hdr->tile_ctr[a.fixup_pass ? 1 : 0];
       int load_tile = -1;
       int next_tile = (int)atomicAdd(ctr, 1u);   // fetched one tile ahead: the atomic's latency hides
       int ld_vg = 0;                             // (half, group) of the next step to load (in order)
@@ -2750,12 +2811,15 @@ static cudaError_t launch_tc_pool_any(const WinArgs& a0, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// W = 32 / 128: the keys-on-lanes form as its own launch (returns at once when the head
-// sets need the exact recomputation, which the SIMT pass launched after it does).
+// W = 32 / 128: the keys-on-lanes form as its own launch.  The first pass always pools:
+// with the moments pass's head sets, which the exact branch (k_tc_stats<DT, true>, launched
+// before it) may overturn; the re-run returns at once unless they were overturned.
 template <int DT, int WIN>
 __global__ void __launch_bounds__(kPTThreads, 1)
     k_tc_pool_lanes(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                     const __grid_constant__ WinArgs a) {
+  const Header* hdr = reinterpret_cast<const Header*>(a.ws);
+  if (a.fixup_pass && *reinterpret_cast<const volatile int32_t*>(&hdr->fixup) == 0) return;
   tc_pool_t_body<DT, WIN>(tmq, tmk, a);
 }
 
@@ -3156,10 +3220,7 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
     } else if (row < nrows) {
       const int ch = (row - 2 * HW) / pl.W, rr = (row - 2 * HW) % pl.W;
       const int src = (ch == 1 && pl.hi_rows) ? 1 : 0;
-      // the SIMT pass (the exact branch beside a keys-on-lanes pass) writes one partial
-      // per 64-key tile, the keys-on-lanes forms one per 32 keys
-      const int nrs = (pl.lanes_pool && exact) ? pl.ncol_tiles : pl.rs_parts;
-      e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, nrs, (size_t)pl.W, q, kReduceStreams);
+      e = sum_parts(rspart + (size_t)src * pl.rs_parts * pl.W + rr, pl.rs_parts, (size_t)pl.W, q, kReduceStreams);
     }
     sp[q][lane] = e;
     __syncthreads();
@@ -3170,7 +3231,7 @@ __global__ void __launch_bounds__(32 * kReduceStreams) k_pool_reduce(WinArgs a) 
     }
     __syncthreads();   // sp is reused by the next block
   }
-  if ((pl.tc_pool || pl.lanes_pool) && !exact) {
+  if (pl.lanes_pool || (pl.tc_pool && !exact)) {
     // column sums and g totals behind the keys-on-lanes pooling pass: pool_blocks row-block
     // partials per key (4, or 8 for W = 128), one 64-key slice per warp, added in a fixed order
     const float* colpart = reinterpret_cast<const float*>(a.ws + pl.off_colpart);   // [2][pool_blocks][n_pad]
@@ -3263,11 +3324,17 @@ static cudaError_t launch_window_t(const WinArgs& a, int stage, cudaStream_t st)
         const cudaError_t e = stage == 1 ? launch_tc_pool_any<DT>(b, st) : launch_tc_pool<DT>(b, st);
         if (e != cudaSuccess) return e;
         launched = true;
-      } else if (pl.lanes_pool && stage == 1) {
-        // keys-on-lanes pooling (settled head sets); the SIMT pass below returns at once
-        // then, and runs the exact branch otherwise
+      } else if (pl.lanes_pool) {
+        // the exact branch's clamped entropy / mass on the tensor cores (returns at once when
+        // the moments pass settled the head sets), then keys-on-lanes pooling; the re-run
+        // pools again only when the exact sets differ
+        if (stage == 1) {
+          const cudaError_t e = launch_tc_stats<DT, true>(b, st);
+          if (e != cudaSuccess) return e;
+        }
         const cudaError_t e = launch_tc_pool_lanes<DT>(b, st);
         if (e != cudaSuccess) return e;
+        launched = true;
       }
     }
     if (!launched) k_window_pool<DT><<<pl.ncol_tiles, 256, pool_smem<DT>(pl), st>>>(b);

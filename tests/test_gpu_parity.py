@@ -643,6 +643,57 @@ def test_selection_ties_follow_torch_cuda(n, budget, mode):
     assert torch.equal(idx, ref)
 
 
+@pytest.mark.parametrize("W,B", [(32, 512), (128, 1024)])
+def test_exact_branch_other_windows(W, B, parity_report):
+    """Windows of 32 and 128 rows when the moments pass cannot settle the head sets
+    (header word need_exact = 1): the clamped entropy and transient mass are recomputed on
+    the tensor cores (the moments kernel in its exact form) beside the keys-on-lanes
+    pooling.  Query heads identical within each KV group tie their entropies, so the
+    10-head selection boundary falls inside a tied group; the kept set is checked against
+    the oracle."""
+    from submission_folder_b200.cluster import cli_cluster_kwargs
+    from submission_folder_b200.synth import make_layer
+    dev = _cuda()
+    n = 4096
+    q, k, v = make_layer(n, seed=W + 7, window=W, planted=32, dtype="bf16", device="cpu")
+    q = q.reshape(8, 4, *q.shape[1:])[:, :1].expand(8, 4, *q.shape[1:]).reshape(q.shape).contiguous()
+    p = CircuitKVCluster(**cli_cluster_kwargs(W, B)).params(n)
+    ko, vo, idx, sc = ops.score_evict(p, q.to(dev), k.to(dev), v.to(dev), want_scores=True)
+    torch.cuda.synchronize()
+    ws = ops._workspaces[(dev.type, dev.index)]
+    assert int(ws[56:60].cpu().view(torch.int32).item()) == 1   # Header.need_exact
+    assert ops.read_status(dev) == 0
+    op = O.Params(window_size=W, max_capacity_prompt=B)
+    r = O.update_kv(q.float().numpy(), k.float().numpy(), v.float().numpy(), 4, op, dtype="bf16")
+    check_kept(f"exact_w{W}", idx.cpu().numpy(), sc.cpu().numpy(), r.keep_idx, r.combined, r.qi, r.hi,
+               op, n, False, parity_report)
+
+
+@pytest.mark.parametrize("W", [32, 128])
+def test_speculated_head_set_wrong_other_windows(W, parity_report):
+    """The re-run path for windows of 32 and 128 rows: the moments pass's QI set differs
+    from the exact one (need_exact = 1 and fixup = 1 after the call) and the keys-on-lanes
+    pooling re-runs with the exact sets."""
+    from submission_folder_b200.cluster import cli_cluster_kwargs
+    dev = _cuda()
+    n, B = 4096, 512
+    q, k, v = _flip_case(n=n, W=W)
+    kw = cli_cluster_kwargs(W, B)
+    p = CircuitKVCluster(**kw).params(n)
+    to = lambda x: torch.from_numpy(x).to(torch.bfloat16).to(dev)
+    ko, vo, idx, sc = ops.score_evict(p, to(q), to(k), to(v), want_scores=True)
+    torch.cuda.synchronize()
+    ws = ops._workspaces[(dev.type, dev.index)]
+    assert int(ws[56:60].cpu().view(torch.int32).item()) == 1   # Header.need_exact
+    assert int(ws[12:16].cpu().view(torch.int32).item()) == 1   # Header.fixup
+    assert ops.read_status(dev) == 0
+    op = O.Params(**{a: b for a, b in kw.items() if a in O.Params.__dataclass_fields__})
+    r = O.update_kv(q, k, v, 4, op, dtype="bf16")
+    assert 12 in r.choice.qi_heads and 1 not in r.choice.qi_heads
+    check_kept(f"speculated_set_wrong_w{W}", idx.cpu().numpy(), sc.cpu().numpy(), r.keep_idx, r.combined, r.qi,
+               r.hi, op, n, False, parity_report)
+
+
 @pytest.mark.parametrize("n,W,B,dtype", [(8192, 32, 819, "bf16"), (6000, 128, 1024, "bf16"), (4096, 32, 512, "fp16"),
                                          (20000, 128, 2048, "fp16")])
 def test_keys_on_lanes_pooling_other_windows(n, W, B, dtype, parity_report):
