@@ -2521,23 +2521,6 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
   }
   __shared__ float4 smask[2 * kMaxHeads / 4];   // per KV group: QI, HI membership factors of its 4 heads
   __shared__ int s_hi_kind;                      // kHiMeanAll / kHiMean / kHiMax / kHiNone
-  if (threadIdx.x == 0)
-    s_hi_kind = pl.hi_rows == 0 ? kHiNone
-              : (hdr->hi_mode == 1 ? kHiMax
-                 : (hdr->hi_heads == (pl.H >= 64 ? ~0ull : (1ull << pl.H) - 1ull) ? kHiMeanAll : kHiMean));
-  if (threadIdx.x < 2 * ngroups) {
-    const int g = threadIdx.x >> 1;
-    const uint32_t m = (uint32_t)(((threadIdx.x & 1) ? hdr->hi_heads : hdr->qi_heads) >> (g * G)) & 0xFu;
-    smask[threadIdx.x] = make_float4((m & 1u) ? 1.f : 0.f, (m & 2u) ? 1.f : 0.f, (m & 4u) ? 1.f : 0.f, (m & 8u) ? 1.f : 0.f);
-  }
-  {   // negated log-sum-exp re-laid as [group][window row][head of the group] (one float4 per row)
-    const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);   // [H][W]
-    float* sl = reinterpret_cast<float*>(base + Ly.off_lse);
-    for (int i = threadIdx.x; i < pl.H * W; i += blockDim.x) {
-      const int h = i / W, r = i % W;
-      sl[((h / G) * W + r) * G + (h % G)] = -__ldcg(lse + i);
-    }
-  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -2607,6 +2590,27 @@ __device__ __forceinline__ void tc_pool_t_body(const CUtensorMap& tmq, const CUt
     __syncwarp();
   } else {
     // ---------------- epilogue: 16 warps ----------------
+    // while the producer's first loads and UMMAs run: the negated log-sum-exp re-laid as
+    // [group][window row][head of the group] (one float4 per row) and the head membership
+    // factors, then the epilogue warps meet at a named barrier (the producer does not wait)
+    if (threadIdx.x == 0)
+      s_hi_kind = pl.hi_rows == 0 ? kHiNone
+                : (hdr->hi_mode == 1 ? kHiMax
+                   : (hdr->hi_heads == (pl.H >= 64 ? ~0ull : (1ull << pl.H) - 1ull) ? kHiMeanAll : kHiMean));
+    if (threadIdx.x < 2 * ngroups) {
+      const int g = threadIdx.x >> 1;
+      const uint32_t m = (uint32_t)(((threadIdx.x & 1) ? hdr->hi_heads : hdr->qi_heads) >> (g * G)) & 0xFu;
+      smask[threadIdx.x] = make_float4((m & 1u) ? 1.f : 0.f, (m & 2u) ? 1.f : 0.f, (m & 4u) ? 1.f : 0.f, (m & 8u) ? 1.f : 0.f);
+    }
+    {
+      const float* lse = reinterpret_cast<const float*>(a.ws + pl.off_lse);   // [H][W]
+      float* sl = reinterpret_cast<float*>(base + Ly.off_lse);
+      for (int i = threadIdx.x; i < pl.H * W; i += 32 * kPTEpiWarps) {
+        const int h = i / W, r = i % W;
+        sl[((h / G) * W + r) * G + (h % G)] = -__ldcg(lse + i);
+      }
+    }
+    asm volatile("bar.sync 2, %0;" ::"r"(32 * kPTEpiWarps) : "memory");
     const int lg = warp & 3, q = warp >> 2;             // TMEM lane group (32 keys), column quarter
     const int key = 32 * lg + lane;                     // this thread's key within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
