@@ -328,7 +328,14 @@ struct HeadSets {
   int hm, nhi, certain;
 };
 
-__device__ HeadSets select_heads_warp(const ckv_params& p, int H, float ent, float mass, float bnd) {
+// The parameters the head selection reads (passed by value: the noinline function below
+// has one copy of its code, which a warm-up warp can run ahead of time).
+struct HeadSelParams {
+  int entropy_aware, top_k_heads, head_selection_mode, hi_pooling_mode, hi_top_k_heads;
+  float hi_mass_cdf, hi_mass_threshold;
+};
+
+__device__ __noinline__ HeadSets select_heads_warp_impl(const HeadSelParams p, int H, float ent, float mass, float bnd) {
   const int lane = threadIdx.x & 31;
   const bool valid = lane < H;
   const uint32_t all32 = H >= 32 ? 0xffffffffu : ((1u << H) - 1u);
@@ -416,6 +423,17 @@ __device__ HeadSets select_heads_warp(const ckv_params& p, int H, float ent, flo
   }
   r.certain = ok ? 1 : 0;
   return r;
+}
+
+CKV_DEV HeadSelParams head_sel_params(const ckv_params& p) {
+  HeadSelParams q;
+  q.entropy_aware = p.entropy_aware; q.top_k_heads = p.top_k_heads;
+  q.head_selection_mode = p.head_selection_mode; q.hi_pooling_mode = p.hi_pooling_mode;
+  q.hi_top_k_heads = p.hi_top_k_heads; q.hi_mass_cdf = p.hi_mass_cdf; q.hi_mass_threshold = p.hi_mass_threshold;
+  return q;
+}
+CKV_DEV HeadSets select_heads_warp(const ckv_params& p, int H, float ent, float mass, float bnd) {
+  return select_heads_warp_impl(head_sel_params(p), H, ent, mass, bnd);
 }
 
 // ---------------------------------------------------------------------------
@@ -595,6 +613,89 @@ __global__ void __launch_bounds__(256) k_window_stats(WinArgs a) {
   stats_finish(a, smem, bg.h0, pl.heads_per_batch, blockIdx.y, gridDim.x, gridDim.y);
 }
 
+// The last CTA of a head group: merges the chunk partials of the group's rows into their
+// log-sum-exp (to lse), the unclamped entropy, the transient mass and the clamp bound (to
+// rowE / rowM / rowB); thread tid of nthreads.  dry: the same loads and arithmetic with
+// every store switched off (the moments pass's warm-up warp runs it ahead of time, so the
+// instructions are in the SM's cache when a last CTA needs them: this code runs once per
+// layer on a few SMs and otherwise spends most of its time being fetched).
+__device__ __noinline__ void merge_group_rows(const float4* part, const float* minx, float* lse, float* rowE,
+                                              float* rowM, float* rowB, int H, int W, int n, int nchunks, int tc_min,
+                                              int i0, int nrows, int tid, int nthreads, bool dry) {
+  // tpr consecutive lanes share a row; each merges every tpr-th chunk, 8 loads in flight
+  int tpr = 1;
+  while (tpr < 8 && tpr * 2 * nrows <= nthreads) tpr *= 2;
+  const int sub = tid % tpr;
+  for (int base = 0; base < nrows * tpr; base += nthreads) {
+    const int li = (base + tid) / tpr;
+    const bool valid = li < nrows;
+    Moments M{-INFINITY, 0.f, 0.f, 0.f};
+    float xmin = INFINITY;
+    if (valid) {
+      for (int c0 = sub; c0 < nchunks; c0 += 8 * tpr) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (c0 + u * tpr < nchunks) v[u] = __ldcg(part + (size_t)(c0 + u * tpr) * H * W + i0 + li);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (c0 + u * tpr < nchunks) M = merge(M, Moments{v[u].x, v[u].y, v[u].z, v[u].w});
+        if (tc_min)
+          for (int u = 0; u < 8; ++u)
+            if (c0 + u * tpr < nchunks) xmin = fminf(xmin, __ldcg(minx + (size_t)(c0 + u * tpr) * H * W + i0 + li));
+      }
+    }
+    for (int o = 1; o < tpr; o <<= 1) {   // lanes of one row are consecutive within a warp
+      Moments O;
+      O.m = __shfl_xor_sync(0xffffffffu, M.m, o);
+      O.z = __shfl_xor_sync(0xffffffffu, M.z, o);
+      O.t = __shfl_xor_sync(0xffffffffu, M.t, o);
+      O.s = __shfl_xor_sync(0xffffffffu, M.s, o);
+      M = merge(M, O);
+      xmin = fminf(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
+    }
+    if (valid && sub == 0) {
+      const float l2z = log2f(M.z);
+      const float iz = 1.0f / M.z;
+      const float L = M.m + l2z;
+      const int r = li % W;
+      const float e = l2z * kLn2 - kLn2 * div_rcp(M.t, M.z, iz) + (float)(W - 1 - r) * kGeps;
+      const float m = 1.f - div_rcp(M.s, M.z, iz);
+      // the clamp at 1e-8 adds at most kGeps per visible entry to the row's entropy; a
+      // row whose smallest probability is above the clamp (with margin) adds nothing
+      const bool clamp_free = tc_min && fmaf(xmin, kLog2e, -L) >= kLog2Eps + 1e-3f;
+      const float bnd = clamp_free ? 0.f : (float)(n - W + r + 1) * kGeps;
+      if (!dry) {
+        lse[i0 + li] = L;
+        rowE[li] = e;
+        rowM[li] = m;
+        rowB[li] = bnd;
+      }
+    }
+  }
+}
+
+// Per-head means of the merged rows (warp `warp` of nw takes heads warp, warp + nw, ...);
+// dry as above.
+__device__ __noinline__ void group_head_means(const float* rowE, const float* rowM, const float* rowB, float* spec,
+                                              int H, int W, int tc_min, int h0, int nh, int warp, int nw, bool dry) {
+  const int lane = threadIdx.x & 31;
+  for (int hl = warp; hl < nh; hl += nw) {
+    float e = 0.f, m = 0.f, b = 0.f;
+    for (int r = lane; r < W; r += 32) {
+      e += rowE[hl * W + r]; m += rowM[hl * W + r]; b += rowB[hl * W + r];
+    }
+    e = warp_sum(e);
+    m = warp_sum(m);
+    b = warp_sum(b);
+    if (lane == 0 && !dry) {
+      spec[h0 + hl] = e / (float)W;
+      spec[H + h0 + hl] = m / (float)W;
+      spec[4 * H + h0 + hl] = tc_min ? b / (float)W : INFINITY;
+    }
+  }
+}
+
 // Last-CTA steps of the moments pass (PU:2905-2999).  The last CTA of each head
 // group merges the chunk partials of the group's rows into their log-sum-exp, the
 // unclamped entropy and the transient mass, and writes the group's per-head means;
@@ -617,71 +718,10 @@ __device__ void stats_finish(const WinArgs& a, char* smem, int h0, int nh, int g
   float* rowE = reinterpret_cast<float*>(smem);                  // [nrows]
   float* rowM = rowE + nrows;
   float* rowB = rowM + nrows;
-  // tpr consecutive lanes share a row; each merges every tpr-th chunk, 8 loads in flight
-  int tpr = 1;
-  while (tpr < 8 && tpr * 2 * nrows <= (int)blockDim.x) tpr *= 2;
-  const int sub = threadIdx.x % tpr;
-  for (int base = 0; base < nrows * tpr; base += blockDim.x) {
-    const int li = (base + threadIdx.x) / tpr;
-    const bool valid = li < nrows;
-    Moments M{-INFINITY, 0.f, 0.f, 0.f};
-    float xmin = INFINITY;
-    if (valid) {
-      for (int c0 = sub; c0 < pl.nstat_chunks; c0 += 8 * tpr) {
-        float4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (c0 + u * tpr < pl.nstat_chunks) v[u] = __ldcg(part + (size_t)(c0 + u * tpr) * pl.H * pl.W + i0 + li);
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (c0 + u * tpr < pl.nstat_chunks) M = merge(M, Moments{v[u].x, v[u].y, v[u].z, v[u].w});
-        if (a.tc_min)
-          for (int u = 0; u < 8; ++u)
-            if (c0 + u * tpr < pl.nstat_chunks)
-              xmin = fminf(xmin, __ldcg(minx + (size_t)(c0 + u * tpr) * pl.H * pl.W + i0 + li));
-      }
-    }
-    for (int o = 1; o < tpr; o <<= 1) {   // lanes of one row are consecutive within a warp
-      Moments O;
-      O.m = __shfl_xor_sync(0xffffffffu, M.m, o);
-      O.z = __shfl_xor_sync(0xffffffffu, M.z, o);
-      O.t = __shfl_xor_sync(0xffffffffu, M.t, o);
-      O.s = __shfl_xor_sync(0xffffffffu, M.s, o);
-      M = merge(M, O);
-      xmin = fminf(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
-    }
-    if (valid && sub == 0) {
-      const float l2z = log2f(M.z);
-      const float iz = 1.0f / M.z;
-      const float L = M.m + l2z;
-      lse[i0 + li] = L;
-      const int r = li % pl.W;
-      rowE[li] = l2z * kLn2 - kLn2 * div_rcp(M.t, M.z, iz) + (float)(pl.W - 1 - r) * kGeps;
-      rowM[li] = 1.f - div_rcp(M.s, M.z, iz);
-      // the clamp at 1e-8 adds at most kGeps per visible entry to the row's entropy; a
-      // row whose smallest probability is above the clamp (with margin) adds nothing
-      const bool clamp_free = a.tc_min && fmaf(xmin, kLog2e, -L) >= kLog2Eps + 1e-3f;
-      rowB[li] = clamp_free ? 0.f : (float)(pl.n - pl.W + r + 1) * kGeps;
-    }
-  }
+  merge_group_rows(part, minx, lse, rowE, rowM, rowB, pl.H, pl.W, pl.n, pl.nstat_chunks, a.tc_min, i0, nrows,
+                   threadIdx.x, blockDim.x, false);
   __syncthreads();
-  {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int hl = warp; hl < nh; hl += nw) {
-      float e = 0.f, m = 0.f, b = 0.f;
-      for (int r = lane; r < pl.W; r += 32) {
-        e += rowE[hl * pl.W + r]; m += rowM[hl * pl.W + r]; b += rowB[hl * pl.W + r];
-      }
-      e = warp_sum(e);
-      m = warp_sum(m);
-      b = warp_sum(b);
-      if (lane == 0) {
-        spec[h0 + hl] = e / (float)pl.W;
-        spec[pl.H + h0 + hl] = m / (float)pl.W;
-        spec[4 * pl.H + h0 + hl] = a.tc_min ? b / (float)pl.W : INFINITY;
-      }
-    }
-  }
+  group_head_means(rowE, rowM, rowB, spec, pl.H, pl.W, a.tc_min, h0, nh, threadIdx.x >> 5, blockDim.x >> 5, false);
   // the last group selects the heads
   __threadfence();
   __syncthreads();
@@ -1514,7 +1554,8 @@ template <> CKV_DEV F2 round_f2<CKV_FP16>(float a, float b, float rs) {
 __device__ __noinline__ float pow_pos(float v, float e) { return v > 0.f ? powf(v, e) : 0.f; }
 
 constexpr int kStatsEpiWarps = 16;                       // epilogue warps of the moments pass
-constexpr int kStatsThreads = 32 * (kStatsEpiWarps + 1);  // + one producer warp
+constexpr int kStatsWarmWarp = kStatsEpiWarps + 1;         // warm-up warp (after the producer warp)
+constexpr int kStatsThreads = 32 * (kStatsEpiWarps + 2);  // + one producer warp + the warm-up warp
 
 // EXACT: the exact branch of the W = 32 / 128 pooling pass instead (returns at once when the
 // moments pass settled the head sets): the same tiles, with each row's log-sum-exp known,
@@ -1616,6 +1657,29 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp == kStatsWarmWarp) {
+    // ---------------- warm-up warp: the last CTA's tail code, dry ----------------
+    // Runs merge_group_rows, group_head_means and the head selection with every store
+    // switched off while the epilogue works, so that if this CTA is the last of its group
+    // (or of all groups) those instructions are already in this SM's cache.  `dry` comes
+    // from an opaque move so the calls keep their one shared copy of the code.
+    if constexpr (!EXACT) {
+      int dryv;
+      asm volatile("mov.b32 %0, 1;" : "=r"(dryv));
+      const bool dry = dryv != 0;
+      const int nrows = pl.G * pl.W, i0 = g * pl.G * pl.W;
+      float* rw = reinterpret_cast<float*>(smem_raw);   // read only (stores are off)
+      merge_group_rows(reinterpret_cast<const float4*>(a.ws + pl.off_stats),
+                       reinterpret_cast<const float*>(a.ws + pl.off_minx), reinterpret_cast<float*>(a.ws + pl.off_lse),
+                       rw, rw + nrows, rw + 2 * nrows, pl.H, pl.W, pl.n, pl.nstat_chunks, 1, i0, nrows, lane,
+                       (int)blockDim.x, dry);
+      group_head_means(rw, rw + nrows, rw + 2 * nrows, reinterpret_cast<float*>(a.ws + pl.off_spec), pl.H, pl.W, 1,
+                       g * pl.G, pl.G, 0, 1, dry);
+      if (dry) {
+        const HeadSets hs = select_heads_warp(a.p, pl.H, (float)lane, 0.5f, 0.f);
+        asm volatile("" ::"l"(hs.qs), "l"(hs.hs), "r"(hs.certain));
+      }
+    }
   } else if constexpr (EXACT) {
     // ---------------- epilogue: clamped entropy and transient mass of this thread's row ----
     // warp (lg, sp) holds keys [64 sp, 64 sp + 64) of each 256-key tile: one 64-key tile
